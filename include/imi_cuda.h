@@ -1,0 +1,109 @@
+/* imi_cuda.h - C-ABI of the B200 decode engine for imi's brain token loop (the Seoul / LFM3 hybrid backbone).
+ *
+ * This is the drop-in boundary for imi's brain (reference: imi/core/seoul.h, struct imi_seoul). Plain pointers and
+ * sizes only; every call returns an imi_cuda_status and leaves a message for imi_cuda_error(). There is no CPU
+ * fallback: without a usable CUDA device every compute call fails with IMI_E_NODEV / IMI_E_CUDA.
+ *
+ * Model: one engine = one GGUF model resident on one GPU (imi_seoul::load, seoul.cpp:93-186).
+ * State: one conversation (attention caches, conv memory, position, latest hidden/logits) resident on the same GPU
+ *        (imi_seoul_state, seoul.h:21-26). The engine itself holds no conversation; imi_seoul's "own" conversation is a
+ *        state the C++ wrapper (imi_seoul_cuda.h) creates.
+ * Step semantics, float order and outputs follow imi_seoul exactly; see each entry point for the reference line. */
+#ifndef IMI_CUDA_H
+#define IMI_CUDA_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct imi_cuda_engine imi_cuda_engine;
+typedef struct imi_cuda_state imi_cuda_state;
+
+typedef enum {
+    IMI_OK = 0,
+    IMI_E_ARG = 1,       /* bad argument (null pointer, token out of range, n <= 0, states of another engine) */
+    IMI_E_FILE = 2,      /* GGUF file missing or unreadable (imi: load() returns false, seoul.cpp:94) */
+    IMI_E_FORMAT = 3,    /* a tensor is missing or has a type/shape the kernels do not read (seoul.cpp:96,162) */
+    IMI_E_CTX_FULL = 4,  /* position would pass n_ctx: nothing is stepped (imi prints "context full", seoul.cpp:353) */
+    IMI_E_CUDA = 5,      /* a CUDA call failed */
+    IMI_E_NOMEM = 6,     /* device (or pinned host) allocation failed */
+    IMI_E_TIMEOUT = 7,   /* a bounded device-side wait gave up (the kernel returned; the context stays usable) */
+    IMI_E_NODEV = 8      /* no CUDA device with the requested index */
+} imi_cuda_status;
+
+typedef struct {
+    int n_embd, n_vocab, n_ctx, n_layer, n_attn, n_head, n_head_kv, head_dim, n_ff, d_conv, n_swa, max_batch;
+    size_t weight_bytes;   /* bytes of layer tables + word table + small parameters on the device */
+    size_t state_bytes;    /* device bytes of one conversation state */
+} imi_cuda_info;
+
+/* Last error message of this thread (never NULL). */
+const char *imi_cuda_error(void);
+
+/* Load a GGUF model onto CUDA device `device` (replaces imi_seoul::load(path, threads, ctx_len), seoul.cpp:93).
+ * n_ctx: positions per conversation; max_batch: most conversations stepped together by imi_cuda_step_multi
+ * (and prefill chunk width of imi_cuda_step_batch is fixed at 128 independent of it). */
+imi_cuda_status imi_cuda_load(const char *gguf_path, int device, int n_ctx, int max_batch, imi_cuda_engine **out);
+void imi_cuda_free(imi_cuda_engine *e);                                     /* ~imi_seoul, seoul.cpp:687-689 */
+imi_cuda_status imi_cuda_get_info(const imi_cuda_engine *e, imi_cuda_info *out);
+
+/* A fresh conversation sized like the engine's (imi_seoul::new_state, seoul.cpp:193-201): position 0, zero conv memory. */
+imi_cuda_status imi_cuda_state_new(imi_cuda_engine *e, imi_cuda_state **out);
+void imi_cuda_state_free(imi_cuda_state *s);
+/* Position 0 and zero conv memory (imi_seoul::reset, seoul.cpp:188-191). */
+imi_cuda_status imi_cuda_state_reset(imi_cuda_state *s);
+int imi_cuda_state_pos(const imi_cuda_state *s);                            /* imi_seoul::pos */
+
+/* One position (imi_seoul::step, seoul.cpp:352-357): token >= 0 reads the word table row, else embd[n_embd] is the
+ * input vector. want_logits adds the word scores (and the greedy pick). IMI_E_CTX_FULL if pos >= n_ctx. */
+imi_cuda_status imi_cuda_step(imi_cuda_state *s, int32_t token, const float *embd, int want_logits);
+
+/* Two conversations one position each, every table read once for both (imi_seoul::step2, seoul.cpp:208-220).
+ * Each gets exactly the numbers its own imi_cuda_step would give. */
+imi_cuda_status imi_cuda_step2(imi_cuda_state *a, int32_t token_a, const float *embd_a, int logits_a,
+                               imi_cuda_state *b, int32_t token_b, const float *embd_b, int logits_b);
+
+/* n distinct conversations of one engine, one position each, one table read for all (n <= max_batch): the
+ * generalisation of step2 to the multi-session case. tokens[i] (or embd + i*n_embd when tokens is NULL or
+ * tokens[i] < 0), want_logits[i] (NULL = all). */
+imi_cuda_status imi_cuda_step_multi(imi_cuda_state *const *s, int n, const int32_t *tokens, const float *embd,
+                                    const int *want_logits);
+
+/* Read n positions of one conversation (imi_seoul::step_batch, seoul.cpp:490-517): tokens[n], or embd[n][n_embd].
+ * hidden and (if want_logits) logits are the last position's; hidden_all[n][n_embd] (host, optional) receives every
+ * position's hidden state. Positions are read in chunks; IMI_E_CTX_FULL (nothing more stepped) when a chunk would
+ * pass n_ctx, as seoul.cpp:498. */
+imi_cuda_status imi_cuda_step_batch(imi_cuda_state *s, const int32_t *tokens, const float *embd, int n,
+                                    int want_logits, float *hidden_all);
+
+/* Greedy decode on the device: `steps` positions for each of n conversations, each step's input being the previous
+ * step's pick (the caller loop of imi/core/hear.cpp:65-72 without a stop word). The first step reads tokens[i]
+ * (or, when tokens is NULL, each conversation's last pick). ids[steps][n] receives every pick. Logits of the last
+ * step stay readable. */
+imi_cuda_status imi_cuda_greedy(imi_cuda_state *const *s, int n, const int32_t *tokens, int steps, int32_t *ids);
+
+/* The latest outputs of a conversation (imi_seoul::hidden / ::logits, seoul.h:51): host copies. */
+imi_cuda_status imi_cuda_get_hidden(const imi_cuda_state *s, float *out /* n_embd */);
+imi_cuda_status imi_cuda_get_logits(const imi_cuda_state *s, float *out /* n_vocab */);
+/* The greedy pick of the latest step with logits: first maximum, lowest id on ties (imi/core/hear.cpp:67-68). */
+imi_cuda_status imi_cuda_get_argmax(const imi_cuda_state *s, int32_t *id, float *value);
+
+/* ---- kernel level (known-answer tests and the isolated table sweep) ---- */
+
+/* Cut x[n] to 8-bit per 32 values on the device (imi_q8::from, tables.cpp:100-109 with imi_cut32, vec.h:47-77):
+ * q[n] int8 codes, d[n/32] scales, s[n/32] = d * sum(q). Host pointers. */
+imi_cuda_status imi_cuda_q8_cut(int device, const float *x, int n, int8_t *q, float *d, float *s);
+
+/* A Q4_0 table (GGUF rows of 18-byte blocks, rows x cols) times ncol 8-bit inputs (xq[ncol][cols], xd/xs[ncol][cols/32])
+ * on the device with imi's 4-bit kernel semantics (imi_q4_group / imi_q4_group2 / imi_q4_group_batch,
+ * tables.cpp:127-177,419-477): out[ncol][rows]. Host pointers; block_dots (optional, ncol == 1) receives the integer
+ * dot of every (row, 32-block) pair [rows][cols/32]. */
+imi_cuda_status imi_cuda_q4_matvec(int device, const uint8_t *q4, int rows, int cols, const int8_t *xq,
+                                   const float *xd, const float *xs, int ncol, float *out, int32_t *block_dots);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,240 @@
+// Shared definitions of the B200 decode engine: per-step column descriptors, kernel argument blocks, and the exact
+// device math that reproduces imi's AVX2 float order (imi/core/vec.h, imi/core/tables.cpp, imi/core/seoul.cpp).
+//
+// Exactness rules used throughout (the library is built with --fmad=false, and every float operation that imi's
+// result depends on is written with an explicitly rounded intrinsic):
+//   * a*b+c that imi computes with _mm256_fmadd_ps  -> __fmaf_rn(a, b, c)
+//   * a*b, a+b, a-b, a/b computed separately         -> __fmul_rn, __fadd_rn, __fsub_rn, __fdiv_rn
+//   * sqrtf, 1/x                                      -> __fsqrt_rn, __fdiv_rn(1, x)
+//   * float <-> fp16 (F16C _cvtss_sh / _cvtph_ps)     -> __float2half_rn / __half2float (both exact or RNE)
+//   * round-half-even to int (_mm256_round_ps)        -> __float2int_rn
+//   * expf                                            -> exp() in double, rounded once to float (correctly rounded;
+//     glibc's expf agrees on all but ~0.06% of inputs)
+//   * cosf/sinf of the rotary angles                  -> tables built on the host with the C library's own cosf/sinf
+#pragma once
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace imi {
+
+constexpr int MV_THREADS = 256;            // threads of a table-read CTA
+constexpr int MV_STAGES = 2;               // weight stages in flight per CTA (TMA bulk copies)
+constexpr int MV_STAGE_BYTES = 36864;      // one K=8192 row group of 8 rows, or 32 rows of K=2048
+constexpr int MV_MAX_COLS = 8;             // inputs sharing one table read in the small-batch kernel
+constexpr int MV_SMEM_BUDGET = 113 * 1024; // two table-read CTAs fit one SM, so the next launch can prefetch early
+
+// Per-conversation scalars that live on the device (the rest of imi_seoul_state is device buffers).
+struct SessDev {
+    int pos;                   // positions read so far (imi_seoul::pos)
+    int next_token;            // greedy pick of the latest step with logits
+    unsigned long long amax;   // running argmax key of the step in flight (0 between steps)
+    float amax_val;
+    int pad;
+};
+
+// One input column of a step. Written by the host before each launch (or left in place for greedy replay).
+struct Col {
+    SessDev *s;
+    __half *kc, *vc;           // [n_attn][n_ctx][kvd]
+    float *ring;               // conv memory [n_conv][d_conv+1][n_embd]; slot of position p is p mod (d_conv+1)
+    float *hid_out;            // where this column's final hidden state goes (null = nowhere)
+    float *logits;             // word scores (null = not wanted)
+    const float *embd;         // device copy of the input vector when token == -1
+    int *picks;                // [n_ctx]: the greedy pick made at each position (written with word scores)
+    int token;                 // >= 0 word id, -1 embd, -2 the session's last pick
+    int off;                   // position = s->pos + off
+    int pos_inc;               // added to s->pos when the step ends
+    int pad;
+};
+
+enum Pro : int {
+    P_EMBED_NORM = 0,   // x = word row | embd; h = norm(x) * w_pre                       (seoul.cpp:363-365,404)
+    P_RESID_NORM = 1,   // x += norm(r) * w_post; h = norm(x) * w_pre                     (seoul.cpp:462-464,473+404)
+    P_CONV = 2,         // u = c * (b*x*w_last + sum_k state_k * w_k)                     (seoul.cpp:410-414)
+    P_CUT = 3,          // the input as it is                                             (seoul.cpp:457,469)
+    P_FINAL = 4,        // x += norm(fo) * w_post; hidden = norm(x) * out_norm            (seoul.cpp:473,476)
+    P_Q8IN = 5          // codes given (known-answer tests)
+};
+enum Epi : int { E_STORE = 0, E_SILU = 1, E_HEAD = 2 };
+
+struct MvArgs {
+    const uint8_t *W;          // table rows: [rows][cols/2 code bytes | cols/32 fp16 scales]
+    int rows, cols, row_bytes, unit, sr;   // sr: rows per stage
+    const Col *cols_d;
+    int ncol;
+    const float *in;           // prologue input vector per column
+    int in_stride;
+    float *xin, *xout;         // residual stream (per column)
+    int x_stride;
+    const float *wpost, *wpre;
+    float eps;
+    const uint8_t *emb;        // word table (same row layout) for P_EMBED_NORM
+    int emb_row_bytes;
+    const float *conv_w;       // [d_conv+1][n_embd]
+    int d_conv, conv_layer, n_embd;
+    int ring_layer;            // >= 0: write the conv memory slots of this layer from ring_src (bcx rows)
+    const float *ring_src;
+    int ring_src_stride;
+    const int8_t *q8_q;        // P_Q8IN: codes [ncol][cols], scales and sums [ncol][cols/32]
+    const float *q8_d, *q8_s;
+    int32_t *dots;             // optional: integer block dots [rows][cols/32] of column 0
+    float *out;
+    int out_stride;
+    unsigned int *done;        // CTA counter (E_HEAD finalize)
+    int *err;
+};
+
+struct AttnArgs {
+    const Col *cols_d;
+    int ncol;
+    const float *qkv;
+    int qkv_stride;
+    float *att;
+    int att_stride;
+    const float *q_norm, *k_norm;
+    float eps, scale;
+    const float *rope_cs, *rope_sn;   // [n_ctx][head_dim/2] for this layer's base (and frequency factors)
+    int ai, n_head, n_head_kv, head_dim, n_ctx, window;
+    int kv_fused;                     // 1: write K/V at the column's position here and use own copies for it
+    int *err;
+};
+
+struct FinalArgs {
+    const Col *cols_d;
+    int ncol;
+    const float *in;                  // fo per column
+    int in_stride;
+    const float *xin;                 // residual (per column)
+    int x_stride;
+    const float *wpost, *out_norm;
+    float eps;
+    int n_embd;
+};
+
+// ---- shared-memory plan of the table-read kernel (host and device agree on it) ----
+struct MvPlan {
+    int stage, bar, xq, xd, xs, fs, dd, vb, vo, red, total;
+};
+__host__ __device__ inline int align_up(int x, int a) { return (x + a - 1) / a * a; }
+__host__ __device__ inline MvPlan mv_plan(int cols, int sr, int nc, int vb_len) {
+    MvPlan p;
+    const int nb = cols / 32, ld = nb + 1;
+    int o = 0;
+    p.stage = o; o += MV_STAGES * MV_STAGE_BYTES;
+    p.bar = o;   o = align_up(o + 8 * MV_STAGES, 16);
+    p.xq = o;    o = align_up(o + nc * cols, 16);
+    p.xd = o;    o = align_up(o + 4 * nc * nb, 16);
+    p.xs = o;    o = align_up(o + 4 * nc * nb, 16);
+    p.fs = o;    o = align_up(o + 4 * nc * sr * ld, 16);
+    p.dd = o;    o = align_up(o + 4 * sr * ld, 16);
+    p.vb = o;    o = align_up(o + 4 * nc * vb_len, 16);
+    p.vo = o;    o = align_up(o + 4 * nc * sr, 16);
+    p.red = o;   o = align_up(o + 4 * 64 + 16 * MV_MAX_COLS * (MV_THREADS / 32), 16);
+    p.total = o;
+    return p;
+}
+
+#ifdef __CUDACC__
+// ---------------- exact scalar helpers ----------------
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+__device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
+__device__ __forceinline__ float exp_cr(float x) { return __double2float_rn(exp((double) x)); }
+
+// imi_rms_scale's AVX2 order (vec.h:20-28) for a vector in shared memory, n a multiple of 32, computed by ONE warp:
+// lane L accumulates x[L], x[L+32], ... with fma (the 4 x 8 lanes a0..a3), then (a0+a1)+(a2+a3) per lane of 8,
+// then imi_hsum's tree ((t0+t4)+(t2+t6)) + ((t1+t5)+(t3+t7)) (vec.h:12-16). Returns 1/sqrt(s/n + eps) to all lanes.
+__device__ __forceinline__ float warp_rms_scale(const float *x, int n, float eps) {
+    const int L = threadIdx.x & 31;
+    float a = 0.0f;
+    for (int i = L; i < n; i += 32) a = __fmaf_rn(x[i], x[i], a);
+    const unsigned F = 0xffffffffu;
+    const float a8 = __shfl_down_sync(F, a, 8), a16 = __shfl_down_sync(F, a, 16), a24 = __shfl_down_sync(F, a, 24);
+    const float t = __fadd_rn(__fadd_rn(a, a8), __fadd_rn(a16, a24));   // lanes 0..7
+    const float r = __fadd_rn(t, __shfl_down_sync(F, t, 4));             // lanes 0..3: t_m + t_{m+4}
+    const float q = __fadd_rn(r, __shfl_down_sync(F, r, 2));             // lane 0: r0+r2, lane 1: r1+r3
+    const float s = __fadd_rn(q, __shfl_down_sync(F, q, 1));             // lane 0
+    const float s0 = __shfl_sync(F, s, 0);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s0, (float) n), eps)));
+}
+
+// imi_cut32 (vec.h:47-77) of one 32-value block held one value per lane: d = max|x|/127, id = 1/d (0 if d == 0),
+// q = round-half-even(x * id); returns q; d and the code sum go to lane-uniform outputs.
+__device__ __forceinline__ int warp_cut32(float v, float &d, int &sum) {
+    const unsigned F = 0xffffffffu;
+    float amax = fabsf(v);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(F, amax, o));
+    d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    const int q = __float2int_rn(__fmul_rn(v, id));
+    int s = q;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(F, s, o);
+    sum = s;
+    return q;
+}
+
+// dot_h of seoul.cpp:29-35: 8 lane accumulators over the row in steps of 8, then imi_hsum's order.
+// q: floats (shared), k: one row of n fp16 loaded as uint4 (8 values each).
+template <int D>
+__device__ __forceinline__ float dot_h8(const float *q, const uint4 *k) {
+    float a[8];
+#pragma unroll
+    for (int l = 0; l < 8; l++) a[l] = 0.0f;
+#pragma unroll
+    for (int w = 0; w < D / 8; w++) {
+        const uint4 v = k[w];
+        const uint32_t u[4] = { v.x, v.y, v.z, v.w };
+#pragma unroll
+        for (int h = 0; h < 4; h++) {
+            a[2 * h] = __fmaf_rn(q[8 * w + 2 * h], h2f((uint16_t) (u[h] & 0xffff)), a[2 * h]);
+            a[2 * h + 1] = __fmaf_rn(q[8 * w + 2 * h + 1], h2f((uint16_t) (u[h] >> 16)), a[2 * h + 1]);
+        }
+    }
+    const float r0 = __fadd_rn(a[0], a[4]), r1 = __fadd_rn(a[1], a[5]), r2 = __fadd_rn(a[2], a[6]),
+                r3 = __fadd_rn(a[3], a[7]);
+    return __fadd_rn(__fadd_rn(r0, r2), __fadd_rn(r1, r3));
+}
+
+// ---------------- PTX wrappers: mbarrier, bulk async copy, programmatic dependent launch ----------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t) __cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// bounded wait (about one second at the boost clock): false if the phase never completed
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity) {
+    const long long t0 = clock64();
+    while (!mbar_try_wait(b, parity))
+        if (clock64() - t0 > 2000000000LL) return false;
+    return true;
+}
+// global -> shared bulk copy completing on an mbarrier (addresses 16-byte aligned, bytes a multiple of 16)
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+#endif
+
+}  // namespace imi

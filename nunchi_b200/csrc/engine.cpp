@@ -1,0 +1,900 @@
+// The decode engine's host side: GGUF load and repack, device residency, conversation states, the per-step kernel
+// schedule (captured once per shape into a CUDA graph and replayed), and the C-ABI of imi_cuda.h.
+//
+// Step schedule (one launch per stop of imi's step, seoul.cpp:402-488; every launch is a programmatic dependent of the
+// previous one):
+//   layer l, conv:      [in_proj: residual + attn_norm + cut] [out_proj: conv + cut] [gate_up: residual + ffn_norm
+//                       + cut, SiLU(gate)*up, conv memory write] [down: cut]
+//   layer l, attention: [qkvg: residual + attn_norm + cut] [attention] [o: cut] [gate_up] [down]
+//   end:                [word table: residual + out_norm -> hidden, cut, scores, first-max pick, position++]
+//                       or, without scores, [final norm, position++]
+#include "../../include/imi_cuda.h"
+#include "gguf_file.h"
+#include "launch.h"
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+namespace imi {
+void rope_table(int n_ctx, int n, float base, const float *ff, float *cs, float *sn);
+}
+using namespace imi;
+
+static thread_local std::string g_err;
+static imi_cuda_status fail(imi_cuda_status st, const std::string &msg) {
+    g_err = msg;
+    return st;
+}
+#define CK(x)                                                                                                 \
+    do {                                                                                                      \
+        cudaError_t e_ = (x);                                                                                 \
+        if (e_ != cudaSuccess) return fail(e_ == cudaErrorMemoryAllocation ? IMI_E_NOMEM : IMI_E_CUDA,        \
+                                           std::string(#x) + ": " + cudaGetErrorString(e_));                  \
+    } while (0)
+
+namespace {
+
+constexpr int STEP_COLS = 8;      // columns per launch (the small-batch table kernel's limit)
+constexpr int BATCH_GROUP = 64;   // step_batch checks the context per 64 positions, as seoul.cpp:496-498
+
+struct TableRef {
+    size_t off = 0;
+    int rows = 0, cols = 0, row_bytes = 0;
+};
+struct LayerRef {
+    bool conv = false, swa = false;
+    int ai = -1, ci = -1;
+    TableRef in_proj, out_proj, qkvg, o, gate_up, down;
+    size_t attn_norm = 0, post_attn_norm = 0, ffn_norm = 0, post_ffn_norm = 0, conv_w = 0, q_norm = 0, k_norm = 0;
+};
+
+}  // namespace
+
+struct imi_cuda_engine {
+    int device = 0, sm_count = 0;
+    cudaStream_t stream = nullptr;
+    int n_embd = 0, n_vocab = 0, n_ctx = 0, n_layer = 0, n_attn = 0, n_conv = 0, n_head = 0, n_head_kv = 0,
+        head_dim = 0, n_ff = 0, d_conv = 0, n_swa = 0, max_batch = 0;
+    float eps = 1e-5f, rope_base = 1e6f, rope_base_swa = 1e4f;
+    uint8_t *w = nullptr;
+    size_t w_bytes = 0;
+    std::vector<LayerRef> layers;
+    TableRef tok;
+    size_t out_norm = 0;
+    float *rope_cs = nullptr, *rope_sn = nullptr;   // [2][n_ctx][head_dim/2]: full layers, window layers
+    int big_n = 0;
+    float *X = nullptr, *big = nullptr, *y = nullptr, *att = nullptr, *act = nullptr, *fo = nullptr, *embd = nullptr,
+          *hid = nullptr;
+    Col *cols_d = nullptr, *cols_h = nullptr;
+    float *embd_h = nullptr;
+    unsigned *done = nullptr;
+    int *err = nullptr;
+    cudaEvent_t staged = nullptr;   // the last host->device copy of the staging buffers has run
+    std::map<int, cudaGraphExec_t> graphs;
+    size_t state_bytes = 0;
+    const float *f32(size_t off) const { return (const float *) (w + off); }
+    ~imi_cuda_engine();
+};
+
+struct imi_cuda_state {
+    imi_cuda_engine *e = nullptr;
+    void *mem = nullptr;
+    SessDev *s = nullptr;
+    __half *kc = nullptr, *vc = nullptr;
+    float *ring = nullptr, *hidden = nullptr, *logits = nullptr;
+    int *picks = nullptr;
+    int pos = 0;
+};
+
+imi_cuda_engine::~imi_cuda_engine() {
+    cudaSetDevice(device);
+    if (stream) cudaStreamSynchronize(stream);
+    for (auto &g : graphs) cudaGraphExecDestroy(g.second);
+    cudaFree(w);
+    cudaFree(rope_cs);
+    cudaFree(X);
+    cudaFree(cols_d);
+    cudaFreeHost(cols_h);
+    cudaFreeHost(embd_h);
+    if (staged) cudaEventDestroy(staged);
+    if (stream) cudaStreamDestroy(stream);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// load
+// ---------------------------------------------------------------------------------------------------------------
+namespace {
+
+// rows of Q4_0 tables, in order, into the engine's row layout: [cols/2 code bytes | cols/32 fp16 scales]. The code
+// bytes of block j keep the file's order (byte i: column i in the low nibble, column 16+i in the high one).
+void repack_rows(uint8_t *dst, const std::vector<std::pair<const gguf_tensor *, int>> &rows) {
+    for (size_t r = 0; r < rows.size(); r++) {
+        const gguf_tensor *t = rows[r].first;
+        const int nb = (int) (t->ne[0] / 32);
+        const uint8_t *src = t->data + (size_t) rows[r].second * t->row_bytes;
+        uint8_t *codes = dst + r * (size_t) nb * 18, *scales = codes + (size_t) nb * 16;
+        for (int j = 0; j < nb; j++) {
+            memcpy(scales + 2 * j, src + 18 * j, 2);
+            memcpy(codes + 16 * j, src + 18 * j + 2, 16);
+        }
+    }
+}
+
+struct Loader {
+    const gguf_file &f;
+    std::string err;
+    size_t off = 0;
+    std::vector<std::pair<size_t, const gguf_tensor *>> f32s;                                  // (offset, tensor)
+    std::vector<std::pair<size_t, std::vector<std::pair<const gguf_tensor *, int>>>> tables;   // (offset, rows)
+    std::vector<std::pair<size_t, const gguf_tensor *>> convs;                                 // transposed taps
+    explicit Loader(const gguf_file &ff) : f(ff) {}
+    size_t take(size_t n) {
+        const size_t o = off;
+        off = (off + n + 255) / 256 * 256;
+        return o;
+    }
+    const gguf_tensor *need(const std::string &name, int type) {
+        const gguf_tensor *t = f.tensor(name);
+        if (!t) { if (err.empty()) err = "missing tensor " + name; return nullptr; }
+        if (t->type != type || !t->data) {
+            if (err.empty()) err = name + ": type " + std::to_string(t->type) + " is not read by this engine";
+            return nullptr;
+        }
+        return t;
+    }
+    bool vec(const std::string &name, int64_t n, size_t &at) {
+        const gguf_tensor *t = need(name, T_F32);
+        if (!t) return false;
+        if (t->ne[0] * t->ne[1] * t->ne[2] * t->ne[3] != n) { err = name + ": unexpected size"; return false; }
+        at = take((size_t) n * 4);
+        f32s.push_back({ at, t });
+        return true;
+    }
+    bool table(TableRef &tr, const std::vector<std::pair<const gguf_tensor *, int>> &rows) {
+        if (rows.empty()) { err = "empty table"; return false; }
+        const int cols = (int) rows[0].first->ne[0];
+        for (auto &r : rows)
+            if (r.first->ne[0] != cols) { err = r.first->name + ": widths of a stacked table differ"; return false; }
+        if (cols % 256) { err = rows[0].first->name + ": width must be a multiple of 256"; return false; }
+        tr.rows = (int) rows.size();
+        tr.cols = cols;
+        tr.row_bytes = cols / 32 * 18;
+        if (2 * tr.row_bytes > MV_STAGE_BYTES) { err = rows[0].first->name + ": rows too wide"; return false; }
+        tr.off = take((size_t) tr.rows * tr.row_bytes);
+        tables.push_back({ tr.off, rows });
+        return true;
+    }
+    static void all_rows(std::vector<std::pair<const gguf_tensor *, int>> &o, const gguf_tensor *t) {
+        for (int r = 0; r < t->ne[1]; r++) o.push_back({ t, r });
+    }
+};
+
+}  // namespace
+
+static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int max_batch, imi_cuda_engine **out) {
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev <= 0) return fail(IMI_E_NODEV, "no CUDA device");
+    if (device < 0 || device >= ndev) return fail(IMI_E_NODEV, "no CUDA device " + std::to_string(device));
+    if (!path || n_ctx <= 0 || max_batch <= 0) return fail(IMI_E_ARG, "bad load arguments");
+    gguf_file f;
+    if (!f.open(path)) return fail(IMI_E_FILE, f.error);
+    std::unique_ptr<imi_cuda_engine> e(new imi_cuda_engine);
+    e->device = device;
+    e->n_ctx = n_ctx;
+    e->max_batch = max_batch;
+    CK(cudaSetDevice(device));
+    CK(cudaDeviceGetAttribute(&e->sm_count, cudaDevAttrMultiProcessorCount, device));
+
+    // hyperparameters: the keys and defaults of seoul.cpp:99-114
+    e->eps = f.key_f("lfm3.attention.layer_norm_rms_epsilon", 1e-5f);
+    e->rope_base = f.key_f("lfm3.rope.freq_base", 1e6f);
+    e->rope_base_swa = f.key_f("lfm3.rope.freq_base_swa", 1e4f);
+    e->n_swa = (int) f.key_i("lfm3.attention.sliding_window", 0);
+    e->d_conv = (int) f.key_i("lfm3.shortconv.l_cache", 7) - 1;
+    e->n_head = (int) f.key_i("lfm3.attention.head_count", 16);
+    e->head_dim = (int) f.key_i("lfm3.attention.key_length", 128);
+    e->n_layer = (int) f.key_i("lfm3.block_count", 0);
+    const gguf_value *swa_pat = f.value("lfm3.attention.sliding_window_pattern");
+
+    Loader L(f);
+    const gguf_tensor *te = L.need("token_embd.weight", T_Q4_0);
+    if (!te) return fail(IMI_E_FORMAT, L.err + " (the word table must be Q4_0 here)");
+    e->n_embd = (int) te->ne[0];
+    e->n_vocab = (int) te->ne[1];
+    if (e->n_embd % 256) return fail(IMI_E_FORMAT, "n_embd must be a multiple of 256");
+    if (e->n_layer <= 0 || e->d_conv < 1 || e->head_dim <= 0) return fail(IMI_E_FORMAT, "bad lfm3 hyperparameters");
+    const int E = e->n_embd;
+    {
+        std::vector<std::pair<const gguf_tensor *, int>> rows;
+        Loader::all_rows(rows, te);
+        if (!L.table(e->tok, rows)) return fail(IMI_E_FORMAT, L.err);
+    }
+    if (!L.vec("output_norm.weight", E, e->out_norm)) return fail(IMI_E_FORMAT, L.err);
+    const gguf_tensor *rf = f.tensor("rope_freqs.weight");
+    if (rf && (rf->type != T_F32 || rf->ne[0] != e->head_dim / 2)) return fail(IMI_E_FORMAT, "rope_freqs.weight: bad shape");
+
+    e->layers.resize(e->n_layer);
+    for (int il = 0; il < e->n_layer; il++) {
+        LayerRef &Lr = e->layers[il];
+        const std::string p = "blk." + std::to_string(il) + ".";
+        if (!L.vec(p + "attn_norm.weight", E, Lr.attn_norm) || !L.vec(p + "post_attention_norm.weight", E, Lr.post_attn_norm) ||
+            !L.vec(p + "ffn_norm.weight", E, Lr.ffn_norm) || !L.vec(p + "post_ffw_norm.weight", E, Lr.post_ffn_norm))
+            return fail(IMI_E_FORMAT, L.err);
+        std::vector<std::pair<const gguf_tensor *, int>> rows;
+        if (f.tensor(p + "shortconv.conv.weight")) {
+            Lr.conv = true;
+            Lr.ci = e->n_conv++;
+            const gguf_tensor *cw = L.need(p + "shortconv.conv.weight", T_F32);
+            if (!cw) return fail(IMI_E_FORMAT, L.err);
+            if (cw->ne[0] != e->d_conv + 1 || cw->ne[1] != E) return fail(IMI_E_FORMAT, p + "shortconv.conv.weight: bad shape");
+            Lr.conv_w = L.take((size_t) (e->d_conv + 1) * E * 4);
+            L.convs.push_back({ Lr.conv_w, cw });
+            const gguf_tensor *ip = L.need(p + "shortconv.in_proj.weight", T_Q4_0), *op = L.need(p + "shortconv.out_proj.weight", T_Q4_0);
+            if (!ip || !op) return fail(IMI_E_FORMAT, L.err);
+            if (ip->ne[0] != E || ip->ne[1] != 3 * E || op->ne[0] != E || op->ne[1] != E) return fail(IMI_E_FORMAT, p + "shortconv: bad shapes");
+            Loader::all_rows(rows, ip);
+            if (!L.table(Lr.in_proj, rows)) return fail(IMI_E_FORMAT, L.err);
+            rows.clear();
+            Loader::all_rows(rows, op);
+            if (!L.table(Lr.out_proj, rows)) return fail(IMI_E_FORMAT, L.err);
+        } else {
+            const gguf_tensor *q = L.need(p + "attn_q.weight", T_Q4_0), *k = L.need(p + "attn_k.weight", T_Q4_0),
+                              *v = L.need(p + "attn_v.weight", T_Q4_0), *g = L.need(p + "attn_gate.weight", T_Q4_0),
+                              *o = L.need(p + "attn_output.weight", T_Q4_0);
+            if (!q || !k || !v || !g || !o) return fail(IMI_E_FORMAT, L.err);
+            const int D = e->head_dim;
+            e->n_head_kv = (int) (k->ne[1] / D);   // seoul.cpp:153
+            if (q->ne[1] != (int64_t) e->n_head * D || k->ne[1] != v->ne[1] || k->ne[1] % D || g->ne[1] != e->n_head ||
+                o->ne[0] != (int64_t) e->n_head * D || o->ne[1] != E || q->ne[0] != E)
+                return fail(IMI_E_FORMAT, p + "attention: bad shapes");
+            if (e->n_head_kv <= 0 || e->n_head % e->n_head_kv) return fail(IMI_E_FORMAT, "heads do not group");
+            for (auto *t : { q, k, v, g }) Loader::all_rows(rows, t);   // q|k|v|gate stacked, seoul.cpp:147
+            if (!L.table(Lr.qkvg, rows)) return fail(IMI_E_FORMAT, L.err);
+            rows.clear();
+            Loader::all_rows(rows, o);
+            if (!L.table(Lr.o, rows)) return fail(IMI_E_FORMAT, L.err);
+            if (!L.vec(p + "attn_q_norm.weight", D, Lr.q_norm) || !L.vec(p + "attn_k_norm.weight", D, Lr.k_norm))
+                return fail(IMI_E_FORMAT, L.err);
+            Lr.swa = swa_pat && swa_pat->type == 9 && swa_pat->arr_type == 7 && (uint64_t) il < swa_pat->arr_n &&
+                     swa_pat->arr[il] != 0;
+            Lr.ai = e->n_attn++;
+        }
+        const gguf_tensor *fg = L.need(p + "ffn_gate.weight", T_Q4_0), *fu = L.need(p + "ffn_up.weight", T_Q4_0),
+                          *fd = L.need(p + "ffn_down.weight", T_Q4_0);
+        if (!fg || !fu || !fd) return fail(IMI_E_FORMAT, L.err);
+        e->n_ff = (int) fg->ne[1];
+        if (fu->ne[1] != e->n_ff || fg->ne[0] != E || fu->ne[0] != E || fd->ne[0] != e->n_ff || fd->ne[1] != E)
+            return fail(IMI_E_FORMAT, p + "ffn: bad shapes");
+        rows.clear();
+        for (int t = 0; t < e->n_ff; t++) { rows.push_back({ fg, t }); rows.push_back({ fu, t }); }   // (gate_i, up_i)
+        if (!L.table(Lr.gate_up, rows)) return fail(IMI_E_FORMAT, L.err);
+        rows.clear();
+        Loader::all_rows(rows, fd);
+        if (!L.table(Lr.down, rows)) return fail(IMI_E_FORMAT, L.err);
+    }
+    if (e->n_attn && !attn_supported(e->head_dim, e->n_head / e->n_head_kv, e->n_ctx))
+        return fail(IMI_E_FORMAT, "attention shape (head_dim " + std::to_string(e->head_dim) + ", group " +
+                                      std::to_string(e->n_head / std::max(1, e->n_head_kv)) + ", n_ctx " +
+                                      std::to_string(n_ctx) + ") not supported");
+    if ((e->n_head * e->head_dim) % 256) return fail(IMI_E_FORMAT, "n_head * head_dim must be a multiple of 256");
+    e->w_bytes = L.off;
+    CK(cudaMalloc(&e->w, e->w_bytes));
+
+    // upload: tables through a pinned staging buffer, small vectors directly
+    size_t stage_max = 0;
+    for (auto &t : L.tables) stage_max = std::max(stage_max, t.second.size() * (size_t) (t.second[0].first->ne[0] / 32 * 18));
+    for (auto &c : L.convs) stage_max = std::max(stage_max, (size_t) (c.second->ne[0] * c.second->ne[1] * 4));
+    uint8_t *stg = nullptr;
+    CK(cudaMallocHost(&stg, stage_max));
+    std::unique_ptr<uint8_t, decltype(&cudaFreeHost)> stg_guard(stg, cudaFreeHost);
+    for (auto &t : L.tables) {
+        repack_rows(stg, t.second);
+        CK(cudaMemcpy(e->w + t.first, stg, t.second.size() * (size_t) (t.second[0].first->ne[0] / 32 * 18),
+                      cudaMemcpyHostToDevice));
+    }
+    for (auto &c : L.convs) {   // file [channel][tap] -> [tap][channel] (seoul.cpp:136-141)
+        const int K = (int) c.second->ne[0], C = (int) c.second->ne[1];
+        float *dst = (float *) stg;
+        const float *src = (const float *) c.second->data;
+        for (int ch = 0; ch < C; ch++)
+            for (int k = 0; k < K; k++) dst[(size_t) k * C + ch] = src[(size_t) ch * K + k];
+        CK(cudaMemcpy(e->w + c.first, stg, (size_t) K * C * 4, cudaMemcpyHostToDevice));
+    }
+    for (auto &v : L.f32s) CK(cudaMemcpy(e->w + v.first, v.second->data, v.second->nbytes, cudaMemcpyHostToDevice));
+
+    // rotary tables: full layers use freq_base and rope_freqs, window layers freq_base_swa (seoul.cpp:428-429)
+    if (e->n_attn) {
+        const int D = e->head_dim;
+        const size_t per = (size_t) n_ctx * (D / 2);
+        std::vector<float> cs(2 * per), sn(2 * per);
+        imi::rope_table(n_ctx, D, e->rope_base, rf ? (const float *) rf->data : nullptr, cs.data(), sn.data());
+        imi::rope_table(n_ctx, D, e->rope_base_swa, nullptr, cs.data() + per, sn.data() + per);
+        CK(cudaMalloc(&e->rope_cs, 4 * per * 4));
+        e->rope_sn = e->rope_cs + 2 * per;
+        CK(cudaMemcpy(e->rope_cs, cs.data(), 2 * per * 4, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(e->rope_sn, sn.data(), 2 * per * 4, cudaMemcpyHostToDevice));
+    }
+
+    // per-column scratch
+    const int HD = e->n_head * e->head_dim, kvd = e->n_head_kv * e->head_dim;
+    e->big_n = std::max(3 * E, HD + 2 * kvd + e->n_head);
+    const size_t per_col = (size_t) 2 * E + e->big_n + E + HD + e->n_ff + E + E + E;
+    CK(cudaMalloc(&e->X, per_col * STEP_COLS * 4));
+    e->big = e->X + (size_t) 2 * E * STEP_COLS;
+    e->y = e->big + (size_t) e->big_n * STEP_COLS;
+    e->att = e->y + (size_t) E * STEP_COLS;
+    e->act = e->att + (size_t) HD * STEP_COLS;
+    e->fo = e->act + (size_t) e->n_ff * STEP_COLS;
+    e->embd = e->fo + (size_t) E * STEP_COLS;
+    e->hid = e->embd + (size_t) E * STEP_COLS;
+    CK(cudaMalloc(&e->cols_d, sizeof(Col) * STEP_COLS + 64));
+    e->done = (unsigned *) (e->cols_d + STEP_COLS);
+    e->err = (int *) (e->done + 4);
+    CK(cudaMemset(e->cols_d, 0, sizeof(Col) * STEP_COLS + 64));
+    CK(cudaMallocHost(&e->cols_h, sizeof(Col) * STEP_COLS));
+    CK(cudaMallocHost(&e->embd_h, (size_t) E * 4 * STEP_COLS));
+    memset(e->cols_h, 0, sizeof(Col) * STEP_COLS);
+    CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+    CK(cudaEventCreateWithFlags(&e->staged, cudaEventDisableTiming));
+    CK(prepare_kernels());
+    e->state_bytes = sizeof(SessDev) + (size_t) 2 * e->n_attn * n_ctx * kvd * 2 +
+                     (size_t) e->n_conv * (e->d_conv + 1) * E * 4 + (size_t) E * 4 + (size_t) e->n_vocab * 4 +
+                     (size_t) n_ctx * 4 + 6 * 256;
+    CK(cudaDeviceSynchronize());
+    *out = e.release();
+    return IMI_OK;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// the step schedule
+// ---------------------------------------------------------------------------------------------------------------
+namespace {
+
+enum StepKind { K_DECODE = 0, K_PREFILL = 1, K_HEAD_ONLY = 2 };
+
+int pick_sr(int pro, const TableRef &t, int unit, int ncol, int E) {
+    int sr = std::min(64, MV_STAGE_BYTES / t.row_bytes);
+    if (unit == 2) sr &= ~1;
+    while (sr > unit && table_smem(pro, t.cols, sr, ncol, E) > (size_t) MV_SMEM_BUDGET) sr -= unit;
+    return std::max(sr, unit);
+}
+
+cudaError_t table_launch(imi_cuda_engine *e, const TableRef &t, int pro, int epi, MvArgs a) {
+    a.W = e->w + t.off;
+    a.rows = t.rows;
+    a.cols = t.cols;
+    a.row_bytes = t.row_bytes;
+    a.unit = epi == E_SILU ? 2 : 1;
+    a.sr = pick_sr(pro, t, a.unit, a.ncol, e->n_embd);
+    const int grid = std::max(1, std::min(e->sm_count, t.rows / a.unit));
+    return launch_table(pro, epi, a, grid, e->stream, true);
+}
+
+cudaError_t enqueue_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind) {
+    const int E = e->n_embd, HD = e->n_head * e->head_dim;
+    MvArgs b = {};
+    b.cols_d = e->cols_d;
+    b.ncol = ncol;
+    b.eps = e->eps;
+    b.n_embd = E;
+    b.d_conv = e->d_conv;
+    b.ring_layer = -1;
+    b.emb = e->w + e->tok.off;
+    b.emb_row_bytes = e->tok.row_bytes;
+    b.x_stride = 2 * E;
+    b.err = e->err;
+    b.done = e->done;
+    float *X0 = e->X, *X1 = e->X + E;
+    cudaError_t r;
+    if (kind == K_HEAD_ONLY) {   // word scores of a hidden state already computed (seoul.cpp:507-516)
+        MvArgs a = b;
+        a.in = e->hid;
+        a.in_stride = E;
+        return table_launch(e, e->tok, P_CUT, E_HEAD, a);
+    }
+    for (int il = 0; il < e->n_layer; il++) {
+        const LayerRef &L = e->layers[il];
+        MvArgs a = b;
+        a.wpre = e->f32(L.attn_norm);
+        a.xout = X0;
+        a.out = e->big;
+        a.out_stride = e->big_n;
+        int pro = P_EMBED_NORM;
+        if (il > 0) {
+            pro = P_RESID_NORM;
+            a.in = e->fo;
+            a.in_stride = E;
+            a.xin = X1;
+            a.wpost = e->f32(e->layers[il - 1].post_ffn_norm);
+        }
+        if ((r = table_launch(e, L.conv ? L.in_proj : L.qkvg, pro, E_STORE, a)) != cudaSuccess) return r;
+        if (L.conv) {
+            a = b;
+            a.in = e->big;
+            a.in_stride = e->big_n;
+            a.conv_w = e->f32(L.conv_w);
+            a.conv_layer = L.ci;
+            a.out = e->y;
+            a.out_stride = E;
+            if ((r = table_launch(e, L.out_proj, P_CONV, E_STORE, a)) != cudaSuccess) return r;
+        } else {
+            AttnArgs t = {};
+            t.cols_d = e->cols_d;
+            t.ncol = ncol;
+            t.qkv = e->big;
+            t.qkv_stride = e->big_n;
+            t.att = e->att;
+            t.att_stride = HD;
+            t.q_norm = e->f32(L.q_norm);
+            t.k_norm = e->f32(L.k_norm);
+            t.eps = e->eps;
+            t.scale = 1.0f / sqrtf((float) e->head_dim);   // seoul.cpp:432
+            const size_t per = (size_t) e->n_ctx * (e->head_dim / 2);
+            t.rope_cs = e->rope_cs + (L.swa ? per : 0);
+            t.rope_sn = e->rope_sn + (L.swa ? per : 0);
+            t.ai = L.ai;
+            t.n_head = e->n_head;
+            t.n_head_kv = e->n_head_kv;
+            t.head_dim = e->head_dim;
+            t.n_ctx = e->n_ctx;
+            t.window = (L.swa && e->n_swa > 0) ? e->n_swa : 0;   // seoul.cpp:431
+            t.err = e->err;
+            t.kv_fused = kind == K_DECODE;
+            if (kind == K_PREFILL && (r = launch_kvwrite(t, e->stream, true)) != cudaSuccess) return r;
+            if ((r = launch_attn(t, e->stream, true)) != cudaSuccess) return r;
+            a = b;
+            a.in = e->att;
+            a.in_stride = HD;
+            a.out = e->y;
+            a.out_stride = E;
+            if ((r = table_launch(e, L.o, P_CUT, E_STORE, a)) != cudaSuccess) return r;
+        }
+        a = b;
+        a.in = e->y;
+        a.in_stride = E;
+        a.xin = X0;
+        a.xout = X1;
+        a.wpost = e->f32(L.post_attn_norm);
+        a.wpre = e->f32(L.ffn_norm);
+        a.out = e->act;
+        a.out_stride = e->n_ff;
+        if (L.conv) {
+            a.ring_layer = L.ci;
+            a.ring_src = e->big;
+            a.ring_src_stride = e->big_n;
+        }
+        if ((r = table_launch(e, L.gate_up, P_RESID_NORM, E_SILU, a)) != cudaSuccess) return r;
+        a = b;
+        a.in = e->act;
+        a.in_stride = e->n_ff;
+        a.out = e->fo;
+        a.out_stride = E;
+        if ((r = table_launch(e, L.down, P_CUT, E_STORE, a)) != cudaSuccess) return r;
+    }
+    const LayerRef &last = e->layers.back();
+    if (head) {
+        MvArgs a = b;
+        a.in = e->fo;
+        a.in_stride = E;
+        a.xin = X1;
+        a.wpost = e->f32(last.post_ffn_norm);
+        a.wpre = e->f32(e->out_norm);
+        return table_launch(e, e->tok, P_FINAL, E_HEAD, a);
+    }
+    FinalArgs fa = {};
+    fa.cols_d = e->cols_d;
+    fa.ncol = ncol;
+    fa.in = e->fo;
+    fa.in_stride = E;
+    fa.xin = X1;
+    fa.x_stride = 2 * E;
+    fa.wpost = e->f32(last.post_ffn_norm);
+    fa.out_norm = e->f32(e->out_norm);
+    fa.eps = e->eps;
+    fa.n_embd = E;
+    return launch_final(fa, e->stream, true);
+}
+
+imi_cuda_status run_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind, bool copy_cols) {
+    if (copy_cols) {
+        CK(cudaMemcpyAsync(e->cols_d, e->cols_h, sizeof(Col) * ncol, cudaMemcpyHostToDevice, e->stream));
+        CK(cudaEventRecord(e->staged, e->stream));
+    }
+    const int key = ncol * 8 + (head ? 4 : 0) + (int) kind;
+    auto it = e->graphs.find(key);
+    if (it == e->graphs.end()) {
+        cudaGraph_t g = nullptr;
+        CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+        const cudaError_t r = enqueue_step(e, ncol, head, kind);
+        const cudaError_t r2 = cudaStreamEndCapture(e->stream, &g);
+        if (r != cudaSuccess || r2 != cudaSuccess) {
+            if (g) cudaGraphDestroy(g);
+            return fail(IMI_E_CUDA, std::string("step capture: ") + cudaGetErrorString(r != cudaSuccess ? r : r2));
+        }
+        cudaGraphExec_t ge = nullptr;
+        const cudaError_t r3 = cudaGraphInstantiate(&ge, g, 0);
+        cudaGraphDestroy(g);
+        if (r3 != cudaSuccess) return fail(IMI_E_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(r3));
+        it = e->graphs.emplace(key, ge).first;
+    }
+    CK(cudaGraphLaunch(it->second, e->stream));
+    return IMI_OK;
+}
+
+// the staging buffers may be rewritten once the previous step's copy has run
+imi_cuda_status staging_wait(imi_cuda_engine *e) {
+    CK(cudaEventSynchronize(e->staged));
+    return IMI_OK;
+}
+
+Col decode_col(imi_cuda_state *s, int32_t token, bool has_embd, int c, bool want) {
+    imi_cuda_engine *e = s->e;
+    Col k = {};
+    k.s = s->s;
+    k.kc = s->kc;
+    k.vc = s->vc;
+    k.ring = s->ring;
+    k.hid_out = s->hidden;
+    k.logits = want ? s->logits : nullptr;
+    k.embd = has_embd ? e->embd + (size_t) c * e->n_embd : nullptr;
+    k.picks = s->picks;
+    k.token = token >= 0 ? token : (has_embd ? -1 : -2);
+    k.off = 0;
+    k.pos_inc = 1;
+    return k;
+}
+
+imi_cuda_status check_err(imi_cuda_engine *e) {
+    int h = 0;
+    CK(cudaMemcpyAsync(&h, e->err, 4, cudaMemcpyDeviceToHost, e->stream));
+    CK(cudaStreamSynchronize(e->stream));
+    if (h) {
+        CK(cudaMemsetAsync(e->err, 0, 4, e->stream));
+        return fail(IMI_E_TIMEOUT, "a device-side wait gave up (code " + std::to_string(h) + ")");
+    }
+    return IMI_OK;
+}
+
+// one decode step of n <= STEP_COLS distinct conversations
+imi_cuda_status step_group(imi_cuda_state *const *s, int n, const int32_t *tokens, const float *embd,
+                           const int *want, bool any_logits_forced) {
+    imi_cuda_engine *e = s[0]->e;
+    imi_cuda_status st;
+    if ((st = staging_wait(e)) != IMI_OK) return st;
+    bool head = any_logits_forced;
+    bool any_embd = false;
+    for (int c = 0; c < n; c++) {
+        const int32_t t = tokens ? tokens[c] : -1;
+        if (t >= e->n_vocab) return fail(IMI_E_ARG, "token out of range");
+        const bool he = t < 0;
+        if (he && !embd) return fail(IMI_E_ARG, "no token and no input vector");
+        if (he) memcpy(e->embd_h + (size_t) c * e->n_embd, embd + (size_t) c * e->n_embd, (size_t) e->n_embd * 4);
+        any_embd |= he;
+        const bool w = want ? want[c] != 0 : true;
+        head |= w;
+        e->cols_h[c] = decode_col(s[c], t, he, c, w);
+    }
+    if (any_embd) CK(cudaMemcpyAsync(e->embd, e->embd_h, (size_t) n * e->n_embd * 4, cudaMemcpyHostToDevice, e->stream));
+    if ((st = run_step(e, n, head, K_DECODE, true)) != IMI_OK) return st;
+    for (int c = 0; c < n; c++) s[c]->pos++;
+    return IMI_OK;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------------------------------------------
+// C-ABI
+// ---------------------------------------------------------------------------------------------------------------
+extern "C" {
+
+const char *imi_cuda_error(void) { return g_err.c_str(); }
+
+imi_cuda_status imi_cuda_load(const char *path, int device, int n_ctx, int max_batch, imi_cuda_engine **out) {
+    if (!out) return fail(IMI_E_ARG, "out is null");
+    *out = nullptr;
+    return load_impl(path, device, n_ctx, max_batch, out);
+}
+
+void imi_cuda_free(imi_cuda_engine *e) { delete e; }
+
+imi_cuda_status imi_cuda_get_info(const imi_cuda_engine *e, imi_cuda_info *o) {
+    if (!e || !o) return fail(IMI_E_ARG, "null argument");
+    o->n_embd = e->n_embd; o->n_vocab = e->n_vocab; o->n_ctx = e->n_ctx; o->n_layer = e->n_layer; o->n_attn = e->n_attn;
+    o->n_head = e->n_head; o->n_head_kv = e->n_head_kv; o->head_dim = e->head_dim; o->n_ff = e->n_ff;
+    o->d_conv = e->d_conv; o->n_swa = e->n_swa; o->max_batch = e->max_batch;
+    o->weight_bytes = e->w_bytes;
+    o->state_bytes = e->state_bytes;
+    return IMI_OK;
+}
+
+imi_cuda_status imi_cuda_state_new(imi_cuda_engine *e, imi_cuda_state **out) {
+    if (!e || !out) return fail(IMI_E_ARG, "null argument");
+    CK(cudaSetDevice(e->device));
+    std::unique_ptr<imi_cuda_state> s(new imi_cuda_state);
+    s->e = e;
+    const int E = e->n_embd, kvd = e->n_head_kv * e->head_dim;
+    size_t o = 0;
+    auto take = [&](size_t n) { const size_t r = o; o = (o + n + 255) / 256 * 256; return r; };
+    const size_t o_s = take(sizeof(SessDev)), o_k = take((size_t) e->n_attn * e->n_ctx * kvd * 2),
+                 o_v = take((size_t) e->n_attn * e->n_ctx * kvd * 2),
+                 o_r = take((size_t) e->n_conv * (e->d_conv + 1) * E * 4), o_h = take((size_t) E * 4),
+                 o_l = take((size_t) e->n_vocab * 4), o_p = take((size_t) e->n_ctx * 4);
+    CK(cudaMalloc(&s->mem, o));
+    uint8_t *m = (uint8_t *) s->mem;
+    s->s = (SessDev *) (m + o_s);
+    s->kc = (__half *) (m + o_k);
+    s->vc = (__half *) (m + o_v);
+    s->ring = (float *) (m + o_r);
+    s->hidden = (float *) (m + o_h);
+    s->logits = (float *) (m + o_l);
+    s->picks = (int *) (m + o_p);
+    CK(cudaMemsetAsync(s->mem, 0, o, e->stream));
+    CK(cudaStreamSynchronize(e->stream));
+    *out = s.release();
+    return IMI_OK;
+}
+
+void imi_cuda_state_free(imi_cuda_state *s) {
+    if (!s) return;
+    cudaSetDevice(s->e->device);
+    cudaStreamSynchronize(s->e->stream);
+    cudaFree(s->mem);
+    delete s;
+}
+
+imi_cuda_status imi_cuda_state_reset(imi_cuda_state *s) {
+    if (!s) return fail(IMI_E_ARG, "null state");
+    imi_cuda_engine *e = s->e;
+    CK(cudaSetDevice(e->device));
+    CK(cudaMemsetAsync(s->s, 0, sizeof(SessDev), e->stream));
+    CK(cudaMemsetAsync(s->ring, 0, (size_t) e->n_conv * (e->d_conv + 1) * e->n_embd * 4, e->stream));
+    s->pos = 0;
+    return IMI_OK;
+}
+
+int imi_cuda_state_pos(const imi_cuda_state *s) { return s ? s->pos : -1; }
+
+imi_cuda_status imi_cuda_step(imi_cuda_state *s, int32_t token, const float *embd, int want_logits) {
+    if (!s) return fail(IMI_E_ARG, "null state");
+    if (s->pos >= s->e->n_ctx) return fail(IMI_E_CTX_FULL, "context full (" + std::to_string(s->e->n_ctx) + ")");
+    CK(cudaSetDevice(s->e->device));
+    imi_cuda_state *const arr[1] = { s };
+    const int w = want_logits != 0;
+    return step_group(arr, 1, &token, embd, &w, false);
+}
+
+imi_cuda_status imi_cuda_step2(imi_cuda_state *a, int32_t ta, const float *ea, int la, imi_cuda_state *b, int32_t tb,
+                               const float *eb, int lb) {
+    if (!a || !b || a == b || a->e != b->e) return fail(IMI_E_ARG, "step2 needs two states of one engine");
+    imi_cuda_engine *e = a->e;
+    if (a->pos >= e->n_ctx || b->pos >= e->n_ctx) return fail(IMI_E_CTX_FULL, "context full (" + std::to_string(e->n_ctx) + ")");
+    CK(cudaSetDevice(e->device));
+    imi_cuda_state *const arr[2] = { a, b };
+    const int32_t t[2] = { ta, tb };
+    const int w[2] = { la != 0, lb != 0 };
+    std::vector<float> emb;
+    const float *ep = nullptr;
+    if (ta < 0 || tb < 0) {
+        emb.assign((size_t) 2 * e->n_embd, 0.0f);
+        if (ta < 0) { if (!ea) return fail(IMI_E_ARG, "no token and no input vector"); memcpy(emb.data(), ea, (size_t) e->n_embd * 4); }
+        if (tb < 0) { if (!eb) return fail(IMI_E_ARG, "no token and no input vector"); memcpy(emb.data() + e->n_embd, eb, (size_t) e->n_embd * 4); }
+        ep = emb.data();
+    }
+    return step_group(arr, 2, t, ep, w, false);
+}
+
+imi_cuda_status imi_cuda_step_multi(imi_cuda_state *const *s, int n, const int32_t *tokens, const float *embd,
+                                    const int *want_logits) {
+    if (!s || n <= 0) return fail(IMI_E_ARG, "no states");
+    imi_cuda_engine *e = s[0]->e;
+    if (n > e->max_batch) return fail(IMI_E_ARG, "more states than max_batch");
+    for (int i = 0; i < n; i++) {
+        if (!s[i] || s[i]->e != e) return fail(IMI_E_ARG, "states of another engine");
+        for (int j = 0; j < i; j++) if (s[j] == s[i]) return fail(IMI_E_ARG, "a state appears twice");
+        if (s[i]->pos >= e->n_ctx) return fail(IMI_E_CTX_FULL, "context full (" + std::to_string(e->n_ctx) + ")");
+    }
+    CK(cudaSetDevice(e->device));
+    for (int i0 = 0; i0 < n; i0 += STEP_COLS) {
+        const int m = std::min(STEP_COLS, n - i0);
+        std::vector<int32_t> t(m);
+        for (int c = 0; c < m; c++) t[c] = tokens ? tokens[i0 + c] : -1;
+        imi_cuda_status st = step_group(s + i0, m, t.data(), embd ? embd + (size_t) i0 * e->n_embd : nullptr,
+                                        want_logits ? want_logits + i0 : nullptr, false);
+        if (st != IMI_OK) return st;
+    }
+    return IMI_OK;
+}
+
+imi_cuda_status imi_cuda_step_batch(imi_cuda_state *s, const int32_t *tokens, const float *embd, int n, int want_logits,
+                                    float *hidden_all) {
+    if (!s || n <= 0 || (!tokens && !embd)) return fail(IMI_E_ARG, "bad step_batch arguments");
+    imi_cuda_engine *e = s->e;
+    const int E = e->n_embd;
+    CK(cudaSetDevice(e->device));
+    for (int g0 = 0; g0 < n; g0 += BATCH_GROUP) {
+        const int gn = std::min(BATCH_GROUP, n - g0);
+        if (s->pos + gn > e->n_ctx) return fail(IMI_E_CTX_FULL, "context full (" + std::to_string(e->n_ctx) + ")");
+        for (int i0 = g0; i0 < g0 + gn; i0 += STEP_COLS) {
+            const int m = std::min(STEP_COLS, g0 + gn - i0);
+            imi_cuda_status st;
+            if ((st = staging_wait(e)) != IMI_OK) return st;
+            for (int c = 0; c < m; c++) {
+                const int32_t t = tokens ? tokens[i0 + c] : -1;
+                if (t >= e->n_vocab) return fail(IMI_E_ARG, "token out of range");
+                if (t < 0) memcpy(e->embd_h + (size_t) c * E, embd + (size_t) (i0 + c) * E, (size_t) E * 4);
+                Col k = decode_col(s, t, t < 0, c, false);
+                k.hid_out = e->hid + (size_t) c * E;
+                k.off = c;
+                k.pos_inc = c == m - 1 ? m : 0;
+                e->cols_h[c] = k;
+            }
+            if (!tokens) CK(cudaMemcpyAsync(e->embd, e->embd_h, (size_t) m * E * 4, cudaMemcpyHostToDevice, e->stream));
+            if ((st = run_step(e, m, false, K_PREFILL, true)) != IMI_OK) return st;
+            CK(cudaMemcpyAsync(s->hidden, e->hid + (size_t) (m - 1) * E, (size_t) E * 4, cudaMemcpyDeviceToDevice, e->stream));
+            if (hidden_all) {
+                CK(cudaMemcpyAsync(hidden_all + (size_t) i0 * E, e->hid, (size_t) m * E * 4, cudaMemcpyDeviceToHost, e->stream));
+                CK(cudaStreamSynchronize(e->stream));
+            }
+            s->pos += m;
+        }
+    }
+    if (want_logits) {   // the last position's word scores (seoul.cpp:507-516)
+        imi_cuda_status st;
+        if ((st = staging_wait(e)) != IMI_OK) return st;
+        Col k = decode_col(s, 0, false, 0, true);
+        k.off = -1;
+        k.pos_inc = 0;
+        e->cols_h[0] = k;
+        CK(cudaMemcpyAsync(e->hid, s->hidden, (size_t) E * 4, cudaMemcpyDeviceToDevice, e->stream));
+        if ((st = run_step(e, 1, true, K_HEAD_ONLY, true)) != IMI_OK) return st;
+    }
+    return IMI_OK;
+}
+
+imi_cuda_status imi_cuda_greedy(imi_cuda_state *const *s, int n, const int32_t *tokens, int steps, int32_t *ids) {
+    if (!s || n <= 0 || steps <= 0) return fail(IMI_E_ARG, "bad greedy arguments");
+    imi_cuda_engine *e = s[0]->e;
+    if (n > STEP_COLS) return fail(IMI_E_ARG, "greedy runs at most 8 conversations per call");
+    for (int i = 0; i < n; i++) {
+        if (!s[i] || s[i]->e != e) return fail(IMI_E_ARG, "states of another engine");
+        if (s[i]->pos + steps > e->n_ctx) return fail(IMI_E_CTX_FULL, "context full (" + std::to_string(e->n_ctx) + ")");
+    }
+    CK(cudaSetDevice(e->device));
+    std::vector<int> pos0(n);
+    for (int i = 0; i < n; i++) pos0[i] = s[i]->pos;
+    imi_cuda_status st;
+    if ((st = staging_wait(e)) != IMI_OK) return st;
+    for (int c = 0; c < n; c++) e->cols_h[c] = decode_col(s[c], tokens ? tokens[c] : -2, false, c, true);
+    if ((st = run_step(e, n, true, K_DECODE, true)) != IMI_OK) return st;
+    for (int c = 0; c < n; c++) s[c]->pos++;
+    if (steps > 1) {
+        if ((st = staging_wait(e)) != IMI_OK) return st;
+        for (int c = 0; c < n; c++) e->cols_h[c].token = -2;
+        if ((st = run_step(e, n, true, K_DECODE, true)) != IMI_OK) return st;
+        for (int c = 0; c < n; c++) s[c]->pos++;
+        for (int k = 2; k < steps; k++) {
+            if ((st = run_step(e, n, true, K_DECODE, false)) != IMI_OK) return st;
+            for (int c = 0; c < n; c++) s[c]->pos++;
+        }
+    }
+    if (ids) {
+        std::vector<int32_t> tmp((size_t) steps);
+        for (int c = 0; c < n; c++) {
+            CK(cudaMemcpyAsync(tmp.data(), s[c]->picks + pos0[c], (size_t) steps * 4, cudaMemcpyDeviceToHost, e->stream));
+            CK(cudaStreamSynchronize(e->stream));
+            for (int k = 0; k < steps; k++) ids[(size_t) k * n + c] = tmp[k];
+        }
+    }
+    return check_err(e);
+}
+
+imi_cuda_status imi_cuda_get_hidden(const imi_cuda_state *s, float *out) {
+    if (!s || !out) return fail(IMI_E_ARG, "null argument");
+    CK(cudaSetDevice(s->e->device));
+    CK(cudaMemcpyAsync(out, s->hidden, (size_t) s->e->n_embd * 4, cudaMemcpyDeviceToHost, s->e->stream));
+    return check_err(s->e);
+}
+
+imi_cuda_status imi_cuda_get_logits(const imi_cuda_state *s, float *out) {
+    if (!s || !out) return fail(IMI_E_ARG, "null argument");
+    CK(cudaSetDevice(s->e->device));
+    CK(cudaMemcpyAsync(out, s->logits, (size_t) s->e->n_vocab * 4, cudaMemcpyDeviceToHost, s->e->stream));
+    return check_err(s->e);
+}
+
+imi_cuda_status imi_cuda_get_argmax(const imi_cuda_state *s, int32_t *id, float *value) {
+    if (!s || !id) return fail(IMI_E_ARG, "null argument");
+    CK(cudaSetDevice(s->e->device));
+    SessDev h;
+    CK(cudaMemcpyAsync(&h, s->s, sizeof h, cudaMemcpyDeviceToHost, s->e->stream));
+    imi_cuda_status st = check_err(s->e);
+    *id = h.next_token;
+    if (value) *value = h.amax_val;
+    return st;
+}
+
+imi_cuda_status imi_cuda_q8_cut(int device, const float *x, int n, int8_t *q, float *d, float *s) {
+    if (!x || !q || !d || !s || n <= 0 || n % 32) return fail(IMI_E_ARG, "bad q8_cut arguments");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) return fail(IMI_E_NODEV, "no CUDA device");
+    CK(cudaSetDevice(device));
+    uint8_t *m = nullptr;
+    const size_t nb = (size_t) n / 32;
+    CK(cudaMalloc(&m, (size_t) n * 4 + n + 8 * nb + 64));
+    float *dx = (float *) m;
+    int8_t *dq = (int8_t *) (m + (size_t) n * 4);
+    float *dd = (float *) (m + (size_t) n * 5 + (16 - (n * 5) % 16) % 16), *ds = dd + nb;
+    cudaError_t r = cudaMemcpy(dx, x, (size_t) n * 4, cudaMemcpyHostToDevice);
+    if (r == cudaSuccess) r = launch_q8_cut(dx, n, dq, dd, ds, 0);
+    if (r == cudaSuccess) r = cudaMemcpy(q, dq, n, cudaMemcpyDeviceToHost);
+    if (r == cudaSuccess) r = cudaMemcpy(d, dd, nb * 4, cudaMemcpyDeviceToHost);
+    if (r == cudaSuccess) r = cudaMemcpy(s, ds, nb * 4, cudaMemcpyDeviceToHost);
+    cudaFree(m);
+    if (r != cudaSuccess) return fail(IMI_E_CUDA, std::string("q8_cut: ") + cudaGetErrorString(r));
+    return IMI_OK;
+}
+
+imi_cuda_status imi_cuda_q4_matvec(int device, const uint8_t *q4, int rows, int cols, const int8_t *xq, const float *xd,
+                                   const float *xs, int ncol, float *out, int32_t *dots) {
+    if (!q4 || !xq || !xd || !xs || !out || rows <= 0 || cols <= 0 || cols % 256 || ncol < 1 || ncol > MV_MAX_COLS ||
+        (dots && ncol != 1))
+        return fail(IMI_E_ARG, "bad q4_matvec arguments (cols a multiple of 256, 1..8 inputs)");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) return fail(IMI_E_NODEV, "no CUDA device");
+    CK(cudaSetDevice(device));
+    CK(prepare_kernels());
+    const int nb = cols / 32, row_bytes = nb * 18;
+    std::vector<uint8_t> packed((size_t) rows * row_bytes);
+    for (int r = 0; r < rows; r++)
+        for (int j = 0; j < nb; j++) {
+            const uint8_t *src = q4 + ((size_t) r * nb + j) * 18;
+            uint8_t *row = packed.data() + (size_t) r * row_bytes;
+            memcpy(row + (size_t) nb * 16 + 2 * j, src, 2);
+            memcpy(row + 16 * j, src + 2, 16);
+        }
+    const size_t b_w = packed.size(), b_q = (size_t) ncol * cols, b_ds = (size_t) ncol * nb * 4,
+                 b_o = (size_t) ncol * rows * 4, b_dots = dots ? (size_t) rows * nb * 4 : 0;
+    auto al = [](size_t x) { return (x + 255) / 256 * 256; };
+    uint8_t *m = nullptr;
+    CK(cudaMalloc(&m, al(b_w) + al(b_q) + 2 * al(b_ds) + al(b_o) + al(b_dots) + al(sizeof(Col) * MV_MAX_COLS) + 256));
+    uint8_t *p = m;
+    uint8_t *dW = p; p += al(b_w);
+    int8_t *dq = (int8_t *) p; p += al(b_q);
+    float *dd = (float *) p; p += al(b_ds);
+    float *ds = (float *) p; p += al(b_ds);
+    float *dout = (float *) p; p += al(b_o);
+    int32_t *ddots = dots ? (int32_t *) p : nullptr; p += al(b_dots);
+    Col *dcols = (Col *) p; p += al(sizeof(Col) * MV_MAX_COLS);
+    int *derr = (int *) p;
+    cudaError_t r = cudaMemcpy(dW, packed.data(), b_w, cudaMemcpyHostToDevice);
+    if (r == cudaSuccess) r = cudaMemcpy(dq, xq, b_q, cudaMemcpyHostToDevice);
+    if (r == cudaSuccess) r = cudaMemcpy(dd, xd, b_ds, cudaMemcpyHostToDevice);
+    if (r == cudaSuccess) r = cudaMemcpy(ds, xs, b_ds, cudaMemcpyHostToDevice);
+    if (r == cudaSuccess) r = cudaMemset(dcols, 0, sizeof(Col) * MV_MAX_COLS + 256);
+    if (r == cudaSuccess) {
+        MvArgs a = {};
+        a.W = dW; a.rows = rows; a.cols = cols; a.row_bytes = row_bytes; a.unit = 1;
+        a.cols_d = dcols; a.ncol = ncol; a.q8_q = dq; a.q8_d = dd; a.q8_s = ds; a.dots = ddots;
+        a.out = dout; a.out_stride = rows; a.err = derr; a.ring_layer = -1;
+        TableRef t; t.rows = rows; t.cols = cols; t.row_bytes = row_bytes;
+        a.sr = pick_sr(P_Q8IN, t, 1, ncol, 0);
+        int sms = 148;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+        r = launch_table(P_Q8IN, E_STORE, a, std::max(1, std::min(sms, rows)), 0, false);
+    }
+    if (r == cudaSuccess) r = cudaMemcpy(out, dout, b_o, cudaMemcpyDeviceToHost);
+    if (r == cudaSuccess && dots) r = cudaMemcpy(dots, ddots, b_dots, cudaMemcpyDeviceToHost);
+    int herr = 0;
+    if (r == cudaSuccess) r = cudaMemcpy(&herr, derr, 4, cudaMemcpyDeviceToHost);
+    cudaFree(m);
+    if (r != cudaSuccess) return fail(IMI_E_CUDA, std::string("q4_matvec: ") + cudaGetErrorString(r));
+    if (herr) return fail(IMI_E_TIMEOUT, "q4_matvec: a device-side wait gave up");
+    return IMI_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,16 @@
+// Host entry points of the kernels (kernels.cu).
+#pragma once
+#include "common.cuh"
+
+namespace imi {
+// one table read; `pro` / `epi` pick the input preparation and the output stage (common.cuh: Pro, Epi)
+cudaError_t launch_table(int pro, int epi, const MvArgs &a, int grid, cudaStream_t st, bool pdl);
+size_t table_smem(int pro, int cols, int sr, int ncol, int n_embd);
+int table_nc_slot(int ncol);
+cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st, bool pdl);
+bool attn_supported(int head_dim, int grp, int n_ctx);
+cudaError_t launch_kvwrite(const AttnArgs &a, cudaStream_t st, bool pdl);
+cudaError_t launch_final(const FinalArgs &a, cudaStream_t st, bool pdl);
+cudaError_t prepare_kernels();
+cudaError_t launch_q8_cut(const float *x, int n, int8_t *q, float *d, float *s, cudaStream_t st);
+}  // namespace imi
