@@ -1,0 +1,317 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 decode engine for imi's brain token loop.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload ride2|b1]
+
+Workload (the batch-2 "riding" step): the Seoul-shaped synthetic backbone (seed 0);
+conversation A prefilled with 1024 random ids (seed 1), conversation B with 256 (seed 2); then every timed step is
+one step2 (imi_seoul::step2, seoul.cpp:208): both conversations advance one greedy position on one read of every
+table. `--workload b1` runs configs[0] instead (32-token prompt, one conversation). Under torchrun each rank runs
+the same workload on its own GPU (whole conversations per GPU, no collective): weak scaling.
+
+One JSON line on rank 0: `value` = tokens/s of the whole job with everything resident on the device (CUDA events on
+the engine's stream, max over ranks); `e2e` = the same through the public step2 + argmax calls with host token input
+and a host read of both picks every step; `roofline` = the table-read kernel's bandwidth against the measured HBM
+peak; `cpu_baseline` = the reference's own CPU code (oracle/_ref) on this host.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+A_PROMPT, B_PROMPT, B1_PROMPT = 1024, 256, 32
+KV_BYTES_PER_POS = None   # filled from the engine shape
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["ride2", "b1"], default="ride2")
+    ap.add_argument("--cpu-steps", type=int, default=0, help="reference CPU sample size in steps (0 = auto)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+class Ranks:
+    """RANK / WORLD_SIZE / LOCAL_RANK from torchrun; host-side barrier and max over a gloo group."""
+
+    def __init__(self):
+        self.rank = int(os.environ.get("RANK", 0))
+        self.world = int(os.environ.get("WORLD_SIZE", 1))
+        self.local = int(os.environ.get("LOCAL_RANK", 0))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+            self.dist = dist
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max(self, x: float) -> float:
+        if self.world == 1:
+            return x
+        import torch
+        t = torch.tensor([x], dtype=torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.world > 1:
+            self.dist.destroy_process_group()
+
+
+class Clocks:
+    """nvidia-smi samples every 200 ms while the timed region runs (median SM clock under load, throttle reasons)."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.proc, self.path = index, None, None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(prefix="imi_clocks_", suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.index), "-f", self.path],
+                                         stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        self.proc.wait()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                p = [x.strip() for x in line.split(",")]
+                if len(p) >= 10:
+                    rows.append(p)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        busy = [r for r in rows if (num(r[4]) or 0) > 0] or rows
+        sm = [num(r[1]) for r in busy if num(r[1])]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for r in rows for k in range(4) if r[6 + k].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": num(rows[0][2]),
+                "samples": len(rows), "reasons": reasons}
+
+
+def peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def workload_desc(args) -> dict:
+    if args.workload == "ride2":
+        return {"workload": "configs[1] riding step2: Seoul-shaped Q4_0 backbone (seed 0), conversation A after a "
+                            f"{A_PROMPT}-id prompt, B after {B_PROMPT} ids, greedy, one table read per step for both",
+                "tokens_per_step": 2, "prompts": [A_PROMPT, B_PROMPT]}
+    return {"workload": f"configs[0] batch-1 greedy decode: Seoul-shaped Q4_0 backbone (seed 0), {B1_PROMPT}-id prompt",
+            "tokens_per_step": 1, "prompts": [B1_PROMPT]}
+
+
+def step_bytes(info, positions) -> int:
+    """Algorithmic HBM bytes of one step: every weight byte once, plus each conversation's K/V read over its
+    positions and written at the new one, plus the conv memory read and written."""
+    kvd = info.n_head_kv * info.head_dim
+    kv = sum((p + 1) * info.n_attn * kvd * 2 * 2 + info.n_attn * kvd * 2 * 2 for p in positions)
+    conv = len(positions) * (info.n_layer - info.n_attn) * 2 * info.d_conv * info.n_embd * 4
+    return int(info.weight_bytes + kv + conv)
+
+
+def run_ours(args, ranks: Ranks) -> dict:
+    import torch
+    import nunchi_b200 as nb
+    from nunchi_b200 import synth
+    torch.cuda.set_device(ranks.local)
+    wl = workload_desc(args)
+    prompts = wl["prompts"]
+    n_ctx = max(prompts) + args.warmup + 2 * args.steps + 16
+    path = synth.cached_gguf("seoul", 0)
+    eng = nb.Engine(path, device=ranks.local, n_ctx=n_ctx, max_batch=8)
+    info = eng.info
+    states = [eng.new_state() for _ in prompts]
+    for i, (s, n) in enumerate(zip(states, prompts)):
+        s.step_batch(synth.random_ids(n, info.n_vocab, 1 + i), want_logits=True)
+    st = torch.cuda.ExternalStream(eng.stream)
+    ev = lambda: torch.cuda.Event(enable_timing=True)   # noqa: E731
+    nb.greedy(states, args.warmup)
+    torch.cuda.synchronize()
+    ranks.barrier()
+    pos0 = [s.pos for s in states]
+    clocks = Clocks(ranks.local)
+    clocks.start()
+    e0, e1 = ev(), ev()
+    e0.record(st)
+    nb.greedy(states, args.steps)
+    e1.record(st)
+    e1.synchronize()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ranks.barrier()
+    ms = ranks.max(e0.elapsed_time(e1))
+    tps = wl["tokens_per_step"]
+    value = ranks.world * tps * args.steps / (ms / 1e3)
+    mid = [p + args.steps // 2 for p in pos0]
+    out = {"ms": ms, "value": value, "clocks": clk, "info": info, "mid_positions": mid}
+    out["step_bytes"] = step_bytes(info, mid)
+    out["launches"] = eng.launches_per_step(len(states)) * args.steps
+    # end to end through the public API: host token in, step, host read of the pick, every step
+    if not args.no_e2e:
+        picks = [s.argmax()[0] for s in states]
+        ranks.barrier()
+        e2, e3 = ev(), ev()
+        torch.cuda.synchronize()
+        e2.record(st)
+        for _ in range(args.steps):
+            if len(states) == 2:
+                nb.step2(states[0], picks[0], None, True, states[1], picks[1], None, True)
+            else:
+                states[0].step(picks[0])
+            picks = [s.argmax()[0] for s in states]
+        e3.record(st)
+        e3.synchronize()
+        ms_e2e = ranks.max(e2.elapsed_time(e3))
+        col_bytes, sess_bytes = 80, 24
+        out["e2e"] = {"value": ranks.world * tps * args.steps / (ms_e2e / 1e3), "unit": "tok/s",
+                      "h2d_bytes_per_step": col_bytes * len(states), "d2h_bytes_per_step": (sess_bytes + 4) * len(states),
+                      "ms_per_step": ms_e2e / args.steps}
+    # the table-read kernel alone: every layer table back to back (imi_seoul::bench_tables)
+    t_ms, t_bytes = eng.bench_tables(ncol=len(states), reps=20)
+    out["tables"] = {"ms": t_ms, "bytes": t_bytes}
+    for s in states:
+        s.close()
+    eng.close()
+    return out
+
+
+def run_reference_cpu(args, steps: int) -> dict:
+    """The reference's own CPU path (imi/core/seoul.cpp + tables.cpp compiled from the reference tree into
+    oracle/_ref) on this host's cores: the same workload, `steps` timed positions after the same prompts."""
+    import oracle
+    from nunchi_b200 import synth
+    wl = workload_desc(args)
+    prompts = wl["prompts"]
+    threads = os.cpu_count() or 1
+    if not oracle.reference_available():
+        raise RuntimeError("oracle/_ref/libimi_ref.so is not built")
+    n_ctx = max(prompts) + steps + 8
+    r = oracle.Reference(synth.cached_gguf("seoul", 0), n_ctx=n_ctx, threads=threads)
+    t0 = time.perf_counter()
+    other = r.new_state() if len(prompts) == 2 else None
+    if other is not None:   # B's prompt through the brain's own conversation, then parked in `other`
+        r.step_batch(synth.random_ids(prompts[1], r.n_vocab, 2), want_logits=True)
+        r.swap_state(other)
+    r.step_batch(synth.random_ids(prompts[0], r.n_vocab, 1), want_logits=True)
+    prefill_s = time.perf_counter() - t0
+    ta = int(np.argmax(r.logits))
+    tb = int(np.argmax(other.logits)) if other is not None else None
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        if other is not None:
+            r.step2(ta, None, True, other, tb, None, True)
+            ta, tb = int(np.argmax(r.logits)), int(np.argmax(other.logits))
+        else:
+            r.step(ta)
+            ta = int(np.argmax(r.logits))
+    dt = time.perf_counter() - t0
+    tps = wl["tokens_per_step"]
+    return {"value": tps * steps / dt, "unit": "tok/s", "cores": threads, "kind": "reference",
+            "sample": f"{steps} steps ({tps * steps} tokens) of the same workload after the same prompts "
+                      f"(prefill {prefill_s:.1f} s, not timed); imi_seoul from the reference's seoul.cpp/tables.cpp, "
+                      f"AVX2, {threads} threads", "ms_per_step": dt / steps * 1e3}
+
+
+def cpu_steps(args) -> int:
+    if args.cpu_steps:
+        return args.cpu_steps
+    return 64 if args.workload == "ride2" else 128
+
+
+def main():
+    args = parse()
+    ranks = Ranks()
+    wl = workload_desc(args)
+    metric = ("decode tok/s, batch-2 riding step (step2), Seoul-shaped Q4_0 backbone" if args.workload == "ride2"
+              else "decode tok/s, batch-1 greedy step, Seoul-shaped Q4_0 backbone")
+    base = {"metric": metric, "unit": "tok/s", "n_gpus": ranks.world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int4 x int8 -> int32 block dots, fp32 scale and accumulate", "data": "synthetic",
+            "config": {"workload": wl["workload"], "parallelism": f"whole conversations per GPU x{ranks.world}, "
+                       "no collective", "l2": "no flush: every step reads ~696 MB of weights (> 126 MB L2)"}}
+    if args.impl == "reference":
+        if ranks.rank != 0:
+            ranks.close()
+            return
+        ref = run_reference_cpu(args, args.steps)
+        line = dict(base, impl="reference", value=ref["value"], ms_per_step=ref["ms_per_step"], n_gpus=ranks.world,
+                    cpu_baseline={k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                    e2e={"value": ref["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
+        print(json.dumps(line), flush=True)
+        ranks.close()
+        return
+    r = run_ours(args, ranks)
+    pk = peaks()
+    t_gbs = r["tables"]["bytes"] / (r["tables"]["ms"] / 1e3) / 1e9
+    step_ms = r["ms"] / args.steps
+    line = dict(base, value=r["value"], ms_per_step=step_ms, gpu_launches=r["launches"], clocks=r["clocks"])
+    line["roofline"] = {
+        "kernel": "k_table (every layer table of a step, read back to back: imi_seoul::bench_tables)",
+        "bound": "hbm", "achieved": t_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": t_gbs / pk["hbm_gbs"],
+        "peak_source": pk["source"], "traffic": None,
+        "algorithmic_bytes_per_launch": r["tables"]["bytes"], "launch_ms": r["tables"]["ms"]}
+    sb = r["step_bytes"]
+    line["step_roofline"] = {"bytes_per_step": sb, "achieved_gbs": sb / (step_ms / 1e3) / 1e9,
+                             "frac": sb / (step_ms / 1e3) / 1e9 / pk["hbm_gbs"], "peak_source": pk["source"]}
+    if "e2e" in r:
+        line["e2e"] = r["e2e"]
+    if ranks.rank == 0 and ranks.world == 1 and not args.no_cpu_baseline:
+        try:
+            ref = run_reference_cpu(args, cpu_steps(args))
+            line["cpu_baseline"] = {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        except Exception as ex:   # the reference build is missing: say so, keep the GPU line
+            line["cpu_baseline"] = {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference",
+                                    "sample": f"unavailable: {ex}"}
+    if ranks.rank == 0:
+        print(json.dumps(line), flush=True)
+    ranks.close()
+
+
+if __name__ == "__main__":
+    main()

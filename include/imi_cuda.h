@@ -90,6 +90,17 @@ imi_cuda_status imi_cuda_get_logits(const imi_cuda_state *s, float *out /* n_voc
 /* The greedy pick of the latest step with logits: first maximum, lowest id on ties (imi/core/hear.cpp:67-68). */
 imi_cuda_status imi_cuda_get_argmax(const imi_cuda_state *s, int32_t *id, float *value);
 
+/* ---- measurement ---- */
+
+/* The CUDA stream (cudaStream_t) every launch of this engine goes to, for callers that time on the device. */
+void *imi_cuda_stream(const imi_cuda_engine *e);
+/* Kernel launches of one step of n conversations (with or without word scores). */
+int imi_cuda_launches_per_step(const imi_cuda_engine *e, int n, int want_logits);
+/* Every layer table read back to back with ncol (1..8) inputs riding each read, as imi_seoul::bench_tables
+ * (seoul.cpp:657-685): *ms = mean milliseconds per pass over `reps` passes (after one untimed pass), *bytes = table
+ * bytes read per pass. */
+imi_cuda_status imi_cuda_bench_tables(imi_cuda_engine *e, int ncol, int reps, float *ms, size_t *bytes);
+
 /* ---- kernel level (known-answer tests and the isolated table sweep) ---- */
 
 /* Cut x[n] to 8-bit per 32 values on the device (imi_q8::from, tables.cpp:100-109 with imi_cut32, vec.h:47-77):

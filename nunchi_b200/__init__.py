@@ -64,6 +64,10 @@ def lib():
         L.imi_cuda_get_hidden.argtypes = [_vp, _fp]
         L.imi_cuda_get_logits.argtypes = [_vp, _fp]
         L.imi_cuda_get_argmax.argtypes = [_vp, C.POINTER(C.c_int32), C.POINTER(C.c_float)]
+        L.imi_cuda_stream.restype = _vp
+        L.imi_cuda_stream.argtypes = [_vp]
+        L.imi_cuda_launches_per_step.argtypes = [_vp, C.c_int, C.c_int]
+        L.imi_cuda_bench_tables.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(C.c_float), C.POINTER(C.c_size_t)]
         L.imi_cuda_q8_cut.argtypes = [C.c_int, _fp, C.c_int, _vp, _fp, _fp]
         L.imi_cuda_q4_matvec.argtypes = [C.c_int, _vp, C.c_int, C.c_int, _vp, _fp, _fp, C.c_int, _fp, _ip]
         _L = L
@@ -110,6 +114,20 @@ class Engine:
 
     def new_state(self) -> "State":
         return State(self)
+
+    @property
+    def stream(self) -> int:
+        """cudaStream_t of every launch of this engine (as an integer handle)."""
+        return int(lib().imi_cuda_stream(self.h) or 0)
+
+    def launches_per_step(self, n: int = 1, want_logits: bool = True) -> int:
+        return lib().imi_cuda_launches_per_step(self.h, n, int(bool(want_logits)))
+
+    def bench_tables(self, ncol: int = 1, reps: int = 20):
+        """imi_seoul::bench_tables: all layer tables back to back; (mean ms per pass, table bytes per pass)."""
+        ms, b = C.c_float(), C.c_size_t()
+        _check(lib().imi_cuda_bench_tables(self.h, ncol, reps, C.byref(ms), C.byref(b)))
+        return float(ms.value), int(b.value)
 
 
 class State:

@@ -897,4 +897,63 @@ imi_cuda_status imi_cuda_q4_matvec(int device, const uint8_t *q4, int rows, int 
     return IMI_OK;
 }
 
+void *imi_cuda_stream(const imi_cuda_engine *e) { return e ? (void *) e->stream : nullptr; }
+
+int imi_cuda_launches_per_step(const imi_cuda_engine *e, int n, int want_logits) {
+    if (!e || n <= 0) return 0;
+    const int groups = (n + STEP_COLS - 1) / STEP_COLS;
+    int per = 0;
+    for (auto &L : e->layers) per += L.conv ? 4 : 5;
+    return groups * (per + 1);   // + word table (or the final norm without scores)
+    (void) want_logits;
+}
+
+imi_cuda_status imi_cuda_bench_tables(imi_cuda_engine *e, int ncol, int reps, float *ms, size_t *bytes) {
+    if (!e || ncol < 1 || ncol > STEP_COLS || reps < 1 || !ms) return fail(IMI_E_ARG, "bad bench_tables arguments");
+    CK(cudaSetDevice(e->device));
+    std::vector<const TableRef *> ws;
+    for (auto &L : e->layers)
+        for (const TableRef *t : { &L.in_proj, &L.out_proj, &L.qkvg, &L.o, &L.gate_up, &L.down })
+            if (t->rows) ws.push_back(t);
+    size_t b = 0;
+    for (auto *t : ws) b += (size_t) t->rows * t->row_bytes;
+    if (bytes) *bytes = b;
+    // inputs: the act scratch (zeros after allocation is fine: the integer work does not depend on values)
+    CK(cudaMemsetAsync(e->X, 0, (size_t) (2 * e->n_embd + e->big_n + e->n_embd + e->n_head * e->head_dim + e->n_ff) * 4 * STEP_COLS, e->stream));
+    auto pass = [&]() -> cudaError_t {
+        for (auto *t : ws) {
+            MvArgs a = {};
+            a.cols_d = e->cols_d; a.ncol = ncol; a.eps = e->eps; a.n_embd = e->n_embd; a.ring_layer = -1;
+            a.err = e->err; a.in = e->act; a.in_stride = 0; a.out = e->big; a.out_stride = 0;   // big >= 2 n_ff floats
+            cudaError_t r = table_launch(e, *t, P_CUT, E_STORE, a);
+            if (r != cudaSuccess) return r;
+        }
+        return cudaSuccess;
+    };
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    const cudaError_t r = pass();
+    const cudaError_t r2 = cudaStreamEndCapture(e->stream, &g);
+    if (r != cudaSuccess || r2 != cudaSuccess) { if (g) cudaGraphDestroy(g); return fail(IMI_E_CUDA, "bench_tables capture"); }
+    const cudaError_t r3 = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    if (r3 != cudaSuccess) return fail(IMI_E_CUDA, "bench_tables instantiate");
+    cudaEvent_t e0, e1;
+    CK(cudaEventCreate(&e0));
+    CK(cudaEventCreate(&e1));
+    CK(cudaGraphLaunch(ge, e->stream));
+    CK(cudaEventRecord(e0, e->stream));
+    for (int i = 0; i < reps; i++) CK(cudaGraphLaunch(ge, e->stream));
+    CK(cudaEventRecord(e1, e->stream));
+    CK(cudaEventSynchronize(e1));
+    float t = 0;
+    CK(cudaEventElapsedTime(&t, e0, e1));
+    *ms = t / reps;
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaGraphExecDestroy(ge);
+    return check_err(e);
+}
+
 }  // extern "C"
