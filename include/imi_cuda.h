@@ -84,6 +84,16 @@ imi_cuda_status imi_cuda_step_batch(imi_cuda_state *s, const int32_t *tokens, co
  * step stay readable. */
 imi_cuda_status imi_cuda_greedy(imi_cuda_state *const *s, int n, const int32_t *tokens, int steps, int32_t *ids);
 
+/* Checkpoint / resume of one conversation (the content of imi_seoul_state, seoul.h:21-26) as a host byte image:
+ *   int32 magic 0x53494d49 ("IMIS"), version 1, pos, n_attn, n_ctx, kv_dim, n_conv, d_conv, n_embd, n_vocab, next_pick;
+ *   K cache [n_attn][pos][kv_dim] fp16, V cache likewise (positions 0..pos-1 only);
+ *   conv memory [n_conv][d_conv][n_embd] fp32, oldest first (imi's layout, seoul.h:47);
+ *   hidden [n_embd] fp32, logits [n_vocab] fp32.
+ * save: buf NULL -> *size receives the bytes needed; else the image is written (cap >= that size).
+ * load: into a state of an engine with the same shape and an n_ctx >= the image's pos. */
+imi_cuda_status imi_cuda_state_save(const imi_cuda_state *s, void *buf, size_t cap, size_t *size);
+imi_cuda_status imi_cuda_state_load(imi_cuda_state *s, const void *buf, size_t size);
+
 /* The latest outputs of a conversation (imi_seoul::hidden / ::logits, seoul.h:51): host copies. */
 imi_cuda_status imi_cuda_get_hidden(const imi_cuda_state *s, float *out /* n_embd */);
 imi_cuda_status imi_cuda_get_logits(const imi_cuda_state *s, float *out /* n_vocab */);
@@ -100,6 +110,13 @@ int imi_cuda_launches_per_step(const imi_cuda_engine *e, int n, int want_logits)
  * (seoul.cpp:657-685): *ms = mean milliseconds per pass over `reps` passes (after one untimed pass), *bytes = table
  * bytes read per pass. */
 imi_cuda_status imi_cuda_bench_tables(imi_cuda_engine *e, int ncol, int reps, float *ms, size_t *bytes);
+
+/* Diagnostics: read table `which` (0 in_proj/qkvg, 1 out_proj/o, 2 gate_up, 3 down) of layer `layer`
+ * once, alone, with ncol inputs, and return per-CTA phase timestamps in ns: trace[cta][16] (0 start, 1 after the
+ * dependency wait, 2 after input preparation, 3+s after stage s's integer phase, 14 end of the float chains).
+ * *grid receives the number of CTAs; trace must hold 148*16 values on a B200. */
+imi_cuda_status imi_cuda_trace_table(imi_cuda_engine *e, int layer, int which, int ncol, unsigned long long *trace,
+                                     int *grid);
 
 /* ---- kernel level (known-answer tests and the isolated table sweep) ---- */
 

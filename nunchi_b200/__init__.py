@@ -68,6 +68,9 @@ def lib():
         L.imi_cuda_stream.argtypes = [_vp]
         L.imi_cuda_launches_per_step.argtypes = [_vp, C.c_int, C.c_int]
         L.imi_cuda_bench_tables.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(C.c_float), C.POINTER(C.c_size_t)]
+        L.imi_cuda_trace_table.argtypes = [_vp, C.c_int, C.c_int, C.c_int, _vp, C.POINTER(C.c_int)]
+        L.imi_cuda_state_save.argtypes = [_vp, _vp, C.c_size_t, C.POINTER(C.c_size_t)]
+        L.imi_cuda_state_load.argtypes = [_vp, _vp, C.c_size_t]
         L.imi_cuda_q8_cut.argtypes = [C.c_int, _fp, C.c_int, _vp, _fp, _fp]
         L.imi_cuda_q4_matvec.argtypes = [C.c_int, _vp, C.c_int, C.c_int, _vp, _fp, _fp, C.c_int, _fp, _ip]
         _L = L
@@ -130,6 +133,14 @@ class Engine:
         return float(ms.value), int(b.value)
 
 
+def trace_table(engine: "Engine", layer: int, which: int, ncol: int = 1) -> np.ndarray:
+    """Diagnostics: per-CTA phase timestamps (ns) of one table read (imi_cuda_trace_table)."""
+    buf = np.zeros((1024, 16), np.uint64)
+    g = C.c_int()
+    _check(lib().imi_cuda_trace_table(engine.h, layer, which, ncol, _ptr(buf), C.byref(g)))
+    return buf[: g.value]
+
+
 class State:
     """One conversation on the device (imi_seoul_state, seoul.h:21-26)."""
 
@@ -180,6 +191,35 @@ class State:
         out = np.zeros(self.engine.n_vocab, np.float32)
         _check(lib().imi_cuda_get_logits(self.h, _ptr(out)))
         return out
+
+    def save(self) -> bytes:
+        """Checkpoint of this conversation (imi_cuda_state_save: position, K/V, conv memory, outputs)."""
+        n = C.c_size_t()
+        _check(lib().imi_cuda_state_save(self.h, None, 0, C.byref(n)))
+        buf = np.zeros(n.value, np.uint8)
+        _check(lib().imi_cuda_state_save(self.h, _ptr(buf), n.value, C.byref(n)))
+        return buf.tobytes()
+
+    def load(self, image: bytes):
+        buf = np.frombuffer(image, np.uint8).copy()
+        _check(lib().imi_cuda_state_load(self.h, _ptr(buf), buf.size))
+
+    def unpack(self, image: bytes = None) -> dict:
+        """The checkpoint's fields as arrays (pos, k, v [n_attn][pos][kvd] fp16 bits, conv [n_conv][d_conv][E])."""
+        b = image if image is not None else self.save()
+        h = np.frombuffer(b[:44], np.int32)
+        pos, na, _, kvd, nconv, dconv, E, V = (int(x) for x in h[2:10])
+        o = 44
+        def take(n, dt, shape):
+            nonlocal o
+            a = np.frombuffer(b[o:o + n * np.dtype(dt).itemsize], dt).reshape(shape)
+            o += n * np.dtype(dt).itemsize
+            return a
+        k = take(na * pos * kvd, np.uint16, (na, pos, kvd))
+        v = take(na * pos * kvd, np.uint16, (na, pos, kvd))
+        conv = take(nconv * dconv * E, np.float32, (nconv, dconv, E))
+        hid = take(E, np.float32, (E,))
+        return {"pos": pos, "k": k, "v": v, "conv": conv, "hidden": hid, "next_pick": int(h[10])}
 
     def argmax(self):
         i, v = C.c_int32(), C.c_float()

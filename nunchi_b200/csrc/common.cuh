@@ -18,7 +18,10 @@
 
 namespace imi {
 
-constexpr int MV_THREADS = 256;            // threads of a table-read CTA
+constexpr int MV_IWARPS = 8;               // table-read CTA: warps computing integer block dots
+constexpr int MV_CWARPS = 4;               // warps running the per-row float chains (and the output stage)
+constexpr int MV_ITHREADS = 32 * MV_IWARPS, MV_CTHREADS = 32 * MV_CWARPS;
+constexpr int MV_THREADS = MV_ITHREADS + MV_CTHREADS;
 constexpr int MV_STAGES = 2;               // weight stages in flight per CTA (TMA bulk copies)
 constexpr int MV_STAGE_BYTES = 36864;      // one K=8192 row group of 8 rows, or 32 rows of K=2048
 constexpr int MV_MAX_COLS = 8;             // inputs sharing one table read in the small-batch kernel
@@ -83,7 +86,14 @@ struct MvArgs {
     int out_stride;
     unsigned int *done;        // CTA counter (E_HEAD finalize)
     int *err;
+    unsigned long long *trace; // optional: per-CTA phase timestamps (ns), [grid][MV_TRACE] (diagnostics only)
+    // E_SILU: the 8-bit cut of the produced values, per column [c][rows/2] codes and [c][rows/64] scales / sums,
+    // made here (each CTA owns whole 32-value blocks: unit = 64 rows) so the next read only loads codes
+    int8_t *q8o_q;
+    float *q8o_d, *q8o_s;
+    int ab_len;                // produced values per column a CTA holds (max over CTAs)
 };
+constexpr int MV_TRACE = 16;
 
 struct AttnArgs {
     const Col *cols_d;
@@ -98,6 +108,8 @@ struct AttnArgs {
     int ai, n_head, n_head_kv, head_dim, n_ctx, window;
     int kv_fused;                     // 1: write K/V at the column's position here and use own copies for it
     int *err;
+    int8_t *q8o_q;                    // the 8-bit cut of the attention output, per column [c][n_head*head_dim] codes,
+    float *q8o_d, *q8o_s;             // [c][n_head*head_dim/32] scales and scale*sums (the o table reads only these)
 };
 
 struct FinalArgs {
@@ -113,26 +125,36 @@ struct FinalArgs {
 };
 
 // ---- shared-memory plan of the table-read kernel (host and device agree on it) ----
+// fs: integer block dots as floats, [2 buffers][nc][sr][nb+4]; dd: block scales (fp16 bits), [2][sr][nb+4];
+// vb: prologue vectors [nc][vb_len] (overlapping fs/dd); red: reductions and argmax partials.
 struct MvPlan {
-    int stage, bar, xq, xd, xs, fs, dd, vb, vo, red, total;
+    int stage, bar, xq, xd, xs, fs, dd, vb, vo, ab, red, total;
 };
 __host__ __device__ inline int align_up(int x, int a) { return (x + a - 1) / a * a; }
-__host__ __device__ inline MvPlan mv_plan(int cols, int sr, int nc, int vb_len) {
+__host__ __device__ inline MvPlan mv_plan(int cols, int sr, int nc, int vb_len, int ab_len) {
     MvPlan p;
-    const int nb = cols / 32, ld = nb + 1;
+    const int nb = cols / 32, ld = nb + 4;   // row strides: 16-byte aligned, conflict-free for vector loads
     int o = 0;
     p.stage = o; o += MV_STAGES * MV_STAGE_BYTES;
     p.bar = o;   o = align_up(o + 8 * MV_STAGES, 16);
     p.xq = o;    o = align_up(o + nc * cols, 16);
     p.xd = o;    o = align_up(o + 4 * nc * nb, 16);
     p.xs = o;    o = align_up(o + 4 * nc * nb, 16);
-    p.fs = o;    o = align_up(o + 4 * nc * sr * ld, 16);
-    p.dd = o;    o = align_up(o + 4 * sr * ld, 16);
-    p.vb = o;    o = align_up(o + 4 * nc * vb_len, 16);
-    p.vo = o;    o = align_up(o + 4 * nc * sr, 16);
-    p.red = o;   o = align_up(o + 4 * 64 + 16 * MV_MAX_COLS * (MV_THREADS / 32), 16);
+    // the prologue's vectors (vb) are dead before the first block dot is stored: they share the dot buffers' space
+    const int u = o;
+    p.fs = o;    o = align_up(o + 2 * 4 * nc * sr * ld, 16);
+    p.dd = o;    o = align_up(o + 2 * 2 * sr * ld, 16);
+    p.vo = o;
+    p.vb = u;    o = o > align_up(u + 4 * nc * vb_len, 16) ? o : align_up(u + 4 * nc * vb_len, 16);
+    p.ab = o;    o = align_up(o + 4 * nc * ab_len, 16);
+    p.red = o;   o = align_up(o + 4 * 64 + 8 * MV_MAX_COLS * MV_CWARPS + 16, 16);
     p.total = o;
     return p;
+}
+
+// floats per column staged in shared memory by the input preparation of `pro`
+__host__ __device__ inline int mv_vb_len(int pro, int cols, int n_embd) {
+    return pro == P_CUT ? cols : (pro == P_EMBED_NORM || pro == P_RESID_NORM || pro == P_FINAL || pro == P_CONV) ? n_embd : 0;
 }
 
 #ifdef __CUDACC__
@@ -232,6 +254,11 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
                      smem_u32(dst)),
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

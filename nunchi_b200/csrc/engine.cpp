@@ -70,6 +70,8 @@ struct imi_cuda_engine {
     int big_n = 0;
     float *X = nullptr, *big = nullptr, *y = nullptr, *att = nullptr, *act = nullptr, *fo = nullptr, *embd = nullptr,
           *hid = nullptr;
+    int8_t *qa_q = nullptr, *qt_q = nullptr;   // 8-bit cuts of act [col][n_ff] and att [col][n_head*head_dim]
+    float *qa_d = nullptr, *qa_s = nullptr, *qt_d = nullptr, *qt_s = nullptr;
     Col *cols_d = nullptr, *cols_h = nullptr;
     float *embd_h = nullptr;
     unsigned *done = nullptr;
@@ -77,6 +79,7 @@ struct imi_cuda_engine {
     cudaEvent_t staged = nullptr;   // the last host->device copy of the staging buffers has run
     std::map<int, cudaGraphExec_t> graphs;
     size_t state_bytes = 0;
+    uint8_t *qbuf = nullptr;
     const float *f32(size_t off) const { return (const float *) (w + off); }
     ~imi_cuda_engine();
 };
@@ -98,6 +101,7 @@ imi_cuda_engine::~imi_cuda_engine() {
     cudaFree(w);
     cudaFree(rope_cs);
     cudaFree(X);
+    cudaFree(qbuf);
     cudaFree(cols_d);
     cudaFreeHost(cols_h);
     cudaFreeHost(embd_h);
@@ -332,6 +336,19 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
     e->fo = e->act + (size_t) e->n_ff * STEP_COLS;
     e->embd = e->fo + (size_t) E * STEP_COLS;
     e->hid = e->embd + (size_t) E * STEP_COLS;
+    {
+        const size_t na = (size_t) STEP_COLS * e->n_ff, nt = (size_t) STEP_COLS * HD;
+        uint8_t *q = nullptr;
+        CK(cudaMalloc(&q, na + nt + 4 * 2 * (na / 32 + nt / 32) + 1024));
+        e->qbuf = q;
+        e->qa_q = (int8_t *) q;
+        e->qt_q = (int8_t *) (q + na);
+        e->qa_d = (float *) (q + (na + nt + 255) / 256 * 256);
+        e->qa_s = e->qa_d + na / 32;
+        e->qt_d = e->qa_s + na / 32;
+        e->qt_s = e->qt_d + nt / 32;
+        CK(cudaMemset(q, 0, na + nt + 4 * 2 * (na / 32 + nt / 32) + 1024));
+    }
     CK(cudaMalloc(&e->cols_d, sizeof(Col) * STEP_COLS + 64));
     e->done = (unsigned *) (e->cols_d + STEP_COLS);
     e->err = (int *) (e->done + 4);
@@ -357,21 +374,32 @@ namespace {
 
 enum StepKind { K_DECODE = 0, K_PREFILL = 1, K_HEAD_ONLY = 2 };
 
-int pick_sr(int pro, const TableRef &t, int unit, int ncol, int E) {
-    int sr = std::min(64, MV_STAGE_BYTES / t.row_bytes);
-    if (unit == 2) sr &= ~1;
-    while (sr > unit && table_smem(pro, t.cols, sr, ncol, E) > (size_t) MV_SMEM_BUDGET) sr -= unit;
-    return std::max(sr, unit);
+// rows per weight stage: as many as a stage holds (in steps of `gran` rows), fewer if that keeps two CTAs per SM (so
+// the next launch can start early); when even 8 rows do not fit that budget, one CTA per SM with full stages
+int pick_sr(int pro, const TableRef &t, int gran, int ncol, int E, int ab_len) {
+    const int full = std::max(gran, (std::min(64, MV_STAGE_BYTES / t.row_bytes) / gran) * gran);
+    int sr = full;
+    while (sr > gran && table_smem(pro, t.cols, sr, ncol, E, ab_len) > (size_t) MV_SMEM_BUDGET) sr -= gran;
+    if (sr < std::min(8, full)) {
+        sr = full;
+        while (sr > gran && table_smem(pro, t.cols, sr, ncol, E, ab_len) > (size_t) 220 * 1024) sr -= gran;
+    }
+    return std::max(sr, gran);
 }
 
+// one table read: CTAs take whole `unit`s of rows (64 for the SiLU stage, which cuts whole 32-value blocks of its
+// output; else 1), stages hold a multiple of `gran` rows (2 for the SiLU stage's (gate, up) pairs)
 cudaError_t table_launch(imi_cuda_engine *e, const TableRef &t, int pro, int epi, MvArgs a) {
     a.W = e->w + t.off;
     a.rows = t.rows;
     a.cols = t.cols;
     a.row_bytes = t.row_bytes;
-    a.unit = epi == E_SILU ? 2 : 1;
-    a.sr = pick_sr(pro, t, a.unit, a.ncol, e->n_embd);
-    const int grid = std::max(1, std::min(e->sm_count, t.rows / a.unit));
+    const int gran = epi == E_SILU ? 2 : 1;
+    a.unit = epi == E_SILU ? 64 : 1;
+    const int units = t.rows / a.unit;
+    const int grid = std::max(1, std::min(e->sm_count, units));
+    a.ab_len = epi == E_SILU ? (units + grid - 1) / grid * a.unit / 2 : 0;
+    a.sr = pick_sr(pro, t, gran, a.ncol, e->n_embd, a.ab_len);
     return launch_table(pro, epi, a, grid, e->stream, true);
 }
 
@@ -445,14 +473,18 @@ cudaError_t enqueue_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind)
             t.window = (L.swa && e->n_swa > 0) ? e->n_swa : 0;   // seoul.cpp:431
             t.err = e->err;
             t.kv_fused = kind == K_DECODE;
+            t.q8o_q = e->qt_q;
+            t.q8o_d = e->qt_d;
+            t.q8o_s = e->qt_s;
             if (kind == K_PREFILL && (r = launch_kvwrite(t, e->stream, true)) != cudaSuccess) return r;
             if ((r = launch_attn(t, e->stream, true)) != cudaSuccess) return r;
             a = b;
-            a.in = e->att;
-            a.in_stride = HD;
+            a.q8_q = e->qt_q;
+            a.q8_d = e->qt_d;
+            a.q8_s = e->qt_s;
             a.out = e->y;
             a.out_stride = E;
-            if ((r = table_launch(e, L.o, P_CUT, E_STORE, a)) != cudaSuccess) return r;
+            if ((r = table_launch(e, L.o, P_Q8IN, E_STORE, a)) != cudaSuccess) return r;
         }
         a = b;
         a.in = e->y;
@@ -463,6 +495,9 @@ cudaError_t enqueue_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind)
         a.wpre = e->f32(L.ffn_norm);
         a.out = e->act;
         a.out_stride = e->n_ff;
+        a.q8o_q = e->qa_q;
+        a.q8o_d = e->qa_d;
+        a.q8o_s = e->qa_s;
         if (L.conv) {
             a.ring_layer = L.ci;
             a.ring_src = e->big;
@@ -470,11 +505,12 @@ cudaError_t enqueue_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind)
         }
         if ((r = table_launch(e, L.gate_up, P_RESID_NORM, E_SILU, a)) != cudaSuccess) return r;
         a = b;
-        a.in = e->act;
-        a.in_stride = e->n_ff;
+        a.q8_q = e->qa_q;
+        a.q8_d = e->qa_d;
+        a.q8_s = e->qa_s;
         a.out = e->fo;
         a.out_stride = E;
-        if ((r = table_launch(e, L.down, P_CUT, E_STORE, a)) != cudaSuccess) return r;
+        if ((r = table_launch(e, L.down, P_Q8IN, E_STORE, a)) != cudaSuccess) return r;
     }
     const LayerRef &last = e->layers.back();
     if (head) {
@@ -882,7 +918,7 @@ imi_cuda_status imi_cuda_q4_matvec(int device, const uint8_t *q4, int rows, int 
         a.cols_d = dcols; a.ncol = ncol; a.q8_q = dq; a.q8_d = dd; a.q8_s = ds; a.dots = ddots;
         a.out = dout; a.out_stride = rows; a.err = derr; a.ring_layer = -1;
         TableRef t; t.rows = rows; t.cols = cols; t.row_bytes = row_bytes;
-        a.sr = pick_sr(P_Q8IN, t, 1, ncol, 0);
+        a.sr = pick_sr(P_Q8IN, t, 1, ncol, 0, 0);
         int sms = 148;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
         r = launch_table(P_Q8IN, E_STORE, a, std::max(1, std::min(sms, rows)), 0, false);
@@ -924,8 +960,8 @@ imi_cuda_status imi_cuda_bench_tables(imi_cuda_engine *e, int ncol, int reps, fl
         for (auto *t : ws) {
             MvArgs a = {};
             a.cols_d = e->cols_d; a.ncol = ncol; a.eps = e->eps; a.n_embd = e->n_embd; a.ring_layer = -1;
-            a.err = e->err; a.in = e->act; a.in_stride = 0; a.out = e->big; a.out_stride = 0;   // big >= 2 n_ff floats
-            cudaError_t r = table_launch(e, *t, P_CUT, E_STORE, a);
+            a.err = e->err; a.q8_q = e->qa_q; a.q8_d = e->qa_d; a.q8_s = e->qa_s; a.out = e->big; a.out_stride = 0;
+            cudaError_t r = table_launch(e, *t, P_Q8IN, E_STORE, a);   // codes given: big holds >= 2 n_ff floats
             if (r != cudaSuccess) return r;
         }
         return cudaSuccess;
@@ -954,6 +990,119 @@ imi_cuda_status imi_cuda_bench_tables(imi_cuda_engine *e, int ncol, int reps, fl
     cudaEventDestroy(e1);
     cudaGraphExecDestroy(ge);
     return check_err(e);
+}
+
+imi_cuda_status imi_cuda_trace_table(imi_cuda_engine *e, int layer, int which, int ncol, unsigned long long *trace,
+                                     int *grid) {
+    if (!e || !trace || !grid || layer < 0 || layer >= e->n_layer || which < 0 || which > 3 || ncol < 1 ||
+        ncol > STEP_COLS)
+        return fail(IMI_E_ARG, "bad trace_table arguments");
+    CK(cudaSetDevice(e->device));
+    const LayerRef &L = e->layers[layer];
+    const TableRef *t = which == 0 ? (L.conv ? &L.in_proj : &L.qkvg) : which == 1 ? (L.conv ? &L.out_proj : &L.o)
+                        : which == 2 ? &L.gate_up : &L.down;
+    if ((size_t) (t->rows) > (size_t) e->big_n * STEP_COLS) return fail(IMI_E_ARG, "table too tall for the scratch");
+    MvArgs a = {};
+    a.cols_d = e->cols_d; a.ncol = ncol; a.eps = e->eps; a.n_embd = e->n_embd; a.ring_layer = -1;
+    a.err = e->err; a.q8_q = e->qa_q; a.q8_d = e->qa_d; a.q8_s = e->qa_s; a.out = e->big; a.out_stride = 0;
+    const int epi = E_STORE;   // the output stage of the traced read: a plain store (same table bytes, same phases)
+    const int g = std::max(1, std::min(e->sm_count, t->rows));
+    unsigned long long *d = nullptr;
+    CK(cudaMalloc(&d, (size_t) g * MV_TRACE * 8));
+    CK(cudaMemsetAsync(d, 0, (size_t) g * MV_TRACE * 8, e->stream));
+    a.trace = d;
+    a.W = e->w + t->off; a.rows = t->rows; a.cols = t->cols; a.row_bytes = t->row_bytes;
+    a.unit = epi == E_SILU ? 2 : 1;
+    a.sr = pick_sr(P_Q8IN, *t, 1, ncol, e->n_embd, 0);
+    cudaError_t r = launch_table(P_Q8IN, epi, a, g, e->stream, false);
+    if (r == cudaSuccess) r = cudaMemcpyAsync(trace, d, (size_t) g * MV_TRACE * 8, cudaMemcpyDeviceToHost, e->stream);
+    if (r == cudaSuccess) r = cudaStreamSynchronize(e->stream);
+    cudaFree(d);
+    if (r != cudaSuccess) return fail(IMI_E_CUDA, std::string("trace_table: ") + cudaGetErrorString(r));
+    *grid = g;
+    return check_err(e);
+}
+
+namespace {
+struct StateImage {
+    int32_t magic, version, pos, n_attn, n_ctx, kvd, n_conv, d_conv, n_embd, n_vocab, next_pick;
+};
+size_t image_bytes(const imi_cuda_engine *e, int pos) {
+    const size_t kvd = (size_t) e->n_head_kv * e->head_dim;
+    return sizeof(StateImage) + 2 * (size_t) e->n_attn * pos * kvd * 2 + (size_t) e->n_conv * e->d_conv * e->n_embd * 4 +
+           (size_t) e->n_embd * 4 + (size_t) e->n_vocab * 4;
+}
+}  // namespace
+
+imi_cuda_status imi_cuda_state_save(const imi_cuda_state *s, void *buf, size_t cap, size_t *size) {
+    if (!s || !size) return fail(IMI_E_ARG, "null argument");
+    const imi_cuda_engine *e = s->e;
+    const size_t need = image_bytes(e, s->pos);
+    *size = need;
+    if (!buf) return IMI_OK;
+    if (cap < need) return fail(IMI_E_ARG, "buffer too small for the state image");
+    CK(cudaSetDevice(e->device));
+    CK(cudaStreamSynchronize(e->stream));
+    SessDev sd;
+    CK(cudaMemcpy(&sd, s->s, sizeof sd, cudaMemcpyDeviceToHost));
+    if (sd.pos != s->pos)
+        return fail(IMI_E_CUDA, "device position " + std::to_string(sd.pos) + " disagrees with " + std::to_string(s->pos));
+    const int kvd = e->n_head_kv * e->head_dim, R = e->d_conv + 1, E = e->n_embd, pos = s->pos;
+    StateImage h = { 0x53494d49, 1, pos, e->n_attn, e->n_ctx, kvd, e->n_conv, e->d_conv, E, e->n_vocab, sd.next_token };
+    uint8_t *o = (uint8_t *) buf;
+    memcpy(o, &h, sizeof h);
+    o += sizeof h;
+    for (const __half *cache : { s->kc, s->vc })
+        for (int a = 0; a < e->n_attn; a++) {
+            CK(cudaMemcpy(o, cache + (size_t) a * e->n_ctx * kvd, (size_t) pos * kvd * 2, cudaMemcpyDeviceToHost));
+            o += (size_t) pos * kvd * 2;
+        }
+    for (int l = 0; l < e->n_conv; l++)
+        for (int k = 0; k < e->d_conv; k++) {   // tap k holds position pos - d_conv + k (zero before position 0)
+            const int slot = (((pos - e->d_conv + k) % R) + R) % R;
+            CK(cudaMemcpy(o, s->ring + ((size_t) l * R + slot) * E, (size_t) E * 4, cudaMemcpyDeviceToHost));
+            o += (size_t) E * 4;
+        }
+    CK(cudaMemcpy(o, s->hidden, (size_t) E * 4, cudaMemcpyDeviceToHost));
+    o += (size_t) E * 4;
+    CK(cudaMemcpy(o, s->logits, (size_t) e->n_vocab * 4, cudaMemcpyDeviceToHost));
+    return IMI_OK;
+}
+
+imi_cuda_status imi_cuda_state_load(imi_cuda_state *s, const void *buf, size_t size) {
+    if (!s || !buf || size < sizeof(StateImage)) return fail(IMI_E_ARG, "bad state image");
+    imi_cuda_engine *e = s->e;
+    StateImage h;
+    memcpy(&h, buf, sizeof h);
+    const int kvd = e->n_head_kv * e->head_dim, R = e->d_conv + 1, E = e->n_embd;
+    if (h.magic != 0x53494d49 || h.version != 1 || h.n_attn != e->n_attn || h.kvd != kvd || h.n_conv != e->n_conv ||
+        h.d_conv != e->d_conv || h.n_embd != E || h.n_vocab != e->n_vocab || h.pos < 0 || h.pos > e->n_ctx ||
+        size < image_bytes(e, h.pos))
+        return fail(IMI_E_FORMAT, "state image does not fit this engine");
+    CK(cudaSetDevice(e->device));
+    CK(cudaStreamSynchronize(e->stream));
+    const uint8_t *i = (const uint8_t *) buf + sizeof h;
+    for (__half *cache : { s->kc, s->vc })
+        for (int a = 0; a < e->n_attn; a++) {
+            CK(cudaMemcpy(cache + (size_t) a * e->n_ctx * kvd, i, (size_t) h.pos * kvd * 2, cudaMemcpyHostToDevice));
+            i += (size_t) h.pos * kvd * 2;
+        }
+    CK(cudaMemset(s->ring, 0, (size_t) e->n_conv * R * E * 4));
+    for (int l = 0; l < e->n_conv; l++)
+        for (int k = 0; k < e->d_conv; k++) {
+            const int slot = (((h.pos - e->d_conv + k) % R) + R) % R;
+            CK(cudaMemcpy(s->ring + ((size_t) l * R + slot) * E, i, (size_t) E * 4, cudaMemcpyHostToDevice));
+            i += (size_t) E * 4;
+        }
+    CK(cudaMemcpy(s->hidden, i, (size_t) E * 4, cudaMemcpyHostToDevice));
+    i += (size_t) E * 4;
+    CK(cudaMemcpy(s->logits, i, (size_t) e->n_vocab * 4, cudaMemcpyHostToDevice));
+    SessDev sd = {};
+    sd.pos = h.pos;
+    sd.next_token = h.next_pick;
+    CK(cudaMemcpy(s->s, &sd, sizeof sd, cudaMemcpyHostToDevice));
+    s->pos = h.pos;
+    return IMI_OK;
 }
 
 }  // extern "C"

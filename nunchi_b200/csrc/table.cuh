@@ -1,0 +1,462 @@
+// k_table: one 4-bit table times up to 8 inputs ("columns"): the replacement of imi_q4_group / imi_q4_group2 /
+// imi_q4_group_batch (imi/core/tables.cpp:127-177,419-477) together with the small math imi's threads repeat before
+// every table read (norms, residual adds, the short conv, the 8-bit cut; seoul.cpp:402-474).
+//
+// Per CTA: a contiguous slice of rows. Weights arrive in stages by TMA bulk copies (cp.async.bulk + mbarrier),
+// issued before the kernel waits on its predecessor (programmatic dependent launch), so a table's first bytes stream
+// while the previous launch finishes. Every CTA prepares the input itself (it is tiny), as every imi thread does.
+//
+// Two warp roles per CTA, pipelined over the stages through double-buffered shared memory and named barriers:
+//   integer warps (8): dot_j = sum of 32 4-bit codes x 32 8-bit input codes for every (row, block j), with dp4a,
+//                       stored as floats (exact: |dot| < 2^24), plus the rows' block scales;
+//   chain warps (4):    one thread per (input, row): the float result in the exact order of group_avx2<false>
+//                       (tables.cpp:127-143):  acc = fma(dot_j, d_j * dx_j, acc),  cor = fma(d_j, sx_j, cor)  for j in
+//                       order, out = acc - 8 cor with one rounding; then the output stage (store, SiLU(gate)*up, or
+//                       word scores with the first-maximum pick).
+#pragma once
+#include "common.cuh"
+
+namespace imi {
+
+// named barriers (0 is __syncthreads)
+enum : int { NB_INT = 1, NB_READY = 2 /* +buffer */, NB_FREE = 4 /* +buffer */, NB_TAIL = 7 };
+__device__ __forceinline__ void nbar_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void nbar_arrive(int id, int count) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+// all `count` threads of barrier `id` learn whether every one of them passed `v`
+__device__ __forceinline__ bool nbar_and(int id, int count, bool v) {
+    uint32_t r;
+    asm volatile("{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}"
+                 : "=r"(r)
+                 : "r"((uint32_t) v), "r"(id), "r"(count)
+                 : "memory");
+    return r != 0;
+}
+
+// imi_cut32 (vec.h:47-77) of one 32-value block held by ONE thread: d = max|x|/127, id = 1/d (0 if d == 0),
+// q = round-half-even(x * id). Writes 32 codes (16-byte aligned), d and d * sum(q).
+__device__ __forceinline__ void cut32(const float (&v)[32], int8_t *q, float *d_out, float *s_out) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 32; k++) amax = fmaxf(amax, fabsf(v[k]));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    int sum = 0;
+    uint32_t w[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) w[k] = 0;
+#pragma unroll
+    for (int k = 0; k < 32; k++) {
+        const int c = __float2int_rn(__fmul_rn(v[k], id));
+        sum += c;
+        w[k >> 2] |= ((uint32_t) c & 0xffu) << (8 * (k & 3));
+    }
+    uint4 *qo = (uint4 *) q;
+    qo[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    qo[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    *d_out = d;
+    *s_out = __fmul_rn(d, (float) sum);
+}
+
+// 32 consecutive floats (16-byte aligned) into registers
+__device__ __forceinline__ void load32(const float *p, float (&v)[32]) {
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const float4 f = ((const float4 *) p)[k];
+        v[4 * k] = f.x; v[4 * k + 1] = f.y; v[4 * k + 2] = f.z; v[4 * k + 3] = f.w;
+    }
+}
+
+// the word table row of `tok` as floats: d * (code - 8); codes of block j at bytes 16j.., scales after the codes
+__device__ __forceinline__ float word_value(const uint8_t *row, int cols, int i) {
+    const int j = i >> 5, k = i & 31;
+    const uint8_t b = row[16 * j + (k & 15)];
+    const int code = k < 16 ? (b & 15) : (b >> 4);
+    const uint16_t dh = *(const uint16_t *) (row + cols / 2 + 2 * j);
+    return __fmul_rn(h2f(dh), (float) (code - 8));
+}
+
+// copy n floats (n % 4 == 0, both 16-byte aligned) with all threads
+__device__ __forceinline__ void copy_vec(float *dst, const float *src, int n) {
+    for (int i = 4 * threadIdx.x; i < n; i += 4 * MV_THREADS) *(float4 *) (dst + i) = *(const float4 *) (src + i);
+}
+
+// input preparation, all MV_THREADS threads, all columns at once; ends with a __syncthreads
+template <int PRO, int NC>
+__device__ void table_prologue(const MvArgs &a, const MvPlan &P, uint8_t *sm) {
+    int8_t *xq = (int8_t *) (sm + P.xq);
+    float *xd = (float *) (sm + P.xd), *xs = (float *) (sm + P.xs), *vb = (float *) (sm + P.vb);
+    float *red = (float *) (sm + P.red);
+    const int tid = threadIdx.x, warp = tid >> 5, nc = a.ncol, K = a.cols, nb = K / 32, E = a.n_embd;
+    const int VL = mv_vb_len(PRO, K, E);
+    const bool lead = blockIdx.x == 0;
+    if (PRO == P_Q8IN) {   // codes made by the producer of the input (or given): [c][K], [c][K/32]
+        for (int i = tid; i < nc * K / 16; i += MV_THREADS) ((int4 *) xq)[i] = ((const int4 *) a.q8_q)[i];
+        for (int j = tid; j < nc * nb; j += MV_THREADS) {
+            xd[j] = a.q8_d[j];
+            xs[j] = a.q8_s[j];
+        }
+        __syncthreads();
+        return;
+    }
+    // 1. every column's vector into shared memory (coalesced)
+    if (PRO == P_CUT || PRO == P_RESID_NORM || PRO == P_FINAL) {
+        for (int c = 0; c < nc; c++) copy_vec(vb + c * VL, a.in + (size_t) c * a.in_stride, PRO == P_CUT ? K : E);
+    } else if (PRO == P_EMBED_NORM) {
+        for (int c = 0; c < nc; c++) {
+            const Col &col = a.cols_d[c];
+            int tok = col.token;
+            if (tok == -2) tok = col.s->next_token;
+            if (tok >= 0) {
+                const uint8_t *row = a.emb + (size_t) tok * a.emb_row_bytes;
+                for (int i = tid; i < E; i += MV_THREADS) vb[c * VL + i] = word_value(row, E, i);
+            } else {
+                copy_vec(vb + c * VL, col.embd, E);
+            }
+        }
+    } else if (PRO == P_CONV) {
+        // seoul.cpp:410-414 (run) and 566-576 (run_batch): u = c * (b*x*w[d_conv] + sum_k st_k * w_k), st_k the b*x of
+        // position p - d_conv + k: from this step's earlier columns of the same conversation when that position is in
+        // this step, else from the conv memory ring
+        const int R = a.d_conv + 1;
+        for (int c = 0; c < nc; c++) {
+            const Col &col = a.cols_d[c];
+            const float *bcx = a.in + (size_t) c * a.in_stride;
+            const int p = col.s->pos + col.off;
+            const float *ring = col.ring + (size_t) a.conv_layer * R * E;
+            for (int e = tid; e < E; e += MV_THREADS) {
+                float u = __fmul_rn(__fmul_rn(bcx[e], bcx[2 * E + e]), a.conv_w[(size_t) a.d_conv * E + e]);
+                for (int k = 0; k < a.d_conv; k++) {
+                    const int qp = p - a.d_conv + k;
+                    float st;
+                    if (qp >= p - col.off) {
+                        const float *ob = a.in + (size_t) (c - a.d_conv + k) * a.in_stride;
+                        st = __fmul_rn(ob[e], ob[2 * E + e]);
+                    } else {
+                        st = ring[(size_t) (((qp % R) + R) % R) * E + e];
+                    }
+                    u = __fadd_rn(u, __fmul_rn(st, a.conv_w[(size_t) k * E + e]));
+                }
+                vb[c * VL + e] = __fmul_rn(u, bcx[E + e]);
+            }
+        }
+    }
+    __syncthreads();
+    const bool norm = PRO == P_EMBED_NORM || PRO == P_RESID_NORM || PRO == P_FINAL;
+    if (PRO == P_RESID_NORM || PRO == P_FINAL) {   // x += norm(r) * w_post (imi_norm_mul_add, vec.h:41-44)
+        if (warp < nc) {
+            const float sc = warp_rms_scale(vb + warp * VL, E, a.eps);
+            if ((tid & 31) == 0) red[warp] = sc;
+        }
+        __syncthreads();
+        for (int c = 0; c < nc; c++) {
+            const float sc = red[c];
+            const float *x = a.xin + (size_t) c * a.x_stride;
+            for (int i = tid; i < E; i += MV_THREADS)
+                vb[c * VL + i] = __fadd_rn(x[i], __fmul_rn(__fmul_rn(vb[c * VL + i], sc), a.wpost[i]));
+        }
+        __syncthreads();
+    }
+    if (norm) {
+        if (lead && a.xout)
+            for (int c = 0; c < nc; c++) copy_vec(a.xout + (size_t) c * a.x_stride, vb + c * VL, E);
+        if (warp < nc) {   // h = norm(x) * w_pre (imi_norm_mul, vec.h:36-39)
+            const float sc = warp_rms_scale(vb + warp * VL, E, a.eps);
+            if ((tid & 31) == 0) red[32 + warp] = sc;
+        }
+        __syncthreads();
+    }
+    // 2. the 8-bit cut, one thread per (column, 32-value block)
+    for (int t = tid; t < nc * nb; t += MV_THREADS) {
+        const int c = t / nb, j = t - c * nb;
+        float v[32];
+        load32(vb + c * VL + 32 * j, v);
+        if (norm) {
+            const float sc = red[32 + c];
+            float w[32];
+            load32(a.wpre + 32 * j, w);
+#pragma unroll
+            for (int k = 0; k < 32; k++) v[k] = __fmul_rn(__fmul_rn(v[k], sc), w[k]);
+            if (PRO == P_FINAL && lead && a.cols_d[c].hid_out) {
+                float *hid = a.cols_d[c].hid_out + 32 * j;
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+                    ((float4 *) hid)[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+            }
+        }
+        cut32(v, xq + c * K + 32 * j, xd + t, xs + t);
+    }
+    // conv memory: the slot of each column's position takes b*x (seoul.cpp:419-423); written one launch after the conv
+    // read it, so no CTA of the reading launch can see it early
+    if (a.ring_layer >= 0 && lead) {
+        const int R = a.d_conv + 1;
+        for (int c = 0; c < nc; c++) {
+            const Col &col = a.cols_d[c];
+            const int p = col.s->pos + col.off;
+            const float *bcx = a.ring_src + (size_t) c * a.ring_src_stride;
+            float *slot = col.ring + ((size_t) a.ring_layer * R + p % R) * E;
+            for (int e = tid; e < E; e += MV_THREADS) slot[e] = __fmul_rn(bcx[e], bcx[2 * E + e]);
+        }
+    }
+    __syncthreads();
+}
+
+__device__ __forceinline__ int dot_block(const uint4 c, const int *x) {
+    const int l0 = (int) (c.x & 0x0f0f0f0fu), l1 = (int) (c.y & 0x0f0f0f0fu), l2 = (int) (c.z & 0x0f0f0f0fu),
+              l3 = (int) (c.w & 0x0f0f0f0fu);
+    const int h0 = (int) ((c.x >> 4) & 0x0f0f0f0fu), h1 = (int) ((c.y >> 4) & 0x0f0f0f0fu),
+              h2 = (int) ((c.z >> 4) & 0x0f0f0f0fu), h3 = (int) ((c.w >> 4) & 0x0f0f0f0fu);
+    int s = __dp4a(l0, x[0], 0);
+    s = __dp4a(l1, x[1], s);
+    s = __dp4a(l2, x[2], s);
+    s = __dp4a(l3, x[3], s);
+    s = __dp4a(h0, x[4], s);
+    s = __dp4a(h1, x[5], s);
+    s = __dp4a(h2, x[6], s);
+    s = __dp4a(h3, x[7], s);
+    return s;
+}
+
+__device__ __forceinline__ unsigned long long amax_key(float v, int idx) {
+    v = v + 0.0f;   // -0 -> +0: equal values compare equal and the lowest id wins
+    const uint32_t b = __float_as_uint(v);
+    const uint32_t o = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((unsigned long long) o << 32) | (unsigned long long) (0xffffffffu - (uint32_t) idx);
+}
+__device__ __forceinline__ float amax_val(unsigned long long k) {
+    const uint32_t o = (uint32_t) (k >> 32);
+    return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
+}
+
+// the two fma chains of one (input, row), blocks in order (group_avx2<false>, tables.cpp:134-142)
+__device__ __forceinline__ float row_chain(const float *f, const uint16_t *d, const float *xdc, const float *xsc,
+                                           int nb) {
+    float acc = 0.0f, cor = 0.0f;
+    for (int j = 0; j < nb; j += 4) {   // nb is a multiple of 8
+        const float4 fv = *(const float4 *) (f + j), xv = *(const float4 *) (xdc + j), sv = *(const float4 *) (xsc + j);
+        const uint2 dv = *(const uint2 *) (d + j);
+        const float d0 = h2f((uint16_t) (dv.x & 0xffff)), d1 = h2f((uint16_t) (dv.x >> 16)),
+                    d2 = h2f((uint16_t) (dv.y & 0xffff)), d3 = h2f((uint16_t) (dv.y >> 16));
+        acc = __fmaf_rn(fv.x, __fmul_rn(d0, xv.x), acc);
+        cor = __fmaf_rn(d0, sv.x, cor);
+        acc = __fmaf_rn(fv.y, __fmul_rn(d1, xv.y), acc);
+        cor = __fmaf_rn(d1, sv.y, cor);
+        acc = __fmaf_rn(fv.z, __fmul_rn(d2, xv.z), acc);
+        cor = __fmaf_rn(d2, sv.z, cor);
+        acc = __fmaf_rn(fv.w, __fmul_rn(d3, xv.w), acc);
+        cor = __fmaf_rn(d3, sv.w, cor);
+    }
+    return __fmaf_rn(-8.0f, cor, acc);
+}
+
+template <int PRO, int EPI, int NC>
+__global__ void __launch_bounds__(MV_THREADS, 2) k_table(const __grid_constant__ MvArgs a) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    __shared__ int abort_flag, last_cta;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, K = a.cols, nb = K / 32, ld = nb + 4,
+              nc = a.ncol, sr = a.sr;
+    const MvPlan P = mv_plan(K, sr, NC, mv_vb_len(PRO, K, a.n_embd), a.ab_len);
+    uint8_t *stage = sm + P.stage;
+    uint64_t *bar = (uint64_t *) (sm + P.bar);
+    const int8_t *xq = (const int8_t *) (sm + P.xq);
+    const float *xd = (const float *) (sm + P.xd), *xs = (const float *) (sm + P.xs);
+    float *fs = (float *) (sm + P.fs), *red = (float *) (sm + P.red), *ab = (float *) (sm + P.ab);
+    uint16_t *dd = (uint16_t *) (sm + P.dd);
+
+    const int units = a.rows / a.unit;
+    const int u0 = (int) ((long long) units * blockIdx.x / gridDim.x),
+              u1 = (int) ((long long) units * (blockIdx.x + 1) / gridDim.x);
+    const int r0 = u0 * a.unit, nrows = (u1 - u0) * a.unit;
+    const int nst = (nrows + sr - 1) / sr;
+
+    unsigned long long *trace = a.trace ? a.trace + (size_t) blockIdx.x * MV_TRACE : nullptr;
+    if (trace && tid == 0) trace[0] = global_ns();
+    if (tid == 0) {
+        for (int b = 0; b < MV_STAGES; b++) mbar_init(&bar[b], 1);
+        fence_barrier_init();
+        abort_flag = 0;
+    }
+    __syncthreads();
+    auto issue = [&](int st) {
+        const int rr = st * sr, n = min(sr, nrows - rr);
+        const uint32_t bytes = (uint32_t) n * (uint32_t) a.row_bytes;
+        uint64_t *b = &bar[st % MV_STAGES];
+        mbar_expect_tx(b, bytes);
+        bulk_g2s(stage + (st % MV_STAGES) * MV_STAGE_BYTES, a.W + (size_t) (r0 + rr) * a.row_bytes, bytes, b);
+    };
+    if (tid == 0)   // the weights do not depend on the previous launch: start them before waiting on it
+        for (int st = 0; st < min(MV_STAGES, nst); st++) issue(st);
+    pdl_trigger();
+    pdl_wait();
+    if (trace && tid == 0) trace[1] = global_ns();
+    table_prologue<PRO, NC>(a, P, sm);
+    if (trace && tid == 0) trace[2] = global_ns();
+
+    if (warp < MV_IWARPS) {
+        // ---------------- integer warps ----------------
+        const int it = tid;
+        const bool fixed_j = (MV_ITHREADS % nb) == 0;   // nb divides 256: each thread keeps one block column
+        const int j0 = fixed_j ? it % nb : 0, rstep = fixed_j ? MV_ITHREADS / nb : 0;
+        constexpr int NX = NC <= 2 ? NC : 1;
+        int xw[NX][8];
+        if (NC <= 2 && fixed_j) {
+#pragma unroll
+            for (int c = 0; c < NX; c++) {
+                const int4 *xp = (const int4 *) (xq + c * K + 32 * j0);
+                const int4 x0 = xp[0], x1 = xp[1];
+                xw[c][0] = x0.x; xw[c][1] = x0.y; xw[c][2] = x0.z; xw[c][3] = x0.w;
+                xw[c][4] = x1.x; xw[c][5] = x1.y; xw[c][6] = x1.z; xw[c][7] = x1.w;
+            }
+        }
+        const int nchunk = nb / 4;   // 8-byte chunks of a row's scales (scale rows are nb + 4 halfs: 8-byte aligned)
+        for (int st = 0; st < nst; st++) {
+            const int b = st & 1;
+            bool ok = mbar_wait(&bar[st % MV_STAGES], (uint32_t) ((st / MV_STAGES) & 1));
+            ok = nbar_and(NB_INT, MV_ITHREADS, ok);
+            if (!ok && it == 0) { abort_flag = 1; atomicExch(a.err, 7); }
+            if (st >= 2) nbar_sync(NB_FREE + b, MV_THREADS);   // the chains are done with buffer b
+            if (ok) {
+                const int rb = st * sr, nr = min(sr, nrows - rb);
+                const uint8_t *sb = stage + (st % MV_STAGES) * MV_STAGE_BYTES;
+                float *f = fs + b * NC * sr * ld;
+                uint16_t *dq = dd + b * sr * ld;
+                for (int idx = it; idx < nr * nchunk; idx += MV_ITHREADS) {   // the rows' scales
+                    const int r = idx / nchunk, k = idx - r * nchunk;
+                    *(uint2 *) (dq + r * ld + 4 * k) = *(const uint2 *) (sb + (size_t) r * a.row_bytes + K / 2 + 8 * k);
+                }
+                auto one = [&](int r, int j, bool cached) {
+                    const uint4 code = *(const uint4 *) (sb + (size_t) r * a.row_bytes + 16 * j);
+#pragma unroll
+                    for (int c = 0; c < NC; c++) {
+                        if (c < nc) {
+                            int s;
+                            if (NC <= 2 && cached) {
+                                s = dot_block(code, xw[c < NX ? c : 0]);
+                            } else {
+                                const int4 *xp = (const int4 *) (xq + c * K + 32 * j);
+                                const int4 x0 = xp[0], x1 = xp[1];
+                                const int x8[8] = { x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w };
+                                s = dot_block(code, x8);
+                            }
+                            f[(c * sr + r) * ld + j] = __int2float_rn(s);
+                            if (c == 0 && a.dots) a.dots[(size_t) (r0 + rb + r) * nb + j] = s;
+                        }
+                    }
+                };
+                if (fixed_j) {
+                    for (int r = it / nb; r < nr; r += rstep) one(r, j0, true);
+                } else {
+                    for (int idx = it; idx < nr * nb; idx += MV_ITHREADS) one(idx / nb, idx % nb, false);
+                }
+            }
+            nbar_sync(NB_INT, MV_ITHREADS);   // every integer thread is done with this stage buffer
+            if (trace && it == 0 && st < 11) trace[3 + st] = global_ns();
+            if (it == 0 && ok && st + MV_STAGES < nst) {
+                fence_proxy_async();
+                issue(st + MV_STAGES);
+            }
+            nbar_arrive(NB_READY + b, MV_THREADS);
+        }
+        for (int st = max(nst - 2, 0); st < nst; st++) nbar_sync(NB_FREE + (st & 1), MV_THREADS);
+        return;
+    }
+
+    // ---------------- chain warps: one thread per (input, row) ----------------
+    const int ct = tid - MV_ITHREADS;
+    unsigned long long best[NC];
+#pragma unroll
+    for (int c = 0; c < NC; c++) best[c] = 0ull;
+    for (int st = 0; st < nst; st++) {
+        const int b = st & 1;
+        nbar_sync(NB_READY + b, MV_THREADS);
+        const bool ok = abort_flag == 0;
+        const int rb = st * sr, nr = min(sr, nrows - rb);
+        const float *f = fs + b * NC * sr * ld;
+        const uint16_t *dq = dd + b * sr * ld;
+        if (ok) {
+            for (int base = 0; base < nc * nr; base += MV_CTHREADS) {   // warp-uniform trip count
+                const int t = base + ct;
+                const bool act = t < nc * nr;
+                const int c = act ? t / nr : 0, r = act ? t - c * nr : 0;
+                float v = 0.0f;
+                if (act) v = row_chain(f + (c * sr + r) * ld, dq + r * ld, xd + c * nb, xs + c * nb, nb);
+                if (EPI == E_STORE) {
+                    if (act) a.out[(size_t) c * a.out_stride + r0 + rb + r] = v;
+                } else if (EPI == E_SILU) {   // rows (2i, 2i+1) are (gate_i, up_i): act_i = silu(gate) * up (seoul.cpp:384-391)
+                    const float u = __shfl_down_sync(0xffffffffu, v, 1);
+                    if (act && (r & 1) == 0) {
+                        const float sl = __fdiv_rn(v, __fadd_rn(1.0f, exp_cr(-v)));
+                        const float y = __fmul_rn(sl, u);
+                        a.out[(size_t) c * a.out_stride + (r0 + rb + r) / 2] = y;
+                        if (a.q8o_q) ab[c * a.ab_len + (rb + r) / 2] = y;
+                    }
+                } else if (act) {   // E_HEAD: word scores and the running first maximum
+                    const int row = r0 + rb + r;
+                    float *lg = a.cols_d[c].logits;
+                    if (lg) lg[row] = v;
+#pragma unroll
+                    for (int cc = 0; cc < NC; cc++)
+                        if (cc == c) {
+                            const unsigned long long k = amax_key(v, row);
+                            best[cc] = k > best[cc] ? k : best[cc];
+                        }
+                }
+            }
+        }
+        nbar_arrive(NB_FREE + b, MV_THREADS);
+    }
+    if (trace && ct == 0) trace[14] = global_ns();
+    if (EPI == E_SILU && a.q8o_q && abort_flag == 0) {   // the cut of this CTA's whole 32-value blocks (imi_cut32)
+        nbar_sync(NB_TAIL, MV_CTHREADS);
+        const int nblk = nrows / 64, half = a.rows / 2;
+        for (int t = ct; t < nc * nblk; t += MV_CTHREADS) {
+            const int c = t / nblk, k = t - c * nblk;
+            float v[32];
+            load32(ab + c * a.ab_len + 32 * k, v);
+            const int blk = r0 / 64 + k;
+            cut32(v, a.q8o_q + (size_t) c * half + 32 * blk, a.q8o_d + (size_t) c * (half / 32) + blk,
+                  a.q8o_s + (size_t) c * (half / 32) + blk);
+        }
+    }
+
+    if (EPI == E_HEAD) {   // the step ends here: pick, position, counters (one CTA, the last to finish)
+        unsigned long long *wbest = (unsigned long long *) (red + 64);
+        const int cw = warp - MV_IWARPS;
+#pragma unroll
+        for (int c = 0; c < NC; c++) {
+            unsigned long long k = best[c];
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+                const unsigned long long u = __shfl_xor_sync(0xffffffffu, k, o);
+                k = u > k ? u : k;
+            }
+            if (lane == 0) wbest[c * MV_CWARPS + cw] = k;
+        }
+        nbar_sync(NB_TAIL, MV_CTHREADS);
+        if (ct < nc && abort_flag == 0) {
+            unsigned long long k = 0;
+            for (int w = 0; w < MV_CWARPS; w++) k = wbest[ct * MV_CWARPS + w] > k ? wbest[ct * MV_CWARPS + w] : k;
+            atomicMax(&a.cols_d[ct].s->amax, k);
+        }
+        __threadfence();
+        nbar_sync(NB_TAIL, MV_CTHREADS);
+        if (ct == 0) last_cta = atomicAdd(a.done, 1u) == gridDim.x - 1;
+        nbar_sync(NB_TAIL, MV_CTHREADS);
+        if (last_cta && ct < nc) {
+            __threadfence();
+            const Col col = a.cols_d[ct];
+            const unsigned long long k = atomicExch(&col.s->amax, 0ull);
+            const int id = (int) (0xffffffffu - (uint32_t) (k & 0xffffffffu));
+            col.s->next_token = id;
+            col.s->amax_val = amax_val(k);
+            if (col.picks) col.picks[col.s->pos + col.off] = id;
+            if (col.pos_inc) atomicAdd(&col.s->pos, col.pos_inc);
+        }
+        if (last_cta && ct == 0) *a.done = 0;
+    }
+}
+
+}  // namespace imi

@@ -55,13 +55,14 @@ class Shape:
 SEOUL = Shape()
 # small shapes for the CPU suite and quick GPU parity checks. n_embd must be a multiple of 256 (imi reads the word
 # table in 256-wide pieces, seoul.cpp:236,363) and n_head a multiple of 8 (the stacked q|k|v|gate table is read in
-# 8-row groups, tables.cpp:68)
-TINY = Shape(n_embd=256, n_layer=4, attn_layers=(1, 3), n_head=8, n_head_kv=2, head_dim=64, n_ff=512,
+# 8-row groups, tables.cpp:68). n_head * head_dim equals n_embd, as in Seoul: the reference's batched read cuts the
+# attention output with the n_embd-wide input shape (seoul.cpp:554,623), so only such shapes give it one meaning
+TINY = Shape(n_embd=512, n_layer=4, attn_layers=(1, 3), n_head=8, n_head_kv=2, head_dim=64, n_ff=1024,
              n_vocab=1003)
 SMALL = Shape(n_embd=512, n_layer=6, attn_layers=(2, 4), n_head=8, n_head_kv=2, head_dim=64, n_ff=1536,
               n_vocab=4099)
 # the real Seoul geometry's attention (heads of 128, sliding-window layers, rope_freqs), scaled down
-WIDE_HEADS = Shape(n_embd=512, n_layer=4, attn_layers=(1, 2, 3), n_head=8, n_head_kv=2, head_dim=128, n_ff=1024,
+WIDE_HEADS = Shape(n_embd=1024, n_layer=4, attn_layers=(1, 2, 3), n_head=8, n_head_kv=2, head_dim=128, n_ff=2048,
                    n_vocab=2001, n_swa=8, swa_layers=(2,), rope_freqs=True)
 
 SHAPES = {"seoul": SEOUL, "tiny": TINY, "small": SMALL, "wide_heads": WIDE_HEADS}

@@ -1,0 +1,54 @@
+"""Kernel-level parity on the GPU (B200): the 8-bit cut and the 4-bit table kernel against the oracle, bit for bit.
+Integer block dots and 8-bit codes are integer work: bit-exact. The float outputs of the table kernel are also
+bit-exact, because the kernel keeps imi's per-row accumulation order (tables.cpp:127-143)."""
+import numpy as np
+import pytest
+
+import nunchi_b200 as nb
+import oracle
+from nunchi_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def test_cut_bit_exact():
+    rng = np.random.default_rng(0)
+    x = np.concatenate([rng.standard_normal(4096), rng.standard_normal(4096) * 1e-3, rng.standard_normal(4096) * 50,
+                        np.zeros(32), np.linspace(-3, 3, 32), 127.0 * np.arange(32) / 31.0, np.full(32, 1e-30)])
+    x = x.astype(np.float32)
+    q, d, s = nb.q8_cut(x)
+    qo, do, so = oracle.cut(x)
+    assert np.array_equal(q, qo)
+    assert np.array_equal(bits(d), bits(do)) and np.array_equal(bits(s), bits(so))
+
+
+@pytest.mark.parametrize("rows,cols,ncol", [(8, 256, 1), (64, 512, 1), (2048, 2048, 1), (300, 8192, 1), (1003, 512, 1),
+                                            (2048, 2048, 2), (1000, 512, 3), (97, 2048, 8), (5, 1024, 5)])
+def test_q4_table_bit_exact(rows, cols, ncol):
+    rng = np.random.default_rng(rows * 7 + cols + ncol)
+    q4 = synth._q4_0(rng, rows, cols).reshape(-1)
+    x = rng.standard_normal((ncol, cols)).astype(np.float32)
+    cuts = [oracle.cut(v) for v in x]
+    cq, cd, cs = (np.concatenate([c[k] for c in cuts]) for k in range(3))
+    want = oracle.q4_matvec(q4, rows, cols, cq, cd, cs)
+    if ncol == 1:
+        out, dots = nb.q4_matvec(q4, rows, cols, cq, cd, cs, dots=True)
+        assert np.array_equal(dots, oracle.block_dots(q4, rows, cols, cq)), "integer block dots differ"
+    else:
+        out = nb.q4_matvec(q4, rows, cols, cq, cd, cs)
+    assert np.array_equal(bits(out), bits(want))
+
+
+def test_q4_table_matches_reference_golden():
+    """The reference's own imi_q4_group / group2 / group_batch outputs (committed golden) on the device."""
+    import os
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "ref_tiny.npz"))
+    rows, cols = 64, 512
+    q, d, s = (np.concatenate([g[k][i] for i in range(5)]) for k in ("kat_q", "kat_d", "kat_s"))
+    out = nb.q4_matvec(g["kat_q4"], rows, cols, q, d, s)
+    assert np.array_equal(bits(out), bits(g["kat_out5"]))
+    assert np.array_equal(bits(nb.q4_matvec(g["kat_q4"], rows, cols, q[:cols], d[:16], s[:16])), bits(g["kat_out1"]))

@@ -1,0 +1,211 @@
+"""Step-level parity on the GPU (B200) against the oracle (the C restatement of imi's step, itself pinned bit-exact to
+the reference's own code).
+
+Float tolerances:
+  * error budget (north star): against the reference's fp64 truth key (committed golden), the engine's relative L2
+    error of the word scores is within 1e-3 of imi's own error at every position (test_error_budget_vs_truth_key);
+  * direct comparison: the engine keeps imi's float order everywhere, so most steps are bit-identical; the one
+    operation that can differ is expf (correctly rounded on the device; glibc's agrees on all but ~0.06% of inputs).
+    A 1-ulp difference there can move one 8-bit activation code by one step (1/127 of its block's maximum), and that
+    change stays in the attention cache, so direct comparisons allow TOL = 1e-2 of max|score|;
+  * greedy picks are identical except where the oracle's top two scores are within 1e-4 of max|score| (logged).
+"""
+import numpy as np
+import pytest
+
+import nunchi_b200 as nb
+import oracle
+from nunchi_b200 import synth
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+BUDGET = 1e-3
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def rel(a, b):
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def follow_greedy(o, ids):
+    """Run the oracle's greedy loop beside the device's picks: step k reads the previous pick (the first step reads
+    the pick after the prompt) and ids[k] is the pick step k makes. Every pick must match unless the oracle's top two
+    scores are within 1e-4 of max|score| there (a tie: logged, and the comparison stops, the paths part).
+    Returns how many picks matched."""
+    t = int(np.argmax(o.logits))
+    for k, got in enumerate(ids):
+        o.step(t)
+        lo = o.logits
+        t = int(np.argmax(lo))
+        if int(got) != t:
+            top2 = np.sort(lo)[-2:]
+            assert top2[1] - top2[0] <= 1e-4 * np.abs(lo).max(), f"greedy pick {k}: device {got} oracle {t}"
+            print(f"greedy pick {k}: near-tie ({top2[1] - top2[0]:.3g}), paths part here")
+            return k
+    return len(ids)
+
+
+def close_scores(lg, lo, log, where):
+    r = rel(lg, lo)
+    assert r <= TOL, f"{where}: scores differ by {r:.3g} of max"
+    top2 = np.sort(lo)[-2:]
+    tie = (top2[1] - top2[0]) <= 1e-4 * np.abs(lo).max()
+    if int(np.argmax(lg)) != int(np.argmax(lo)):
+        assert tie, f"{where}: greedy pick differs without a tie"
+        log.append(where)
+    return r
+
+
+@pytest.mark.parametrize("name,n", [("tiny", 40), ("small", 24), ("wide_heads", 30)])
+def test_steps_match_oracle(name, n):
+    path = synth.cached_gguf(name)
+    o = oracle.Oracle(path, n_ctx=128)
+    g = nb.Seoul(path, ctx_len=128)
+    exact, ties = 0, []
+    for i, t in enumerate(synth.random_ids(n, o.n_vocab, 3)):
+        o.step(int(t))
+        g.step(int(t))
+        ho, hg, lo, lg = o.hidden, g.hidden, o.logits, g.logits
+        assert rel(hg, ho) <= TOL, f"hidden at {i}"
+        close_scores(lg, lo, ties, f"{name} position {i}")
+        assert g.state.argmax()[0] == int(np.argmax(lg)), "device pick is not the first maximum of its scores"
+        exact += np.array_equal(bits(hg), bits(ho)) and np.array_equal(bits(lg), bits(lo))
+    print(f"{name}: {exact}/{n} steps bit-identical, ties {ties}")
+    assert exact >= n // 2
+
+
+@pytest.mark.parametrize("name", ["tiny", "wide_heads", "seoul"])
+def test_error_budget_vs_truth_key(name):
+    """The reference's fp64 truth key (imi/ref/ref_exact.py, committed in tests/golden): the engine's score error is
+    imi's own error within 1e-3 (metric of imi/ref/compare.py: relative L2 per position)."""
+    import os
+    gd = os.path.join(os.path.dirname(__file__), "golden")
+    ref, truth = np.load(os.path.join(gd, f"ref_{name}.npz")), np.load(os.path.join(gd, f"truth_{name}.npz"))
+    g = nb.Seoul(synth.cached_gguf(name), ctx_len=64)
+    for i, t in enumerate(ref["tokens"]):
+        g.step(int(t))
+        th = truth["hidden"][i]
+        e_imi = np.linalg.norm(ref["hidden"][i] - th) / np.linalg.norm(th)
+        e_gpu = np.linalg.norm(g.hidden - th) / np.linalg.norm(th)
+        assert abs(e_gpu - e_imi) <= BUDGET, f"hidden error at {i}: engine {e_gpu:.4g} imi {e_imi:.4g}"
+        if i < len(truth["logits_full"]):
+            tl = truth["logits_full"][i]
+            e_imi = np.linalg.norm(ref["logits_full"][i] - tl) / np.linalg.norm(tl)
+            e_gpu = np.linalg.norm(g.logits - tl) / np.linalg.norm(tl)
+            assert abs(e_gpu - e_imi) <= BUDGET, f"score error at {i}: engine {e_gpu:.4g} imi {e_imi:.4g}"
+        assert int(np.argmax(g.logits)) == int(ref["logits_top_ids"][i][0]) or \
+            ref["logits_top_vals"][i][0] - ref["logits_top_vals"][i][1] <= 1e-4 * np.abs(ref["logits_top_vals"][i]).max()
+
+
+def test_embedding_input_and_hidden_only(tiny_path):
+    o = oracle.Oracle(tiny_path, n_ctx=64)
+    g = nb.Seoul(tiny_path, ctx_len=64)
+    emb = (0.5 * np.random.default_rng(4).standard_normal((6, g.n_embd))).astype(np.float32)
+    for i in range(6):
+        o.step(-1, emb[i], want_logits=False)
+        g.step(-1, emb[i], want_logits=False)
+        assert rel(g.hidden, o.hidden) <= TOL
+    assert g.pos == 6
+
+
+def test_riding_is_byte_identical_to_alone(tiny_path):
+    e = nb.Engine(tiny_path, n_ctx=128)
+    a, b, a1, b1 = (e.new_state() for _ in range(4))
+    ta, tb = synth.random_ids(20, e.n_vocab, 5), synth.random_ids(30, e.n_vocab, 6)
+    for i in range(10):   # B starts ahead: the two conversations sit at different positions
+        b.step(tb[i])
+        b1.step(tb[i])
+    for i in range(20):
+        nb.step2(a, ta[i], None, True, b, tb[10 + i], None, i % 3 != 0)
+        a1.step(ta[i])
+        b1.step(tb[10 + i], want_logits=i % 3 != 0)
+        assert np.array_equal(bits(a.logits), bits(a1.logits)) and np.array_equal(bits(a.hidden), bits(a1.hidden))
+        assert np.array_equal(bits(b.hidden), bits(b1.hidden))
+        if i % 3:
+            assert np.array_equal(bits(b.logits), bits(b1.logits))
+    assert a.pos == 20 and b.pos == 30
+
+
+@pytest.mark.parametrize("n", [3, 8, 11])
+def test_step_multi_is_byte_identical_to_alone(tiny_path, n):
+    e = nb.Engine(tiny_path, n_ctx=64, max_batch=16)
+    multi = [e.new_state() for _ in range(n)]
+    alone = [e.new_state() for _ in range(n)]
+    toks = synth.random_ids(4 * n, e.n_vocab, 9).reshape(4, n)
+    for k in range(4):
+        nb.step_multi(multi, toks[k])
+        for i in range(n):
+            alone[i].step(toks[k, i])
+    for m, a in zip(multi, alone):
+        assert np.array_equal(bits(m.logits), bits(a.logits)) and m.pos == a.pos == 4
+
+
+@pytest.mark.parametrize("name", ["tiny", "wide_heads"])
+def test_step_batch_matches_oracle(name):
+    path = synth.cached_gguf(name)
+    o = oracle.Oracle(path, n_ctx=256)
+    g = nb.Engine(path, n_ctx=256).new_state()
+    toks = synth.random_ids(77, o.n_vocab, 8)          # 64 + 13: crosses the 64-position context check
+    ho = o.step_batch(tokens=toks, want_logits=True, hidden_all=True)
+    hg = g.step_batch(tokens=toks, want_logits=True, hidden_all=True)
+    assert max(rel(hg[i], ho[i]) for i in range(len(toks))) <= TOL
+    assert rel(g.logits, o.logits) <= TOL and g.pos == o.pos == 77
+    emb = (0.5 * np.random.default_rng(3).standard_normal((19, o.n_embd))).astype(np.float32)
+    ho = o.step_batch(embd=emb, want_logits=False, hidden_all=True)
+    hg = g.step_batch(embd=emb, want_logits=False, hidden_all=True)
+    assert max(rel(hg[i], ho[i]) for i in range(19)) <= TOL
+    # decoding continues from the batched state exactly as from stepped positions
+    o.step(5)
+    g.step(5)
+    assert rel(g.logits, o.logits) <= TOL
+
+
+def test_greedy_on_device_matches_oracle(small_path):
+    o = oracle.Oracle(small_path, n_ctx=128)
+    e = nb.Engine(small_path, n_ctx=128)
+    s = e.new_state()
+    prompt = synth.random_ids(12, e.n_vocab, 2)
+    s.step_batch(prompt, want_logits=True)
+    o.step_batch(tokens=prompt, want_logits=True)
+    ids = nb.greedy([s], 40)[:, 0]
+    assert follow_greedy(o, ids) >= 0
+
+
+def test_context_full_and_reset(tiny_path):
+    e = nb.Engine(tiny_path, n_ctx=4)
+    s = e.new_state()
+    for t in (1, 2, 3, 4):
+        s.step(t)
+    with pytest.raises(nb.ContextFull):
+        s.step(5)
+    assert s.pos == 4
+    s.reset()
+    with pytest.raises(nb.ContextFull):
+        s.step_batch(np.arange(5, dtype=np.int32))
+    assert s.pos == 0
+    s.step(1)
+    o = oracle.Oracle(tiny_path, n_ctx=4)
+    o.step(1)
+    assert rel(s.logits, o.logits) <= TOL
+    with pytest.raises(nb.ImiError):
+        s.step(e.n_vocab)   # token out of range
+
+
+def test_seoul_greedy_128_steps(seoul_path):
+    """32-id prompt, then 128 greedy steps, against the oracle running the same greedy loop."""
+    o = oracle.Oracle(seoul_path, n_ctx=192)
+    e = nb.Engine(seoul_path, n_ctx=192)
+    s = e.new_state()
+    prompt = synth.random_ids(32, e.n_vocab, 0)
+    s.step_batch(prompt, want_logits=True)
+    o.step_batch(tokens=prompt, want_logits=True)
+    assert rel(s.logits, o.logits) <= TOL
+    ids = nb.greedy([s], 128)[:, 0]
+    k = follow_greedy(o, ids)
+    if k == 128:
+        worst = rel(s.logits, o.logits)
+        print(f"seoul: 128 greedy picks identical, last-step score difference {worst:.3g}")
+        assert worst <= TOL

@@ -1,0 +1,153 @@
+"""The oracle pinned to the reference: its C restatement against the reference's own code (built from the reference
+tree into oracle/_ref) and against committed golden outputs of that code and of the reference's fp64 truth key.
+CPU only."""
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from nunchi_b200 import synth
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+GOLD = os.path.join(HERE, "golden")
+needs_ref = pytest.mark.skipif(not oracle.reference_available(), reason="oracle/_ref not built (no reference tree)")
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def gold(kind, name):
+    return np.load(os.path.join(GOLD, f"{kind}_{name}.npz"))
+
+
+# ---------------- small math ----------------
+
+def test_f2h_round_to_nearest_even_matches_numpy():
+    rng = np.random.default_rng(0)
+    vals = np.concatenate([rng.standard_normal(20000) * s for s in (1e-8, 1e-6, 1e-4, 1, 100, 3e4)]).astype(np.float32)
+    edge = np.array([0.0, -0.0, 65504, 65519.99, 65520, 1e9, -1e9, 6.1e-5, 5.96e-8, 2.98e-8, 2.99e-8, np.inf, -np.inf],
+                    np.float32)
+    ties = (np.arange(1, 2048, dtype=np.float32) + 0.5) * np.float32(2.0 ** -10)   # exact halfway cases
+    for x in np.concatenate([vals, edge, ties]):
+        assert oracle.f2h(x) == int(np.float32(x).astype(np.float16).view(np.uint16)), x
+
+
+def test_cut_edge_cases():
+    x = np.zeros(128, np.float32)
+    x[32:64] = 1e-30                      # tiny block (its scale's reciprocal still finite)
+    x[64:96] = np.linspace(-3, 3, 32)     # includes exact .5 products
+    x[96:128] = 127.0 * np.arange(32) / 31.0
+    q, d, s = oracle.cut(x)
+    assert (q[:32] == 0).all() and d[0] == 0 and s[0] == 0
+    assert np.abs(q).max() <= 127
+    for j in range(4):
+        qq = np.rint(x[32 * j:32 * j + 32] * (np.float32(1) / d[j] if d[j] else 0)).astype(np.int64)
+        assert (qq == q[32 * j:32 * j + 32]).all()
+
+
+# ---------------- against the golden outputs of the reference's own code ----------------
+
+@pytest.mark.parametrize("name", ["tiny", "wide_heads"])
+def test_kernels_match_reference_golden(name):
+    g = gold("ref", name)
+    rows, cols = 64, 512
+    for i, v in enumerate(g["kat_x"]):
+        q, d, s = oracle.cut(v)
+        assert np.array_equal(q, g["kat_q"][i]) and np.array_equal(bits(d), bits(g["kat_d"][i]))
+        assert np.array_equal(bits(s), bits(g["kat_s"][i]))
+    q = np.concatenate([oracle.cut(v)[0] for v in g["kat_x"]])
+    d = np.concatenate([oracle.cut(v)[1] for v in g["kat_x"]])
+    s = np.concatenate([oracle.cut(v)[2] for v in g["kat_x"]])
+    out = oracle.q4_matvec(g["kat_q4"], rows, cols, q, d, s)
+    assert np.array_equal(bits(out[:1]), bits(g["kat_out1"]))   # imi_q4_group
+    assert np.array_equal(bits(out[:2]), bits(g["kat_out2"]))   # imi_q4_group2
+    assert np.array_equal(bits(out), bits(g["kat_out5"]))       # imi_q8b + imi_q4_group_batch
+
+
+@pytest.mark.parametrize("name", ["tiny", "wide_heads"])
+def test_steps_match_reference_golden(name):
+    g = gold("ref", name)
+    o = oracle.Oracle(synth.cached_gguf(name), n_ctx=256)
+    for i, t in enumerate(g["tokens"]):
+        assert o.step(int(t)) == 0
+        assert np.array_equal(bits(o.hidden), bits(g["hidden"][i])), f"hidden differs at position {i}"
+        lg = o.logits
+        if i < len(g["logits_full"]):
+            assert np.array_equal(bits(lg), bits(g["logits_full"][i])), f"logits differ at position {i}"
+        assert np.array_equal(np.argsort(-lg, kind="stable")[:16], g["logits_top_ids"][i])
+
+
+def test_seoul_steps_match_reference_golden(seoul_path):
+    g = gold("ref", "seoul")
+    o = oracle.Oracle(seoul_path, n_ctx=64)
+    for i, t in enumerate(g["tokens"]):
+        o.step(int(t))
+        assert np.array_equal(bits(o.hidden), bits(g["hidden"][i])), f"hidden differs at position {i}"
+        lg = o.logits
+        if i < len(g["logits_full"]):
+            assert np.array_equal(bits(lg), bits(g["logits_full"][i]))
+        assert np.array_equal(np.argsort(-lg, kind="stable")[:16], g["logits_top_ids"][i])
+        assert lg.astype(np.float64).sum() == pytest.approx(g["logits_sum"][i], rel=1e-12)
+
+
+@pytest.mark.parametrize("name", ["tiny", "wide_heads"])
+def test_step_batch_matches_reference_golden(name):
+    g = gold("ref", name)
+    o = oracle.Oracle(synth.cached_gguf(name), n_ctx=256)
+    ha = o.step_batch(embd=g["batch_embd"], want_logits=True, hidden_all=True)
+    assert np.array_equal(bits(ha), bits(g["batch_hidden"]))
+    assert np.array_equal(bits(o.logits), bits(g["batch_logits_full"][0]))
+
+
+@pytest.mark.parametrize("name", ["tiny", "wide_heads", "seoul"])
+def test_oracle_error_budget_against_truth_key(name):
+    """imi's own error against the fp64 truth key (the reference's ref_exact.py, compare.py metrics): the oracle must
+    sit at exactly the reference's budget; it is recorded here so the GPU tests can hold the engine to it."""
+    g, t = gold("ref", name), gold("truth", name)
+    eh = np.linalg.norm(g["hidden"] - t["hidden"], axis=1) / np.linalg.norm(t["hidden"], axis=1)
+    assert eh.max() < 0.15, eh   # 8-bit input cuts: a few percent (seoul_check.cpp:36-43 metrics)
+    full = len(t["logits_full"])
+    lg_ref = g["logits_full"][:full]
+    el = np.linalg.norm(lg_ref - t["logits_full"], axis=1) / np.linalg.norm(t["logits_full"], axis=1)
+    assert el.max() < 0.15, el
+
+
+# ---------------- live against the reference build (where the reference tree is present) ----------------
+
+@needs_ref
+@pytest.mark.parametrize("name", ["tiny", "small", "wide_heads"])
+def test_steps_match_reference_live(name):
+    path = synth.cached_gguf(name)
+    o, r = oracle.Oracle(path, n_ctx=128), oracle.Reference(path, n_ctx=128)
+    for t in synth.random_ids(20, o.n_vocab, 5):
+        o.step(int(t))
+        r.step(int(t))
+        assert np.array_equal(bits(o.hidden), bits(r.hidden)) and np.array_equal(bits(o.logits), bits(r.logits))
+
+
+@needs_ref
+def test_riding_and_state_swap_match_reference_live(tiny_path):
+    """The reference's step2 gives each conversation the numbers of its own step (seoul.cpp:222-224)."""
+    r = oracle.Reference(tiny_path, n_ctx=64)
+    o = oracle.Oracle(tiny_path, n_ctx=64)
+    ob = o.new_state()
+    b = r.new_state()
+    ta, tb = synth.random_ids(12, r.n_vocab, 1), synth.random_ids(12, r.n_vocab, 2)
+    for i in range(12):
+        r.step2(int(ta[i]), None, True, b, int(tb[i]), None, True)
+        o.step(int(ta[i]))
+        ob.step(int(tb[i]))
+        assert np.array_equal(bits(r.hidden), bits(o.hidden)) and np.array_equal(bits(b.logits), bits(ob.logits))
+
+
+@needs_ref
+def test_context_full_is_refused_like_the_reference(tiny_path):
+    o = oracle.Oracle(tiny_path, n_ctx=3)
+    for t in (1, 2, 3):
+        assert o.step(t) == 0
+    assert o.step(4) == 1 and o.pos == 3          # seoul.cpp:353: no step
+    o.reset()
+    with pytest.raises(RuntimeError):
+        o.step_batch(tokens=np.arange(4, dtype=np.int32))   # seoul.cpp:498
