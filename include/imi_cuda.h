@@ -118,6 +118,13 @@ imi_cuda_status imi_cuda_bench_tables(imi_cuda_engine *e, int ncol, int reps, fl
 imi_cuda_status imi_cuda_trace_table(imi_cuda_engine *e, int layer, int which, int ncol, unsigned long long *trace,
                                      int *grid);
 
+/* Diagnostics: one decode step of `s` (token given) launched directly (not from a graph) with every launch writing
+ * per-CTA phase timestamps (ns): out[launch][n_sm][16] as in imi_cuda_trace_table (attention / final norm: 0 start,
+ * 1 after the dependency wait, 14 end). kinds[launch]: 10*input+output kind of a table read, 100 attention, 101 final
+ * norm; grids[launch]: CTAs. *n receives the number of launches (at most max_launches). */
+imi_cuda_status imi_cuda_trace_step(imi_cuda_state *s, int32_t token, int want_logits, unsigned long long *out,
+                                    int max_launches, int *kinds, int *grids, int *n);
+
 /* ---- kernel level (known-answer tests and the isolated table sweep) ---- */
 
 /* Cut x[n] to 8-bit per 32 values on the device (imi_q8::from, tables.cpp:100-109 with imi_cut32, vec.h:47-77):

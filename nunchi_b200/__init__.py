@@ -71,6 +71,7 @@ def lib():
         L.imi_cuda_trace_table.argtypes = [_vp, C.c_int, C.c_int, C.c_int, _vp, C.POINTER(C.c_int)]
         L.imi_cuda_state_save.argtypes = [_vp, _vp, C.c_size_t, C.POINTER(C.c_size_t)]
         L.imi_cuda_state_load.argtypes = [_vp, _vp, C.c_size_t]
+        L.imi_cuda_trace_step.argtypes = [_vp, C.c_int32, C.c_int, _vp, C.c_int, _vp, _vp, C.POINTER(C.c_int)]
         L.imi_cuda_q8_cut.argtypes = [C.c_int, _fp, C.c_int, _vp, _fp, _fp]
         L.imi_cuda_q4_matvec.argtypes = [C.c_int, _vp, C.c_int, C.c_int, _vp, _fp, _fp, C.c_int, _fp, _ip]
         _L = L
@@ -139,6 +140,17 @@ def trace_table(engine: "Engine", layer: int, which: int, ncol: int = 1) -> np.n
     g = C.c_int()
     _check(lib().imi_cuda_trace_table(engine.h, layer, which, ncol, _ptr(buf), C.byref(g)))
     return buf[: g.value]
+
+
+def trace_step(state: "State", token: int, want_logits: bool = True, max_launches: int = 256):
+    """Diagnostics: per-launch per-CTA phase timestamps (ns) of one decode step (imi_cuda_trace_step)."""
+    nsm = 148
+    out = np.zeros((max_launches, nsm, 16), np.uint64)
+    kinds, grids = np.zeros(max_launches, np.int32), np.zeros(max_launches, np.int32)
+    n = C.c_int()
+    _check(lib().imi_cuda_trace_step(state.h, int(token), int(bool(want_logits)), _ptr(out), max_launches, _ptr(kinds),
+                                     _ptr(grids), C.byref(n)))
+    return out[: n.value], kinds[: n.value], grids[: n.value]
 
 
 class State:

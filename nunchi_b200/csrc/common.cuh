@@ -110,6 +110,7 @@ struct AttnArgs {
     int *err;
     int8_t *q8o_q;                    // the 8-bit cut of the attention output, per column [c][n_head*head_dim] codes,
     float *q8o_d, *q8o_s;             // [c][n_head*head_dim/32] scales and scale*sums (the o table reads only these)
+    unsigned long long *trace;        // optional: per-CTA timestamps (ns), [grid][MV_TRACE]: 0 start, 1 after wait, 14 end
 };
 
 struct FinalArgs {
@@ -122,6 +123,7 @@ struct FinalArgs {
     const float *wpost, *out_norm;
     float eps;
     int n_embd;
+    unsigned long long *trace;        // optional: per-CTA timestamps (ns), [grid][MV_TRACE]
 };
 
 // ---- shared-memory plan of the table-read kernel (host and device agree on it) ----
@@ -153,8 +155,11 @@ __host__ __device__ inline MvPlan mv_plan(int cols, int sr, int nc, int vb_len, 
 }
 
 // floats per column staged in shared memory by the input preparation of `pro`
-__host__ __device__ inline int mv_vb_len(int pro, int cols, int n_embd) {
-    return pro == P_CUT ? cols : (pro == P_EMBED_NORM || pro == P_RESID_NORM || pro == P_FINAL || pro == P_CONV) ? n_embd : 0;
+__host__ __device__ inline int mv_vb_len(int pro, int cols, int n_embd, int nc) {
+    // P_RESID_NORM / P_FINAL stage two vectors per column (the post-normed input and the residual) for up to 2
+    // columns; with more, the residual is read from global memory where it is used
+    return pro == P_CUT ? cols : (pro == P_RESID_NORM || pro == P_FINAL) ? (nc <= 2 ? 2 : 1) * n_embd
+                               : (pro == P_EMBED_NORM || pro == P_CONV) ? n_embd : 0;
 }
 
 #ifdef __CUDACC__
@@ -259,6 +264,10 @@ __device__ __forceinline__ unsigned long long global_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
     return t;
+}
+// bulk prefetch of global memory into L2 (16-byte aligned address, size a multiple of 16)
+__device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

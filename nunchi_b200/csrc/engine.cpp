@@ -80,6 +80,16 @@ struct imi_cuda_engine {
     std::map<int, cudaGraphExec_t> graphs;
     size_t state_bytes = 0;
     uint8_t *qbuf = nullptr;
+    // diagnostics: when trace_buf is set, every launch enqueued gets its own [grid][MV_TRACE] slice
+    unsigned long long *trace_buf = nullptr;
+    int trace_n = 0, trace_max = 0;
+    std::vector<int> trace_kind, trace_grid;
+    unsigned long long *trace_slot(int kind, int grid) {
+        if (!trace_buf || trace_n >= trace_max) return nullptr;
+        trace_kind.push_back(kind);
+        trace_grid.push_back(grid);
+        return trace_buf + (size_t) (trace_n++) * sm_count * MV_TRACE;
+    }
     const float *f32(size_t off) const { return (const float *) (w + off); }
     ~imi_cuda_engine();
 };
@@ -212,6 +222,8 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
     e->n_vocab = (int) te->ne[1];
     if (e->n_embd % 256) return fail(IMI_E_FORMAT, "n_embd must be a multiple of 256");
     if (e->n_layer <= 0 || e->d_conv < 1 || e->head_dim <= 0) return fail(IMI_E_FORMAT, "bad lfm3 hyperparameters");
+    if (e->d_conv > 8 || e->n_embd > 6144)   // the input preparation keeps 8 taps / 4 x 384 float4 chunks in registers
+        return fail(IMI_E_FORMAT, "conv width above 9 or n_embd above 6144 is not supported");
     const int E = e->n_embd;
     {
         std::vector<std::pair<const gguf_tensor *, int>> rows;
@@ -400,6 +412,7 @@ cudaError_t table_launch(imi_cuda_engine *e, const TableRef &t, int pro, int epi
     const int grid = std::max(1, std::min(e->sm_count, units));
     a.ab_len = epi == E_SILU ? (units + grid - 1) / grid * a.unit / 2 : 0;
     a.sr = pick_sr(pro, t, gran, a.ncol, e->n_embd, a.ab_len);
+    if (!a.trace) a.trace = e->trace_slot(10 * pro + epi, grid);
     return launch_table(pro, epi, a, grid, e->stream, true);
 }
 
@@ -477,6 +490,7 @@ cudaError_t enqueue_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind)
             t.q8o_d = e->qt_d;
             t.q8o_s = e->qt_s;
             if (kind == K_PREFILL && (r = launch_kvwrite(t, e->stream, true)) != cudaSuccess) return r;
+            t.trace = e->trace_slot(100, e->n_head_kv * ncol);
             if ((r = launch_attn(t, e->stream, true)) != cudaSuccess) return r;
             a = b;
             a.q8_q = e->qt_q;
@@ -533,6 +547,7 @@ cudaError_t enqueue_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind)
     fa.out_norm = e->f32(e->out_norm);
     fa.eps = e->eps;
     fa.n_embd = E;
+    fa.trace = e->trace_slot(101, ncol);
     return launch_final(fa, e->stream, true);
 }
 
@@ -1103,6 +1118,36 @@ imi_cuda_status imi_cuda_state_load(imi_cuda_state *s, const void *buf, size_t s
     CK(cudaMemcpy(s->s, &sd, sizeof sd, cudaMemcpyHostToDevice));
     s->pos = h.pos;
     return IMI_OK;
+}
+
+imi_cuda_status imi_cuda_trace_step(imi_cuda_state *s, int32_t token, int want_logits, unsigned long long *out,
+                                    int max_launches, int *kinds, int *grids, int *n) {
+    if (!s || !out || !kinds || !grids || !n || max_launches <= 0) return fail(IMI_E_ARG, "bad trace_step arguments");
+    imi_cuda_engine *e = s->e;
+    if (s->pos >= e->n_ctx) return fail(IMI_E_CTX_FULL, "context full");
+    if (token < 0 || token >= e->n_vocab) return fail(IMI_E_ARG, "token out of range");
+    CK(cudaSetDevice(e->device));
+    imi_cuda_status st;
+    if ((st = staging_wait(e)) != IMI_OK) return st;
+    const size_t per = (size_t) e->sm_count * MV_TRACE;
+    CK(cudaMalloc(&e->trace_buf, per * max_launches * 8));
+    CK(cudaMemsetAsync(e->trace_buf, 0, per * max_launches * 8, e->stream));
+    e->trace_n = 0;
+    e->trace_max = max_launches;
+    e->trace_kind.clear();
+    e->trace_grid.clear();
+    e->cols_h[0] = decode_col(s, token, false, 0, want_logits != 0);
+    CK(cudaMemcpyAsync(e->cols_d, e->cols_h, sizeof(Col), cudaMemcpyHostToDevice, e->stream));
+    cudaError_t r = enqueue_step(e, 1, want_logits != 0, K_DECODE);
+    if (r == cudaSuccess) r = cudaMemcpyAsync(out, e->trace_buf, per * e->trace_n * 8, cudaMemcpyDeviceToHost, e->stream);
+    if (r == cudaSuccess) r = cudaStreamSynchronize(e->stream);
+    cudaFree(e->trace_buf);
+    e->trace_buf = nullptr;
+    if (r != cudaSuccess) return fail(IMI_E_CUDA, std::string("trace_step: ") + cudaGetErrorString(r));
+    *n = e->trace_n;
+    for (int i = 0; i < e->trace_n; i++) { kinds[i] = e->trace_kind[i]; grids[i] = e->trace_grid[i]; }
+    s->pos++;
+    return check_err(e);
 }
 
 }  // extern "C"

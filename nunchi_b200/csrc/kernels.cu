@@ -34,8 +34,11 @@ __device__ __forceinline__ void resid_add(float *vb, const float *r, const float
 __global__ void __launch_bounds__(256) k_final(const __grid_constant__ FinalArgs a) {
     extern __shared__ __align__(16) uint8_t smf[];
     float *v = (float *) smf, *red = v + a.n_embd;
+    unsigned long long *trace = a.trace ? a.trace + (size_t) blockIdx.x * MV_TRACE : nullptr;
+    if (trace && threadIdx.x == 0) trace[0] = global_ns();
     pdl_trigger();
     pdl_wait();
+    if (trace && threadIdx.x == 0) trace[1] = global_ns();
     const int c = blockIdx.x, E = a.n_embd;
     const Col col = a.cols_d[c];
     resid_add(v, a.in + (size_t) c * a.in_stride, a.xin + (size_t) c * a.x_stride, a.wpost, E, a.eps, red, 0);
@@ -49,6 +52,7 @@ __global__ void __launch_bounds__(256) k_final(const __grid_constant__ FinalArgs
         for (int i = threadIdx.x; i < E; i += blockDim.x) col.hid_out[i] = __fmul_rn(__fmul_rn(v[i], sc), a.out_norm[i]);
     __syncthreads();
     if (threadIdx.x == 0 && col.pos_inc) atomicAdd(&col.s->pos, col.pos_inc);   // several columns may share a conversation
+    if (trace && threadIdx.x == 0) trace[14] = global_ns();
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -137,6 +141,8 @@ __global__ void __launch_bounds__(GRP *D) k_attn(const __grid_constant__ AttnArg
     extern __shared__ __align__(16) uint8_t sma[];
     constexpr int NT = GRP * D, NW = NT / 32;
     const AttnPlan L = attn_plan(D, GRP, a.n_ctx);
+    unsigned long long *trace = a.trace ? a.trace + (size_t) (blockIdx.y * gridDim.x + blockIdx.x) * MV_TRACE : nullptr;
+    if (trace && threadIdx.x == 0) trace[0] = global_ns();
     float *q = (float *) (sma + L.q);          // [GRP][D] rotated queries
     float *qtmp = (float *) (sma + L.qtmp);    // [GRP][D] norm scratch per head
     float *ktmp = (float *) (sma + L.ktmp), *tmp = (float *) (sma + L.tmp);   // [D], [D]
@@ -149,6 +155,7 @@ __global__ void __launch_bounds__(GRP *D) k_attn(const __grid_constant__ AttnArg
     pdl_trigger();
     pdl_wait();
     const int g = blockIdx.x, c = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (trace && tid == 0) trace[1] = global_ns();
     const int H = a.n_head, kvd = a.n_head_kv * D;
     const Col col = a.cols_d[c];
     const int p = col.s->pos + col.off;
@@ -273,6 +280,7 @@ __global__ void __launch_bounds__(GRP *D) k_attn(const __grid_constant__ AttnArg
         qtmp[hh * D + i] = y;
     }
     // the 8-bit cut of this group's output blocks (imi_cut32 of seoul.cpp:457), so the o table only loads codes
+    if (trace && tid == 0) trace[13] = global_ns();
     if (a.q8o_q) {
         __syncthreads();
         const int HD = H * D;
@@ -284,6 +292,7 @@ __global__ void __launch_bounds__(GRP *D) k_attn(const __grid_constant__ AttnArg
                   a.q8o_s + (size_t) c * (HD / 32) + blk);
         }
     }
+    if (trace && tid == 0) trace[14] = global_ns();
 }
 
 __host__ __device__ inline size_t attn_smem_bytes(int D, int GRP, int n_ctx) { return attn_plan(D, GRP, n_ctx).total; }

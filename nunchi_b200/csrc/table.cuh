@@ -84,14 +84,18 @@ __device__ __forceinline__ void copy_vec(float *dst, const float *src, int n) {
     for (int i = 4 * threadIdx.x; i < n; i += 4 * MV_THREADS) *(float4 *) (dst + i) = *(const float4 *) (src + i);
 }
 
-// input preparation, all MV_THREADS threads, all columns at once; ends with a __syncthreads
+// input preparation, all MV_THREADS threads, all columns at once; ends with a __syncthreads.
+// Every global read of the activations is issued in one batch right after the dependency wait (one L2 round trip);
+// the norm weights go to registers (each thread keeps the float4 chunks q = tid, tid + MV_THREADS, ...).
+constexpr int PQ = 4;   // float4 chunks of an n_embd vector per thread (n_embd <= 4 * PQ * MV_THREADS = 6144)
 template <int PRO, int NC>
 __device__ void table_prologue(const MvArgs &a, const MvPlan &P, uint8_t *sm) {
     int8_t *xq = (int8_t *) (sm + P.xq);
     float *xd = (float *) (sm + P.xd), *xs = (float *) (sm + P.xs), *vb = (float *) (sm + P.vb);
     float *red = (float *) (sm + P.red);
-    const int tid = threadIdx.x, warp = tid >> 5, nc = a.ncol, K = a.cols, nb = K / 32, E = a.n_embd;
-    const int VL = mv_vb_len(PRO, K, E);
+    const int tid = threadIdx.x, warp = tid >> 5, nc = a.ncol, K = a.cols, nb = K / 32, E = a.n_embd, nq = E / 4;
+    const int VL = mv_vb_len(PRO, K, E, NC);
+    const bool x_in_smem = NC <= 2;   // the residual staged beside r (else read where it is used)
     const bool lead = blockIdx.x == 0;
     if (PRO == P_Q8IN) {   // codes made by the producer of the input (or given): [c][K], [c][K/32]
         for (int i = tid; i < nc * K / 16; i += MV_THREADS) ((int4 *) xq)[i] = ((const int4 *) a.q8_q)[i];
@@ -102,17 +106,60 @@ __device__ void table_prologue(const MvArgs &a, const MvPlan &P, uint8_t *sm) {
         __syncthreads();
         return;
     }
-    // 1. every column's vector into shared memory (coalesced)
-    if (PRO == P_CUT || PRO == P_RESID_NORM || PRO == P_FINAL) {
-        for (int c = 0; c < nc; c++) copy_vec(vb + c * VL, a.in + (size_t) c * a.in_stride, PRO == P_CUT ? K : E);
+    const bool norm = PRO == P_EMBED_NORM || PRO == P_RESID_NORM || PRO == P_FINAL;
+    const bool resid = PRO == P_RESID_NORM || PRO == P_FINAL;
+    float4 wpo[PQ], wpr[PQ];
+    if (norm) {
+#pragma unroll
+        for (int k = 0; k < PQ; k++) {
+            const int q = tid + k * MV_THREADS;
+            if (q < nq) {
+                wpr[k] = ((const float4 *) a.wpre)[q];
+                if (resid) wpo[k] = ((const float4 *) a.wpost)[q];
+            }
+        }
+    }
+    // 1. the activations into shared memory
+    if (PRO == P_CUT) {
+        for (int c = 0; c < nc; c++) copy_vec(vb + c * VL, a.in + (size_t) c * a.in_stride, K);
+    } else if (resid) {   // [c]: r (the table output to post-norm) then x (the residual stream)
+        for (int c = 0; c < nc; c++) {
+            const float4 *r4 = (const float4 *) (a.in + (size_t) c * a.in_stride);
+            const float4 *x4 = (const float4 *) (a.xin + (size_t) c * a.x_stride);
+            float4 rv[PQ], xv[PQ];
+#pragma unroll
+            for (int k = 0; k < PQ; k++) {
+                const int q = tid + k * MV_THREADS;
+                if (q < nq) { rv[k] = r4[q]; if (x_in_smem) xv[k] = x4[q]; }
+            }
+#pragma unroll
+            for (int k = 0; k < PQ; k++) {
+                const int q = tid + k * MV_THREADS;
+                if (q < nq) {
+                    ((float4 *) (vb + c * VL))[q] = rv[k];
+                    if (x_in_smem) ((float4 *) (vb + c * VL + E))[q] = xv[k];
+                }
+            }
+        }
     } else if (PRO == P_EMBED_NORM) {
         for (int c = 0; c < nc; c++) {
             const Col &col = a.cols_d[c];
             int tok = col.token;
             if (tok == -2) tok = col.s->next_token;
-            if (tok >= 0) {
+            if (tok >= 0) {   // d * (code - 8): 4 values of one block per chunk
                 const uint8_t *row = a.emb + (size_t) tok * a.emb_row_bytes;
-                for (int i = tid; i < E; i += MV_THREADS) vb[c * VL + i] = word_value(row, E, i);
+                for (int q = tid; q < nq; q += MV_THREADS) {
+                    const int j = q >> 3, k0 = (4 * q) & 31;
+                    const uint32_t w = *(const uint32_t *) (row + 16 * j + (k0 & 15));
+                    const float d = h2f(*(const uint16_t *) (row + E / 2 + 2 * j));
+                    const int sh = k0 < 16 ? 0 : 4;
+                    float4 v;
+                    v.x = __fmul_rn(d, (float) ((int) ((w >> sh) & 15) - 8));
+                    v.y = __fmul_rn(d, (float) ((int) ((w >> (8 + sh)) & 15) - 8));
+                    v.z = __fmul_rn(d, (float) ((int) ((w >> (16 + sh)) & 15) - 8));
+                    v.w = __fmul_rn(d, (float) ((int) ((w >> (24 + sh)) & 15) - 8));
+                    ((float4 *) (vb + c * VL))[q] = v;
+                }
             } else {
                 copy_vec(vb + c * VL, col.embd, E);
             }
@@ -120,33 +167,51 @@ __device__ void table_prologue(const MvArgs &a, const MvPlan &P, uint8_t *sm) {
     } else if (PRO == P_CONV) {
         // seoul.cpp:410-414 (run) and 566-576 (run_batch): u = c * (b*x*w[d_conv] + sum_k st_k * w_k), st_k the b*x of
         // position p - d_conv + k: from this step's earlier columns of the same conversation when that position is in
-        // this step, else from the conv memory ring
+        // this step, else from the conv memory ring. Per chunk of 4 channels, all loads first.
         const int R = a.d_conv + 1;
         for (int c = 0; c < nc; c++) {
             const Col &col = a.cols_d[c];
             const float *bcx = a.in + (size_t) c * a.in_stride;
             const int p = col.s->pos + col.off;
             const float *ring = col.ring + (size_t) a.conv_layer * R * E;
-            for (int e = tid; e < E; e += MV_THREADS) {
-                float u = __fmul_rn(__fmul_rn(bcx[e], bcx[2 * E + e]), a.conv_w[(size_t) a.d_conv * E + e]);
-                for (int k = 0; k < a.d_conv; k++) {
-                    const int qp = p - a.d_conv + k;
-                    float st;
-                    if (qp >= p - col.off) {
-                        const float *ob = a.in + (size_t) (c - a.d_conv + k) * a.in_stride;
-                        st = __fmul_rn(ob[e], ob[2 * E + e]);
-                    } else {
-                        st = ring[(size_t) (((qp % R) + R) % R) * E + e];
+            for (int q = tid; q < nq; q += MV_THREADS) {
+                const float4 b4 = ((const float4 *) bcx)[q], c4 = ((const float4 *) (bcx + E))[q],
+                             x4 = ((const float4 *) (bcx + 2 * E))[q];
+                const float4 wl = ((const float4 *) (a.conv_w + (size_t) a.d_conv * E))[q];
+                float4 st[8], wk[8];
+#pragma unroll
+                for (int k = 0; k < 8; k++) {
+                    if (k < a.d_conv) {
+                        const int qp = p - a.d_conv + k;
+                        wk[k] = ((const float4 *) (a.conv_w + (size_t) k * E))[q];
+                        if (qp >= p - col.off) {
+                            const float *ob = a.in + (size_t) (c - a.d_conv + k) * a.in_stride;
+                            const float4 ob4 = ((const float4 *) ob)[q], ox4 = ((const float4 *) (ob + 2 * E))[q];
+                            st[k] = make_float4(__fmul_rn(ob4.x, ox4.x), __fmul_rn(ob4.y, ox4.y), __fmul_rn(ob4.z, ox4.z),
+                                                __fmul_rn(ob4.w, ox4.w));
+                        } else {
+                            st[k] = ((const float4 *) (ring + (size_t) (((qp % R) + R) % R) * E))[q];
+                        }
                     }
-                    u = __fadd_rn(u, __fmul_rn(st, a.conv_w[(size_t) k * E + e]));
                 }
-                vb[c * VL + e] = __fmul_rn(u, bcx[E + e]);
+                float u[4] = { __fmul_rn(__fmul_rn(b4.x, x4.x), wl.x), __fmul_rn(__fmul_rn(b4.y, x4.y), wl.y),
+                               __fmul_rn(__fmul_rn(b4.z, x4.z), wl.z), __fmul_rn(__fmul_rn(b4.w, x4.w), wl.w) };
+#pragma unroll
+                for (int k = 0; k < 8; k++) {
+                    if (k < a.d_conv) {
+                        u[0] = __fadd_rn(u[0], __fmul_rn(st[k].x, wk[k].x));
+                        u[1] = __fadd_rn(u[1], __fmul_rn(st[k].y, wk[k].y));
+                        u[2] = __fadd_rn(u[2], __fmul_rn(st[k].z, wk[k].z));
+                        u[3] = __fadd_rn(u[3], __fmul_rn(st[k].w, wk[k].w));
+                    }
+                }
+                ((float4 *) (vb + c * VL))[q] =
+                    make_float4(__fmul_rn(u[0], c4.x), __fmul_rn(u[1], c4.y), __fmul_rn(u[2], c4.z), __fmul_rn(u[3], c4.w));
             }
         }
     }
     __syncthreads();
-    const bool norm = PRO == P_EMBED_NORM || PRO == P_RESID_NORM || PRO == P_FINAL;
-    if (PRO == P_RESID_NORM || PRO == P_FINAL) {   // x += norm(r) * w_post (imi_norm_mul_add, vec.h:41-44)
+    if (resid) {   // x += norm(r) * w_post (imi_norm_mul_add, vec.h:41-44); the new x replaces r in place
         if (warp < nc) {
             const float sc = warp_rms_scale(vb + warp * VL, E, a.eps);
             if ((tid & 31) == 0) red[warp] = sc;
@@ -154,18 +219,51 @@ __device__ void table_prologue(const MvArgs &a, const MvPlan &P, uint8_t *sm) {
         __syncthreads();
         for (int c = 0; c < nc; c++) {
             const float sc = red[c];
-            const float *x = a.xin + (size_t) c * a.x_stride;
-            for (int i = tid; i < E; i += MV_THREADS)
-                vb[c * VL + i] = __fadd_rn(x[i], __fmul_rn(__fmul_rn(vb[c * VL + i], sc), a.wpost[i]));
+            float4 *v4 = (float4 *) (vb + c * VL);
+            const float4 *x4 = x_in_smem ? (const float4 *) (vb + c * VL + E) : (const float4 *) (a.xin + (size_t) c * a.x_stride);
+#pragma unroll
+            for (int k = 0; k < PQ; k++) {
+                const int q = tid + k * MV_THREADS;
+                if (q < nq) {
+                    const float4 r = v4[q], x = x4[q], w = wpo[k];
+                    const float4 y = make_float4(__fadd_rn(x.x, __fmul_rn(__fmul_rn(r.x, sc), w.x)),
+                                                 __fadd_rn(x.y, __fmul_rn(__fmul_rn(r.y, sc), w.y)),
+                                                 __fadd_rn(x.z, __fmul_rn(__fmul_rn(r.z, sc), w.z)),
+                                                 __fadd_rn(x.w, __fmul_rn(__fmul_rn(r.w, sc), w.w)));
+                    v4[q] = y;
+                    if (a.xout && (int) (q % gridDim.x) == (int) blockIdx.x)   // the residual stream, spread over CTAs
+                        ((float4 *) (a.xout + (size_t) c * a.x_stride))[q] = y;
+                }
+            }
         }
         __syncthreads();
+    } else if (PRO == P_EMBED_NORM && a.xout) {
+        for (int c = 0; c < nc; c++)
+            for (int q = tid; q < nq; q += MV_THREADS)
+                if ((int) (q % gridDim.x) == (int) blockIdx.x)
+                    ((float4 *) (a.xout + (size_t) c * a.x_stride))[q] = ((const float4 *) (vb + c * VL))[q];
     }
-    if (norm) {
-        if (lead && a.xout)
-            for (int c = 0; c < nc; c++) copy_vec(a.xout + (size_t) c * a.x_stride, vb + c * VL, E);
-        if (warp < nc) {   // h = norm(x) * w_pre (imi_norm_mul, vec.h:36-39)
+    if (norm) {   // h = norm(x) * w_pre (imi_norm_mul, vec.h:36-39), in place
+        if (warp < nc) {
             const float sc = warp_rms_scale(vb + warp * VL, E, a.eps);
             if ((tid & 31) == 0) red[32 + warp] = sc;
+        }
+        __syncthreads();
+        for (int c = 0; c < nc; c++) {
+            const float sc = red[32 + c];
+            float4 *v4 = (float4 *) (vb + c * VL);
+            float *hid = PRO == P_FINAL ? a.cols_d[c].hid_out : nullptr;
+#pragma unroll
+            for (int k = 0; k < PQ; k++) {
+                const int q = tid + k * MV_THREADS;
+                if (q < nq) {
+                    const float4 x = v4[q], w = wpr[k];
+                    const float4 h = make_float4(__fmul_rn(__fmul_rn(x.x, sc), w.x), __fmul_rn(__fmul_rn(x.y, sc), w.y),
+                                                 __fmul_rn(__fmul_rn(x.z, sc), w.z), __fmul_rn(__fmul_rn(x.w, sc), w.w));
+                    v4[q] = h;
+                    if (hid && (int) (q % gridDim.x) == (int) blockIdx.x) ((float4 *) hid)[q] = h;
+                }
+            }
         }
         __syncthreads();
     }
@@ -174,31 +272,22 @@ __device__ void table_prologue(const MvArgs &a, const MvPlan &P, uint8_t *sm) {
         const int c = t / nb, j = t - c * nb;
         float v[32];
         load32(vb + c * VL + 32 * j, v);
-        if (norm) {
-            const float sc = red[32 + c];
-            float w[32];
-            load32(a.wpre + 32 * j, w);
-#pragma unroll
-            for (int k = 0; k < 32; k++) v[k] = __fmul_rn(__fmul_rn(v[k], sc), w[k]);
-            if (PRO == P_FINAL && lead && a.cols_d[c].hid_out) {
-                float *hid = a.cols_d[c].hid_out + 32 * j;
-#pragma unroll
-                for (int k = 0; k < 8; k++)
-                    ((float4 *) hid)[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
-            }
-        }
         cut32(v, xq + c * K + 32 * j, xd + t, xs + t);
     }
     // conv memory: the slot of each column's position takes b*x (seoul.cpp:419-423); written one launch after the conv
-    // read it, so no CTA of the reading launch can see it early
-    if (a.ring_layer >= 0 && lead) {
+    // read it, so no CTA of the reading launch can see it early; spread over the CTAs
+    if (a.ring_layer >= 0) {
         const int R = a.d_conv + 1;
         for (int c = 0; c < nc; c++) {
             const Col &col = a.cols_d[c];
             const int p = col.s->pos + col.off;
             const float *bcx = a.ring_src + (size_t) c * a.ring_src_stride;
-            float *slot = col.ring + ((size_t) a.ring_layer * R + p % R) * E;
-            for (int e = tid; e < E; e += MV_THREADS) slot[e] = __fmul_rn(bcx[e], bcx[2 * E + e]);
+            float4 *slot = (float4 *) (col.ring + ((size_t) a.ring_layer * R + p % R) * E);
+            for (int q = blockIdx.x * MV_THREADS + tid; q < nq; q += gridDim.x * MV_THREADS) {
+                const float4 b4 = ((const float4 *) bcx)[q], x4 = ((const float4 *) (bcx + 2 * E))[q];
+                slot[q] = make_float4(__fmul_rn(b4.x, x4.x), __fmul_rn(b4.y, x4.y), __fmul_rn(b4.z, x4.z),
+                                      __fmul_rn(b4.w, x4.w));
+            }
         }
     }
     __syncthreads();
@@ -258,7 +347,7 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_table(const __grid_constant__
     __shared__ int abort_flag, last_cta;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, K = a.cols, nb = K / 32, ld = nb + 4,
               nc = a.ncol, sr = a.sr;
-    const MvPlan P = mv_plan(K, sr, NC, mv_vb_len(PRO, K, a.n_embd), a.ab_len);
+    const MvPlan P = mv_plan(K, sr, NC, mv_vb_len(PRO, K, a.n_embd, NC), a.ab_len);
     uint8_t *stage = sm + P.stage;
     uint64_t *bar = (uint64_t *) (sm + P.bar);
     const int8_t *xq = (const int8_t *) (sm + P.xq);
@@ -287,8 +376,13 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_table(const __grid_constant__
         mbar_expect_tx(b, bytes);
         bulk_g2s(stage + (st % MV_STAGES) * MV_STAGE_BYTES, a.W + (size_t) (r0 + rr) * a.row_bytes, bytes, b);
     };
-    if (tid == 0)   // the weights do not depend on the previous launch: start them before waiting on it
+    if (tid == 0) {   // the weights do not depend on the previous launch: start them before waiting on it
         for (int st = 0; st < min(MV_STAGES, nst); st++) issue(st);
+        // and the rest of this CTA's slice into L2, so HBM streams the whole table while the stages are consumed
+        const size_t beg = (size_t) min(MV_STAGES * sr, nrows) * a.row_bytes, end = (size_t) nrows * a.row_bytes;
+        const uint8_t *base = a.W + (size_t) r0 * a.row_bytes;
+        for (size_t o = beg; o < end; o += 65536) prefetch_l2(base + o, (uint32_t) min((size_t) 65536, end - o));
+    }
     pdl_trigger();
     pdl_wait();
     if (trace && tid == 0) trace[1] = global_ns();
