@@ -138,6 +138,29 @@ imi_cuda_status imi_cuda_q8_cut(int device, const float *x, int n, int8_t *q, fl
 imi_cuda_status imi_cuda_q4_matvec(int device, const uint8_t *q4, int rows, int cols, const int8_t *xq,
                                    const float *xd, const float *xs, int ncol, float *out, int32_t *block_dots);
 
+/* ---- without allocation ---- */
+
+/* No counterpart in the reference (imi's own path has no device memory): imi_cuda_q4_matvec on device buffers that
+ * allocates nothing. It exists for callers that must not allocate device memory while they run: cudaFree waits for
+ * every stream of the device (a caller sharing the GPU with a running decode loop would stall it), a cudaMalloc may
+ * fail once a memory pool or another framework's caching allocator holds the free memory, and some callers run where
+ * allocating is not allowed at all (a real-time audio callback, an allocator hook).
+ *
+ * q4: the table as GGUF Q4_0 rows (rows x cols, 18-byte blocks); xq[ncol][cols] (16-byte aligned), xd, xs[ncol][cols/32]
+ * and out[ncol][rows]: all device memory of `device`; results as imi_cuda_q4_matvec gives them. stream: a cudaStream_t
+ * of that device (NULL: the default stream); the call returns once its work on that stream is done.
+ * Scratch: one static device array of this library per device (IMI_CUDA_STATIC_TABLE_BYTES for the table in the
+ * kernels' row layout, plus 4 KiB). The call clears what must start at zero (the column descriptors and the error
+ * flag) on the stream itself, so nothing needs to be zero beforehand. A table above IMI_CUDA_STATIC_TABLE_BYTES
+ * (rows * cols / 32 * 18 bytes) is refused with IMI_E_ARG.
+ * The first call on a device looks the scratch address up (cudaGetSymbolAddress, with that device current) and sets
+ * the kernels' shared-memory limits; a caller that captures CUDA work into a graph makes that first call before it
+ * starts capturing. The scratch is shared: two calls on the same device that overlap in time (from two host threads,
+ * or on two streams) race on it and corrupt each other's results; callers serialise them. */
+#define IMI_CUDA_STATIC_TABLE_BYTES 16777216u
+imi_cuda_status imi_cuda_q4_matvec_static(int device, const uint8_t *q4, int rows, int cols, const int8_t *xq,
+                                          const float *xd, const float *xs, int ncol, float *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -74,6 +74,7 @@ def lib():
         L.imi_cuda_trace_step.argtypes = [_vp, C.c_int32, C.c_int, _vp, C.c_int, _vp, _vp, C.POINTER(C.c_int)]
         L.imi_cuda_q8_cut.argtypes = [C.c_int, _fp, C.c_int, _vp, _fp, _fp]
         L.imi_cuda_q4_matvec.argtypes = [C.c_int, _vp, C.c_int, C.c_int, _vp, _fp, _fp, C.c_int, _fp, _ip]
+        L.imi_cuda_q4_matvec_static.argtypes = [C.c_int, _vp, C.c_int, C.c_int, _vp, _vp, _vp, C.c_int, _vp, _vp]
         _L = L
     return _L
 

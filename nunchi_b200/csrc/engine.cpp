@@ -17,6 +17,7 @@
 #include <cstring>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -945,6 +946,99 @@ imi_cuda_status imi_cuda_q4_matvec(int device, const uint8_t *q4, int rows, int 
     cudaFree(m);
     if (r != cudaSuccess) return fail(IMI_E_CUDA, std::string("q4_matvec: ") + cudaGetErrorString(r));
     if (herr) return fail(IMI_E_TIMEOUT, "q4_matvec: a device-side wait gave up");
+    return IMI_OK;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// the same table read without allocating (imi_cuda_q4_matvec_static)
+// ---------------------------------------------------------------------------------------------------------------
+// Some callers must not allocate device memory while they run: cudaFree waits for every stream of the device, so a
+// caller sharing the GPU with a running decode loop would stall it; a process whose HBM is already held by a memory
+// pool or another framework's caching allocator may see a fresh cudaMalloc fail; and a caller on a thread with a
+// fixed budget (an audio callback, an allocator hook) may not allocate at all. For them the read below keeps its
+// scratch in this library's own device memory, reserved once when the library's device code is loaded into a
+// context: [STATIC_HEAD: column descriptors, error flag | the repacked table, at most IMI_CUDA_STATIC_TABLE_BYTES].
+namespace {
+constexpr size_t STATIC_HEAD = 4096;
+constexpr size_t STATIC_ERR = 2048;   // offset of the device-side error flag inside the head
+constexpr int STATIC_MAX_DEVICES = 64;
+static_assert(sizeof(Col) * MV_MAX_COLS <= STATIC_ERR, "column descriptors overflow the static head");
+__device__ __align__(256) uint8_t g_static_scratch[STATIC_HEAD + IMI_CUDA_STATIC_TABLE_BYTES];
+std::mutex g_static_mu;
+uint8_t *g_static_addr[STATIC_MAX_DEVICES];   // the scratch's device address, per device (null until looked up)
+
+bool on_device(const void *p, int device) {
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return (at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged) && at.device == device;
+}
+}  // namespace
+
+imi_cuda_status imi_cuda_q4_matvec_static(int device, const uint8_t *q4, int rows, int cols, const int8_t *xq,
+                                          const float *xd, const float *xs, int ncol, float *out, void *stream) {
+    if (!q4 || !xq || !xd || !xs || !out || rows <= 0 || cols <= 0 || cols % 256 || ncol < 1 || ncol > MV_MAX_COLS)
+        return fail(IMI_E_ARG, "bad q4_matvec_static arguments (cols a multiple of 256, 1..8 inputs)");
+    const int nb = cols / 32, row_bytes = nb * 18;
+    const size_t table = (size_t) rows * row_bytes;
+    if (table > IMI_CUDA_STATIC_TABLE_BYTES)
+        return fail(IMI_E_ARG, "q4_matvec_static: the table takes " + std::to_string(table) +
+                                   " bytes (rows * cols / 32 * 18); the static scratch holds at most " +
+                                   std::to_string((size_t) IMI_CUDA_STATIC_TABLE_BYTES));
+    if ((uintptr_t) xq % 16 || (uintptr_t) xd % 4 || (uintptr_t) xs % 4 || (uintptr_t) out % 4)
+        return fail(IMI_E_ARG, "q4_matvec_static: xq must be 16-byte aligned, xd, xs and out 4-byte aligned");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev || device >= STATIC_MAX_DEVICES)
+        return fail(IMI_E_NODEV, "no CUDA device");
+    int prev = 0;
+    CK(cudaGetDevice(&prev));
+    CK(cudaSetDevice(device));
+    struct Restore {
+        int d;
+        ~Restore() { cudaSetDevice(d); }
+    } restore{ prev };
+    for (const void *p : { (const void *) q4, (const void *) xq, (const void *) xd, (const void *) xs, (const void *) out })
+        if (!on_device(p, device))
+            return fail(IMI_E_ARG, "q4_matvec_static: every buffer must be device memory of device " + std::to_string(device));
+    uint8_t *scratch = nullptr;
+    {   // once per device, with that device current: the scratch's address and the kernels' shared-memory limits
+        std::lock_guard<std::mutex> g(g_static_mu);
+        if (!g_static_addr[device]) {
+            CK(prepare_kernels());
+            void *p = nullptr;
+            const cudaError_t r = cudaGetSymbolAddress(&p, g_static_scratch);
+            if (r != cudaSuccess || !p)
+                return fail(IMI_E_CUDA, std::string("q4_matvec_static: scratch address: ") + cudaGetErrorString(r));
+            g_static_addr[device] = (uint8_t *) p;
+        }
+        scratch = g_static_addr[device];
+    }
+    cudaStream_t st = (cudaStream_t) stream;
+    Col *dcols = (Col *) scratch;
+    int *derr = (int *) (scratch + STATIC_ERR);
+    uint8_t *dW = scratch + STATIC_HEAD;
+    // the descriptors and the error flag must start at zero: cleared here, on the stream, before the kernels; the
+    // table area needs no clearing (the repack writes all of it before the read)
+    cudaError_t r = cudaMemsetAsync(scratch, 0, STATIC_HEAD, st);
+    if (r == cudaSuccess) r = launch_q4_repack(q4, rows, nb, dW, st);
+    if (r == cudaSuccess) {
+        MvArgs a = {};
+        a.W = dW; a.rows = rows; a.cols = cols; a.row_bytes = row_bytes; a.unit = 1;
+        a.cols_d = dcols; a.ncol = ncol; a.q8_q = xq; a.q8_d = xd; a.q8_s = xs;
+        a.out = out; a.out_stride = rows; a.err = derr; a.ring_layer = -1;
+        TableRef t; t.rows = rows; t.cols = cols; t.row_bytes = row_bytes;
+        a.sr = pick_sr(P_Q8IN, t, 1, ncol, 0, 0);
+        int sms = 148;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+        r = launch_table(P_Q8IN, E_STORE, a, std::max(1, std::min(sms, rows)), st, false);
+    }
+    int herr = 0;
+    if (r == cudaSuccess) r = cudaMemcpyAsync(&herr, derr, 4, cudaMemcpyDeviceToHost, st);
+    if (r == cudaSuccess) r = cudaStreamSynchronize(st);
+    if (r != cudaSuccess) return fail(IMI_E_CUDA, std::string("q4_matvec_static: ") + cudaGetErrorString(r));
+    if (herr) return fail(IMI_E_TIMEOUT, "q4_matvec_static: a device-side wait gave up");
     return IMI_OK;
 }
 

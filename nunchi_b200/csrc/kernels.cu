@@ -313,6 +313,21 @@ __global__ void k_q8_cut(const float *x, int n, int8_t *q, float *d, float *s) {
     }
 }
 
+// GGUF Q4_0 rows (blocks of 18 bytes: fp16 scale, then 16 code bytes) into the table kernel's row layout
+// [cols/2 code bytes | cols/32 fp16 scales]; one thread per block, byte copies (GGUF blocks are only 2-byte aligned)
+__global__ void k_q4_repack(const uint8_t *src, int rows, int nb, uint8_t *dst) {
+    const size_t i = (size_t) blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t) rows * nb) return;
+    const size_t r = i / nb;
+    const int j = (int) (i - r * nb);
+    const uint8_t *b = src + i * 18;
+    uint8_t *row = dst + r * (size_t) nb * 18;
+#pragma unroll
+    for (int k = 0; k < 16; k++) row[16 * j + k] = b[2 + k];
+    row[(size_t) nb * 16 + 2 * j] = b[0];
+    row[(size_t) nb * 16 + 2 * j + 1] = b[1];
+}
+
 }  // namespace imi
 
 #include "launch.inc"

@@ -13,4 +13,6 @@ cudaError_t launch_kvwrite(const AttnArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_final(const FinalArgs &a, cudaStream_t st, bool pdl);
 cudaError_t prepare_kernels();
 cudaError_t launch_q8_cut(const float *x, int n, int8_t *q, float *d, float *s, cudaStream_t st);
+// GGUF Q4_0 rows (device) into the table kernel's row layout (device), on stream st
+cudaError_t launch_q4_repack(const uint8_t *src, int rows, int nb, uint8_t *dst, cudaStream_t st);
 }  // namespace imi
