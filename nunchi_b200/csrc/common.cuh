@@ -76,7 +76,8 @@ struct MvArgs {
     int emb_row_bytes;
     const float *conv_w;       // [d_conv+1][n_embd]
     int d_conv, conv_layer, n_embd;
-    int ring_layer;            // >= 0: write the conv memory slots of this layer from ring_src (bcx rows)
+    int ring_layer;            // >= 0: write the conv memory slots of this layer from ring_src (bcx rows); in P_CONV
+                               // (a step of distinct conversations) the conv's own input is written to it
     const float *ring_src;
     int ring_src_stride;
     const int8_t *q8_q;        // P_Q8IN: codes [ncol][cols], scales and sums [ncol][cols/32]
@@ -128,9 +129,16 @@ struct FinalArgs {
 
 // ---- shared-memory plan of the table-read kernel (host and device agree on it) ----
 // fs: integer block dots as floats, [2 buffers][nc][sr][nb+4]; dd: block scales (fp16 bits), [2][sr][nb+4];
-// vb: prologue vectors [nc][vb_len] (overlapping fs/dd); red: reductions and argmax partials.
+// vb: prologue vectors [nc][vb_len] (overlapping fs/dd); pc: per-column facts read before the dependency wait;
+// red: reductions and argmax partials.
+struct PreCol {
+    const SessDev *s;
+    float *ring;
+    const float *embd;
+    int pos, off, tok, pad;
+};
 struct MvPlan {
-    int stage, bar, xq, xd, xs, fs, dd, vb, vo, ab, red, total;
+    int stage, bar, xq, xd, xs, fs, dd, vb, vo, ab, pc, red, total;
 };
 __host__ __device__ inline int align_up(int x, int a) { return (x + a - 1) / a * a; }
 __host__ __device__ inline MvPlan mv_plan(int cols, int sr, int nc, int vb_len, int ab_len) {
@@ -149,17 +157,19 @@ __host__ __device__ inline MvPlan mv_plan(int cols, int sr, int nc, int vb_len, 
     p.vo = o;
     p.vb = u;    o = o > align_up(u + 4 * nc * vb_len, 16) ? o : align_up(u + 4 * nc * vb_len, 16);
     p.ab = o;    o = align_up(o + 4 * nc * ab_len, 16);
+    p.pc = o;    o = align_up(o + (int) sizeof(PreCol) * MV_MAX_COLS, 16);
     p.red = o;   o = align_up(o + 4 * 64 + 8 * MV_MAX_COLS * MV_CWARPS + 16, 16);
     p.total = o;
     return p;
 }
 
 // floats per column staged in shared memory by the input preparation of `pro`
-__host__ __device__ inline int mv_vb_len(int pro, int cols, int n_embd, int nc) {
+__host__ __device__ inline int mv_vb_len(int pro, int cols, int n_embd, int nc, int d_conv) {
     // P_RESID_NORM / P_FINAL stage two vectors per column (the post-normed input and the residual) for up to 2
-    // columns; with more, the residual is read from global memory where it is used
+    // columns; with more, the residual is read from global memory where it is used. P_CONV keeps, for up to 2
+    // columns, the product of every tap made before the dependency wait: [d_conv][n_embd].
     return pro == P_CUT ? cols : (pro == P_RESID_NORM || pro == P_FINAL) ? (nc <= 2 ? 2 : 1) * n_embd
-                               : (pro == P_EMBED_NORM || pro == P_CONV) ? n_embd : 0;
+                               : pro == P_EMBED_NORM ? n_embd : pro == P_CONV ? (nc <= 2 ? d_conv : 0) * n_embd : 0;
 }
 
 #ifdef __CUDACC__
@@ -174,7 +184,15 @@ __device__ __forceinline__ float exp_cr(float x) { return __double2float_rn(exp(
 __device__ __forceinline__ float warp_rms_scale(const float *x, int n, float eps) {
     const int L = threadIdx.x & 31;
     float a = 0.0f;
-    for (int i = L; i < n; i += 32) a = __fmaf_rn(x[i], x[i], a);
+    int i = L;
+    for (; i + 15 * 32 < n; i += 16 * 32) {   // 16 loads in flight, then the lane's fmas in order
+        float v[16];
+#pragma unroll
+        for (int k = 0; k < 16; k++) v[k] = x[i + 32 * k];
+#pragma unroll
+        for (int k = 0; k < 16; k++) a = __fmaf_rn(v[k], v[k], a);
+    }
+    for (; i < n; i += 32) a = __fmaf_rn(x[i], x[i], a);
     const unsigned F = 0xffffffffu;
     const float a8 = __shfl_down_sync(F, a, 8), a16 = __shfl_down_sync(F, a, 16), a24 = __shfl_down_sync(F, a, 24);
     const float t = __fadd_rn(__fadd_rn(a, a8), __fadd_rn(a16, a24));   // lanes 0..7
@@ -200,6 +218,42 @@ __device__ __forceinline__ int warp_cut32(float v, float &d, int &sum) {
     for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(F, s, o);
     sum = s;
     return q;
+}
+
+// imi_cut32 of one 32-value block held by 8 consecutive lanes (lane & 7 = g holds values 4g..4g+3): the same
+// d, id, codes and sum as warp_cut32. Every lane of the warp calls it (each group of 8 reduces among itself).
+// Returns this lane's 4 codes packed in a word (value 4g in the low byte); d and the block's code sum to every lane.
+__device__ __forceinline__ uint32_t cut32_g8(float4 v, float &d, int &sum) {
+    const unsigned F = 0xffffffffu;
+    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    amax = fmaxf(amax, __shfl_xor_sync(F, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(F, amax, 2));
+    amax = fmaxf(amax, __shfl_xor_sync(F, amax, 4));
+    d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    const int q0 = __float2int_rn(__fmul_rn(v.x, id)), q1 = __float2int_rn(__fmul_rn(v.y, id)),
+              q2 = __float2int_rn(__fmul_rn(v.z, id)), q3 = __float2int_rn(__fmul_rn(v.w, id));
+    int s = (q0 + q1) + (q2 + q3);
+    s += __shfl_xor_sync(F, s, 1);
+    s += __shfl_xor_sync(F, s, 2);
+    s += __shfl_xor_sync(F, s, 4);
+    sum = s;
+    return ((uint32_t) q0 & 0xffu) | (((uint32_t) q1 & 0xffu) << 8) | (((uint32_t) q2 & 0xffu) << 16) |
+           ((uint32_t) q3 << 24);
+}
+// cut32_g8 of chunk q (values 4q..4q+3) with the results stored when `act`: codes at q8 + 4q, the block's scale
+// and scale * code sum at d[q / 8], s[q / 8] (written by lane g == 0). All 32 lanes call it.
+__device__ __forceinline__ void cut_chunk(float4 v, bool act, int q, int8_t *q8, float *d, float *s) {
+    float dv;
+    int sum;
+    const uint32_t w = cut32_g8(act ? v : make_float4(0.0f, 0.0f, 0.0f, 0.0f), dv, sum);
+    if (act) {
+        *(uint32_t *) (q8 + 4 * q) = w;
+        if ((q & 7) == 0) {
+            d[q >> 3] = dv;
+            s[q >> 3] = __fmul_rn(dv, (float) sum);
+        }
+    }
 }
 
 // dot_h of seoul.cpp:29-35: 8 lane accumulators over the row in steps of 8, then imi_hsum's order.
@@ -268,6 +322,17 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // bulk prefetch of global memory into L2 (16-byte aligned address, size a multiple of 16)
 __device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+// 16-byte global -> shared copy without registers (cp.async, L2 only: the source may be fresh from the last launch)
+__device__ __forceinline__ void cp16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// a coherent (L2) read of a value another launch may change
+__device__ __forceinline__ int ld_relaxed(const int *p) {
+    int v;
+    asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

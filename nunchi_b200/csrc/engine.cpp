@@ -389,13 +389,13 @@ enum StepKind { K_DECODE = 0, K_PREFILL = 1, K_HEAD_ONLY = 2 };
 
 // rows per weight stage: as many as a stage holds (in steps of `gran` rows), fewer if that keeps two CTAs per SM (so
 // the next launch can start early); when even 8 rows do not fit that budget, one CTA per SM with full stages
-int pick_sr(int pro, const TableRef &t, int gran, int ncol, int E, int ab_len) {
+int pick_sr(int pro, const TableRef &t, int gran, int ncol, int E, int ab_len, int d_conv = 0) {
     const int full = std::max(gran, (std::min(64, MV_STAGE_BYTES / t.row_bytes) / gran) * gran);
     int sr = full;
-    while (sr > gran && table_smem(pro, t.cols, sr, ncol, E, ab_len) > (size_t) MV_SMEM_BUDGET) sr -= gran;
+    while (sr > gran && table_smem(pro, t.cols, sr, ncol, E, ab_len, d_conv) > (size_t) MV_SMEM_BUDGET) sr -= gran;
     if (sr < std::min(8, full)) {
         sr = full;
-        while (sr > gran && table_smem(pro, t.cols, sr, ncol, E, ab_len) > (size_t) 220 * 1024) sr -= gran;
+        while (sr > gran && table_smem(pro, t.cols, sr, ncol, E, ab_len, d_conv) > (size_t) 220 * 1024) sr -= gran;
     }
     return std::max(sr, gran);
 }
@@ -412,7 +412,7 @@ cudaError_t table_launch(imi_cuda_engine *e, const TableRef &t, int pro, int epi
     const int units = t.rows / a.unit;
     const int grid = std::max(1, std::min(e->sm_count, units));
     a.ab_len = epi == E_SILU ? (units + grid - 1) / grid * a.unit / 2 : 0;
-    a.sr = pick_sr(pro, t, gran, a.ncol, e->n_embd, a.ab_len);
+    a.sr = pick_sr(pro, t, gran, a.ncol, e->n_embd, a.ab_len, a.d_conv);
     if (!a.trace) a.trace = e->trace_slot(10 * pro + epi, grid);
     return launch_table(pro, epi, a, grid, e->stream, true);
 }
@@ -463,6 +463,9 @@ cudaError_t enqueue_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind)
             a.conv_layer = L.ci;
             a.out = e->y;
             a.out_stride = E;
+            // a step of distinct conversations (one position each) writes the conv memory right here: no column of it
+            // reads the slot it writes; a prefill chunk writes it one launch later (the gate_up read)
+            if (kind == K_DECODE) a.ring_layer = L.ci;
             if ((r = table_launch(e, L.out_proj, P_CONV, E_STORE, a)) != cudaSuccess) return r;
         } else {
             AttnArgs t = {};
@@ -513,7 +516,7 @@ cudaError_t enqueue_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind)
         a.q8o_q = e->qa_q;
         a.q8o_d = e->qa_d;
         a.q8o_s = e->qa_s;
-        if (L.conv) {
+        if (L.conv && kind != K_DECODE) {
             a.ring_layer = L.ci;
             a.ring_src = e->big;
             a.ring_src_stride = e->big_n;
@@ -814,6 +817,7 @@ imi_cuda_status imi_cuda_greedy(imi_cuda_state *const *s, int n, const int32_t *
     if (n > STEP_COLS) return fail(IMI_E_ARG, "greedy runs at most 8 conversations per call");
     for (int i = 0; i < n; i++) {
         if (!s[i] || s[i]->e != e) return fail(IMI_E_ARG, "states of another engine");
+        for (int j = 0; j < i; j++) if (s[j] == s[i]) return fail(IMI_E_ARG, "a state appears twice");
         if (s[i]->pos + steps > e->n_ctx) return fail(IMI_E_CTX_FULL, "context full (" + std::to_string(e->n_ctx) + ")");
     }
     CK(cudaSetDevice(e->device));

@@ -70,144 +70,218 @@ __device__ __forceinline__ void load32(const float *p, float (&v)[32]) {
     }
 }
 
-// the word table row of `tok` as floats: d * (code - 8); codes of block j at bytes 16j.., scales after the codes
-__device__ __forceinline__ float word_value(const uint8_t *row, int cols, int i) {
-    const int j = i >> 5, k = i & 31;
-    const uint8_t b = row[16 * j + (k & 15)];
-    const int code = k < 16 ? (b & 15) : (b >> 4);
-    const uint16_t dh = *(const uint16_t *) (row + cols / 2 + 2 * j);
-    return __fmul_rn(h2f(dh), (float) (code - 8));
+// ---------------- input preparation ----------------
+// Each thread owns the float4 chunks q = tid, tid + MV_THREADS, ... of an n_embd vector in every phase. MV_THREADS is
+// a multiple of 32, so the 8 lanes holding chunks 8m..8m+7 hold one 32-value block, which cut_chunk cuts in place:
+// the residual update, the norm and the 8-bit cut stay in registers; only the RMS reductions (one warp per column,
+// imi's lane order) read the vector from shared memory.
+constexpr int PQ = 4;   // chunks per thread (n_embd <= 4 * PQ * MV_THREADS = 6144)
+struct PreRegs {
+    float4 wpr[PQ], wpo[PQ];
+};
+
+// the word table row of `tok`, chunk q: d * (code - 8) for values 4q..4q+3 (codes of block j at bytes 16j..,
+// values 0..15 in the low nibbles, 16..31 in the high ones; scales after the codes)
+__device__ __forceinline__ float4 word_chunk(const uint8_t *row, int cols, int q) {
+    const int j = q >> 3, k0 = (4 * q) & 31;
+    const uint32_t w = *(const uint32_t *) (row + 16 * j + (k0 & 15));
+    const float d = h2f(*(const uint16_t *) (row + cols / 2 + 2 * j));
+    const int sh = k0 < 16 ? 0 : 4;
+    return make_float4(__fmul_rn(d, (float) ((int) ((w >> sh) & 15) - 8)),
+                       __fmul_rn(d, (float) ((int) ((w >> (8 + sh)) & 15) - 8)),
+                       __fmul_rn(d, (float) ((int) ((w >> (16 + sh)) & 15) - 8)),
+                       __fmul_rn(d, (float) ((int) ((w >> (24 + sh)) & 15) - 8)));
+}
+__device__ __forceinline__ float4 mul4(float4 a, float4 b) {
+    return make_float4(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y), __fmul_rn(a.z, b.z), __fmul_rn(a.w, b.w));
+}
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+    return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+}
+__device__ __forceinline__ float4 scl4(float4 a, float s) {
+    return make_float4(__fmul_rn(a.x, s), __fmul_rn(a.y, s), __fmul_rn(a.z, s), __fmul_rn(a.w, s));
+}
+// ring slot of position qp (negative before position d_conv: those slots hold zeros)
+__device__ __forceinline__ int ring_slot(int qp, int R) { return ((qp % R) + R) % R; }
+
+// conv tap products st_k * w_k (seoul.cpp:410-414) of one column for this thread's chunks, for the taps whose
+// position lies before the step (read from the conv memory ring, positions counted from `p0`): prod[k][n_embd]
+__device__ __forceinline__ void conv_ring_products(const MvArgs &a, const PreCol &pc, int p0, float *prod) {
+    const int E = a.n_embd, nq = E / 4, R = a.d_conv + 1, p = p0 + pc.off;
+    const float *ring = pc.ring + (size_t) a.conv_layer * R * E;
+    for (int k = 0; k < a.d_conv; k++) {
+        const int qp = p - a.d_conv + k;
+        if (qp >= p0) break;   // this tap and the later ones come from this step's own columns
+        const float4 *st = (const float4 *) (ring + (size_t) ring_slot(qp, R) * E);
+        const float4 *wk = (const float4 *) (a.conv_w + (size_t) k * E);
+        for (int q = threadIdx.x; q < nq; q += MV_THREADS)
+            ((float4 *) (prod + (size_t) k * E))[q] = mul4(__ldcg(st + q), wk[q]);
+    }
 }
 
-// copy n floats (n % 4 == 0, both 16-byte aligned) with all threads
-__device__ __forceinline__ void copy_vec(float *dst, const float *src, int n) {
-    for (int i = 4 * threadIdx.x; i < n; i += 4 * MV_THREADS) *(float4 *) (dst + i) = *(const float4 *) (src + i);
-}
-
-// input preparation, all MV_THREADS threads, all columns at once; ends with a __syncthreads.
-// Every global read of the activations is issued in one batch right after the dependency wait (one L2 round trip);
-// the norm weights go to registers (each thread keeps the float4 chunks q = tid, tid + MV_THREADS, ...).
-constexpr int PQ = 4;   // float4 chunks of an n_embd vector per thread (n_embd <= 4 * PQ * MV_THREADS = 6144)
+// Part 1, before the dependency wait: what does not depend on the launches in flight. The column descriptors (written
+// before the step was launched) into shared memory, the norm weights into registers, the word row of a given token,
+// and (up to 2 columns) the products of the conv taps read from the conv memory under the position read now; part 2
+// reads the position again and recomputes those products if it moved (it moves only at the end of a step).
 template <int PRO, int NC>
-__device__ void table_prologue(const MvArgs &a, const MvPlan &P, uint8_t *sm) {
-    int8_t *xq = (int8_t *) (sm + P.xq);
-    float *xd = (float *) (sm + P.xd), *xs = (float *) (sm + P.xs), *vb = (float *) (sm + P.vb);
-    float *red = (float *) (sm + P.red);
-    const int tid = threadIdx.x, warp = tid >> 5, nc = a.ncol, K = a.cols, nb = K / 32, E = a.n_embd, nq = E / 4;
-    const int VL = mv_vb_len(PRO, K, E, NC);
-    const bool x_in_smem = NC <= 2;   // the residual staged beside r (else read where it is used)
-    const bool lead = blockIdx.x == 0;
-    if (PRO == P_Q8IN) {   // codes made by the producer of the input (or given): [c][K], [c][K/32]
-        for (int i = tid; i < nc * K / 16; i += MV_THREADS) ((int4 *) xq)[i] = ((const int4 *) a.q8_q)[i];
-        for (int j = tid; j < nc * nb; j += MV_THREADS) {
-            xd[j] = a.q8_d[j];
-            xs[j] = a.q8_s[j];
-        }
-        __syncthreads();
-        return;
+__device__ __forceinline__ void table_preload(const MvArgs &a, const MvPlan &P, uint8_t *sm, PreRegs &pr) {
+    if (PRO == P_Q8IN || PRO == P_CUT) return;
+    const int tid = threadIdx.x, nc = a.ncol, E = a.n_embd, nq = E / 4;
+    PreCol *pc = (PreCol *) (sm + P.pc);
+    float *vb = (float *) (sm + P.vb);
+    const int VL = mv_vb_len(PRO, a.cols, E, NC, a.d_conv);
+    if (tid < nc) {
+        const Col &col = a.cols_d[tid];
+        PreCol c;
+        c.s = col.s;
+        c.ring = col.ring;
+        c.embd = col.embd;
+        c.off = col.off;
+        c.tok = col.token;
+        c.pos = PRO == P_CONV ? ld_relaxed(&col.s->pos) : 0;
+        c.pad = 0;
+        pc[tid] = c;
     }
     const bool norm = PRO == P_EMBED_NORM || PRO == P_RESID_NORM || PRO == P_FINAL;
     const bool resid = PRO == P_RESID_NORM || PRO == P_FINAL;
-    float4 wpo[PQ], wpr[PQ];
     if (norm) {
 #pragma unroll
         for (int k = 0; k < PQ; k++) {
             const int q = tid + k * MV_THREADS;
             if (q < nq) {
-                wpr[k] = ((const float4 *) a.wpre)[q];
-                if (resid) wpo[k] = ((const float4 *) a.wpost)[q];
+                pr.wpr[k] = ((const float4 *) a.wpre)[q];
+                if (resid) pr.wpo[k] = ((const float4 *) a.wpost)[q];
             }
         }
     }
-    // 1. the activations into shared memory
-    if (PRO == P_CUT) {
-        for (int c = 0; c < nc; c++) copy_vec(vb + c * VL, a.in + (size_t) c * a.in_stride, K);
-    } else if (resid) {   // [c]: r (the table output to post-norm) then x (the residual stream)
+    __syncthreads();
+    if (PRO == P_EMBED_NORM) {
         for (int c = 0; c < nc; c++) {
-            const float4 *r4 = (const float4 *) (a.in + (size_t) c * a.in_stride);
-            const float4 *x4 = (const float4 *) (a.xin + (size_t) c * a.x_stride);
-            float4 rv[PQ], xv[PQ];
-#pragma unroll
-            for (int k = 0; k < PQ; k++) {
-                const int q = tid + k * MV_THREADS;
-                if (q < nq) { rv[k] = r4[q]; if (x_in_smem) xv[k] = x4[q]; }
-            }
-#pragma unroll
-            for (int k = 0; k < PQ; k++) {
-                const int q = tid + k * MV_THREADS;
-                if (q < nq) {
-                    ((float4 *) (vb + c * VL))[q] = rv[k];
-                    if (x_in_smem) ((float4 *) (vb + c * VL + E))[q] = xv[k];
-                }
-            }
-        }
-    } else if (PRO == P_EMBED_NORM) {
-        for (int c = 0; c < nc; c++) {
-            const Col &col = a.cols_d[c];
-            int tok = col.token;
-            if (tok == -2) tok = col.s->next_token;
-            if (tok >= 0) {   // d * (code - 8): 4 values of one block per chunk
+            const int tok = pc[c].tok;
+            if (tok >= 0) {
                 const uint8_t *row = a.emb + (size_t) tok * a.emb_row_bytes;
-                for (int q = tid; q < nq; q += MV_THREADS) {
-                    const int j = q >> 3, k0 = (4 * q) & 31;
-                    const uint32_t w = *(const uint32_t *) (row + 16 * j + (k0 & 15));
-                    const float d = h2f(*(const uint16_t *) (row + E / 2 + 2 * j));
-                    const int sh = k0 < 16 ? 0 : 4;
-                    float4 v;
-                    v.x = __fmul_rn(d, (float) ((int) ((w >> sh) & 15) - 8));
-                    v.y = __fmul_rn(d, (float) ((int) ((w >> (8 + sh)) & 15) - 8));
-                    v.z = __fmul_rn(d, (float) ((int) ((w >> (16 + sh)) & 15) - 8));
-                    v.w = __fmul_rn(d, (float) ((int) ((w >> (24 + sh)) & 15) - 8));
-                    ((float4 *) (vb + c * VL))[q] = v;
-                }
-            } else {
-                copy_vec(vb + c * VL, col.embd, E);
+                for (int q = tid; q < nq; q += MV_THREADS) ((float4 *) (vb + c * VL))[q] = word_chunk(row, E, q);
+            } else if (tok == -1) {
+                for (int q = tid; q < nq; q += MV_THREADS) ((float4 *) (vb + c * VL))[q] = ((const float4 *) pc[c].embd)[q];
             }
         }
-    } else if (PRO == P_CONV) {
+    } else if (PRO == P_CONV && NC <= 2) {
+        for (int c = 0; c < nc; c++) conv_ring_products(a, pc[c], pc[c].pos, vb + c * VL);
+    }
+}
+
+// Part 2, after the dependency wait, all MV_THREADS threads, all columns; ends with a __syncthreads. The activations
+// the previous launches produced arrive in one batch (cp.async, one L2 round trip).
+template <int PRO, int NC>
+__device__ void table_prologue(const MvArgs &a, const MvPlan &P, uint8_t *sm, const PreRegs &pr) {
+    int8_t *xq = (int8_t *) (sm + P.xq);
+    float *xd = (float *) (sm + P.xd), *xs = (float *) (sm + P.xs), *vb = (float *) (sm + P.vb);
+    float *red = (float *) (sm + P.red);
+    const PreCol *pc = (const PreCol *) (sm + P.pc);
+    const int tid = threadIdx.x, warp = tid >> 5, nc = a.ncol, K = a.cols, nb = K / 32, E = a.n_embd, nq = E / 4;
+    const int VL = mv_vb_len(PRO, K, E, NC, a.d_conv);
+    if (PRO == P_Q8IN) {   // codes made by the producer of the input (or given): [c][K], [c][K/32]
+        for (int i = tid; i < nc * K / 16; i += MV_THREADS) cp16(xq + 16 * i, a.q8_q + 16 * i);
+        for (int j = tid; j < nc * nb; j += MV_THREADS) {
+            xd[j] = a.q8_d[j];
+            xs[j] = a.q8_s[j];
+        }
+        cp_wait_all();
+        __syncthreads();
+        return;
+    }
+    if (PRO == P_CUT) {   // the input as it is (seoul.cpp:457,469)
+        const int nk = K / 4;
+        for (int c = 0; c < nc; c++)
+            for (int q0 = 0; q0 < nk; q0 += MV_THREADS) {
+                const int q = q0 + tid;
+                const bool act = q < nk;
+                const float4 v = act ? ((const float4 *) (a.in + (size_t) c * a.in_stride))[q] : make_float4(0, 0, 0, 0);
+                cut_chunk(v, act, q, xq + c * K, xd + c * nb, xs + c * nb);
+            }
+        __syncthreads();
+        return;
+    }
+    if (PRO == P_CONV) {
         // seoul.cpp:410-414 (run) and 566-576 (run_batch): u = c * (b*x*w[d_conv] + sum_k st_k * w_k), st_k the b*x of
         // position p - d_conv + k: from this step's earlier columns of the same conversation when that position is in
-        // this step, else from the conv memory ring. Per chunk of 4 channels, all loads first.
+        // this step, else from the conv memory ring; u is cut where it is made
         const int R = a.d_conv + 1;
+        const float4 *wl = (const float4 *) (a.conv_w + (size_t) a.d_conv * E);
         for (int c = 0; c < nc; c++) {
-            const Col &col = a.cols_d[c];
-            const float *bcx = a.in + (size_t) c * a.in_stride;
-            const int p = col.s->pos + col.off;
+            const PreCol &col = pc[c];
+            const int p0 = ld_relaxed(&col.s->pos), p = p0 + col.off;
+            const bool pre = NC <= 2 && p0 == col.pos;   // the products made before the wait hold for this position
+            const float *prod = vb + c * VL;
+            const float4 *bcx = (const float4 *) (a.in + (size_t) c * a.in_stride);
             const float *ring = col.ring + (size_t) a.conv_layer * R * E;
-            for (int q = tid; q < nq; q += MV_THREADS) {
-                const float4 b4 = ((const float4 *) bcx)[q], c4 = ((const float4 *) (bcx + E))[q],
-                             x4 = ((const float4 *) (bcx + 2 * E))[q];
-                const float4 wl = ((const float4 *) (a.conv_w + (size_t) a.d_conv * E))[q];
-                float4 st[8], wk[8];
+            float4 *slot = a.ring_layer >= 0 ? (float4 *) (ring + (size_t) (p % R) * E) : nullptr;
+            for (int q0 = 0; q0 < nq; q0 += 2 * MV_THREADS) {   // two chunks per round, their loads first
+                int qq[2];
+                bool act[2];
+                float4 bv[2], cv[2], xv[2], wv[2];
 #pragma unroll
-                for (int k = 0; k < 8; k++) {
-                    if (k < a.d_conv) {
-                        const int qp = p - a.d_conv + k;
-                        wk[k] = ((const float4 *) (a.conv_w + (size_t) k * E))[q];
-                        if (qp >= p - col.off) {
-                            const float *ob = a.in + (size_t) (c - a.d_conv + k) * a.in_stride;
-                            const float4 ob4 = ((const float4 *) ob)[q], ox4 = ((const float4 *) (ob + 2 * E))[q];
-                            st[k] = make_float4(__fmul_rn(ob4.x, ox4.x), __fmul_rn(ob4.y, ox4.y), __fmul_rn(ob4.z, ox4.z),
-                                                __fmul_rn(ob4.w, ox4.w));
+                for (int h = 0; h < 2; h++) {
+                    qq[h] = q0 + tid + h * MV_THREADS;
+                    act[h] = qq[h] < nq;
+                    const int qs = act[h] ? qq[h] : 0;
+                    bv[h] = bcx[qs];
+                    cv[h] = bcx[nq + qs];
+                    xv[h] = bcx[2 * nq + qs];
+                    wv[h] = wl[qs];
+                }
+                float4 sv[2], u[2];
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    sv[h] = mul4(bv[h], xv[h]);
+                    u[h] = mul4(sv[h], wv[h]);
+                }
+                for (int k = 0; k < a.d_conv; k++) {
+                    const int qp = p - a.d_conv + k;
+                    const float4 *wk = (const float4 *) (a.conv_w + (size_t) k * E);
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        const int qs = act[h] ? qq[h] : 0;
+                        float4 pk;
+                        if (qp >= p0) {   // column c - d_conv + k of this step (a prefill chunk of one conversation)
+                            const float4 *ob = (const float4 *) (a.in + (size_t) (c - a.d_conv + k) * a.in_stride);
+                            pk = mul4(mul4(ob[qs], ob[2 * nq + qs]), wk[qs]);
+                        } else if (pre) {
+                            pk = ((const float4 *) (prod + (size_t) k * E))[qs];
                         } else {
-                            st[k] = ((const float4 *) (ring + (size_t) (((qp % R) + R) % R) * E))[q];
+                            pk = mul4(__ldcg((const float4 *) (ring + (size_t) ring_slot(qp, R) * E) + qs), wk[qs]);
                         }
+                        u[h] = add4(u[h], pk);
                     }
                 }
-                float u[4] = { __fmul_rn(__fmul_rn(b4.x, x4.x), wl.x), __fmul_rn(__fmul_rn(b4.y, x4.y), wl.y),
-                               __fmul_rn(__fmul_rn(b4.z, x4.z), wl.z), __fmul_rn(__fmul_rn(b4.w, x4.w), wl.w) };
 #pragma unroll
-                for (int k = 0; k < 8; k++) {
-                    if (k < a.d_conv) {
-                        u[0] = __fadd_rn(u[0], __fmul_rn(st[k].x, wk[k].x));
-                        u[1] = __fadd_rn(u[1], __fmul_rn(st[k].y, wk[k].y));
-                        u[2] = __fadd_rn(u[2], __fmul_rn(st[k].z, wk[k].z));
-                        u[3] = __fadd_rn(u[3], __fmul_rn(st[k].w, wk[k].w));
-                    }
+                for (int h = 0; h < 2; h++) {
+                    if (q0 + h * MV_THREADS < nq)   // CTA-uniform: skip rounds with no chunk at all
+                        cut_chunk(mul4(u[h], cv[h]), act[h], qq[h], xq + c * K, xd + c * nb, xs + c * nb);
+                    // conv memory: slot p mod (d_conv + 1) takes b*x (seoul.cpp:419-423); no column of this step reads
+                    // it (the host sets ring_layer here only for steps of distinct conversations); spread over the CTAs
+                    if (slot && act[h] && (int) (qq[h] % gridDim.x) == (int) blockIdx.x) slot[qq[h]] = sv[h];
                 }
-                ((float4 *) (vb + c * VL))[q] =
-                    make_float4(__fmul_rn(u[0], c4.x), __fmul_rn(u[1], c4.y), __fmul_rn(u[2], c4.z), __fmul_rn(u[3], c4.w));
             }
+        }
+        __syncthreads();
+        return;
+    }
+    // P_EMBED_NORM, P_RESID_NORM, P_FINAL
+    const bool resid = PRO == P_RESID_NORM || PRO == P_FINAL;
+    const bool x_in_smem = NC <= 2;   // the residual staged beside r (else read where it is used)
+    if (resid) {   // [c]: r (the table output to post-norm) then x (the residual stream)
+        for (int c = 0; c < nc; c++)
+            for (int q = tid; q < nq; q += MV_THREADS) {
+                cp16(vb + c * VL + 4 * q, a.in + (size_t) c * a.in_stride + 4 * q);
+                if (x_in_smem) cp16(vb + c * VL + E + 4 * q, a.xin + (size_t) c * a.x_stride + 4 * q);
+            }
+        cp_wait_all();
+    } else {
+        for (int c = 0; c < nc; c++) {
+            if (pc[c].tok != -2) continue;   // the greedy pick of the conversation's last step
+            const uint8_t *row = a.emb + (size_t) pc[c].s->next_token * a.emb_row_bytes;
+            for (int q = tid; q < nq; q += MV_THREADS) ((float4 *) (vb + c * VL))[q] = word_chunk(row, E, q);
         }
     }
     __syncthreads();
@@ -225,11 +299,7 @@ __device__ void table_prologue(const MvArgs &a, const MvPlan &P, uint8_t *sm) {
             for (int k = 0; k < PQ; k++) {
                 const int q = tid + k * MV_THREADS;
                 if (q < nq) {
-                    const float4 r = v4[q], x = x4[q], w = wpo[k];
-                    const float4 y = make_float4(__fadd_rn(x.x, __fmul_rn(__fmul_rn(r.x, sc), w.x)),
-                                                 __fadd_rn(x.y, __fmul_rn(__fmul_rn(r.y, sc), w.y)),
-                                                 __fadd_rn(x.z, __fmul_rn(__fmul_rn(r.z, sc), w.z)),
-                                                 __fadd_rn(x.w, __fmul_rn(__fmul_rn(r.w, sc), w.w)));
+                    const float4 y = add4(x4[q], mul4(scl4(v4[q], sc), pr.wpo[k]));
                     v4[q] = y;
                     if (a.xout && (int) (q % gridDim.x) == (int) blockIdx.x)   // the residual stream, spread over CTAs
                         ((float4 *) (a.xout + (size_t) c * a.x_stride))[q] = y;
@@ -237,45 +307,34 @@ __device__ void table_prologue(const MvArgs &a, const MvPlan &P, uint8_t *sm) {
             }
         }
         __syncthreads();
-    } else if (PRO == P_EMBED_NORM && a.xout) {
+    } else if (a.xout) {
         for (int c = 0; c < nc; c++)
             for (int q = tid; q < nq; q += MV_THREADS)
                 if ((int) (q % gridDim.x) == (int) blockIdx.x)
                     ((float4 *) (a.xout + (size_t) c * a.x_stride))[q] = ((const float4 *) (vb + c * VL))[q];
     }
-    if (norm) {   // h = norm(x) * w_pre (imi_norm_mul, vec.h:36-39), in place
-        if (warp < nc) {
-            const float sc = warp_rms_scale(vb + warp * VL, E, a.eps);
-            if ((tid & 31) == 0) red[32 + warp] = sc;
-        }
-        __syncthreads();
-        for (int c = 0; c < nc; c++) {
-            const float sc = red[32 + c];
-            float4 *v4 = (float4 *) (vb + c * VL);
-            float *hid = PRO == P_FINAL ? a.cols_d[c].hid_out : nullptr;
+    // h = norm(x) * w_pre (imi_norm_mul, vec.h:36-39), cut where it is made
+    if (warp < nc) {
+        const float sc = warp_rms_scale(vb + warp * VL, E, a.eps);
+        if ((tid & 31) == 0) red[32 + warp] = sc;
+    }
+    __syncthreads();
+    for (int c = 0; c < nc; c++) {
+        const float sc = red[32 + c];
+        const float4 *v4 = (const float4 *) (vb + c * VL);
+        float *hid = PRO == P_FINAL ? a.cols_d[c].hid_out : nullptr;
 #pragma unroll
-            for (int k = 0; k < PQ; k++) {
-                const int q = tid + k * MV_THREADS;
-                if (q < nq) {
-                    const float4 x = v4[q], w = wpr[k];
-                    const float4 h = make_float4(__fmul_rn(__fmul_rn(x.x, sc), w.x), __fmul_rn(__fmul_rn(x.y, sc), w.y),
-                                                 __fmul_rn(__fmul_rn(x.z, sc), w.z), __fmul_rn(__fmul_rn(x.w, sc), w.w));
-                    v4[q] = h;
-                    if (hid && (int) (q % gridDim.x) == (int) blockIdx.x) ((float4 *) hid)[q] = h;
-                }
-            }
+        for (int k = 0; k < PQ; k++) {
+            if (k * MV_THREADS >= nq) break;   // CTA-uniform
+            const int q = tid + k * MV_THREADS;
+            const bool act = q < nq;
+            const float4 h = act ? mul4(scl4(v4[q], sc), pr.wpr[k]) : make_float4(0, 0, 0, 0);
+            if (hid && act && (int) (q % gridDim.x) == (int) blockIdx.x) ((float4 *) hid)[q] = h;
+            cut_chunk(h, act, q, xq + c * K, xd + c * nb, xs + c * nb);
         }
-        __syncthreads();
     }
-    // 2. the 8-bit cut, one thread per (column, 32-value block)
-    for (int t = tid; t < nc * nb; t += MV_THREADS) {
-        const int c = t / nb, j = t - c * nb;
-        float v[32];
-        load32(vb + c * VL + 32 * j, v);
-        cut32(v, xq + c * K + 32 * j, xd + t, xs + t);
-    }
-    // conv memory: the slot of each column's position takes b*x (seoul.cpp:419-423); written one launch after the conv
-    // read it, so no CTA of the reading launch can see it early; spread over the CTAs
+    // conv memory of a prefill chunk: the slot of each column's position takes b*x (seoul.cpp:419-423); written one
+    // launch after the conv read it, so no CTA of the reading launch can see it early; spread over the CTAs
     if (a.ring_layer >= 0) {
         const int R = a.d_conv + 1;
         for (int c = 0; c < nc; c++) {
@@ -283,11 +342,8 @@ __device__ void table_prologue(const MvArgs &a, const MvPlan &P, uint8_t *sm) {
             const int p = col.s->pos + col.off;
             const float *bcx = a.ring_src + (size_t) c * a.ring_src_stride;
             float4 *slot = (float4 *) (col.ring + ((size_t) a.ring_layer * R + p % R) * E);
-            for (int q = blockIdx.x * MV_THREADS + tid; q < nq; q += gridDim.x * MV_THREADS) {
-                const float4 b4 = ((const float4 *) bcx)[q], x4 = ((const float4 *) (bcx + 2 * E))[q];
-                slot[q] = make_float4(__fmul_rn(b4.x, x4.x), __fmul_rn(b4.y, x4.y), __fmul_rn(b4.z, x4.z),
-                                      __fmul_rn(b4.w, x4.w));
-            }
+            for (int q = blockIdx.x * MV_THREADS + tid; q < nq; q += gridDim.x * MV_THREADS)
+                slot[q] = mul4(((const float4 *) bcx)[q], ((const float4 *) (bcx + 2 * E))[q]);
         }
     }
     __syncthreads();
@@ -347,7 +403,7 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_table(const __grid_constant__
     __shared__ int abort_flag, last_cta;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, K = a.cols, nb = K / 32, ld = nb + 4,
               nc = a.ncol, sr = a.sr;
-    const MvPlan P = mv_plan(K, sr, NC, mv_vb_len(PRO, K, a.n_embd, NC), a.ab_len);
+    const MvPlan P = mv_plan(K, sr, NC, mv_vb_len(PRO, K, a.n_embd, NC, a.d_conv), a.ab_len);
     uint8_t *stage = sm + P.stage;
     uint64_t *bar = (uint64_t *) (sm + P.bar);
     const int8_t *xq = (const int8_t *) (sm + P.xq);
@@ -384,9 +440,12 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_table(const __grid_constant__
         for (size_t o = beg; o < end; o += 65536) prefetch_l2(base + o, (uint32_t) min((size_t) 65536, end - o));
     }
     pdl_trigger();
+    PreRegs pr;
+    table_preload<PRO, NC>(a, P, sm, pr);
+    if (trace && tid == 0) trace[15] = global_ns();
     pdl_wait();
     if (trace && tid == 0) trace[1] = global_ns();
-    table_prologue<PRO, NC>(a, P, sm);
+    table_prologue<PRO, NC>(a, P, sm, pr);
     if (trace && tid == 0) trace[2] = global_ns();
 
     if (warp < MV_IWARPS) {
