@@ -417,6 +417,11 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_table(const __grid_constant__
     const int r0 = u0 * a.unit, nrows = (u1 - u0) * a.unit;
     const int nst = (nrows + sr - 1) / sr;
 
+    {   // later phases read the parameter block piecemeal; reading every word of it once now, before the dependency
+        // wait, brings it on chip while nothing waits on it
+        __shared__ volatile int pwarm[(sizeof(MvArgs) + 3) / 4];
+        if (tid < (int) (sizeof(MvArgs) / 4)) pwarm[tid] = reinterpret_cast<const int *>(&a)[tid];
+    }
     unsigned long long *trace = a.trace ? a.trace + (size_t) blockIdx.x * MV_TRACE : nullptr;
     if (trace && tid == 0) trace[0] = global_ns();
     if (tid == 0) {
