@@ -494,7 +494,7 @@ cudaError_t enqueue_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind)
             t.q8o_d = e->qt_d;
             t.q8o_s = e->qt_s;
             if (kind == K_PREFILL && (r = launch_kvwrite(t, e->stream, true)) != cudaSuccess) return r;
-            t.trace = e->trace_slot(100, e->n_head_kv * ncol);
+            t.trace = e->trace_slot(100, e->n_head * ncol);
             if ((r = launch_attn(t, e->stream, true)) != cudaSuccess) return r;
             a = b;
             a.q8_q = e->qt_q;

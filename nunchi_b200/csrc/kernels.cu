@@ -1,8 +1,8 @@
 // sm_100a kernels of the decode engine.
 //
 // k_table (table.cuh): the 4-bit table reads with the small math of imi's step folded in.
-// k_attn: decode attention for one (column, kv head): q/k RMSNorm, NEOX rotation, fp16 K/V write, scores, softmax,
-//   P.V and the sigmoid gate, in the float order of seoul.cpp:425-453.
+// k_attn: decode attention for one (query head, column): q/k RMSNorm, NEOX rotation, fp16 K/V write, scores,
+//   softmax, P.V and the sigmoid gate, in the float order of seoul.cpp:425-453.
 #include "common.cuh"
 #include "table.cuh"
 
@@ -59,26 +59,27 @@ __global__ void __launch_bounds__(256) k_final(const __grid_constant__ FinalArgs
 // attention
 // ---------------------------------------------------------------------------------------------------------------
 
+// k_attn: one CTA of ATT_NT threads per (query head, column). The cached V rows the P.V chain reads arrive in shared
+// memory in tiles of 64 KB (two in flight, cp.async), issued before the scores so the copies overlap them.
+constexpr int ATT_NT = 128, ATT_NW = ATT_NT / 32;
+__host__ __device__ inline int attn_vtile(int D) { return 32768 / D; }   // positions per V tile (64 KB of fp16)
 // shared-memory plan of k_attn (host and device agree on it); every region 16-byte aligned
 struct AttnPlan {
-    size_t q, qtmp, ktmp, tmp, mx, inv, dsum, wmax, kh, vh, sc, total;
+    size_t q, ktmp, tmp, y, kh, vh, red, vt, sc, total;
 };
-__host__ __device__ inline AttnPlan attn_plan(int D, int GRP, int n_ctx) {
+__host__ __device__ inline AttnPlan attn_plan(int D, int n_ctx) {
     AttnPlan p;
-    const int NW = GRP * D / 32;
     size_t o = 0;
     auto take = [&](size_t n) { const size_t r = o; o = (o + n + 15) / 16 * 16; return r; };
-    p.q = take(4 * (size_t) GRP * D);
-    p.qtmp = take(4 * (size_t) GRP * D);
+    p.q = take(4 * (size_t) D);
     p.ktmp = take(4 * (size_t) D);
     p.tmp = take(4 * (size_t) D);
-    p.mx = take(4 * (size_t) GRP);
-    p.inv = take(4 * (size_t) GRP);
-    p.dsum = take(8 * (size_t) GRP * NW);
-    p.wmax = take(4 * (size_t) GRP * NW);
+    p.y = take(4 * (size_t) D);
     p.kh = take(2 * (size_t) D);
     p.vh = take(2 * (size_t) D);
-    p.sc = take(4 * (size_t) GRP * n_ctx);
+    p.red = take(8 * ATT_NW + 4 * ATT_NW + 16);
+    p.vt = take(2 * (size_t) attn_vtile(D) * D * 2);
+    p.sc = take(4 * (size_t) n_ctx);
     p.total = o;
     return p;
 }
@@ -135,167 +136,157 @@ __global__ void __launch_bounds__(32) k_kvwrite(const __grid_constant__ AttnArgs
     }
 }
 
-// one CTA per (kv head g, column): the GRP query heads of the group, GRP*D threads
-template <int D, int GRP>
-__global__ void __launch_bounds__(GRP *D) k_attn(const __grid_constant__ AttnArgs a) {
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// decode / prefill attention of query head h for column c (seoul.cpp:425-453 and 589-621): q RMSNorm + rotation,
+// this position's K/V (decode: made here and written to the caches by the group's first head), scores by dot_h,
+// softmax with a double sum, the serial P.V chain over positions in order, the sigmoid gate, and the 8-bit cut of
+// the head's output blocks for the o table.
+template <int D>
+__global__ void __launch_bounds__(ATT_NT) k_attn(const __grid_constant__ AttnArgs a) {
     extern __shared__ __align__(16) uint8_t sma[];
-    constexpr int NT = GRP * D, NW = NT / 32;
-    const AttnPlan L = attn_plan(D, GRP, a.n_ctx);
+    const AttnPlan L = attn_plan(D, a.n_ctx);
+    const int h = blockIdx.x, c = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     unsigned long long *trace = a.trace ? a.trace + (size_t) (blockIdx.y * gridDim.x + blockIdx.x) * MV_TRACE : nullptr;
-    if (trace && threadIdx.x == 0) trace[0] = global_ns();
-    float *q = (float *) (sma + L.q);          // [GRP][D] rotated queries
-    float *qtmp = (float *) (sma + L.qtmp);    // [GRP][D] norm scratch per head
-    float *ktmp = (float *) (sma + L.ktmp), *tmp = (float *) (sma + L.tmp);   // [D], [D]
-    float *mx = (float *) (sma + L.mx), *inv = (float *) (sma + L.inv);       // [GRP]
-    double *dsum = (double *) (sma + L.dsum);  // [GRP][NW]
-    float *wmax = (float *) (sma + L.wmax);    // [GRP][NW]
-    uint16_t *kh = (uint16_t *) (sma + L.kh), *vh = (uint16_t *) (sma + L.vh);   // [D] fp16 (16-byte aligned)
-    float *sc = (float *) (sma + L.sc);        // [GRP][n_ctx] scores, then probabilities
+    if (trace && tid == 0) trace[0] = global_ns();
+    float *q = (float *) (sma + L.q), *ktmp = (float *) (sma + L.ktmp), *tmp = (float *) (sma + L.tmp);
+    float *y = (float *) (sma + L.y), *sc = (float *) (sma + L.sc);
+    uint16_t *kh = (uint16_t *) (sma + L.kh), *vh = (uint16_t *) (sma + L.vh), *vt = (uint16_t *) (sma + L.vt);
+    double *dsum = (double *) (sma + L.red);
+    float *wmax = (float *) (sma + L.red + 8 * ATT_NW), *mx = wmax + ATT_NW, *inv = mx + 1;
 
     pdl_trigger();
     pdl_wait();
-    const int g = blockIdx.x, c = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (trace && tid == 0) trace[1] = global_ns();
-    const int H = a.n_head, kvd = a.n_head_kv * D;
+    const int H = a.n_head, grp = H / a.n_head_kv, g = h / grp, kvd = a.n_head_kv * D;
     const Col col = a.cols_d[c];
     const int p = col.s->pos + col.off;
     const float *qkv = a.qkv + (size_t) c * a.qkv_stride;
     const float *cs = a.rope_cs + (size_t) p * (D / 2), *sn = a.rope_sn + (size_t) p * (D / 2);
-    const uint16_t *kc = (const uint16_t *) col.kc + (size_t) a.ai * a.n_ctx * kvd + g * D;
-    const uint16_t *vc = (const uint16_t *) col.vc + (size_t) a.ai * a.n_ctx * kvd + g * D;
-
-    // this position's K and V (written to the caches here when fused)
-    if (a.kv_fused) {
-        kv_make<D>(a, qkv, g, p, ktmp, tmp, kh, vh);
-        __syncthreads();
-        if (tid < D) {
-            ((uint16_t *) kc)[(size_t) p * kvd + tid] = kh[tid];
-            ((uint16_t *) vc)[(size_t) p * kvd + tid] = vh[tid];
+    uint16_t *kc = (uint16_t *) col.kc + (size_t) a.ai * a.n_ctx * kvd + g * D;
+    uint16_t *vc = (uint16_t *) col.vc + (size_t) a.ai * a.n_ctx * kvd + g * D;
+    const int s0 = a.window > 0 ? max(0, p - a.window + 1) : 0, nk = p - s0 + 1;
+    const int ng = a.kv_fused ? nk - 1 : nk;   // positions whose V is read from the cache
+    const int VT = attn_vtile(D), ntile = (ng + VT - 1) / VT;
+    auto load_tile = [&](int k) {
+        uint16_t *dst = vt + (size_t) (k & 1) * VT * D;
+        const int t0 = k * VT, n = min(VT, ng - t0);
+        for (int i = tid; i < n * (D / 8); i += ATT_NT) {
+            const int t = i / (D / 8), ch = i - t * (D / 8);
+            cp16(dst + (size_t) t * D + 8 * ch, vc + (size_t) (s0 + t0 + t) * kvd + 8 * ch);
         }
-    }
-    // the group's queries: RMSNorm + rotation, one warp per head (seoul.cpp:442-443)
-    for (int hh = warp; hh < GRP; hh += NW) {
-        float *qh = q + hh * D;
-        const int h = g * GRP + hh;
-        for (int i = lane; i < D; i += 32) qh[i] = qkv[h * D + i];
+        cp_commit();
+    };
+    if (ntile > 0) load_tile(0);
+    if (ntile > 1) load_tile(1);
+
+    // this position's K and V (warp 0) and the rotated query (warp 1)
+    if (a.kv_fused) kv_make<D>(a, qkv, g, p, ktmp, tmp, kh, vh);
+    if (warp == 1) {
+        for (int i = lane; i < D; i += 32) q[i] = qkv[h * D + i];
         __syncwarp();
-        norm_rope<D>(qh, a.q_norm, cs, sn, a.eps, qtmp + hh * D);
+        norm_rope<D>(q, a.q_norm, cs, sn, a.eps, y);
     }
     __syncthreads();
+    if (a.kv_fused && h % grp == 0 && tid < D) {
+        kc[(size_t) p * kvd + tid] = kh[tid];
+        vc[(size_t) p * kvd + tid] = vh[tid];
+    }
 
-    const int s0 = a.window > 0 ? max(0, p - a.window + 1) : 0, nk = p - s0 + 1;
-    // scores (seoul.cpp:445): one thread per position, all GRP heads
-    float lmax[GRP];
-#pragma unroll
-    for (int hh = 0; hh < GRP; hh++) lmax[hh] = -INFINITY;
-    for (int t = tid; t < nk; t += NT) {
+    // scores (seoul.cpp:445): one thread per position
+    float lmax = -INFINITY;
+    for (int t = tid; t < nk; t += ATT_NT) {
         const int pt = s0 + t;
         uint4 kr[D / 8];
-        if (a.kv_fused && pt == p) {
+        const uint4 *src = (a.kv_fused && pt == p) ? (const uint4 *) kh : (const uint4 *) (kc + (size_t) pt * kvd);
 #pragma unroll
-            for (int w = 0; w < D / 8; w++) kr[w] = ((const uint4 *) kh)[w];
-        } else {
-            const uint4 *src = (const uint4 *) (kc + (size_t) pt * kvd);
-#pragma unroll
-            for (int w = 0; w < D / 8; w++) kr[w] = src[w];
-        }
-#pragma unroll
-        for (int hh = 0; hh < GRP; hh++) {
-            const float s = __fmul_rn(dot_h8<D>(q + hh * D, kr), a.scale);
-            sc[(size_t) hh * a.n_ctx + t] = s;
-            lmax[hh] = lmax[hh] < s ? s : lmax[hh];
-        }
+        for (int w = 0; w < D / 8; w++) kr[w] = src[w];
+        const float v = __fmul_rn(dot_h8<D>(q, kr), a.scale);
+        sc[t] = v;
+        lmax = lmax < v ? v : lmax;
     }
 #pragma unroll
-    for (int hh = 0; hh < GRP; hh++) {
-        float m = lmax[hh];
-#pragma unroll
-        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (lane == 0) wmax[hh * NW + warp] = m;
-    }
+    for (int o = 16; o; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
+    if (lane == 0) wmax[warp] = lmax;
     __syncthreads();
-    if (tid < GRP) {
-        float m = -INFINITY;
-        for (int w = 0; w < NW; w++) m = fmaxf(m, wmax[tid * NW + w]);
-        mx[tid] = m;
-    }
-    __syncthreads();
+    float m = wmax[0];
+    for (int w = 1; w < ATT_NW; w++) m = fmaxf(m, wmax[w]);
     // exp and the double sum (seoul.cpp:446-448)
-    double lsum[GRP];
-#pragma unroll
-    for (int hh = 0; hh < GRP; hh++) lsum[hh] = 0.0;
-    for (int t = tid; t < nk; t += NT) {
-#pragma unroll
-        for (int hh = 0; hh < GRP; hh++) {
-            float *sp = sc + (size_t) hh * a.n_ctx + t;
-            const float e = exp_cr(__fsub_rn(*sp, mx[hh]));
-            *sp = e;
-            lsum[hh] += (double) e;
-        }
+    double ls = 0.0;
+    for (int t = tid; t < nk; t += ATT_NT) {
+        const float e = exp_cr(__fsub_rn(sc[t], m));
+        sc[t] = e;
+        ls += (double) e;
     }
 #pragma unroll
-    for (int hh = 0; hh < GRP; hh++) {
-        double s = lsum[hh];
-#pragma unroll
-        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) dsum[hh * NW + warp] = s;
+    for (int o = 16; o; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+    if (lane == 0) dsum[warp] = ls;
+    __syncthreads();
+    if (tid == 0) {
+        double t = 0.0;
+        for (int w = 0; w < ATT_NW; w++) t += dsum[w];
+        *inv = __double2float_rn(1.0 / t);
     }
     __syncthreads();
-    if (tid < GRP) {
-        double s = 0.0;
-        for (int w = 0; w < NW; w++) s += dsum[tid * NW + w];
-        inv[tid] = __double2float_rn(1.0 / s);
-    }
-    __syncthreads();
-    for (int t = tid; t < nk; t += NT) {
+    const float iv = *inv;
+    for (int t = tid; t < nk; t += ATT_NT) sc[t] = __fmul_rn(sc[t], iv);
+
+    // P.V (seoul.cpp:449-450): o_i = fma(p_t, v_t,i, o_i) over positions in order; thread i < D owns dimension i
+    float o = 0.0f;
+    for (int k = 0; k < ntile; k++) {
+        if (k + 1 < ntile) cp_wait_group<1>();
+        else cp_wait_group<0>();
+        __syncthreads();
+        if (tid < D) {
+            const uint16_t *vb = vt + (size_t) (k & 1) * VT * D + tid;
+            const float *pr = sc + (size_t) k * VT;
+            const int n = min(VT, ng - k * VT);
+            int t = 0;
+            for (; t + 8 <= n; t += 8) {
+                uint16_t v8[8];
 #pragma unroll
-        for (int hh = 0; hh < GRP; hh++) {
-            float *sp = sc + (size_t) hh * a.n_ctx + t;
-            *sp = __fmul_rn(*sp, inv[hh]);
+                for (int u = 0; u < 8; u++) v8[u] = vb[(size_t) (t + u) * D];
+                const float4 p0 = *(const float4 *) (pr + t), p1 = *(const float4 *) (pr + t + 4);
+                o = __fmaf_rn(p0.x, h2f(v8[0]), o);
+                o = __fmaf_rn(p0.y, h2f(v8[1]), o);
+                o = __fmaf_rn(p0.z, h2f(v8[2]), o);
+                o = __fmaf_rn(p0.w, h2f(v8[3]), o);
+                o = __fmaf_rn(p1.x, h2f(v8[4]), o);
+                o = __fmaf_rn(p1.y, h2f(v8[5]), o);
+                o = __fmaf_rn(p1.z, h2f(v8[6]), o);
+                o = __fmaf_rn(p1.w, h2f(v8[7]), o);
+            }
+            for (; t < n; t++) o = __fmaf_rn(pr[t], h2f(vb[(size_t) t * D]), o);
         }
+        __syncthreads();
+        if (k + 2 < ntile) load_tile(k + 2);
     }
-    __syncthreads();
-    // P.V (seoul.cpp:449-450): o_i = fma(p_t, v_t,i, o_i) over positions in order; thread (head, i)
-    {
-        const int hh = tid / D, i = tid - hh * D;
-        const float *pr = sc + (size_t) hh * a.n_ctx;
-        const int ng = (a.kv_fused && s0 + nk - 1 == p) ? nk - 1 : nk;   // positions read from the cache
-        const uint16_t *vp = vc + (size_t) s0 * kvd + i;
-        float o = 0.0f;
-        int t = 0;
-        for (; t + 8 <= ng; t += 8) {
-            uint16_t v8[8];
-#pragma unroll
-            for (int u = 0; u < 8; u++) v8[u] = vp[(size_t) (t + u) * kvd];
-#pragma unroll
-            for (int u = 0; u < 8; u++) o = __fmaf_rn(pr[t + u], h2f(v8[u]), o);
-        }
-        for (; t < ng; t++) o = __fmaf_rn(pr[t], h2f(vp[(size_t) t * kvd]), o);
-        if (ng < nk) o = __fmaf_rn(pr[nk - 1], h2f(vh[i]), o);
-        const int h = g * GRP + hh;
+    if (tid < D) {
+        if (ng < nk) o = __fmaf_rn(sc[nk - 1], h2f(vh[tid]), o);   // this position's own V
         const float gv = qkv[H * D + 2 * kvd + h];
         const float gate = __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_cr(-gv)));   // seoul.cpp:451
-        const float y = __fmul_rn(o, gate);
-        a.att[(size_t) c * a.att_stride + h * D + i] = y;
-        qtmp[hh * D + i] = y;
+        const float yv = __fmul_rn(o, gate);
+        a.att[(size_t) c * a.att_stride + h * D + tid] = yv;
+        y[tid] = yv;
     }
-    // the 8-bit cut of this group's output blocks (imi_cut32 of seoul.cpp:457), so the o table only loads codes
-    if (trace && tid == 0) trace[13] = global_ns();
-    if (a.q8o_q) {
-        __syncthreads();
+    __syncthreads();
+    // the 8-bit cut of this head's output blocks (imi_cut32 of seoul.cpp:457), so the o table only loads codes
+    if (a.q8o_q && warp == 0) {
         const int HD = H * D;
-        for (int t = tid; t < GRP * D / 32; t += NT) {
-            float v[32];
-            load32(qtmp + 32 * t, v);
-            const int blk = g * GRP * D / 32 + t;
-            cut32(v, a.q8o_q + (size_t) c * HD + 32 * blk, a.q8o_d + (size_t) c * (HD / 32) + blk,
-                  a.q8o_s + (size_t) c * (HD / 32) + blk);
+        for (int q0 = 0; q0 < D / 4; q0 += 32) {
+            const int qi = q0 + lane;
+            const bool act = qi < D / 4;
+            const float4 v = act ? ((const float4 *) y)[qi] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            cut_chunk(v, act, qi, a.q8o_q + (size_t) c * HD + h * D, a.q8o_d + (size_t) c * (HD / 32) + h * D / 32,
+                      a.q8o_s + (size_t) c * (HD / 32) + h * D / 32);
         }
     }
     if (trace && tid == 0) trace[14] = global_ns();
 }
 
-__host__ __device__ inline size_t attn_smem_bytes(int D, int GRP, int n_ctx) { return attn_plan(D, GRP, n_ctx).total; }
+__host__ __device__ inline size_t attn_smem_bytes(int D, int n_ctx) { return attn_plan(D, n_ctx).total; }
 
 // ---------------------------------------------------------------------------------------------------------------
 // known-answer helper: the 8-bit cut of a vector
