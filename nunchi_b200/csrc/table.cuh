@@ -36,40 +36,6 @@ __device__ __forceinline__ bool nbar_and(int id, int count, bool v) {
     return r != 0;
 }
 
-// imi_cut32 (vec.h:47-77) of one 32-value block held by ONE thread: d = max|x|/127, id = 1/d (0 if d == 0),
-// q = round-half-even(x * id). Writes 32 codes (16-byte aligned), d and d * sum(q).
-__device__ __forceinline__ void cut32(const float (&v)[32], int8_t *q, float *d_out, float *s_out) {
-    float amax = 0.0f;
-#pragma unroll
-    for (int k = 0; k < 32; k++) amax = fmaxf(amax, fabsf(v[k]));
-    const float d = __fdiv_rn(amax, 127.0f);
-    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-    int sum = 0;
-    uint32_t w[8];
-#pragma unroll
-    for (int k = 0; k < 8; k++) w[k] = 0;
-#pragma unroll
-    for (int k = 0; k < 32; k++) {
-        const int c = __float2int_rn(__fmul_rn(v[k], id));
-        sum += c;
-        w[k >> 2] |= ((uint32_t) c & 0xffu) << (8 * (k & 3));
-    }
-    uint4 *qo = (uint4 *) q;
-    qo[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    qo[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    *d_out = d;
-    *s_out = __fmul_rn(d, (float) sum);
-}
-
-// 32 consecutive floats (16-byte aligned) into registers
-__device__ __forceinline__ void load32(const float *p, float (&v)[32]) {
-#pragma unroll
-    for (int k = 0; k < 8; k++) {
-        const float4 f = ((const float4 *) p)[k];
-        v[4 * k] = f.x; v[4 * k + 1] = f.y; v[4 * k + 2] = f.z; v[4 * k + 3] = f.w;
-    }
-}
-
 // ---------------- input preparation ----------------
 // Each thread owns the float4 chunks q = tid, tid + MV_THREADS, ... of an n_embd vector in every phase. MV_THREADS is
 // a multiple of 32, so the 8 lanes holding chunks 8m..8m+7 hold one 32-value block, which cut_chunk cuts in place:
@@ -380,7 +346,8 @@ __device__ __forceinline__ float amax_val(unsigned long long k) {
 __device__ __forceinline__ float row_chain(const float *f, const uint16_t *d, const float *xdc, const float *xsc,
                                            int nb) {
     float acc = 0.0f, cor = 0.0f;
-    for (int j = 0; j < nb; j += 4) {   // nb is a multiple of 8
+#pragma unroll 4
+    for (int j = 0; j < nb; j += 4) {   // nb is a multiple of 8; unrolled so later blocks' loads overlap the chain
         const float4 fv = *(const float4 *) (f + j), xv = *(const float4 *) (xdc + j), sv = *(const float4 *) (xsc + j);
         const uint2 dv = *(const uint2 *) (d + j);
         const float d0 = h2f((uint16_t) (dv.x & 0xffff)), d1 = h2f((uint16_t) (dv.x >> 16)),
@@ -569,14 +536,14 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_table(const __grid_constant__
     if (trace && ct == 0) trace[14] = global_ns();
     if (EPI == E_SILU && a.q8o_q && abort_flag == 0) {   // the cut of this CTA's whole 32-value blocks (imi_cut32)
         nbar_sync(NB_TAIL, MV_CTHREADS);
-        const int nblk = nrows / 64, half = a.rows / 2;
-        for (int t = ct; t < nc * nblk; t += MV_CTHREADS) {
-            const int c = t / nblk, k = t - c * nblk;
-            float v[32];
-            load32(ab + c * a.ab_len + 32 * k, v);
-            const int blk = r0 / 64 + k;
-            cut32(v, a.q8o_q + (size_t) c * half + 32 * blk, a.q8o_d + (size_t) c * (half / 32) + blk,
-                  a.q8o_s + (size_t) c * (half / 32) + blk);
+        const int nch = nrows / 8, half = a.rows / 2;   // float4 chunks of produced values per column
+        for (int b0 = 0; b0 < nc * nch; b0 += MV_CTHREADS) {   // 8 lanes per block; a column has whole blocks
+            const int t = b0 + ct;
+            const bool act = t < nc * nch;
+            const int c = act ? t / nch : 0, q = act ? t - c * nch : 0;
+            const float4 v = act ? *(const float4 *) (ab + c * a.ab_len + 4 * q) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            cut_chunk(v, act, q, a.q8o_q + (size_t) c * half + r0 / 2, a.q8o_d + (size_t) c * (half / 32) + r0 / 64,
+                      a.q8o_s + (size_t) c * (half / 32) + r0 / 64);
         }
     }
 
