@@ -18,14 +18,14 @@
 
 namespace imi {
 
-constexpr int MV_IWARPS = 8;               // table-read CTA: warps computing integer block dots
+constexpr int MV_IWARPS = 16;              // table-read CTA (one per SM): warps computing integer block dots
 constexpr int MV_CWARPS = 4;               // warps running the per-row float chains (and the output stage)
 constexpr int MV_ITHREADS = 32 * MV_IWARPS, MV_CTHREADS = 32 * MV_CWARPS;
 constexpr int MV_THREADS = MV_ITHREADS + MV_CTHREADS;
 constexpr int MV_STAGES = 2;               // weight stages in flight per CTA (TMA bulk copies)
 constexpr int MV_STAGE_BYTES = 36864;      // one K=8192 row group of 8 rows, or 32 rows of K=2048
 constexpr int MV_MAX_COLS = 8;             // inputs sharing one table read in the small-batch kernel
-constexpr int MV_SMEM_BUDGET = 113 * 1024; // two table-read CTAs fit one SM, so the next launch can prefetch early
+constexpr int MV_SMEM_BUDGET = 220 * 1024; // shared memory of one table-read CTA (one per SM)
 
 // Per-conversation scalars that live on the device (the rest of imi_seoul_state is device buffers).
 struct SessDev {

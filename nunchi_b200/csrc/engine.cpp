@@ -223,7 +223,7 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
     e->n_vocab = (int) te->ne[1];
     if (e->n_embd % 256) return fail(IMI_E_FORMAT, "n_embd must be a multiple of 256");
     if (e->n_layer <= 0 || e->d_conv < 1 || e->head_dim <= 0) return fail(IMI_E_FORMAT, "bad lfm3 hyperparameters");
-    if (e->d_conv > 8 || e->n_embd > 6144)   // the input preparation keeps 8 taps / 4 x 384 float4 chunks in registers
+    if (e->d_conv > 8 || e->n_embd > 6144)   // the input preparation keeps 8 taps and n_embd/4 float4 chunks in registers
         return fail(IMI_E_FORMAT, "conv width above 9 or n_embd above 6144 is not supported");
     const int E = e->n_embd;
     {

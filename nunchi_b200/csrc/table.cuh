@@ -41,7 +41,7 @@ __device__ __forceinline__ bool nbar_and(int id, int count, bool v) {
 // a multiple of 32, so the 8 lanes holding chunks 8m..8m+7 hold one 32-value block, which cut_chunk cuts in place:
 // the residual update, the norm and the 8-bit cut stay in registers; only the RMS reductions (one warp per column,
 // imi's lane order) read the vector from shared memory.
-constexpr int PQ = 4;   // chunks per thread (n_embd <= 4 * PQ * MV_THREADS = 6144)
+constexpr int PQ = (6144 / 4 + MV_THREADS - 1) / MV_THREADS;   // chunks per thread (n_embd <= 6144)
 struct PreRegs {
     float4 wpr[PQ], wpo[PQ];
 };
@@ -365,7 +365,7 @@ __device__ __forceinline__ float row_chain(const float *f, const uint16_t *d, co
 }
 
 template <int PRO, int EPI, int NC>
-__global__ void __launch_bounds__(MV_THREADS, 2) k_table(const __grid_constant__ MvArgs a) {
+__global__ void __launch_bounds__(MV_THREADS, 1) k_table(const __grid_constant__ MvArgs a) {
     extern __shared__ __align__(128) uint8_t sm[];
     __shared__ int abort_flag, last_cta;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, K = a.cols, nb = K / 32, ld = nb + 4,
