@@ -22,7 +22,7 @@ constexpr int MV_IWARPS = 16;              // table-read CTA (one per SM): warps
 constexpr int MV_CWARPS = 4;               // warps running the per-row float chains (and the output stage)
 constexpr int MV_ITHREADS = 32 * MV_IWARPS, MV_CTHREADS = 32 * MV_CWARPS;
 constexpr int MV_THREADS = MV_ITHREADS + MV_CTHREADS;
-constexpr int MV_STAGES = 2;               // weight stages in flight per CTA (TMA bulk copies)
+constexpr int MV_MAX_STAGES = 8;           // weight stages in flight per CTA at most (TMA bulk copies; MvArgs::nstage)
 constexpr int MV_STAGE_BYTES = 36864;      // one K=8192 row group of 8 rows, or 32 rows of K=2048
 constexpr int MV_MAX_COLS = 8;             // inputs sharing one table read in the small-batch kernel
 constexpr int MV_SMEM_BUDGET = 220 * 1024; // shared memory of one table-read CTA (one per SM)
@@ -64,6 +64,7 @@ enum Epi : int { E_STORE = 0, E_SILU = 1, E_HEAD = 2 };
 struct MvArgs {
     const uint8_t *W;          // table rows: [rows][cols/2 code bytes | cols/32 fp16 scales]
     int rows, cols, row_bytes, unit, sr;   // sr: rows per stage
+    int nstage;                // weight stages in flight (1..MV_MAX_STAGES)
     const Col *cols_d;
     int ncol;
     const float *in;           // prologue input vector per column
@@ -141,12 +142,12 @@ struct MvPlan {
     int stage, bar, xq, xd, xs, fs, dd, vb, vo, ab, pc, red, total;
 };
 __host__ __device__ inline int align_up(int x, int a) { return (x + a - 1) / a * a; }
-__host__ __device__ inline MvPlan mv_plan(int cols, int sr, int nc, int vb_len, int ab_len) {
+__host__ __device__ inline MvPlan mv_plan(int cols, int sr, int nc, int vb_len, int ab_len, int ns) {
     MvPlan p;
     const int nb = cols / 32, ld = nb + 4;   // row strides: 16-byte aligned, conflict-free for vector loads
     int o = 0;
-    p.stage = o; o += MV_STAGES * MV_STAGE_BYTES;
-    p.bar = o;   o = align_up(o + 8 * MV_STAGES, 16);
+    p.stage = o; o += ns * MV_STAGE_BYTES;
+    p.bar = o;   o = align_up(o + 8 * MV_MAX_STAGES, 16);
     p.xq = o;    o = align_up(o + nc * cols, 16);
     p.xd = o;    o = align_up(o + 4 * nc * nb, 16);
     p.xs = o;    o = align_up(o + 4 * nc * nb, 16);

@@ -387,17 +387,24 @@ namespace {
 
 enum StepKind { K_DECODE = 0, K_PREFILL = 1, K_HEAD_ONLY = 2 };
 
-// rows per weight stage: as many as a stage holds (in steps of `gran` rows), fewer if that keeps two CTAs per SM (so
-// the next launch can start early); when even 8 rows do not fit that budget, one CTA per SM with full stages
-int pick_sr(int pro, const TableRef &t, int gran, int ncol, int E, int ab_len, int d_conv = 0) {
-    const int full = std::max(gran, (std::min(64, MV_STAGE_BYTES / t.row_bytes) / gran) * gran);
-    int sr = full;
-    while (sr > gran && table_smem(pro, t.cols, sr, ncol, E, ab_len, d_conv) > (size_t) MV_SMEM_BUDGET) sr -= gran;
-    if (sr < std::min(8, full)) {
-        sr = full;
-        while (sr > gran && table_smem(pro, t.cols, sr, ncol, E, ab_len, d_conv) > (size_t) 220 * 1024) sr -= gran;
+// rows per weight stage (sr) and stages in flight (nstage) of one table read: full stages (at most 64 rows of one
+// MV_STAGE_BYTES stage) and as many of them as the CTA's slice needs (up to MV_MAX_STAGES), within one CTA's shared
+// memory; fewer stages first (down to 2), then fewer rows per stage. a.rows, cols, row_bytes, unit, ncol, n_embd,
+// ab_len and d_conv must be set.
+void plan_stages(MvArgs &a, int pro, int gran, int grid) {
+    const int units = a.rows / a.unit, rows_cta = (units + grid - 1) / grid * a.unit;
+    const int full = std::max(gran, (std::min(64, MV_STAGE_BYTES / a.row_bytes) / gran) * gran);
+    for (int sr = full; sr >= gran; sr -= gran) {
+        const int nst = std::max(1, (rows_cta + sr - 1) / sr);
+        for (int ns = std::min(MV_MAX_STAGES, nst); ns >= std::min(2, nst); ns--)
+            if (table_smem(pro, a.cols, sr, a.ncol, a.n_embd, a.ab_len, a.d_conv, ns) <= (size_t) MV_SMEM_BUDGET) {
+                a.sr = sr;
+                a.nstage = ns;
+                return;
+            }
     }
-    return std::max(sr, gran);
+    a.sr = gran;   // nothing fits: the launch reports the shared-memory excess
+    a.nstage = 1;
 }
 
 // one table read: CTAs take whole `unit`s of rows (64 for the SiLU stage, which cuts whole 32-value blocks of its
@@ -412,7 +419,7 @@ cudaError_t table_launch(imi_cuda_engine *e, const TableRef &t, int pro, int epi
     const int units = t.rows / a.unit;
     const int grid = std::max(1, std::min(e->sm_count, units));
     a.ab_len = epi == E_SILU ? (units + grid - 1) / grid * a.unit / 2 : 0;
-    a.sr = pick_sr(pro, t, gran, a.ncol, e->n_embd, a.ab_len, a.d_conv);
+    plan_stages(a, pro, gran, grid);
     if (!a.trace) a.trace = e->trace_slot(10 * pro + epi, grid);
     return launch_table(pro, epi, a, grid, e->stream, true);
 }
@@ -937,11 +944,11 @@ imi_cuda_status imi_cuda_q4_matvec(int device, const uint8_t *q4, int rows, int 
         a.W = dW; a.rows = rows; a.cols = cols; a.row_bytes = row_bytes; a.unit = 1;
         a.cols_d = dcols; a.ncol = ncol; a.q8_q = dq; a.q8_d = dd; a.q8_s = ds; a.dots = ddots;
         a.out = dout; a.out_stride = rows; a.err = derr; a.ring_layer = -1;
-        TableRef t; t.rows = rows; t.cols = cols; t.row_bytes = row_bytes;
-        a.sr = pick_sr(P_Q8IN, t, 1, ncol, 0, 0);
         int sms = 148;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-        r = launch_table(P_Q8IN, E_STORE, a, std::max(1, std::min(sms, rows)), 0, false);
+        const int grid = std::max(1, std::min(sms, rows));
+        plan_stages(a, P_Q8IN, 1, grid);
+        r = launch_table(P_Q8IN, E_STORE, a, grid, 0, false);
     }
     if (r == cudaSuccess) r = cudaMemcpy(out, dout, b_o, cudaMemcpyDeviceToHost);
     if (r == cudaSuccess && dots) r = cudaMemcpy(dots, ddots, b_dots, cudaMemcpyDeviceToHost);
@@ -1032,11 +1039,11 @@ imi_cuda_status imi_cuda_q4_matvec_static(int device, const uint8_t *q4, int row
         a.W = dW; a.rows = rows; a.cols = cols; a.row_bytes = row_bytes; a.unit = 1;
         a.cols_d = dcols; a.ncol = ncol; a.q8_q = xq; a.q8_d = xd; a.q8_s = xs;
         a.out = out; a.out_stride = rows; a.err = derr; a.ring_layer = -1;
-        TableRef t; t.rows = rows; t.cols = cols; t.row_bytes = row_bytes;
-        a.sr = pick_sr(P_Q8IN, t, 1, ncol, 0, 0);
         int sms = 148;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-        r = launch_table(P_Q8IN, E_STORE, a, std::max(1, std::min(sms, rows)), st, false);
+        const int grid = std::max(1, std::min(sms, rows));
+        plan_stages(a, P_Q8IN, 1, grid);
+        r = launch_table(P_Q8IN, E_STORE, a, grid, st, false);
     }
     int herr = 0;
     if (r == cudaSuccess) r = cudaMemcpyAsync(&herr, derr, 4, cudaMemcpyDeviceToHost, st);
@@ -1126,7 +1133,7 @@ imi_cuda_status imi_cuda_trace_table(imi_cuda_engine *e, int layer, int which, i
     a.trace = d;
     a.W = e->w + t->off; a.rows = t->rows; a.cols = t->cols; a.row_bytes = t->row_bytes;
     a.unit = epi == E_SILU ? 2 : 1;
-    a.sr = pick_sr(P_Q8IN, *t, 1, ncol, e->n_embd, 0);
+    plan_stages(a, P_Q8IN, 1, g);
     cudaError_t r = launch_table(P_Q8IN, epi, a, g, e->stream, false);
     if (r == cudaSuccess) r = cudaMemcpyAsync(trace, d, (size_t) g * MV_TRACE * 8, cudaMemcpyDeviceToHost, e->stream);
     if (r == cudaSuccess) r = cudaStreamSynchronize(e->stream);

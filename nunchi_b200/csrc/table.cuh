@@ -370,7 +370,8 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_table(const __grid_constant__
     __shared__ int abort_flag, last_cta;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, K = a.cols, nb = K / 32, ld = nb + 4,
               nc = a.ncol, sr = a.sr;
-    const MvPlan P = mv_plan(K, sr, NC, mv_vb_len(PRO, K, a.n_embd, NC, a.d_conv), a.ab_len);
+    const int NS = a.nstage;
+    const MvPlan P = mv_plan(K, sr, NC, mv_vb_len(PRO, K, a.n_embd, NC, a.d_conv), a.ab_len, NS);
     uint8_t *stage = sm + P.stage;
     uint64_t *bar = (uint64_t *) (sm + P.bar);
     const int8_t *xq = (const int8_t *) (sm + P.xq);
@@ -392,7 +393,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_table(const __grid_constant__
     unsigned long long *trace = a.trace ? a.trace + (size_t) blockIdx.x * MV_TRACE : nullptr;
     if (trace && tid == 0) trace[0] = global_ns();
     if (tid == 0) {
-        for (int b = 0; b < MV_STAGES; b++) mbar_init(&bar[b], 1);
+        for (int b = 0; b < NS; b++) mbar_init(&bar[b], 1);
         fence_barrier_init();
         abort_flag = 0;
     }
@@ -400,14 +401,14 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_table(const __grid_constant__
     auto issue = [&](int st) {
         const int rr = st * sr, n = min(sr, nrows - rr);
         const uint32_t bytes = (uint32_t) n * (uint32_t) a.row_bytes;
-        uint64_t *b = &bar[st % MV_STAGES];
+        uint64_t *b = &bar[st % NS];
         mbar_expect_tx(b, bytes);
-        bulk_g2s(stage + (st % MV_STAGES) * MV_STAGE_BYTES, a.W + (size_t) (r0 + rr) * a.row_bytes, bytes, b);
+        bulk_g2s(stage + (st % NS) * MV_STAGE_BYTES, a.W + (size_t) (r0 + rr) * a.row_bytes, bytes, b);
     };
     if (tid == 0) {   // the weights do not depend on the previous launch: start them before waiting on it
-        for (int st = 0; st < min(MV_STAGES, nst); st++) issue(st);
+        for (int st = 0; st < min(NS, nst); st++) issue(st);
         // and the rest of this CTA's slice into L2, so HBM streams the whole table while the stages are consumed
-        const size_t beg = (size_t) min(MV_STAGES * sr, nrows) * a.row_bytes, end = (size_t) nrows * a.row_bytes;
+        const size_t beg = (size_t) min(NS * sr, nrows) * a.row_bytes, end = (size_t) nrows * a.row_bytes;
         const uint8_t *base = a.W + (size_t) r0 * a.row_bytes;
         for (size_t o = beg; o < end; o += 65536) prefetch_l2(base + o, (uint32_t) min((size_t) 65536, end - o));
     }
@@ -439,13 +440,13 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_table(const __grid_constant__
         const int nchunk = nb / 4;   // 8-byte chunks of a row's scales (scale rows are nb + 4 halfs: 8-byte aligned)
         for (int st = 0; st < nst; st++) {
             const int b = st & 1;
-            bool ok = mbar_wait(&bar[st % MV_STAGES], (uint32_t) ((st / MV_STAGES) & 1));
+            bool ok = mbar_wait(&bar[st % NS], (uint32_t) ((st / NS) & 1));
             ok = nbar_and(NB_INT, MV_ITHREADS, ok);
             if (!ok && it == 0) { abort_flag = 1; atomicExch(a.err, 7); }
             if (st >= 2) nbar_sync(NB_FREE + b, MV_THREADS);   // the chains are done with buffer b
             if (ok) {
                 const int rb = st * sr, nr = min(sr, nrows - rb);
-                const uint8_t *sb = stage + (st % MV_STAGES) * MV_STAGE_BYTES;
+                const uint8_t *sb = stage + (st % NS) * MV_STAGE_BYTES;
                 float *f = fs + b * NC * sr * ld;
                 uint16_t *dq = dd + b * sr * ld;
                 for (int idx = it; idx < nr * nchunk; idx += MV_ITHREADS) {   // the rows' scales
@@ -479,9 +480,9 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_table(const __grid_constant__
             }
             nbar_sync(NB_INT, MV_ITHREADS);   // every integer thread is done with this stage buffer
             if (trace && it == 0 && st < 11) trace[3 + st] = global_ns();
-            if (it == 0 && ok && st + MV_STAGES < nst) {
+            if (it == 0 && ok && st + NS < nst) {
                 fence_proxy_async();
-                issue(st + MV_STAGES);
+                issue(st + NS);
             }
             nbar_arrive(NB_READY + b, MV_THREADS);
         }
