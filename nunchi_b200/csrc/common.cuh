@@ -22,6 +22,7 @@ constexpr int MV_IWARPS = 16;              // table-read CTA (one per SM): warps
 constexpr int MV_CWARPS = 4;               // warps running the per-row float chains (and the output stage)
 constexpr int MV_ITHREADS = 32 * MV_IWARPS, MV_CTHREADS = 32 * MV_CWARPS;
 constexpr int MV_THREADS = MV_ITHREADS + MV_CTHREADS;
+constexpr int MV_NBUF = 4;                 // block-dot buffers: stage s goes to buffer (and chain warp) s % MV_NBUF
 constexpr int MV_MAX_STAGES = 8;           // weight stages in flight per CTA at most (TMA bulk copies; MvArgs::nstage)
 constexpr int MV_STAGE_BYTES = 36864;      // one K=8192 row group of 8 rows, or 32 rows of K=2048
 constexpr int MV_MAX_COLS = 8;             // inputs sharing one table read in the small-batch kernel
@@ -129,7 +130,7 @@ struct FinalArgs {
 };
 
 // ---- shared-memory plan of the table-read kernel (host and device agree on it) ----
-// fs: integer block dots as floats, [2 buffers][nc][sr][nb+4]; dd: block scales (fp16 bits), [2][sr][nb+4];
+// fs: integer block dots as floats, [MV_NBUF][nc][sr][nb+4]; dd: block scales (fp16 bits), [MV_NBUF][sr][nb+4];
 // vb: prologue vectors [nc][vb_len] (overlapping fs/dd); pc: per-column facts read before the dependency wait;
 // red: reductions and argmax partials.
 struct PreCol {
@@ -153,8 +154,8 @@ __host__ __device__ inline MvPlan mv_plan(int cols, int sr, int nc, int vb_len, 
     p.xs = o;    o = align_up(o + 4 * nc * nb, 16);
     // the prologue's vectors (vb) are dead before the first block dot is stored: they share the dot buffers' space
     const int u = o;
-    p.fs = o;    o = align_up(o + 2 * 4 * nc * sr * ld, 16);
-    p.dd = o;    o = align_up(o + 2 * 2 * sr * ld, 16);
+    p.fs = o;    o = align_up(o + MV_NBUF * 4 * nc * sr * ld, 16);
+    p.dd = o;    o = align_up(o + MV_NBUF * 2 * sr * ld, 16);
     p.vo = o;
     p.vb = u;    o = o > align_up(u + 4 * nc * vb_len, 16) ? o : align_up(u + 4 * nc * vb_len, 16);
     p.ab = o;    o = align_up(o + 4 * nc * ab_len, 16);

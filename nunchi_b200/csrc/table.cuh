@@ -19,7 +19,11 @@
 namespace imi {
 
 // named barriers (0 is __syncthreads)
-enum : int { NB_INT = 1, NB_READY = 2 /* +buffer */, NB_FREE = 4 /* +buffer */, NB_TAIL = 7 };
+// READY + b: the integer warps hand buffer b to chain warp b; FREE + b: chain warp b hands it back (each barrier has
+// the integer threads and one chain warp)
+enum : int { NB_INT = 1, NB_READY = 2 /* +buffer */, NB_FREE = 2 + MV_NBUF /* +buffer */, NB_TAIL = 2 + 2 * MV_NBUF };
+static_assert(NB_TAIL < 16 && MV_NBUF == MV_CWARPS, "named barriers: one buffer per chain warp");
+constexpr int NB_PAIR = MV_ITHREADS + 32;
 __device__ __forceinline__ void nbar_sync(int id, int count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
@@ -439,11 +443,11 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_table(const __grid_constant__
         }
         const int nchunk = nb / 4;   // 8-byte chunks of a row's scales (scale rows are nb + 4 halfs: 8-byte aligned)
         for (int st = 0; st < nst; st++) {
-            const int b = st & 1;
+            const int b = st % MV_NBUF;
             bool ok = mbar_wait(&bar[st % NS], (uint32_t) ((st / NS) & 1));
             ok = nbar_and(NB_INT, MV_ITHREADS, ok);
             if (!ok && it == 0) { abort_flag = 1; atomicExch(a.err, 7); }
-            if (st >= 2) nbar_sync(NB_FREE + b, MV_THREADS);   // the chains are done with buffer b
+            if (st >= MV_NBUF) nbar_sync(NB_FREE + b, NB_PAIR);   // chain warp b is done with buffer b
             if (ok) {
                 const int rb = st * sr, nr = min(sr, nrows - rb);
                 const uint8_t *sb = stage + (st % NS) * MV_STAGE_BYTES;
@@ -472,39 +476,68 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_table(const __grid_constant__
                         }
                     }
                 };
-                if (fixed_j) {
-                    for (int r = it / nb; r < nr; r += rstep) one(r, j0, true);
+                if (fixed_j) {   // rows it/nb + k*rstep, 4 at a time with their code loads first
+                    for (int rr = it / nb; rr < nr; rr += 4 * rstep) {
+                        uint4 code[4];
+#pragma unroll
+                        for (int u = 0; u < 4; u++)
+                            if (rr + u * rstep < nr)
+                                code[u] = *(const uint4 *) (sb + (size_t) (rr + u * rstep) * a.row_bytes + 16 * j0);
+#pragma unroll
+                        for (int u = 0; u < 4; u++) {
+                            const int r = rr + u * rstep;
+                            if (r >= nr) break;
+#pragma unroll
+                            for (int c = 0; c < NC; c++) {
+                                if (c < nc) {
+                                    int s;
+                                    if (NC <= 2) {
+                                        s = dot_block(code[u], xw[c < NX ? c : 0]);
+                                    } else {
+                                        const int4 *xp = (const int4 *) (xq + c * K + 32 * j0);
+                                        const int4 x0 = xp[0], x1 = xp[1];
+                                        const int x8[8] = { x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w };
+                                        s = dot_block(code[u], x8);
+                                    }
+                                    f[(c * sr + r) * ld + j0] = __int2float_rn(s);
+                                    if (c == 0 && a.dots) a.dots[(size_t) (r0 + rb + r) * nb + j0] = s;
+                                }
+                            }
+                        }
+                    }
                 } else {
                     for (int idx = it; idx < nr * nb; idx += MV_ITHREADS) one(idx / nb, idx % nb, false);
                 }
             }
-            nbar_sync(NB_INT, MV_ITHREADS);   // every integer thread is done with this stage buffer
-            if (trace && it == 0 && st < 11) trace[3 + st] = global_ns();
-            if (it == 0 && ok && st + NS < nst) {
-                fence_proxy_async();
-                issue(st + NS);
+            if (st + NS < nst) {   // the slot is refilled: every integer thread must be done with it first
+                nbar_sync(NB_INT, MV_ITHREADS);
+                if (it == 0 && ok) {
+                    fence_proxy_async();
+                    issue(st + NS);
+                }
             }
-            nbar_arrive(NB_READY + b, MV_THREADS);
+            if (trace && it == 0 && st < 11) trace[3 + st] = global_ns();
+            nbar_arrive(NB_READY + b, NB_PAIR);
         }
-        for (int st = max(nst - 2, 0); st < nst; st++) nbar_sync(NB_FREE + (st & 1), MV_THREADS);
+        for (int st = max(nst - MV_NBUF, 0); st < nst; st++) nbar_sync(NB_FREE + st % MV_NBUF, NB_PAIR);
         return;
     }
 
-    // ---------------- chain warps: one thread per (input, row) ----------------
-    const int ct = tid - MV_ITHREADS;
+    // ---------------- chain warps: warp cw takes stages cw, cw + MV_NBUF, ...; one lane per (input, row) ----------------
+    const int ct = tid - MV_ITHREADS, cw = ct >> 5;
     unsigned long long best[NC];
 #pragma unroll
     for (int c = 0; c < NC; c++) best[c] = 0ull;
-    for (int st = 0; st < nst; st++) {
-        const int b = st & 1;
-        nbar_sync(NB_READY + b, MV_THREADS);
+    for (int st = cw; st < nst; st += MV_NBUF) {
+        const int b = cw;
+        nbar_sync(NB_READY + b, NB_PAIR);
         const bool ok = abort_flag == 0;
         const int rb = st * sr, nr = min(sr, nrows - rb);
         const float *f = fs + b * NC * sr * ld;
         const uint16_t *dq = dd + b * sr * ld;
         if (ok) {
-            for (int base = 0; base < nc * nr; base += MV_CTHREADS) {   // warp-uniform trip count
-                const int t = base + ct;
+            for (int base = 0; base < nc * nr; base += 32) {   // warp-uniform trip count
+                const int t = base + lane;
                 const bool act = t < nc * nr;
                 const int c = act ? t / nr : 0, r = act ? t - c * nr : 0;
                 float v = 0.0f;
@@ -532,9 +565,9 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_table(const __grid_constant__
                 }
             }
         }
-        nbar_arrive(NB_FREE + b, MV_THREADS);
+        nbar_arrive(NB_FREE + b, NB_PAIR);
     }
-    if (trace && ct == 0) trace[14] = global_ns();
+    if (trace && lane == 0) atomicMax(&trace[14], global_ns());
     if (EPI == E_SILU && a.q8o_q && abort_flag == 0) {   // the cut of this CTA's whole 32-value blocks (imi_cut32)
         nbar_sync(NB_TAIL, MV_CTHREADS);
         const int nch = nrows / 8, half = a.rows / 2;   // float4 chunks of produced values per column
@@ -550,7 +583,6 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_table(const __grid_constant__
 
     if (EPI == E_HEAD) {   // the step ends here: pick, position, counters (one CTA, the last to finish)
         unsigned long long *wbest = (unsigned long long *) (red + 64);
-        const int cw = warp - MV_IWARPS;
 #pragma unroll
         for (int c = 0; c < NC; c++) {
             unsigned long long k = best[c];
