@@ -158,10 +158,23 @@ __global__ void __launch_bounds__(ATT_NT) k_attn(const __grid_constant__ AttnArg
     float *wmax = (float *) (sma + L.red + 8 * ATT_NW), *mx = wmax + ATT_NW, *inv = mx + 1;
 
     pdl_trigger();
-    pdl_wait();
-    if (trace && tid == 0) trace[1] = global_ns();
     const int H = a.n_head, grp = H / a.n_head_kv, g = h / grp, kvd = a.n_head_kv * D;
     const Col col = a.cols_d[c];
+    if (tid == 0) {   // before the wait: this CTA's share of the layer's cached K and V rows into L2 (a hint only:
+                      // the position read here may be one behind; the rows before it are final)
+        const int pp = ld_relaxed(&col.s->pos) + col.off, ps = a.window > 0 ? max(0, pp - a.window + 1) : 0;
+        const size_t row = (size_t) kvd * 2, bytes = (size_t) max(pp - ps, 0) * row;
+        const size_t share = (bytes / H + 15) / 16 * 16, b0 = (size_t) h * share, b1 = min(b0 + share, bytes);
+        const uint8_t *kb = (const uint8_t *) col.kc + ((size_t) a.ai * a.n_ctx + ps) * row;
+        const uint8_t *vb0 = (const uint8_t *) col.vc + ((size_t) a.ai * a.n_ctx + ps) * row;
+        for (size_t o = b0; o < b1; o += 65536) {
+            const uint32_t n = (uint32_t) min((size_t) 65536, b1 - o);
+            prefetch_l2(kb + o, n);
+            prefetch_l2(vb0 + o, n);
+        }
+    }
+    pdl_wait();
+    if (trace && tid == 0) trace[1] = global_ns();
     const int p = col.s->pos + col.off;
     const float *qkv = a.qkv + (size_t) c * a.qkv_stride;
     const float *cs = a.rope_cs + (size_t) p * (D / 2), *sn = a.rope_sn + (size_t) p * (D / 2);
