@@ -65,7 +65,7 @@ constexpr int ATT_NT = 128, ATT_NW = ATT_NT / 32;
 __host__ __device__ inline int attn_vtile(int D) { return 32768 / D; }   // positions per V tile (64 KB of fp16)
 // shared-memory plan of k_attn (host and device agree on it); every region 16-byte aligned
 struct AttnPlan {
-    size_t q, ktmp, tmp, y, kh, vh, red, vt, sc, total;
+    size_t q, ktmp, tmp, y, kh, vh, rcs, rsn, red, vt, sc, total;
 };
 __host__ __device__ inline AttnPlan attn_plan(int D, int n_ctx) {
     AttnPlan p;
@@ -77,6 +77,8 @@ __host__ __device__ inline AttnPlan attn_plan(int D, int n_ctx) {
     p.y = take(4 * (size_t) D);
     p.kh = take(2 * (size_t) D);
     p.vh = take(2 * (size_t) D);
+    p.rcs = take(4 * (size_t) D / 2);
+    p.rsn = take(4 * (size_t) D / 2);
     p.red = take(8 * ATT_NW + 4 * ATT_NW + 16);
     p.vt = take(2 * (size_t) attn_vtile(D) * D * 2);
     p.sc = take(4 * (size_t) n_ctx);
@@ -157,9 +159,16 @@ __global__ void __launch_bounds__(ATT_NT) k_attn(const __grid_constant__ AttnArg
     double *dsum = (double *) (sma + L.red);
     float *wmax = (float *) (sma + L.red + 8 * ATT_NW), *mx = wmax + ATT_NW, *inv = mx + 1;
 
+    float *rcs = (float *) (sma + L.rcs), *rsn = (float *) (sma + L.rsn);
     pdl_trigger();
     const int H = a.n_head, grp = H / a.n_head_kv, g = h / grp, kvd = a.n_head_kv * D;
     const Col col = a.cols_d[c];
+    // the rotary rows of the position read now (it changes only at the end of a step; checked again after the wait)
+    const int pspec = ld_relaxed(&col.s->pos) + col.off;
+    for (int i = tid; i < D / 2; i += ATT_NT) {
+        rcs[i] = a.rope_cs[(size_t) pspec * (D / 2) + i];
+        rsn[i] = a.rope_sn[(size_t) pspec * (D / 2) + i];
+    }
     if (tid == 0) {   // before the wait: this CTA's share of the layer's cached K and V rows into L2 (a hint only:
                       // the position read here may be one behind; the rows before it are final)
         const int pp = ld_relaxed(&col.s->pos) + col.off, ps = a.window > 0 ? max(0, pp - a.window + 1) : 0;
@@ -175,9 +184,13 @@ __global__ void __launch_bounds__(ATT_NT) k_attn(const __grid_constant__ AttnArg
     }
     pdl_wait();
     if (trace && tid == 0) trace[1] = global_ns();
-    const int p = col.s->pos + col.off;
+    const int p = ld_relaxed(&col.s->pos) + col.off;
     const float *qkv = a.qkv + (size_t) c * a.qkv_stride;
-    const float *cs = a.rope_cs + (size_t) p * (D / 2), *sn = a.rope_sn + (size_t) p * (D / 2);
+    const float *cs = rcs, *sn = rsn;
+    if (p != pspec) {   // the position moved since the rows were read: the table rows themselves
+        cs = a.rope_cs + (size_t) p * (D / 2);
+        sn = a.rope_sn + (size_t) p * (D / 2);
+    }
     uint16_t *kc = (uint16_t *) col.kc + (size_t) a.ai * a.n_ctx * kvd + g * D;
     uint16_t *vc = (uint16_t *) col.vc + (size_t) a.ai * a.n_ctx * kvd + g * D;
     const int s0 = a.window > 0 ? max(0, p - a.window + 1) : 0, nk = p - s0 + 1;
@@ -192,8 +205,7 @@ __global__ void __launch_bounds__(ATT_NT) k_attn(const __grid_constant__ AttnArg
         }
         cp_commit();
     };
-    if (ntile > 0) load_tile(0);
-    if (ntile > 1) load_tile(1);
+    __syncthreads();   // the rotary rows are in shared memory
 
     // this position's K and V (warp 0) and the rotated query (warp 1)
     if (a.kv_fused) kv_make<D>(a, qkv, g, p, ktmp, tmp, kh, vh);
@@ -207,18 +219,33 @@ __global__ void __launch_bounds__(ATT_NT) k_attn(const __grid_constant__ AttnArg
         kc[(size_t) p * kvd + tid] = kh[tid];
         vc[(size_t) p * kvd + tid] = vh[tid];
     }
+    // the cached V rows into shared memory while the scores run
+    if (ntile > 0) load_tile(0);
+    if (ntile > 1) load_tile(1);
 
     // scores (seoul.cpp:445): one thread per position
     float lmax = -INFINITY;
-    for (int t = tid; t < nk; t += ATT_NT) {
-        const int pt = s0 + t;
-        uint4 kr[D / 8];
-        const uint4 *src = (a.kv_fused && pt == p) ? (const uint4 *) kh : (const uint4 *) (kc + (size_t) pt * kvd);
+    constexpr int SB = D == 64 ? 4 : 2;   // positions per thread whose K rows are loaded together
+    for (int t0 = tid; t0 < nk; t0 += SB * ATT_NT) {
+        uint4 kr[SB][D / 8];
 #pragma unroll
-        for (int w = 0; w < D / 8; w++) kr[w] = src[w];
-        const float v = __fmul_rn(dot_h8<D>(q, kr), a.scale);
-        sc[t] = v;
-        lmax = lmax < v ? v : lmax;
+        for (int u = 0; u < SB; u++) {
+            const int t = t0 + u * ATT_NT, pt = s0 + t;
+            if (t < nk) {
+                const uint4 *src = (a.kv_fused && pt == p) ? (const uint4 *) kh : (const uint4 *) (kc + (size_t) pt * kvd);
+#pragma unroll
+                for (int w = 0; w < D / 8; w++) kr[u][w] = src[w];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < SB; u++) {
+            const int t = t0 + u * ATT_NT;
+            if (t < nk) {
+                const float v = __fmul_rn(dot_h8<D>(q, kr[u]), a.scale);
+                sc[t] = v;
+                lmax = lmax < v ? v : lmax;
+            }
+        }
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
@@ -257,6 +284,7 @@ __global__ void __launch_bounds__(ATT_NT) k_attn(const __grid_constant__ AttnArg
             const float *pr = sc + (size_t) k * VT;
             const int n = min(VT, ng - k * VT);
             int t = 0;
+#pragma unroll 4
             for (; t + 8 <= n; t += 8) {
                 uint16_t v8[8];
 #pragma unroll
