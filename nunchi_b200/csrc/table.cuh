@@ -30,16 +30,6 @@ __device__ __forceinline__ void nbar_sync(int id, int count) {
 __device__ __forceinline__ void nbar_arrive(int id, int count) {
     asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
-// all `count` threads of barrier `id` learn whether every one of them passed `v`
-__device__ __forceinline__ bool nbar_and(int id, int count, bool v) {
-    uint32_t r;
-    asm volatile("{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}"
-                 : "=r"(r)
-                 : "r"((uint32_t) v), "r"(id), "r"(count)
-                 : "memory");
-    return r != 0;
-}
-
 // ---------------- input preparation ----------------
 // Each thread owns the float4 chunks q = tid, tid + MV_THREADS, ... of an n_embd vector in every phase. MV_THREADS is
 // a multiple of 32, so the 8 lanes holding chunks 8m..8m+7 hold one 32-value block, which cut_chunk cuts in place:
@@ -444,9 +434,13 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_table(const __grid_constant__
         const int nchunk = nb / 4;   // 8-byte chunks of a row's scales (scale rows are nb + 4 halfs: 8-byte aligned)
         for (int st = 0; st < nst; st++) {
             const int b = st % MV_NBUF;
-            bool ok = mbar_wait(&bar[st % NS], (uint32_t) ((st / NS) & 1));
-            ok = nbar_and(NB_INT, MV_ITHREADS, ok);
-            if (!ok && it == 0) { abort_flag = 1; atomicExch(a.err, 7); }
+            // each thread waits on the stage itself (a phase completes for all at once); a wait that gives up marks
+            // the CTA aborted before this thread's READY arrival, which the chain warp's sync orders after it
+            const bool ok = mbar_wait(&bar[st % NS], (uint32_t) ((st / NS) & 1));
+            if (!ok) {
+                abort_flag = 1;
+                atomicExch(a.err, 7);
+            }
             if (st >= MV_NBUF) nbar_sync(NB_FREE + b, NB_PAIR);   // chain warp b is done with buffer b
             if (ok) {
                 const int rb = st * sr, nr = min(sr, nrows - rb);
