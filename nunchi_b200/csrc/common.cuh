@@ -330,10 +330,11 @@ __device__ __forceinline__ void cp16(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-// a coherent (L2) read of a value another launch may change
+// a coherent (L2) read of a value another launch may change (no compiler barrier: loads that do not depend on it
+// may be issued beside it; it stays after the dependency wait, another volatile asm)
 __device__ __forceinline__ int ld_relaxed(const int *p) {
     int v;
-    asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p));
     return v;
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

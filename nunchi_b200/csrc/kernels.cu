@@ -196,16 +196,20 @@ __global__ void __launch_bounds__(ATT_NT) k_attn(const __grid_constant__ AttnArg
     const int s0 = a.window > 0 ? max(0, p - a.window + 1) : 0, nk = p - s0 + 1;
     const int ng = a.kv_fused ? nk - 1 : nk;   // positions whose V is read from the cache
     const int VT = attn_vtile(D), ntile = (ng + VT - 1) / VT;
-    auto load_tile = [&](int k) {
+    auto load_tile = [&](int k) {   // by warps 2.., idle while warps 0 and 1 make this position's K, V and query
+        if (warp < 2) return;
         uint16_t *dst = vt + (size_t) (k & 1) * VT * D;
         const int t0 = k * VT, n = min(VT, ng - t0);
-        for (int i = tid; i < n * (D / 8); i += ATT_NT) {
+        for (int i = tid - 64; i < n * (D / 8); i += ATT_NT - 64) {
             const int t = i / (D / 8), ch = i - t * (D / 8);
             cp16(dst + (size_t) t * D + 8 * ch, vc + (size_t) (s0 + t0 + t) * kvd + 8 * ch);
         }
         cp_commit();
     };
     __syncthreads();   // the rotary rows are in shared memory
+    // the cached V rows into shared memory while the rest of the setup and the scores run
+    if (ntile > 0) load_tile(0);
+    if (ntile > 1) load_tile(1);
 
     // this position's K and V (warp 0) and the rotated query (warp 1)
     if (a.kv_fused) kv_make<D>(a, qkv, g, p, ktmp, tmp, kh, vh);
@@ -219,9 +223,6 @@ __global__ void __launch_bounds__(ATT_NT) k_attn(const __grid_constant__ AttnArg
         kc[(size_t) p * kvd + tid] = kh[tid];
         vc[(size_t) p * kvd + tid] = vh[tid];
     }
-    // the cached V rows into shared memory while the scores run
-    if (ntile > 0) load_tile(0);
-    if (ntile > 1) load_tile(1);
 
     // scores (seoul.cpp:445): one thread per position
     float lmax = -INFINITY;
