@@ -132,9 +132,9 @@ __device__ __forceinline__ void table_preload(const MvArgs &a, const MvPlan &P, 
 
 // Part 2, after the dependency wait, all MV_THREADS threads, all columns; ends with a __syncthreads. The activations
 // the previous launches produced arrive in one batch (cp.async, one L2 round trip).
-// late_weights() issues the table's bulk copies for the norm/residual reads (P_RESID_NORM, P_FINAL), right after
-// the activation loads are on their way: those few latency-critical loads then go ahead of the copies, which still
-// arrive before the long input preparation ends
+// late_weights() issues the table's bulk copies for the norm/residual reads (P_RESID_NORM, P_FINAL) once the
+// activations are in shared memory: those few latency-critical loads go ahead of the copies, which still arrive before
+// the long input preparation ends
 template <int PRO, int NC, class LateW>
 __device__ void table_prologue(const MvArgs &a, const MvPlan &P, uint8_t *sm, const PreRegs &pr, LateW &&late_weights) {
     int8_t *xq = (int8_t *) (sm + P.xq);
@@ -239,7 +239,6 @@ __device__ void table_prologue(const MvArgs &a, const MvPlan &P, uint8_t *sm, co
                 cp16(vb + c * VL + 4 * q, a.in + (size_t) c * a.in_stride + 4 * q);
                 if (x_in_smem) cp16(vb + c * VL + E + 4 * q, a.xin + (size_t) c * a.x_stride + 4 * q);
             }
-        late_weights();
         cp_wait_all();
     } else {
         for (int c = 0; c < nc; c++) {
@@ -249,6 +248,7 @@ __device__ void table_prologue(const MvArgs &a, const MvPlan &P, uint8_t *sm, co
         }
     }
     __syncthreads();
+    late_weights();
     if (resid) {   // x += norm(r) * w_post (imi_norm_mul_add, vec.h:41-44); the new x replaces r in place
         if (warp < nc) {
             const float sc = warp_rms_scale(vb + warp * VL, E, a.eps);
@@ -403,23 +403,25 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_table(const __grid_constant__
         mbar_expect_tx(b, bytes);
         bulk_g2s(stage + (st % NS) * MV_STAGE_BYTES, a.W + (size_t) (r0 + rr) * a.row_bytes, bytes, b);
     };
-    auto issue_weights = [&]() {
-        if (tid == 0) {   // the first stages, and the rest of this CTA's slice into L2 so HBM streams the whole table
-            for (int st = 0; st < min(NS, nst); st++) issue(st);
-            const size_t beg = (size_t) min(NS * sr, nrows) * a.row_bytes, end = (size_t) nrows * a.row_bytes;
-            const uint8_t *base = a.W + (size_t) r0 * a.row_bytes;
-            for (size_t o = beg; o < end; o += 65536) prefetch_l2(base + o, (uint32_t) min((size_t) 65536, end - o));
-        }
+    auto issue_weights = [&]() {   // by one thread: the first stages, and the rest of this CTA's slice into L2 so HBM
+                                   // streams the whole table
+        for (int st = 0; st < min(NS, nst); st++) issue(st);
+        const size_t beg = (size_t) min(NS * sr, nrows) * a.row_bytes, end = (size_t) nrows * a.row_bytes;
+        const uint8_t *base = a.W + (size_t) r0 * a.row_bytes;
+        for (size_t o = beg; o < end; o += 65536) prefetch_l2(base + o, (uint32_t) min((size_t) 65536, end - o));
     };
     constexpr bool late = PRO == P_RESID_NORM || PRO == P_FINAL;
-    if (!late) issue_weights();   // the weights do not depend on the previous launch: start them before waiting on it
+    // the weights do not depend on the previous launch: start them before waiting on it
+    if (!late && tid == 0) issue_weights();
     pdl_trigger();
     PreRegs pr;
     table_preload<PRO, NC>(a, P, sm, pr);
     if (trace && tid == 0) trace[15] = global_ns();
     pdl_wait();
     if (trace && tid == 0) trace[1] = global_ns();
-    table_prologue<PRO, NC>(a, P, sm, pr, [&]() { if (late) issue_weights(); });
+    // norm/residual reads: issued once the activations are in, by a lane of the last warp, which holds the fewest
+    // chunks of the input preparation (none while n_embd / 4 <= MV_THREADS - 32)
+    table_prologue<PRO, NC>(a, P, sm, pr, [&]() { if (late && tid == MV_THREADS - 32) issue_weights(); });
     if (trace && tid == 0) trace[2] = global_ns();
 
     if (warp < MV_IWARPS) {
