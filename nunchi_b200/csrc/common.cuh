@@ -187,12 +187,20 @@ __device__ __forceinline__ float warp_rms_scale(const float *x, int n, float eps
     const int L = threadIdx.x & 31;
     float a = 0.0f;
     int i = L;
-    for (; i + 15 * 32 < n; i += 16 * 32) {   // 16 loads in flight, then the lane's fmas in order
+    if (i + 15 * 32 < n) {
         float v[16];
 #pragma unroll
         for (int k = 0; k < 16; k++) v[k] = x[i + 32 * k];
+        for (; i + 15 * 32 < n; i += 16 * 32) {   // the next 16 values load while these 16 accumulate, in order
+            float w[16];
+            const bool more = i + 16 * 32 + 15 * 32 < n;
 #pragma unroll
-        for (int k = 0; k < 16; k++) a = __fmaf_rn(v[k], v[k], a);
+            for (int k = 0; k < 16; k++) w[k] = more ? x[i + 16 * 32 + 32 * k] : 0.0f;
+#pragma unroll
+            for (int k = 0; k < 16; k++) a = __fmaf_rn(v[k], v[k], a);
+#pragma unroll
+            for (int k = 0; k < 16; k++) v[k] = w[k];
+        }
     }
     for (; i < n; i += 32) a = __fmaf_rn(x[i], x[i], a);
     const unsigned F = 0xffffffffu;
