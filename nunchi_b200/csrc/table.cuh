@@ -340,24 +340,51 @@ __device__ __forceinline__ float amax_val(unsigned long long k) {
     return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
 }
 
-// the two fma chains of one (input, row), blocks in order (group_avx2<false>, tables.cpp:134-142)
+// the two fma chains of one (input, row), blocks in order (group_avx2<false>, tables.cpp:134-142); the next 8
+// blocks' operands load while these 8 blocks run (nb is a multiple of 8)
 __device__ __forceinline__ float row_chain(const float *f, const uint16_t *d, const float *xdc, const float *xsc,
                                            int nb) {
     float acc = 0.0f, cor = 0.0f;
-#pragma unroll 4
-    for (int j = 0; j < nb; j += 4) {   // nb is a multiple of 8; unrolled so later blocks' loads overlap the chain
-        const float4 fv = *(const float4 *) (f + j), xv = *(const float4 *) (xdc + j), sv = *(const float4 *) (xsc + j);
-        const uint2 dv = *(const uint2 *) (d + j);
-        const float d0 = h2f((uint16_t) (dv.x & 0xffff)), d1 = h2f((uint16_t) (dv.x >> 16)),
-                    d2 = h2f((uint16_t) (dv.y & 0xffff)), d3 = h2f((uint16_t) (dv.y >> 16));
-        acc = __fmaf_rn(fv.x, __fmul_rn(d0, xv.x), acc);
-        cor = __fmaf_rn(d0, sv.x, cor);
-        acc = __fmaf_rn(fv.y, __fmul_rn(d1, xv.y), acc);
-        cor = __fmaf_rn(d1, sv.y, cor);
-        acc = __fmaf_rn(fv.z, __fmul_rn(d2, xv.z), acc);
-        cor = __fmaf_rn(d2, sv.z, cor);
-        acc = __fmaf_rn(fv.w, __fmul_rn(d3, xv.w), acc);
-        cor = __fmaf_rn(d3, sv.w, cor);
+    float4 fv[2], xv[2], sv[2];
+    uint2 dv[2];
+#pragma unroll
+    for (int g = 0; g < 2; g++) {
+        fv[g] = *(const float4 *) (f + 4 * g);
+        xv[g] = *(const float4 *) (xdc + 4 * g);
+        sv[g] = *(const float4 *) (xsc + 4 * g);
+        dv[g] = *(const uint2 *) (d + 4 * g);
+    }
+    for (int j = 0; j < nb; j += 8) {
+        const int jn = j + 8 < nb ? j + 8 : j;   // the last round reloads its own blocks (in bounds, unused)
+        float4 fn[2], xn[2], sn[2];
+        uint2 dn[2];
+#pragma unroll
+        for (int g = 0; g < 2; g++) {
+            fn[g] = *(const float4 *) (f + jn + 4 * g);
+            xn[g] = *(const float4 *) (xdc + jn + 4 * g);
+            sn[g] = *(const float4 *) (xsc + jn + 4 * g);
+            dn[g] = *(const uint2 *) (d + jn + 4 * g);
+        }
+#pragma unroll
+        for (int g = 0; g < 2; g++) {
+            const float d0 = h2f((uint16_t) (dv[g].x & 0xffff)), d1 = h2f((uint16_t) (dv[g].x >> 16)),
+                        d2 = h2f((uint16_t) (dv[g].y & 0xffff)), d3 = h2f((uint16_t) (dv[g].y >> 16));
+            acc = __fmaf_rn(fv[g].x, __fmul_rn(d0, xv[g].x), acc);
+            cor = __fmaf_rn(d0, sv[g].x, cor);
+            acc = __fmaf_rn(fv[g].y, __fmul_rn(d1, xv[g].y), acc);
+            cor = __fmaf_rn(d1, sv[g].y, cor);
+            acc = __fmaf_rn(fv[g].z, __fmul_rn(d2, xv[g].z), acc);
+            cor = __fmaf_rn(d2, sv[g].z, cor);
+            acc = __fmaf_rn(fv[g].w, __fmul_rn(d3, xv[g].w), acc);
+            cor = __fmaf_rn(d3, sv[g].w, cor);
+        }
+#pragma unroll
+        for (int g = 0; g < 2; g++) {
+            fv[g] = fn[g];
+            xv[g] = xn[g];
+            sv[g] = sn[g];
+            dv[g] = dn[g];
+        }
     }
     return __fmaf_rn(-8.0f, cor, acc);
 }
