@@ -44,7 +44,8 @@ const char *imi_cuda_error(void);
 
 /* Load a GGUF model onto CUDA device `device` (replaces imi_seoul::load(path, threads, ctx_len), seoul.cpp:93).
  * n_ctx: positions per conversation; max_batch: most conversations stepped together by imi_cuda_step_multi
- * (and prefill chunk width of imi_cuda_step_batch is fixed at 128 independent of it). */
+ * (and prefill chunk width of imi_cuda_step_batch is fixed at 128 independent of it). An engine and its states are
+ * used by one host thread at a time: they share the engine's stream, its staging buffers and its read-back buffer. */
 imi_cuda_status imi_cuda_load(const char *gguf_path, int device, int n_ctx, int max_batch, imi_cuda_engine **out);
 void imi_cuda_free(imi_cuda_engine *e);                                     /* ~imi_seoul, seoul.cpp:687-689 */
 imi_cuda_status imi_cuda_get_info(const imi_cuda_engine *e, imi_cuda_info *out);

@@ -75,6 +75,9 @@ struct imi_cuda_engine {
     float *qa_d = nullptr, *qa_s = nullptr, *qt_d = nullptr, *qt_s = nullptr;
     Col *cols_d = nullptr, *cols_h = nullptr;
     float *embd_h = nullptr;
+    // pinned: what the host reads back after a step (a session record at 0, the error word at 128), so the read is a
+    // small DMA into page-locked memory instead of a staged copy into pageable memory
+    uint8_t *reply_h = nullptr;
     unsigned *done = nullptr;
     int *err = nullptr;
     cudaEvent_t staged = nullptr;   // the last host->device copy of the staging buffers has run
@@ -116,6 +119,7 @@ imi_cuda_engine::~imi_cuda_engine() {
     cudaFree(cols_d);
     cudaFreeHost(cols_h);
     cudaFreeHost(embd_h);
+    cudaFreeHost(reply_h);
     if (staged) cudaEventDestroy(staged);
     if (stream) cudaStreamDestroy(stream);
 }
@@ -368,6 +372,7 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
     CK(cudaMemset(e->cols_d, 0, sizeof(Col) * STEP_COLS + 64));
     CK(cudaMallocHost(&e->cols_h, sizeof(Col) * STEP_COLS));
     CK(cudaMallocHost(&e->embd_h, (size_t) E * 4 * STEP_COLS));
+    CK(cudaMallocHost(&e->reply_h, 256));
     memset(e->cols_h, 0, sizeof(Col) * STEP_COLS);
     CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
     CK(cudaEventCreateWithFlags(&e->staged, cudaEventDisableTiming));
@@ -611,10 +616,12 @@ Col decode_col(imi_cuda_state *s, int32_t token, bool has_embd, int c, bool want
     return k;
 }
 
+static_assert(sizeof(SessDev) <= 128, "the session record fits the first half of the reply buffer");
 imi_cuda_status check_err(imi_cuda_engine *e) {
-    int h = 0;
-    CK(cudaMemcpyAsync(&h, e->err, 4, cudaMemcpyDeviceToHost, e->stream));
+    int *hp = (int *) (e->reply_h + 128);
+    CK(cudaMemcpyAsync(hp, e->err, 4, cudaMemcpyDeviceToHost, e->stream));
     CK(cudaStreamSynchronize(e->stream));
+    const int h = *hp;
     if (h) {
         CK(cudaMemsetAsync(e->err, 0, 4, e->stream));
         return fail(IMI_E_TIMEOUT, "a device-side wait gave up (code " + std::to_string(h) + ")");
@@ -873,11 +880,12 @@ imi_cuda_status imi_cuda_get_logits(const imi_cuda_state *s, float *out) {
 imi_cuda_status imi_cuda_get_argmax(const imi_cuda_state *s, int32_t *id, float *value) {
     if (!s || !id) return fail(IMI_E_ARG, "null argument");
     CK(cudaSetDevice(s->e->device));
-    SessDev h;
-    CK(cudaMemcpyAsync(&h, s->s, sizeof h, cudaMemcpyDeviceToHost, s->e->stream));
+    // the session record and the error word in one synchronisation (check_err enqueues its copy behind this one)
+    SessDev *h = (SessDev *) s->e->reply_h;
+    CK(cudaMemcpyAsync(h, s->s, sizeof *h, cudaMemcpyDeviceToHost, s->e->stream));
     imi_cuda_status st = check_err(s->e);
-    *id = h.next_token;
-    if (value) *value = h.amax_val;
+    *id = h->next_token;
+    if (value) *value = h->amax_val;
     return st;
 }
 
