@@ -75,9 +75,13 @@ struct imi_cuda_engine {
     float *qa_d = nullptr, *qa_s = nullptr, *qt_d = nullptr, *qt_s = nullptr;
     Col *cols_d = nullptr, *cols_h = nullptr;
     float *embd_h = nullptr;
-    // pinned: what the host reads back after a step (a session record at 0, the error word at 128), so the read is a
-    // small DMA into page-locked memory instead of a staged copy into pageable memory
+    // pinned: what the host reads back after a step (session records at 32-byte slots from 0, the error word at 256),
+    // so the read is a small DMA into page-locked memory instead of a staged copy into pageable memory. One read
+    // brings every conversation of the last step; it stays valid until anything changes a session (gen moves on).
     uint8_t *reply_h = nullptr;
+    uint64_t gen = 1, reply_gen = 0;
+    int last_n = 0, reply_n = 0;
+    const SessDev *last_s[STEP_COLS] = {}, *reply_src[STEP_COLS] = {};
     unsigned *done = nullptr;
     int *err = nullptr;
     cudaEvent_t staged = nullptr;   // the last host->device copy of the staging buffers has run
@@ -372,7 +376,7 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
     CK(cudaMemset(e->cols_d, 0, sizeof(Col) * STEP_COLS + 64));
     CK(cudaMallocHost(&e->cols_h, sizeof(Col) * STEP_COLS));
     CK(cudaMallocHost(&e->embd_h, (size_t) E * 4 * STEP_COLS));
-    CK(cudaMallocHost(&e->reply_h, 256));
+    CK(cudaMallocHost(&e->reply_h, 512));
     memset(e->cols_h, 0, sizeof(Col) * STEP_COLS);
     CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
     CK(cudaEventCreateWithFlags(&e->staged, cudaEventDisableTiming));
@@ -568,6 +572,9 @@ cudaError_t enqueue_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind)
 }
 
 imi_cuda_status run_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind, bool copy_cols) {
+    e->gen++;
+    e->last_n = std::min(ncol, STEP_COLS);
+    for (int c = 0; c < e->last_n; c++) e->last_s[c] = e->cols_h[c].s;
     if (copy_cols) {
         CK(cudaMemcpyAsync(e->cols_d, e->cols_h, sizeof(Col) * ncol, cudaMemcpyHostToDevice, e->stream));
         CK(cudaEventRecord(e->staged, e->stream));
@@ -616,9 +623,9 @@ Col decode_col(imi_cuda_state *s, int32_t token, bool has_embd, int c, bool want
     return k;
 }
 
-static_assert(sizeof(SessDev) <= 128, "the session record fits the first half of the reply buffer");
+static_assert(sizeof(SessDev) <= 32, "a session record fits its slot of the reply buffer");
 imi_cuda_status check_err(imi_cuda_engine *e) {
-    int *hp = (int *) (e->reply_h + 128);
+    int *hp = (int *) (e->reply_h + 256);
     CK(cudaMemcpyAsync(hp, e->err, 4, cudaMemcpyDeviceToHost, e->stream));
     CK(cudaStreamSynchronize(e->stream));
     const int h = *hp;
@@ -683,6 +690,7 @@ imi_cuda_status imi_cuda_get_info(const imi_cuda_engine *e, imi_cuda_info *o) {
 
 imi_cuda_status imi_cuda_state_new(imi_cuda_engine *e, imi_cuda_state **out) {
     if (!e || !out) return fail(IMI_E_ARG, "null argument");
+    e->gen++;
     CK(cudaSetDevice(e->device));
     std::unique_ptr<imi_cuda_state> s(new imi_cuda_state);
     s->e = e;
@@ -710,6 +718,7 @@ imi_cuda_status imi_cuda_state_new(imi_cuda_engine *e, imi_cuda_state **out) {
 
 void imi_cuda_state_free(imi_cuda_state *s) {
     if (!s) return;
+    s->e->gen++;
     cudaSetDevice(s->e->device);
     cudaStreamSynchronize(s->e->stream);
     cudaFree(s->mem);
@@ -720,6 +729,7 @@ imi_cuda_status imi_cuda_state_reset(imi_cuda_state *s) {
     if (!s) return fail(IMI_E_ARG, "null state");
     imi_cuda_engine *e = s->e;
     CK(cudaSetDevice(e->device));
+    e->gen++;
     CK(cudaMemsetAsync(s->s, 0, sizeof(SessDev), e->stream));
     CK(cudaMemsetAsync(s->ring, 0, (size_t) e->n_conv * (e->d_conv + 1) * e->n_embd * 4, e->stream));
     s->pos = 0;
@@ -880,13 +890,30 @@ imi_cuda_status imi_cuda_get_logits(const imi_cuda_state *s, float *out) {
 imi_cuda_status imi_cuda_get_argmax(const imi_cuda_state *s, int32_t *id, float *value) {
     if (!s || !id) return fail(IMI_E_ARG, "null argument");
     CK(cudaSetDevice(s->e->device));
-    // the session record and the error word in one synchronisation (check_err enqueues its copy behind this one)
-    SessDev *h = (SessDev *) s->e->reply_h;
-    CK(cudaMemcpyAsync(h, s->s, sizeof *h, cudaMemcpyDeviceToHost, s->e->stream));
-    imi_cuda_status st = check_err(s->e);
-    *id = h->next_token;
-    if (value) *value = h->amax_val;
-    return st;
+    imi_cuda_engine *e = s->e;
+    if (e->reply_gen != e->gen) {
+        // the records of every conversation of the last step (when s is one of them) and the error word, in one
+        // synchronisation: the next conversation's pick of the same step then needs no device round trip
+        bool in_last = false;
+        for (int c = 0; c < e->last_n; c++) in_last |= e->last_s[c] == s->s;
+        e->reply_n = in_last ? e->last_n : 1;
+        for (int c = 0; c < e->reply_n; c++) {
+            e->reply_src[c] = in_last ? e->last_s[c] : s->s;
+            CK(cudaMemcpyAsync(e->reply_h + 32 * c, e->reply_src[c], sizeof(SessDev), cudaMemcpyDeviceToHost, e->stream));
+        }
+        const imi_cuda_status st = check_err(e);
+        if (st != IMI_OK) return st;
+        e->reply_gen = e->gen;
+    }
+    for (int c = 0; c < e->reply_n; c++)
+        if (e->reply_src[c] == s->s) {
+            const SessDev *h = (const SessDev *) (e->reply_h + 32 * c);
+            *id = h->next_token;
+            if (value) *value = h->amax_val;
+            return IMI_OK;
+        }
+    e->reply_gen = 0;   // not among the records read (cannot happen: s was read above); read again
+    return imi_cuda_get_argmax(s, id, value);
 }
 
 imi_cuda_status imi_cuda_q8_cut(int device, const float *x, int n, int8_t *q, float *d, float *s) {
@@ -1200,6 +1227,7 @@ imi_cuda_status imi_cuda_state_save(const imi_cuda_state *s, void *buf, size_t c
 imi_cuda_status imi_cuda_state_load(imi_cuda_state *s, const void *buf, size_t size) {
     if (!s || !buf || size < sizeof(StateImage)) return fail(IMI_E_ARG, "bad state image");
     imi_cuda_engine *e = s->e;
+    e->gen++;
     StateImage h;
     memcpy(&h, buf, sizeof h);
     const int kvd = e->n_head_kv * e->head_dim, R = e->d_conv + 1, E = e->n_embd;
@@ -1250,6 +1278,7 @@ imi_cuda_status imi_cuda_trace_step(imi_cuda_state *s, int32_t token, int want_l
     e->trace_kind.clear();
     e->trace_grid.clear();
     e->cols_h[0] = decode_col(s, token, false, 0, want_logits != 0);
+    e->gen++;
     CK(cudaMemcpyAsync(e->cols_d, e->cols_h, sizeof(Col), cudaMemcpyHostToDevice, e->stream));
     cudaError_t r = enqueue_step(e, 1, want_logits != 0, K_DECODE);
     if (r == cudaSuccess) r = cudaMemcpyAsync(out, e->trace_buf, per * e->trace_n * 8, cudaMemcpyDeviceToHost, e->stream);

@@ -129,6 +129,31 @@ def test_riding_is_byte_identical_to_alone(tiny_path):
     assert a.pos == 20 and b.pos == 30
 
 
+def test_picks_read_back_after_riding_reset_load_and_free(tiny_path):
+    """The pick of each conversation read after a riding step (one read brings both), and read again after anything
+    that changes a conversation: a reset, a checkpoint load, a freed and re-created state."""
+    e = nb.Engine(tiny_path, n_ctx=64)
+    a, b = e.new_state(), e.new_state()
+    ta, tb = synth.random_ids(6, e.n_vocab, 7), synth.random_ids(6, e.n_vocab, 8)
+    for i in range(6):
+        nb.step2(a, ta[i], None, True, b, tb[i], None, True)
+        assert a.argmax()[0] == int(np.argmax(a.logits)) and b.argmax()[0] == int(np.argmax(b.logits))
+        assert b.argmax() == b.argmax()
+    image = a.save()
+    pick_a = a.argmax()
+    a.step(int(ta[0]))
+    assert a.argmax()[0] == int(np.argmax(a.logits))
+    a.load(image)
+    assert a.argmax()[0] == pick_a[0]
+    b.reset()
+    assert b.argmax()[0] == 0
+    del b
+    c = e.new_state()
+    assert c.argmax()[0] == 0
+    c.step(int(tb[0]))
+    assert c.argmax()[0] == int(np.argmax(c.logits))
+
+
 @pytest.mark.parametrize("n", [3, 8, 11])
 def test_step_multi_is_byte_identical_to_alone(tiny_path, n):
     e = nb.Engine(tiny_path, n_ctx=64, max_batch=16)
