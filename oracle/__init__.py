@@ -226,6 +226,67 @@ def rope_angles(pos: int, n: int, base: float, freq_factor=None):
     return cs, sn
 
 
+# ---- the Q6_K word table of the product's own files (imi_q8k / imi_q6k_row / imi_q6k_dequant_row) ----
+
+def _q6k_lib(L, prefix):
+    f = getattr(L, prefix + "q6k_row")
+    if not getattr(f, "_typed", False):
+        if prefix == "or_":
+            L.or_q8k_from.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]
+            L.or_q6k_row.restype = C.c_float
+            L.or_q6k_row.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
+            L.or_q6k_dequant_row.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+        else:
+            L.oref_q8k_from.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]
+            L.oref_q6k_row.restype = C.c_float
+            L.oref_q6k_row.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+            L.oref_q6k_dequant_row.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+        f._typed = True
+    return L
+
+
+def q8k_from(x, reference: bool = False):
+    """imi_q8k::from: int8 codes, an fp32 scale per 256 values and the code sum of every 16 (restatement, or the
+    reference's own function with reference=True)."""
+    x = _arr(x, np.float32)
+    n = x.size
+    q, d, bs = np.zeros(n, np.int8), np.zeros(n // 256, np.float32), np.zeros(n // 16, np.int16)
+    if reference:
+        _q6k_lib(Reference.lib(), "oref_").oref_q8k_from(_ptr(x), n, _ptr(q), _ptr(d), _ptr(bs))
+    else:
+        _q6k_lib(Oracle.lib(), "or_").or_q8k_from(_ptr(x), n, _ptr(q), _ptr(d), _ptr(bs))
+    return q, d, bs
+
+
+def q6k_rows(rows_q6k, x, reference: bool = False) -> np.ndarray:
+    """The word scores of Q6_K rows ([rows][cols/256 * 210] bytes) for the input x (cut by imi_q8k::from inside), in
+    imi's AVX2 order (tables.cpp:235-278): the restatement, or the reference's own imi_q6k_row."""
+    rows_q6k, x = _arr(rows_q6k, np.uint8), _arr(x, np.float32)
+    nbk = x.size // 256
+    out = np.zeros(rows_q6k.shape[0], np.float32)
+    if reference:
+        L = _q6k_lib(Reference.lib(), "oref_")
+        for r in range(rows_q6k.shape[0]):
+            out[r] = L.oref_q6k_row(_ptr(rows_q6k[r]), _ptr(x), nbk)
+    else:
+        L = _q6k_lib(Oracle.lib(), "or_")
+        q, d, bs = q8k_from(x)
+        for r in range(rows_q6k.shape[0]):
+            out[r] = L.or_q6k_row(_ptr(rows_q6k[r]), _ptr(q), _ptr(d), _ptr(bs), nbk)
+    return out
+
+
+def q6k_dequant_row(row, nblocks: int, reference: bool = False) -> np.ndarray:
+    """A Q6_K row as floats (the word lookup, tables.cpp:216-233)."""
+    row = _arr(row, np.uint8)
+    y = np.zeros(256 * nblocks, np.float32)
+    if reference:
+        _q6k_lib(Reference.lib(), "oref_").oref_q6k_dequant_row(_ptr(row), _ptr(y), nblocks)
+    else:
+        _q6k_lib(Oracle.lib(), "or_").or_q6k_dequant_row(_ptr(row), _ptr(y), nblocks)
+    return y
+
+
 # ---- the reference's own code ----
 
 def reference_available() -> bool:

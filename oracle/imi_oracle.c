@@ -444,3 +444,69 @@ int or_step_batch(const or_model *m, or_state *s, const int32_t *tokens, const f
     }
     return 0;
 }
+/* ---- Q6_K word table (imi_q8k / imi_q6k_row / imi_q6k_dequant_row, tables.cpp:200-287) ---- */
+
+/* imi_q8k::from (tables.cpp:200-213): per 256 values amax, d = amax/127, id = d ? 1/d : 0, q = lrintf(x * id),
+ * bsums = the sum of each 16 codes */
+void or_q8k_from(const float *x, int n, int8_t *q, float *d, int16_t *bsums) {
+    for (int j = 0; j < n / 256; j++) {
+        const float *v = x + 256 * j;
+        float amax = 0.0f;
+        for (int i = 0; i < 256; i++) amax = fmaxf(amax, fabsf(v[i]));
+        const float dd = amax / 127.0f, id = dd != 0.0f ? 1.0f / dd : 0.0f;
+        for (int i = 0; i < 256; i++) q[256 * j + i] = (int8_t) lrintf(v[i] * id);
+        for (int s = 0; s < 16; s++) {
+            int t = 0;
+            for (int i = 0; i < 16; i++) t += q[256 * j + 16 * s + i];
+            bsums[16 * j + s] = (int16_t) t;
+        }
+        d[j] = dd;
+    }
+}
+
+/* the 6-bit code of value t (0..255) of a Q6_K block: low 4 bits from ql, high 2 from qh (tables.cpp:223-227) */
+static inline int q6k_code(const uint8_t *blk, int t) {
+    const int n = t / 128, r = t % 128, k = r / 32, l = r % 32;
+    const uint8_t *ql = blk + 64 * n, *qh = blk + 128 + 32 * n;
+    const int lo = k == 0 ? (ql[l] & 15) : k == 1 ? (ql[l + 32] & 15) : k == 2 ? (ql[l] >> 4) : (ql[l + 32] >> 4);
+    return lo | (((qh[l] >> (2 * k)) & 3) << 4);
+}
+
+/* imi_q6k_row, AVX2 order (tables.cpp:235-278). Integer part per 256 block in 8 lanes: lane m takes values
+ * 128n + 32k + 4m .. +3 (n < 2, k < 4) times the scale of their 16 (scales[8n + 2k + (m >= 4)]), minus
+ * 32 * (scales[2m] * bsums[2m] + scales[2m+1] * bsums[2m+1]); exact in int32. Float part: lane m accumulates
+ * fma(d_block * d_x, (float) int_m, acc_m) over the blocks in order; the 8 lanes end as
+ * ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7)). */
+float or_q6k_row(const uint8_t *row, const int8_t *xq, const float *xd, const int16_t *bsums, int nblocks) {
+    float acc[8] = { 0 };
+    for (int i = 0; i < nblocks; i++) {
+        const uint8_t *blk = row + 210 * (size_t) i;
+        const int8_t *sc = (const int8_t *) (blk + 192);
+        const uint16_t dh = (uint16_t) (blk[208] | (blk[209] << 8));
+        const int8_t *x = xq + 256 * (size_t) i;
+        const int16_t *bs = bsums + 16 * (size_t) i;
+        int32_t lane[8];
+        for (int m = 0; m < 8; m++) lane[m] = 0;
+        for (int n = 0; n < 2; n++)
+            for (int k = 0; k < 4; k++)
+                for (int v = 0; v < 32; v++) {
+                    const int t = 128 * n + 32 * k + v;
+                    lane[v / 4] += q6k_code(blk, t) * x[t] * sc[8 * n + 2 * k + (v >= 16)];
+                }
+        for (int m = 0; m < 8; m++) lane[m] -= 32 * (sc[2 * m] * bs[2 * m] + sc[2 * m + 1] * bs[2 * m + 1]);
+        const float s = or_h2f(dh) * xd[i];
+        for (int m = 0; m < 8; m++) acc[m] = fmaf(s, (float) lane[m], acc[m]);
+    }
+    const float r0 = acc[0] + acc[4], r1 = acc[1] + acc[5], r2 = acc[2] + acc[6], r3 = acc[3] + acc[7];
+    return (r0 + r2) + (r1 + r3);
+}
+
+/* imi_q6k_dequant_row (tables.cpp:216-233): value = d * scale * (code - 32), left to right */
+void or_q6k_dequant_row(const uint8_t *row, float *y, int nblocks) {
+    for (int i = 0; i < nblocks; i++) {
+        const uint8_t *blk = row + 210 * (size_t) i;
+        const int8_t *sc = (const int8_t *) (blk + 192);
+        const float d = or_h2f((uint16_t) (blk[208] | (blk[209] << 8)));
+        for (int t = 0; t < 256; t++) y[256 * i + t] = d * (float) sc[t / 16] * (float) (q6k_code(blk, t) - 32);
+    }
+}

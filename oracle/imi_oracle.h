@@ -52,6 +52,12 @@ float or_h2f(uint16_t h);   /* imi_h2f, tables.cpp:20-29 */
 /* the NEOX rotation table used by seoul.cpp:19-28 for one position: cos and sin of angle i (n/2 each) */
 void or_rope_angles(int pos, int n, float base, const float *freq_factor, float *cs, float *sn);
 
+/* ---- the Q6_K word table of the product's own files (next on the path; no GPU path yet) ---- */
+void or_q8k_from(const float *x, int n, int8_t *q, float *d, int16_t *bsums);   /* imi_q8k::from, tables.cpp:200-213 */
+/* one Q6_K row (210 B per 256 values) against an imi_q8k input, imi's AVX2 order (tables.cpp:235-278) */
+float or_q6k_row(const uint8_t *row, const int8_t *xq, const float *xd, const int16_t *bsums, int nblocks);
+void or_q6k_dequant_row(const uint8_t *row, float *y, int nblocks);             /* tables.cpp:216-233 */
+
 #ifdef __cplusplus
 }
 #endif

@@ -151,3 +151,46 @@ def test_context_full_is_refused_like_the_reference(tiny_path):
     o.reset()
     with pytest.raises(RuntimeError):
         o.step_batch(tokens=np.arange(4, dtype=np.int32))   # seoul.cpp:498
+
+
+# ---- the Q6_K word table of the product's own files: the restatement against the reference's own AVX2 code ----
+
+def _q6k_rows(rng, rows, cols, scale_lo=-64, scale_hi=64):
+    """Random Q6_K rows (210 B per 256 values: ql[128], qh[64], int8 scales[16], fp16 d): any bytes form a valid
+    block; scales and d kept in the ranges real files use (or pushed to the int8 ends)."""
+    nbk = cols // 256
+    b = rng.integers(0, 256, size=(rows, nbk, 210), dtype=np.uint8)
+    b[:, :, 192:208] = rng.integers(scale_lo, scale_hi, size=(rows, nbk, 16)).astype(np.int8).view(np.uint8)
+    d = rng.uniform(1e-4, 4e-3, size=(rows, nbk)).astype(np.float16)
+    b[:, :, 208:210] = d.view(np.uint8).reshape(rows, nbk, 2)
+    return b.reshape(rows, nbk * 210)
+
+
+@needs_ref
+@pytest.mark.parametrize("cols,seed", [(256, 0), (2048, 1), (2048, 2), (8192, 3)])
+def test_q6k_word_scores_match_reference(cols, seed):
+    """imi_q8k::from and imi_q6k_row (tables.cpp:200-278): codes, scales and code sums identical, word scores bit
+    for bit, including the saturating ends of the int8 scales and a large-magnitude input."""
+    rng = np.random.default_rng(seed)
+    W = _q6k_rows(rng, 96, cols, *((-128, 128) if seed == 2 else (-64, 64)))
+    x = (rng.standard_normal(cols) * (40.0 if seed == 3 else 1.0)).astype(np.float32)
+    for mine, ref in zip(oracle.q8k_from(x), oracle.q8k_from(x, reference=True)):
+        assert np.array_equal(mine, ref)
+    got, want = oracle.q6k_rows(W, x), oracle.q6k_rows(W, x, reference=True)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@needs_ref
+def test_q6k_zero_input_and_lookup_match_reference():
+    """A zero input block (scale 0, inverse 0: all codes 0) and the row lookup (tables.cpp:216-233)."""
+    rng = np.random.default_rng(9)
+    W = _q6k_rows(rng, 8, 2048)
+    x = rng.standard_normal(2048).astype(np.float32)
+    x[256:512] = 0.0
+    q, d, bs = oracle.q8k_from(x)
+    assert d[1] == 0.0 and not q[256:512].any() and not bs[16:32].any()
+    got, want = oracle.q6k_rows(W, x), oracle.q6k_rows(W, x, reference=True)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    for r in range(8):
+        a, b = oracle.q6k_dequant_row(W[r], 8), oracle.q6k_dequant_row(W[r], 8, reference=True)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
