@@ -73,6 +73,7 @@ def lib():
         L.imi_cuda_state_load.argtypes = [_vp, _vp, C.c_size_t]
         L.imi_cuda_trace_step.argtypes = [_vp, C.c_int32, C.c_int, _vp, C.c_int, _vp, _vp, C.POINTER(C.c_int)]
         L.imi_cuda_q8_cut.argtypes = [C.c_int, _fp, C.c_int, _vp, _fp, _fp]
+        L.imi_cuda_q6k_scores.argtypes = [C.c_int, _vp, C.c_int, C.c_int, _fp, _fp, _vp, _fp, _vp]
         L.imi_cuda_q4_matvec.argtypes = [C.c_int, _vp, C.c_int, C.c_int, _vp, _fp, _fp, C.c_int, _fp, _ip]
         L.imi_cuda_q4_matvec_static.argtypes = [C.c_int, _vp, C.c_int, C.c_int, _vp, _vp, _vp, C.c_int, _vp, _vp]
         _L = L
@@ -276,6 +277,18 @@ def q8_cut(x, device: int = 0):
     q, d, s = np.zeros(n, np.int8), np.zeros(n // 32, np.float32), np.zeros(n // 32, np.float32)
     _check(lib().imi_cuda_q8_cut(device, _ptr(x), n, _ptr(q), _ptr(d), _ptr(s)))
     return q, d, s
+
+
+def q6k_scores(q6k, x, device: int = 0):
+    """Word scores of Q6_K rows ([rows][cols/256 * 210] bytes) for the float input x on the device (imi_q8k::from +
+    imi_q6k_row): (scores[rows], (codes, scales, code sums of the input cut))."""
+    q6k = np.ascontiguousarray(q6k, dtype=np.uint8)
+    x = _f32(x).ravel()
+    rows, cols = q6k.shape[0], x.size
+    out = np.zeros(rows, np.float32)
+    q, d, bs = np.zeros(cols, np.int8), np.zeros(cols // 256, np.float32), np.zeros(cols // 16, np.int16)
+    _check(lib().imi_cuda_q6k_scores(device, _ptr(q6k), rows, cols, _ptr(x), _ptr(out), _ptr(q), _ptr(d), _ptr(bs)))
+    return out, (q, d, bs)
 
 
 def q4_matvec(q4, rows: int, cols: int, xq, xd, xs, dots: bool = False, device: int = 0):

@@ -916,6 +916,38 @@ imi_cuda_status imi_cuda_get_argmax(const imi_cuda_state *s, int32_t *id, float 
     return imi_cuda_get_argmax(s, id, value);
 }
 
+imi_cuda_status imi_cuda_q6k_scores(int device, const uint8_t *q6k, int rows, int cols, const float *x, float *out,
+                                    int8_t *xq, float *xd, int16_t *bsums) {
+    if (!q6k || !x || !out || rows <= 0 || cols <= 0 || cols % 256)
+        return fail(IMI_E_ARG, "bad q6k_scores arguments (cols a multiple of 256)");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) return fail(IMI_E_NODEV, "no CUDA device");
+    CK(cudaSetDevice(device));
+    const int nb = cols / 256;
+    const size_t wbytes = (size_t) rows * nb * 210;
+    // one allocation: x | out | q8k codes | scales | code sums | the rows
+    auto up = [](size_t n) { return (n + 255) / 256 * 256; };
+    const size_t o_x = 0, o_out = up((size_t) cols * 4), o_q = o_out + up((size_t) rows * 4), o_d = o_q + up(cols),
+                 o_b = o_d + up((size_t) nb * 4), o_w = o_b + up((size_t) nb * 32), total = o_w + wbytes;
+    uint8_t *m = nullptr;
+    CK(cudaMalloc(&m, total));
+    cudaError_t r = cudaMemcpy(m + o_x, x, (size_t) cols * 4, cudaMemcpyHostToDevice);
+    if (r == cudaSuccess) r = cudaMemcpy(m + o_w, q6k, wbytes, cudaMemcpyHostToDevice);
+    if (r == cudaSuccess)
+        r = launch_q8k_cut((const float *) (m + o_x), cols, (int8_t *) (m + o_q), (float *) (m + o_d),
+                           (int16_t *) (m + o_b), 0);
+    if (r == cudaSuccess)
+        r = launch_q6k_scores(m + o_w, rows, nb, (const int8_t *) (m + o_q), (const float *) (m + o_d),
+                              (const int16_t *) (m + o_b), (float *) (m + o_out), 0);
+    if (r == cudaSuccess) r = cudaMemcpy(out, m + o_out, (size_t) rows * 4, cudaMemcpyDeviceToHost);
+    if (r == cudaSuccess && xq) r = cudaMemcpy(xq, m + o_q, cols, cudaMemcpyDeviceToHost);
+    if (r == cudaSuccess && xd) r = cudaMemcpy(xd, m + o_d, (size_t) nb * 4, cudaMemcpyDeviceToHost);
+    if (r == cudaSuccess && bsums) r = cudaMemcpy(bsums, m + o_b, (size_t) nb * 32, cudaMemcpyDeviceToHost);
+    cudaFree(m);
+    if (r != cudaSuccess) return fail(IMI_E_CUDA, std::string("q6k_scores: ") + cudaGetErrorString(r));
+    return IMI_OK;
+}
+
 imi_cuda_status imi_cuda_q8_cut(int device, const float *x, int n, int8_t *q, float *d, float *s) {
     if (!x || !q || !d || !s || n <= 0 || n % 32) return fail(IMI_E_ARG, "bad q8_cut arguments");
     int ndev = 0;

@@ -346,6 +346,83 @@ __global__ void k_q8_cut(const float *x, int n, int8_t *q, float *d, float *s) {
     }
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// the Q6_K word table of the product's own files (imi_q8k / imi_q6k_row, tables.cpp:200-278)
+// ---------------------------------------------------------------------------------------------------------------
+// imi_q8k::from: one warp per 256 values (8 per lane, lane L holding values 8L..8L+7): amax, d = amax/127,
+// id = d ? 1/d : 0, q = round-half-even(x * id), the code sum of every 16 values
+__global__ void k_q8k_cut(const float *x, int n, int8_t *q, float *d, int16_t *bsums) {
+    const int lane = threadIdx.x & 31, j = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (j >= n / 256) return;   // whole warps only
+    const float *v = x + 256 * j + 8 * lane;
+    float a[8], amax = 0.0f;
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+        a[u] = v[u];
+        amax = fmaxf(amax, fabsf(a[u]));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float dd = __fdiv_rn(amax, 127.0f), id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
+    int s = 0;
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+        const int c = __float2int_rn(__fmul_rn(a[u], id));
+        q[256 * j + 8 * lane + u] = (int8_t) c;
+        s += c;
+    }
+    s += __shfl_xor_sync(0xffffffffu, s, 1);   // lanes 2m, 2m+1 hold the 16 values of sum m
+    if ((lane & 1) == 0) bsums[16 * j + lane / 2] = (int16_t) s;
+    if (lane == 0) d[j] = dd;
+}
+
+// the word score of one Q6_K row (210 bytes per 256 values: ql[128], qh[64], int8 scales[16], fp16 d) for a q8k
+// input, in imi_q6k_row's AVX2 order: 8 threads per row, thread m the integer lane m (values 128n + 32k + 4m .. +3,
+// n < 2, k < 4, each 4 times the scale of its 16, minus 32 * (scales[2m] bsums[2m] + scales[2m+1] bsums[2m+1]),
+// exact), then lane m's float chain acc = fma(d * dx, float(int), acc) over the blocks in order, and the 8 lanes
+// summed as ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7)).
+__global__ void __launch_bounds__(256) k_q6k_scores(const uint8_t *W, int rows, int nb, const int8_t *xq,
+                                                    const float *xd, const int16_t *bsums, float *out) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x, r = t >> 3, m = t & 7;
+    const bool act = r < rows;
+    const uint8_t *row = W + (size_t) (act ? r : 0) * nb * 210;
+    float acc = 0.0f;
+    for (int i = 0; i < nb; i++) {
+        const uint8_t *b = row + (size_t) i * 210;   // blocks are 2-byte aligned at best: byte loads
+        const int8_t *sc = (const int8_t *) (b + 192);
+        const int8_t *x = xq + 256 * i;
+        int lane = 0;
+#pragma unroll
+        for (int n = 0; n < 2; n++) {
+            uint32_t qh4 = 0;
+#pragma unroll
+            for (int u = 0; u < 4; u++) qh4 |= (uint32_t) b[128 + 32 * n + 4 * m + u] << (8 * u);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const uint8_t *ql = b + 64 * n + (k & 1) * 32 + 4 * m;
+                uint32_t ql4 = 0;
+#pragma unroll
+                for (int u = 0; u < 4; u++) ql4 |= (uint32_t) ql[u] << (8 * u);
+                const uint32_t lo = (k < 2 ? ql4 : ql4 >> 4) & 0x0f0f0f0fu;
+                const uint32_t codes = lo | (((qh4 >> (2 * k)) & 0x03030303u) << 4);
+                const int8_t *xv = x + 128 * n + 32 * k + 4 * m;
+                const int x4 = (int) ((uint32_t) (uint8_t) xv[0] | ((uint32_t) (uint8_t) xv[1] << 8) |
+                                      ((uint32_t) (uint8_t) xv[2] << 16) | ((uint32_t) (uint8_t) xv[3] << 24));
+                lane += __dp4a((int) codes, x4, 0) * (int) sc[8 * n + 2 * k + (m >= 4)];   // codes <= 63: signed is exact
+            }
+        }
+        const int16_t *bs = bsums + 16 * i;
+        lane -= 32 * ((int) sc[2 * m] * bs[2 * m] + (int) sc[2 * m + 1] * bs[2 * m + 1]);
+        const float s = __fmul_rn(h2f((uint16_t) (b[208] | (b[209] << 8))), xd[i]);
+        acc = __fmaf_rn(s, __int2float_rn(lane), acc);
+    }
+    // the 8 lanes of a row sit in 8 consecutive threads (an aligned group of 8 within the warp)
+    const float r4 = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));   // m < 4: a_m + a_{m+4}
+    const float r2 = __fadd_rn(r4, __shfl_down_sync(0xffffffffu, r4, 2));     // m < 2: r_m + r_{m+2}
+    const float r1 = __fadd_rn(r2, __shfl_down_sync(0xffffffffu, r2, 1));     // m = 0: (r0 + r2) + (r1 + r3)
+    if (act && m == 0) out[r] = r1;
+}
+
 // GGUF Q4_0 rows (blocks of 18 bytes: fp16 scale, then 16 code bytes) into the table kernel's row layout
 // [cols/2 code bytes | cols/32 fp16 scales]; one thread per block, byte copies (GGUF blocks are only 2-byte aligned)
 __global__ void k_q4_repack(const uint8_t *src, int rows, int nb, uint8_t *dst) {

@@ -13,6 +13,11 @@ cudaError_t launch_kvwrite(const AttnArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_final(const FinalArgs &a, cudaStream_t st, bool pdl);
 cudaError_t prepare_kernels();
 cudaError_t launch_q8_cut(const float *x, int n, int8_t *q, float *d, float *s, cudaStream_t st);
+// the Q6_K word table: the 256-value input cut (imi_q8k::from) and the word scores (imi_q6k_row), n and cols
+// multiples of 256
+cudaError_t launch_q8k_cut(const float *x, int n, int8_t *q, float *d, int16_t *bsums, cudaStream_t st);
+cudaError_t launch_q6k_scores(const uint8_t *W, int rows, int nb, const int8_t *xq, const float *xd,
+                              const int16_t *bsums, float *out, cudaStream_t st);
 // GGUF Q4_0 rows (device) into the table kernel's row layout (device), on stream st
 cudaError_t launch_q4_repack(const uint8_t *src, int rows, int nb, uint8_t *dst, cudaStream_t st);
 }  // namespace imi

@@ -52,3 +52,31 @@ def test_q4_table_matches_reference_golden():
     out = nb.q4_matvec(g["kat_q4"], rows, cols, q, d, s)
     assert np.array_equal(bits(out), bits(g["kat_out5"]))
     assert np.array_equal(bits(nb.q4_matvec(g["kat_q4"], rows, cols, q[:cols], d[:16], s[:16])), bits(g["kat_out1"]))
+
+
+# ---- the Q6_K word table (the product's own word-table format): device word scores against the oracle ----
+
+def _q6k_rows(rng, rows, cols, scale_lo=-64, scale_hi=64):
+    """Random Q6_K rows: any bytes form valid blocks; int8 scales in [scale_lo, scale_hi), fp16 d in real ranges."""
+    nbk = cols // 256
+    b = rng.integers(0, 256, size=(rows, nbk, 210), dtype=np.uint8)
+    b[:, :, 192:208] = rng.integers(scale_lo, scale_hi, size=(rows, nbk, 16)).astype(np.int8).view(np.uint8)
+    b[:, :, 208:210] = rng.uniform(1e-4, 4e-3, size=(rows, nbk)).astype(np.float16).view(np.uint8).reshape(rows, nbk, 2)
+    return b.reshape(rows, nbk * 210)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("rows,cols,seed", [(1000, 256, 0), (1000, 2048, 1), (333, 8192, 2), (97496, 2048, 3)])
+def test_q6k_word_scores_bit_exact(rows, cols, seed):
+    """imi_q8k::from and imi_q6k_row on the device (imi_cuda_q6k_scores) against the oracle (itself pinned to the
+    reference's own AVX2 code): the input cut identical, every word score bit for bit; seed 2 pushes the scales to
+    the int8 ends and the input to large magnitudes, and one input block is zero (scale 0)."""
+    rng = np.random.default_rng(seed)
+    W = _q6k_rows(rng, rows, cols, *((-128, 128) if seed == 2 else (-64, 64)))
+    x = (rng.standard_normal(cols) * (40.0 if seed == 2 else 1.0)).astype(np.float32)
+    x[:256] = 0.0 if seed == 1 else x[:256]
+    got, cut = nb.q6k_scores(W, x)
+    for mine, want in zip(cut, oracle.q8k_from(x)):
+        assert np.array_equal(mine, want)
+    want = oracle.q6k_rows(W, x)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
