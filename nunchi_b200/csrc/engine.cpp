@@ -918,8 +918,8 @@ imi_cuda_status imi_cuda_get_argmax(const imi_cuda_state *s, int32_t *id, float 
 
 imi_cuda_status imi_cuda_q6k_scores(int device, const uint8_t *q6k, int rows, int cols, const float *x, float *out,
                                     int8_t *xq, float *xd, int16_t *bsums) {
-    if (!q6k || !x || !out || rows <= 0 || cols <= 0 || cols % 256)
-        return fail(IMI_E_ARG, "bad q6k_scores arguments (cols a multiple of 256)");
+    if (!q6k || !x || !out || rows <= 0 || cols <= 0 || cols % 256 || cols > 32768)
+        return fail(IMI_E_ARG, "bad q6k_scores arguments (cols a multiple of 256, at most 32768)");
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) return fail(IMI_E_NODEV, "no CUDA device");
     CK(cudaSetDevice(device));
