@@ -21,7 +21,7 @@ from dataclasses import dataclass, field
 import numpy as np
 
 # ggml type ids used here
-GGML_F32, GGML_F16, GGML_Q4_0 = 0, 1, 2
+GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q6_K = 0, 1, 2, 14
 # gguf value types
 _U32, _I32, _F32, _BOOL, _STR, _ARR, _U64 = 4, 5, 6, 7, 8, 9, 10
 ALIGN = 32
@@ -43,6 +43,7 @@ class Shape:
     n_swa: int = 0                                # sliding window (0 = none)
     swa_layers: tuple = ()                        # attention layers that use the window
     rope_freqs: bool = False                      # write a rope_freqs.weight table
+    word_q6k: bool = False                        # the word table in Q6_K (the product's own format) instead of Q4_0
 
     @property
     def kvd(self) -> int:
@@ -65,7 +66,11 @@ SMALL = Shape(n_embd=512, n_layer=6, attn_layers=(2, 4), n_head=8, n_head_kv=2, 
 WIDE_HEADS = Shape(n_embd=1024, n_layer=4, attn_layers=(1, 2, 3), n_head=8, n_head_kv=2, head_dim=128, n_ff=2048,
                    n_vocab=2001, n_swa=8, swa_layers=(2,), rope_freqs=True)
 
-SHAPES = {"seoul": SEOUL, "tiny": TINY, "small": SMALL, "wide_heads": WIDE_HEADS}
+# TINY with a Q6_K word table, as the product's own files have
+TINY_Q6K = Shape(n_embd=512, n_layer=4, attn_layers=(1, 3), n_head=8, n_head_kv=2, head_dim=64, n_ff=1024,
+                 n_vocab=1003, word_q6k=True)
+
+SHAPES = {"seoul": SEOUL, "tiny": TINY, "small": SMALL, "wide_heads": WIDE_HEADS, "tiny_q6k": TINY_Q6K}
 
 
 def _q4_0(rng: np.random.Generator, rows: int, cols: int) -> np.ndarray:
@@ -78,6 +83,18 @@ def _q4_0(rng: np.random.Generator, rows: int, cols: int) -> np.ndarray:
     return out
 
 
+def _q6k(rng: np.random.Generator, rows: int, cols: int) -> np.ndarray:
+    """A Q6_K table [rows][cols/256 blocks] of 210-byte blocks: ql[128], qh[64] (uniform 6-bit codes), int8 scales[16]
+    in [-8, 8], fp16 d: values d * scale * (code - 32) of the Q4_0 tables' magnitude."""
+    assert cols % 256 == 0
+    nblk = rows * (cols // 256)
+    out = np.empty((nblk, 210), np.uint8)
+    out[:, :192] = rng.integers(0, 256, (nblk, 192), dtype=np.uint8)
+    out[:, 192:208] = rng.integers(-8, 9, (nblk, 16)).astype(np.int8).view(np.uint8)
+    out[:, 208:] = rng.uniform(2e-4, 6e-4, nblk).astype(np.float16).view(np.uint8).reshape(nblk, 2)
+    return out
+
+
 def _norm(rng, n):
     return (1.0 + 0.1 * rng.standard_normal(n)).astype(np.float32)
 
@@ -86,7 +103,10 @@ def tensors(shape: Shape, seed: int = 0):
     """Yield (name, ggml_type, ne (fastest first), bytes) in file order, drawing from one seeded generator."""
     rng = np.random.default_rng(seed)
     E, F = shape.n_embd, shape.n_ff
-    yield "token_embd.weight", GGML_Q4_0, (E, shape.n_vocab), _q4_0(rng, shape.n_vocab, E)
+    if shape.word_q6k:
+        yield "token_embd.weight", GGML_Q6_K, (E, shape.n_vocab), _q6k(rng, shape.n_vocab, E)
+    else:
+        yield "token_embd.weight", GGML_Q4_0, (E, shape.n_vocab), _q4_0(rng, shape.n_vocab, E)
     yield "output_norm.weight", GGML_F32, (E,), _norm(rng, E)
     if shape.rope_freqs:
         ff = (1.0 + rng.uniform(0.0, 3.0, shape.head_dim // 2)).astype(np.float32)

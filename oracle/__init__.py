@@ -297,11 +297,12 @@ class Reference:
     """imi_seoul from the reference's seoul.cpp + tables.cpp (oracle/_ref/libimi_ref.so)."""
 
     _L = None
+    _LIB = "libimi_ref.so"
 
     @classmethod
     def lib(cls):
         if cls._L is None:
-            L = _lib(os.path.join("_ref", "libimi_ref.so"))
+            L = _lib(os.path.join("_ref", cls._LIB))
             L.oref_load.restype = C.c_void_p
             L.oref_load.argtypes = [C.c_char_p, C.c_int, C.c_int]
             L.oref_free.argtypes = [C.c_void_p]
@@ -342,6 +343,18 @@ class Reference:
             self.lib().oref_free(self.h)
         except Exception:
             pass
+
+
+def reference_q6k_available() -> bool:
+    return os.path.exists(os.path.join(HERE, "_ref", "libimi_ref_q6k.so"))
+
+
+class ReferenceQ6K(Reference):
+    """The reference's imi_seoul with its own Q6_K word table (no word-table renames: oracle/_ref/libimi_ref_q6k.so),
+    for files whose token_embd is Q6_K, as the product's are."""
+
+    _L = None
+    _LIB = "libimi_ref_q6k.so"
 
     def reset(self):
         self.lib().oref_reset(self.h)

@@ -27,6 +27,7 @@ struct or_model {
     gm_file f;
     or_layer *L;
     or_table tok;
+    int tok_q6k;   /* the word table is Q6_K (the product's own files) rather than Q4_0 */
     const float *out_norm, *rope_freqs;
     int n_layer, n_embd, n_vocab, n_head, n_head_kv, head_dim, n_ff, d_conv, n_swa, n_ctx, n_attn, n_threads;
     float eps, rope_base, rope_base_swa;
@@ -43,6 +44,7 @@ struct or_state {
     /* scratch */
     float *x, *h, *big, *att, *y, *act, *fo, *sc;
     q8v qi;
+    int16_t *bs;   /* code sums per 16 of the Q6_K head's input cut */
 };
 
 /* ---------------- small math (imi/core/vec.h, imi/core/tables.cpp:20-38) ---------------- */
@@ -203,7 +205,13 @@ or_model *or_load(const char *path, int n_ctx, int n_threads) {
     if (gm_open(path, &m->f) != 0) { snprintf(g_err, sizeof g_err, "%s", gm_error()); free(m); return NULL; }
     gm_file *f = &m->f;
     char nm[128];
-    if (table(f, "token_embd.weight", &m->tok)) goto fail;
+    {
+        const gm_tensor *te = gm_find(f, "token_embd.weight");
+        if (te && te->type == GM_T_Q6_K) {   /* seoul.cpp:95-98: the reference's own word-table format */
+            m->tok.w = te->data; m->tok.cols = (int) te->ne[0]; m->tok.rows = (int) te->ne[1];
+            m->tok.row_bytes = te->row_bytes; m->tok_q6k = 1;
+        } else if (table(f, "token_embd.weight", &m->tok)) goto fail;
+    }
     m->n_embd = m->tok.cols; m->n_vocab = m->tok.rows;
     if (!(m->out_norm = f32(f, "output_norm.weight", 1))) goto fail;
     m->rope_freqs = f32(f, "rope_freqs.weight", 0);
@@ -295,6 +303,7 @@ or_state *or_state_new(const or_model *m) {
     s->qi.q = (int8_t *) calloc(wide, 1);
     s->qi.d = (float *) calloc(wide / 32 + 1, 4);
     s->qi.s = (float *) calloc(wide / 32 + 1, 4);
+    s->bs = (int16_t *) calloc(E / 16 + 1, 2);
     return s;
 }
 void or_state_free(or_state *s) {
@@ -304,7 +313,7 @@ void or_state_free(or_state *s) {
     for (int il = 0; il < s->n_layer; il++) free(s->conv[il]);
     free(s->conv);
     free(s->hidden); free(s->logits); free(s->x); free(s->h); free(s->big); free(s->att); free(s->y); free(s->act);
-    free(s->fo); free(s->sc); free(s->qi.q); free(s->qi.d); free(s->qi.s);
+    free(s->fo); free(s->sc); free(s->qi.q); free(s->qi.d); free(s->qi.s); free(s->bs);
     free(s);
 }
 void or_state_reset(const or_model *m, or_state *s) {   /* seoul.cpp:188-191 (caches are overwritten before use) */
@@ -320,7 +329,25 @@ const float *or_conv_state(const or_state *s, int il) { return s->conv[il]; }
 
 /* ---------------- one position (seoul.cpp:359-488) ---------------- */
 
+/* the word scores of the hidden state: Q6_K (seoul.cpp:479-487 with imi_q8k / imi_q6k_row) or the Q4_0 adapter */
+static void head(const or_model *m, or_state *s, int nt) {
+    const int E = m->n_embd;
+    if (m->tok_q6k) {
+        or_q8k_from(s->hidden, E, s->qi.q, s->qi.d, s->bs);
+#pragma omp parallel for num_threads(nt) schedule(static)
+        for (int r = 0; r < m->n_vocab; r++)
+            s->logits[r] = or_q6k_row(m->tok.w + (size_t) r * m->tok.row_bytes, s->qi.q, s->qi.d, s->bs, E / 256);
+        return;
+    }
+    or_cut(s->hidden, E, s->qi.q, s->qi.d, s->qi.s);
+    matvec(&m->tok, &s->qi, s->logits, nt);
+}
+
 static void lookup(const or_model *m, int32_t token, float *x) {   /* the word row, d * (code - 8) */
+    if (m->tok_q6k) {   /* seoul.cpp:363: imi_q6k_dequant_row */
+        or_q6k_dequant_row(m->tok.w + (size_t) token * m->tok.row_bytes, x, m->n_embd / 256);
+        return;
+    }
     const uint8_t *b = m->tok.w + (size_t) token * m->tok.row_bytes;
     for (int j = 0; j < m->n_embd / 32; j++, b += 18) {
         uint16_t dh; memcpy(&dh, b, 2);
@@ -413,10 +440,7 @@ static void run(const or_model *m, or_state *S, int32_t token, const float *embd
         norm_mul_add(S->fo, L->post_ffn_norm, x, E, eps);                        /* seoul.cpp:473 */
     }
     norm_mul(x, m->out_norm, S->hidden, E, eps);                                  /* seoul.cpp:475-477 */
-    if (want_logits) {                                                            /* seoul.cpp:479-487 (Q4_0 head) */
-        or_cut(S->hidden, E, S->qi.q, S->qi.d, S->qi.s);
-        matvec(&m->tok, &S->qi, S->logits, nt);
-    }
+    if (want_logits) head(m, S, nt);                                              /* seoul.cpp:479-487 */
 }
 
 int or_step(const or_model *m, or_state *s, int32_t token, const float *embd, int want_logits) {
@@ -438,10 +462,7 @@ int or_step_batch(const or_model *m, or_state *s, const int32_t *tokens, const f
             s->pos++;
         }
     }
-    if (want_logits) {   /* seoul.cpp:507-516: the last position's scores */
-        or_cut(s->hidden, E, s->qi.q, s->qi.d, s->qi.s);
-        matvec(&m->tok, &s->qi, s->logits, m->n_threads);
-    }
+    if (want_logits) head(m, s, m->n_threads);   /* seoul.cpp:507-516: the last position's scores */
     return 0;
 }
 /* ---- Q6_K word table (imi_q8k / imi_q6k_row / imi_q6k_dequant_row, tables.cpp:200-287) ---- */

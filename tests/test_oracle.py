@@ -194,3 +194,22 @@ def test_q6k_zero_input_and_lookup_match_reference():
     for r in range(8):
         a, b = oracle.q6k_dequant_row(W[r], 8), oracle.q6k_dequant_row(W[r], 8, reference=True)
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+needs_ref_q6k = pytest.mark.skipif(not oracle.reference_q6k_available(), reason="oracle/_ref not built")
+
+
+@needs_ref_q6k
+def test_q6k_word_table_steps_match_reference_live():
+    """A model with the product's own Q6_K word table (lookup and word scores): the oracle's steps and prefill against
+    the reference's own imi_seoul built without the Q4_0 word-table renames, bit for bit."""
+    path = synth.cached_gguf("tiny_q6k")
+    o, r = oracle.Oracle(path, n_ctx=96), oracle.ReferenceQ6K(path, n_ctx=96)
+    ids = synth.random_ids(24, o.n_vocab, 6)
+    o.step_batch(tokens=ids[:16], want_logits=True)
+    r.step_batch(tokens=ids[:16], want_logits=True)
+    assert np.array_equal(bits(o.logits), bits(r.logits))
+    for t in ids[16:]:
+        o.step(int(t))
+        r.step(int(t))
+        assert np.array_equal(bits(o.hidden), bits(r.hidden)) and np.array_equal(bits(o.logits), bits(r.logits))
