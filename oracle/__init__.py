@@ -345,17 +345,6 @@ class Reference:
             pass
 
 
-def reference_q6k_available() -> bool:
-    return os.path.exists(os.path.join(HERE, "_ref", "libimi_ref_q6k.so"))
-
-
-class ReferenceQ6K(Reference):
-    """The reference's imi_seoul with its own Q6_K word table (no word-table renames: oracle/_ref/libimi_ref_q6k.so),
-    for files whose token_embd is Q6_K, as the product's are."""
-
-    _L = None
-    _LIB = "libimi_ref_q6k.so"
-
     def reset(self):
         self.lib().oref_reset(self.h)
 
@@ -438,3 +427,15 @@ def ref_q4_matvec(q4, rows, cols, x) -> np.ndarray:
     if Reference.lib().oref_q4_matvec(_ptr(q4), rows, cols, _ptr(x), x.shape[0], _ptr(out)) != 0:
         raise ValueError("shape not supported by the reference kernel")
     return out
+
+
+def reference_q6k_available() -> bool:
+    return os.path.exists(os.path.join(HERE, "_ref", "libimi_ref_q6k.so"))
+
+
+class ReferenceQ6K(Reference):
+    """The reference's imi_seoul with its own Q6_K word table (no word-table renames: oracle/_ref/libimi_ref_q6k.so),
+    for files whose token_embd is Q6_K, as the product's are."""
+
+    _L = None
+    _LIB = "libimi_ref_q6k.so"
