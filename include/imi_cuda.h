@@ -135,8 +135,8 @@ imi_cuda_status imi_cuda_q8_cut(int device, const float *x, int n, int8_t *q, fl
 /* Word scores of a Q6_K table (the product's own word-table format: rows of 210-byte blocks per 256 values) for one
  * float input x[cols], on the device: the input cut per 256 values as imi_q8k::from (tables.cpp:200-213), then every
  * row as imi_q6k_row (tables.cpp:235-278, the AVX2 order) -> out[rows]. The cut can be returned too (xq[cols],
- * xd[cols/256], bsums[cols/16]; each may be NULL). cols a multiple of 256, at most 32768; host pointers. The first
- * GPU piece of the Q6_K word table; the decode step does not use it yet (the engine loads Q4_0 word tables only). */
+ * xd[cols/256], bsums[cols/16]; each may be NULL). cols a multiple of 256, at most 32768; host pointers. The kernel
+ * level of the Q6_K word table, which the engine also reads inside its steps when a file carries one. */
 imi_cuda_status imi_cuda_q6k_scores(int device, const uint8_t *q6k, int rows, int cols, const float *x, float *out,
                                     int8_t *xq, float *xd, int16_t *bsums);
 

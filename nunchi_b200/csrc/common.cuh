@@ -76,6 +76,7 @@ struct MvArgs {
     float eps;
     const uint8_t *emb;        // word table (same row layout) for P_EMBED_NORM
     int emb_row_bytes;
+    int emb_q6k;               // 1: the word table is Q6_K (rows of 210-byte blocks per 256 values, as in the file)
     const float *conv_w;       // [d_conv+1][n_embd]
     int d_conv, conv_layer, n_embd;
     int ring_layer;            // >= 0: write the conv memory slots of this layer from ring_src (bcx rows); in P_CONV
@@ -127,6 +128,25 @@ struct FinalArgs {
     float eps;
     int n_embd;
     unsigned long long *trace;        // optional: per-CTA timestamps (ns), [grid][MV_TRACE]
+    // Q6_K word table: the output-normed hidden state also cut per 256 values (imi_q8k::from) into
+    // q8k_q[c][n_embd], q8k_d[c][n_embd/256], q8k_b[c][n_embd/16], and the position left to the word-score launch
+    int8_t *q8k_q;
+    float *q8k_d;
+    int16_t *q8k_b;
+};
+
+// the word scores of a Q6_K word table for ncol inputs cut per 256 values, with the first-maximum pick and the
+// end-of-step bookkeeping of the word-table read (k_q6k_head)
+struct Q6HeadArgs {
+    const Col *cols_d;
+    int ncol;
+    const uint8_t *W;                 // rows of nb 210-byte blocks
+    int rows, nb;
+    const int8_t *xq;                 // [c][256 nb]
+    const float *xd;                  // [c][nb]
+    const int16_t *xb;                // [c][16 nb]
+    unsigned *done;                   // CTAs finished (the last one picks and resets it)
+    unsigned long long *trace;
 };
 
 // ---- shared-memory plan of the table-read kernel (host and device agree on it) ----

@@ -66,6 +66,10 @@ struct imi_cuda_engine {
     size_t w_bytes = 0;
     std::vector<LayerRef> layers;
     TableRef tok;
+    bool tok_q6k = false;   // the word table is Q6_K (kept as in the file) rather than Q4_0
+    int8_t *q8k_q = nullptr;   // Q6_K word table: the hidden state cut per 256 values [col][n_embd], scales, sums
+    float *q8k_d = nullptr;
+    int16_t *q8k_b = nullptr;
     size_t out_norm = 0;
     float *rope_cs = nullptr, *rope_sn = nullptr;   // [2][n_ctx][head_dim/2]: full layers, window layers
     int big_n = 0;
@@ -93,7 +97,7 @@ struct imi_cuda_engine {
     int trace_n = 0, trace_max = 0;
     std::vector<int> trace_kind, trace_grid;
     unsigned long long *trace_slot(int kind, int grid) {
-        if (!trace_buf || trace_n >= trace_max) return nullptr;
+        if (!trace_buf || trace_n >= trace_max || grid > sm_count) return nullptr;   // a slot holds sm_count CTAs
         trace_kind.push_back(kind);
         trace_grid.push_back(grid);
         return trace_buf + (size_t) (trace_n++) * sm_count * MV_TRACE;
@@ -120,6 +124,7 @@ imi_cuda_engine::~imi_cuda_engine() {
     cudaFree(rope_cs);
     cudaFree(X);
     cudaFree(qbuf);
+    cudaFree(q8k_q);
     cudaFree(cols_d);
     cudaFreeHost(cols_h);
     cudaFreeHost(embd_h);
@@ -225,8 +230,10 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
     const gguf_value *swa_pat = f.value("lfm3.attention.sliding_window_pattern");
 
     Loader L(f);
-    const gguf_tensor *te = L.need("token_embd.weight", T_Q4_0);
-    if (!te) return fail(IMI_E_FORMAT, L.err + " (the word table must be Q4_0 here)");
+    const gguf_tensor *te = f.tensor("token_embd.weight");
+    e->tok_q6k = te && te->type == T_Q6_K && te->data;   // the product's own word-table format (seoul.cpp:95-98)
+    if (!e->tok_q6k) te = L.need("token_embd.weight", T_Q4_0);
+    if (!te) return fail(IMI_E_FORMAT, L.err + " (the word table must be Q4_0 or Q6_K here)");
     e->n_embd = (int) te->ne[0];
     e->n_vocab = (int) te->ne[1];
     if (e->n_embd % 256) return fail(IMI_E_FORMAT, "n_embd must be a multiple of 256");
@@ -234,7 +241,13 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
     if (e->d_conv > 8 || e->n_embd > 6144)   // the input preparation keeps 8 taps and n_embd/4 float4 chunks in registers
         return fail(IMI_E_FORMAT, "conv width above 9 or n_embd above 6144 is not supported");
     const int E = e->n_embd;
-    {
+    if (e->tok_q6k) {   // kept as in the file: rows of 210-byte blocks per 256 values, copied as they are
+        e->tok.rows = e->n_vocab;
+        e->tok.cols = E;
+        e->tok.row_bytes = E / 256 * 210;
+        e->tok.off = L.take(te->nbytes);
+        L.f32s.push_back({ e->tok.off, te });
+    } else {
         std::vector<std::pair<const gguf_tensor *, int>> rows;
         Loader::all_rows(rows, te);
         if (!L.table(e->tok, rows)) return fail(IMI_E_FORMAT, L.err);
@@ -370,6 +383,15 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
         e->qt_s = e->qt_d + nt / 32;
         CK(cudaMemset(q, 0, na + nt + 4 * 2 * (na / 32 + nt / 32) + 1024));
     }
+    if (e->tok_q6k) {
+        if (q6k_head_ctas(e->n_vocab, E / 256, STEP_COLS) <= 0) return fail(IMI_E_FORMAT, "Q6_K word table too wide");
+        uint8_t *q = nullptr;
+        const size_t nq = (size_t) STEP_COLS * E, nd = (size_t) STEP_COLS * (E / 256), nbs = (size_t) STEP_COLS * (E / 16);
+        CK(cudaMalloc(&q, nq + 4 * nd + 2 * nbs + 64));
+        e->q8k_q = (int8_t *) q;
+        e->q8k_d = (float *) (q + nq);
+        e->q8k_b = (int16_t *) (q + nq + 4 * nd);
+    }
     CK(cudaMalloc(&e->cols_d, sizeof(Col) * STEP_COLS + 64));
     e->done = (unsigned *) (e->cols_d + STEP_COLS);
     e->err = (int *) (e->done + 4);
@@ -433,6 +455,22 @@ cudaError_t table_launch(imi_cuda_engine *e, const TableRef &t, int pro, int epi
     return launch_table(pro, epi, a, grid, e->stream, true);
 }
 
+// the Q6_K word scores of the step's columns (cut beforehand into q8k_*), the pick and the end of the step
+cudaError_t q6k_head_launch(imi_cuda_engine *e, int ncol) {
+    Q6HeadArgs q = {};
+    q.cols_d = e->cols_d;
+    q.ncol = ncol;
+    q.W = e->w + e->tok.off;
+    q.rows = e->n_vocab;
+    q.nb = e->n_embd / 256;
+    q.xq = e->q8k_q;
+    q.xd = e->q8k_d;
+    q.xb = e->q8k_b;
+    q.done = e->done;
+    q.trace = e->trace_slot(102, q6k_head_ctas(e->n_vocab, q.nb, ncol));
+    return launch_q6k_head(q, e->stream, true);
+}
+
 cudaError_t enqueue_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind) {
     const int E = e->n_embd, HD = e->n_head * e->head_dim;
     MvArgs b = {};
@@ -444,11 +482,19 @@ cudaError_t enqueue_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind)
     b.ring_layer = -1;
     b.emb = e->w + e->tok.off;
     b.emb_row_bytes = e->tok.row_bytes;
+    b.emb_q6k = e->tok_q6k ? 1 : 0;
     b.x_stride = 2 * E;
     b.err = e->err;
     b.done = e->done;
     float *X0 = e->X, *X1 = e->X + E;
     cudaError_t r;
+    if (kind == K_HEAD_ONLY && e->tok_q6k) {   // the same with the Q6_K word table: the 256-value cut, then the head
+        for (int c = 0; c < ncol; c++)
+            if ((r = launch_q8k_cut(e->hid + (size_t) c * E, E, e->q8k_q + (size_t) c * E, e->q8k_d + (size_t) c * (E / 256),
+                                    e->q8k_b + (size_t) c * (E / 16), e->stream)) != cudaSuccess)
+                return r;
+        return q6k_head_launch(e, ncol);
+    }
     if (kind == K_HEAD_ONLY) {   // word scores of a hidden state already computed (seoul.cpp:507-516)
         MvArgs a = b;
         a.in = e->hid;
@@ -547,7 +593,7 @@ cudaError_t enqueue_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind)
         if ((r = table_launch(e, L.down, P_Q8IN, E_STORE, a)) != cudaSuccess) return r;
     }
     const LayerRef &last = e->layers.back();
-    if (head) {
+    if (head && !e->tok_q6k) {
         MvArgs a = b;
         a.in = e->fo;
         a.in_stride = E;
@@ -568,6 +614,13 @@ cudaError_t enqueue_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind)
     fa.eps = e->eps;
     fa.n_embd = E;
     fa.trace = e->trace_slot(101, ncol);
+    if (head) {   // Q6_K word table: the final norm also cuts the hidden state; the word-score launch ends the step
+        fa.q8k_q = e->q8k_q;
+        fa.q8k_d = e->q8k_d;
+        fa.q8k_b = e->q8k_b;
+        if ((r = launch_final(fa, e->stream, true)) != cudaSuccess) return r;
+        return q6k_head_launch(e, ncol);
+    }
     return launch_final(fa, e->stream, true);
 }
 
@@ -1127,8 +1180,8 @@ int imi_cuda_launches_per_step(const imi_cuda_engine *e, int n, int want_logits)
     const int groups = (n + STEP_COLS - 1) / STEP_COLS;
     int per = 0;
     for (auto &L : e->layers) per += L.conv ? 4 : 5;
-    return groups * (per + 1);   // + word table (or the final norm without scores)
-    (void) want_logits;
+    // + the word table (or the final norm without scores); a Q6_K word table takes the final norm and its own read
+    return groups * (per + 1 + (e->tok_q6k && want_logits ? 1 : 0));
 }
 
 imi_cuda_status imi_cuda_bench_tables(imi_cuda_engine *e, int ncol, int reps, float *ms, size_t *bytes) {

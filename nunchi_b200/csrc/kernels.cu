@@ -27,9 +27,34 @@ __device__ __forceinline__ void resid_add(float *vb, const float *r, const float
     __syncthreads();
 }
 
-// ---------------------------------------------------------------------------------------------------------------
+// imi_q8k::from of one 256-value block by one warp (lane L: values 8L..8L+7): amax, d = amax/127, id = d ? 1/d : 0,
+// codes round-half-even(x * id), the code sum of every 16 values (tables.cpp:200-213)
+__device__ __forceinline__ void q8k_block(const float *x, int lane, int8_t *q, float *d, int16_t *bsums) {
+    const float *v = x + 8 * lane;
+    float a[8], amax = 0.0f;
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+        a[u] = v[u];
+        amax = fmaxf(amax, fabsf(a[u]));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float dd = __fdiv_rn(amax, 127.0f), id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
+    int s = 0;
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+        const int c = __float2int_rn(__fmul_rn(a[u], id));
+        q[8 * lane + u] = (int8_t) c;
+        s += c;
+    }
+    s += __shfl_xor_sync(0xffffffffu, s, 1);   // lanes 2m, 2m+1 hold the 16 values of sum m
+    if ((lane & 1) == 0) bsums[lane / 2] = (int16_t) s;
+    if (lane == 0) *d = dd;
+}
+
 // k_final: the last post-norm and the output norm without word scores (seoul.cpp:473-477), one CTA per column;
-// ends the step (position update)
+// ends the step (position update). With a Q6_K word table it also cuts the hidden state per 256 values for the
+// word-score launch that follows (k_q6k_head), which then ends the step.
 // ---------------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) k_final(const __grid_constant__ FinalArgs a) {
     extern __shared__ __align__(16) uint8_t smf[];
@@ -48,6 +73,20 @@ __global__ void __launch_bounds__(256) k_final(const __grid_constant__ FinalArgs
     }
     __syncthreads();
     const float sc = red[1];
+    if (a.q8k_q) {   // Q6_K word table: keep the hidden state, cut it per 256 values (one warp per block)
+        __syncthreads();
+        for (int i = threadIdx.x; i < E; i += blockDim.x) {
+            v[i] = __fmul_rn(__fmul_rn(v[i], sc), a.out_norm[i]);
+            if (col.hid_out) col.hid_out[i] = v[i];
+        }
+        __syncthreads();
+        const int lane = threadIdx.x & 31;
+        for (int j = threadIdx.x >> 5; j < E / 256; j += blockDim.x >> 5)
+            q8k_block(v + 256 * j, lane, a.q8k_q + (size_t) c * E + 256 * j, a.q8k_d + (size_t) c * (E / 256) + j,
+                      a.q8k_b + (size_t) c * (E / 16) + 16 * j);
+        if (trace && threadIdx.x == 0) trace[14] = global_ns();
+        return;   // the word-score launch advances the position after its pick
+    }
     if (col.hid_out)
         for (int i = threadIdx.x; i < E; i += blockDim.x) col.hid_out[i] = __fmul_rn(__fmul_rn(v[i], sc), a.out_norm[i]);
     __syncthreads();
@@ -354,26 +393,7 @@ __global__ void k_q8_cut(const float *x, int n, int8_t *q, float *d, float *s) {
 __global__ void k_q8k_cut(const float *x, int n, int8_t *q, float *d, int16_t *bsums) {
     const int lane = threadIdx.x & 31, j = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (j >= n / 256) return;   // whole warps only
-    const float *v = x + 256 * j + 8 * lane;
-    float a[8], amax = 0.0f;
-#pragma unroll
-    for (int u = 0; u < 8; u++) {
-        a[u] = v[u];
-        amax = fmaxf(amax, fabsf(a[u]));
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float dd = __fdiv_rn(amax, 127.0f), id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
-    int s = 0;
-#pragma unroll
-    for (int u = 0; u < 8; u++) {
-        const int c = __float2int_rn(__fmul_rn(a[u], id));
-        q[256 * j + 8 * lane + u] = (int8_t) c;
-        s += c;
-    }
-    s += __shfl_xor_sync(0xffffffffu, s, 1);   // lanes 2m, 2m+1 hold the 16 values of sum m
-    if ((lane & 1) == 0) bsums[16 * j + lane / 2] = (int16_t) s;
-    if (lane == 0) d[j] = dd;
+    q8k_block(x + 256 * j, lane, q + 256 * j, d + j, bsums + 16 * j);
 }
 
 // the word score of one Q6_K row (210 bytes per 256 values: ql[128], qh[64], int8 scales[16], fp16 d) for a q8k
@@ -430,6 +450,109 @@ __global__ void __launch_bounds__(256) k_q6k_scores(const uint8_t *W, int rows, 
     const float r2 = __fadd_rn(r4, __shfl_down_sync(0xffffffffu, r4, 2));     // m < 2: r_m + r_{m+2}
     const float r1 = __fadd_rn(r2, __shfl_down_sync(0xffffffffu, r2, 1));     // m = 0: (r0 + r2) + (r1 + r3)
     if (act && m == 0) out[r0 + rl] = r1;
+}
+// the word scores of a Q6_K word table for ncol inputs (each cut per 256 values) into each column's logits (when it
+// has them), with imi's greedy pick (the first maximum, the lowest id on ties: the keys of the Q4_0 word-table read),
+// each CTA's best key combined by atomicMax in the conversation record; the last CTA to finish ends the step as the
+// Q4_0 word-table read does (next token, pick, position). Rows staged as in k_q6k_scores.
+__global__ void __launch_bounds__(256) k_q6k_head(const __grid_constant__ Q6HeadArgs a) {
+    extern __shared__ __align__(16) uint8_t smq[];
+    __shared__ unsigned long long wbest[8][MV_MAX_COLS];
+    __shared__ int last_cta;
+    const int tid = threadIdx.x, nb = a.nb, nc = a.ncol, rpc = blockDim.x / 8;
+    unsigned long long *trace = a.trace ? a.trace + (size_t) blockIdx.x * MV_TRACE : nullptr;
+    if (trace && tid == 0) trace[0] = global_ns();
+    pdl_trigger();
+    int8_t *xs = (int8_t *) smq;                       // [c][256 nb]
+    uint8_t *tile = smq + (size_t) 256 * nb * nc;
+    const int r0 = blockIdx.x * rpc, nr = min(rpc, a.rows - r0);
+    const size_t rb = (size_t) nb * 210, bytes = (size_t) nr * rb;
+    const uint8_t *src = a.W + (size_t) r0 * rb;   // the table does not depend on the launches in flight
+    if (((uintptr_t) src & 15) == 0 && (bytes & 15) == 0) {
+        for (size_t i = tid; i < bytes / 16; i += blockDim.x) ((uint4 *) tile)[i] = __ldcs(((const uint4 *) src) + i);
+    } else {
+        for (size_t i = tid; i < bytes / 2; i += blockDim.x) ((uint16_t *) tile)[i] = ((const uint16_t *) src)[i];
+    }
+    pdl_wait();
+    if (trace && tid == 0) trace[1] = global_ns();
+    for (int i = tid; i < 16 * nb * nc; i += blockDim.x) ((uint4 *) xs)[i] = ((const uint4 *) a.xq)[i];
+    __syncthreads();
+    const int rl = tid >> 3, m = tid & 7, warp = tid >> 5, lane = tid & 31;
+    const bool act = rl < nr;
+    const uint8_t *row = tile + (size_t) (act ? rl : 0) * rb;
+    for (int c = 0; c < nc; c++) {
+        const int8_t *x0 = xs + (size_t) c * 256 * nb;
+        const float *xd = a.xd + (size_t) c * nb;
+        const int16_t *xb = a.xb + (size_t) c * 16 * nb;
+        float acc = 0.0f;
+        for (int i = 0; i < nb; i++) {
+            const uint8_t *b = row + (size_t) i * 210;
+            const int8_t *sc = (const int8_t *) (b + 192);
+            int lanesum = 0;
+#pragma unroll
+            for (int n = 0; n < 2; n++) {
+                const uint8_t *qh = b + 128 + 32 * n + 4 * m;
+                const uint32_t qh4 = (uint32_t) qh[0] | ((uint32_t) qh[1] << 8) | ((uint32_t) qh[2] << 16) | ((uint32_t) qh[3] << 24);
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const uint8_t *ql = b + 64 * n + (k & 1) * 32 + 4 * m;
+                    const uint32_t ql4 = (uint32_t) ql[0] | ((uint32_t) ql[1] << 8) | ((uint32_t) ql[2] << 16) | ((uint32_t) ql[3] << 24);
+                    const uint32_t lo = (k < 2 ? ql4 : ql4 >> 4) & 0x0f0f0f0fu;
+                    const uint32_t codes = lo | (((qh4 >> (2 * k)) & 0x03030303u) << 4);
+                    const int x4 = *(const int *) (x0 + 256 * i + 128 * n + 32 * k + 4 * m);
+                    lanesum += __dp4a((int) codes, x4, 0) * (int) sc[8 * n + 2 * k + (m >= 4)];
+                }
+            }
+            const int16_t *bs = xb + 16 * i;
+            lanesum -= 32 * ((int) sc[2 * m] * bs[2 * m] + (int) sc[2 * m + 1] * bs[2 * m + 1]);
+            const float s = __fmul_rn(h2f((uint16_t) (b[208] | (b[209] << 8))), xd[i]);
+            acc = __fmaf_rn(s, __int2float_rn(lanesum), acc);
+        }
+        const float r4 = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
+        const float r2 = __fadd_rn(r4, __shfl_down_sync(0xffffffffu, r4, 2));
+        const float r1 = __fadd_rn(r2, __shfl_down_sync(0xffffffffu, r2, 1));
+        unsigned long long key = 0ull;
+        if (act && m == 0) {
+            const int id = r0 + rl;
+            float *lg = a.cols_d[c].logits;
+            if (lg) lg[id] = r1;
+            key = amax_key(r1, id);
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const unsigned long long u = __shfl_xor_sync(0xffffffffu, key, o);
+            key = u > key ? u : key;
+        }
+        if (lane == 0) wbest[warp][c] = key;
+    }
+    __syncthreads();
+    if (tid < nc) {
+        unsigned long long k = 0ull;
+        for (int w = 0; w < (int) (blockDim.x >> 5); w++) k = wbest[w][tid] > k ? wbest[w][tid] : k;
+        atomicMax(&a.cols_d[tid].s->amax, k);
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last_cta = atomicAdd(a.done, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (last_cta && tid < nc) {
+        __threadfence();
+        const Col col = a.cols_d[tid];
+        const unsigned long long k = atomicExch(&col.s->amax, 0ull);
+        const int id = (int) (0xffffffffu - (uint32_t) (k & 0xffffffffu));
+        col.s->next_token = id;
+        col.s->amax_val = amax_val(k);
+        if (col.picks) col.picks[col.s->pos + col.off] = id;
+        if (col.pos_inc) atomicAdd(&col.s->pos, col.pos_inc);
+    }
+    if (last_cta && tid == 0) *a.done = 0;
+    if (trace && tid == 0) trace[14] = global_ns();
+}
+// rows per CTA of the Q6_K head for nc inputs: a multiple of 4, at most 32, within 220 KB of shared memory
+__host__ __device__ inline int q6k_head_rows_per_cta(int nb, int nc) {
+    const long room = 220L * 1024 - 256L * nb * nc, per = 210L * nb;
+    const long r = room > 0 ? room / per : 0;
+    return (int) ((r > 32 ? 32 : r) / 4 * 4);
 }
 // rows per CTA of k_q6k_scores: a multiple of 4 (whole warps), at most 32, the staged rows within 220 KB (0: too wide)
 __host__ __device__ inline int q6k_rows_per_cta(int nb) {

@@ -18,6 +18,9 @@ cudaError_t launch_q8_cut(const float *x, int n, int8_t *q, float *d, float *s, 
 cudaError_t launch_q8k_cut(const float *x, int n, int8_t *q, float *d, int16_t *bsums, cudaStream_t st);
 cudaError_t launch_q6k_scores(const uint8_t *W, int rows, int nb, const int8_t *xq, const float *xd,
                               const int16_t *bsums, float *out, cudaStream_t st);
+// the Q6_K word table inside a step: word scores for ncol inputs, the greedy pick and the end of the step
+cudaError_t launch_q6k_head(const Q6HeadArgs &a, cudaStream_t st, bool pdl);
+int q6k_head_ctas(int rows, int nb, int nc);   // its grid (0: rows too wide)
 // GGUF Q4_0 rows (device) into the table kernel's row layout (device), on stream st
 cudaError_t launch_q4_repack(const uint8_t *src, int rows, int nb, uint8_t *dst, cudaStream_t st);
 }  // namespace imi

@@ -52,6 +52,25 @@ __device__ __forceinline__ float4 word_chunk(const uint8_t *row, int cols, int q
                        __fmul_rn(d, (float) ((int) ((w >> (16 + sh)) & 15) - 8)),
                        __fmul_rn(d, (float) ((int) ((w >> (24 + sh)) & 15) - 8)));
 }
+// the same for a Q6_K word row (imi_q6k_dequant_row, tables.cpp:216-233): value = d * scale * (code - 32), left to
+// right; code of value t of a block = low 4 bits from ql, high 2 from qh
+__device__ __forceinline__ float4 word_chunk_q6k(const uint8_t *row, int q) {
+    const uint8_t *b = row + (size_t) (q >> 6) * 210;
+    const int t = (4 * q) & 255, n = t >> 7, k = (t & 127) >> 5, l = t & 31;
+    const float d = h2f((uint16_t) (b[208] | (b[209] << 8)));
+    const float ds = __fmul_rn(d, (float) (int8_t) b[192 + (t >> 4)]);
+    const uint8_t *ql = b + 64 * n + (k & 1) * 32 + l, *qh = b + 128 + 32 * n + l;
+    float v[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+        const int lo = k < 2 ? (ql[u] & 15) : (ql[u] >> 4), code = lo | (((qh[u] >> (2 * k)) & 3) << 4);
+        v[u] = __fmul_rn(ds, (float) (code - 32));
+    }
+    return make_float4(v[0], v[1], v[2], v[3]);
+}
+__device__ __forceinline__ float4 word_row_chunk(const MvArgs &a, const uint8_t *row, int cols, int q) {
+    return a.emb_q6k ? word_chunk_q6k(row, q) : word_chunk(row, cols, q);
+}
 __device__ __forceinline__ float4 mul4(float4 a, float4 b) {
     return make_float4(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y), __fmul_rn(a.z, b.z), __fmul_rn(a.w, b.w));
 }
@@ -120,7 +139,7 @@ __device__ __forceinline__ void table_preload(const MvArgs &a, const MvPlan &P, 
             const int tok = pc[c].tok;
             if (tok >= 0) {
                 const uint8_t *row = a.emb + (size_t) tok * a.emb_row_bytes;
-                for (int q = tid; q < nq; q += MV_THREADS) ((float4 *) (vb + c * VL))[q] = word_chunk(row, E, q);
+                for (int q = tid; q < nq; q += MV_THREADS) ((float4 *) (vb + c * VL))[q] = word_row_chunk(a, row, E, q);
             } else if (tok == -1) {
                 for (int q = tid; q < nq; q += MV_THREADS) ((float4 *) (vb + c * VL))[q] = ((const float4 *) pc[c].embd)[q];
             }
@@ -244,7 +263,7 @@ __device__ void table_prologue(const MvArgs &a, const MvPlan &P, uint8_t *sm, co
         for (int c = 0; c < nc; c++) {
             if (pc[c].tok != -2) continue;   // the greedy pick of the conversation's last step
             const uint8_t *row = a.emb + (size_t) pc[c].s->next_token * a.emb_row_bytes;
-            for (int q = tid; q < nq; q += MV_THREADS) ((float4 *) (vb + c * VL))[q] = word_chunk(row, E, q);
+            for (int q = tid; q < nq; q += MV_THREADS) ((float4 *) (vb + c * VL))[q] = word_row_chunk(a, row, E, q);
         }
     }
     __syncthreads();

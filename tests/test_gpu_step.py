@@ -234,3 +234,36 @@ def test_seoul_greedy_128_steps(seoul_path):
         worst = rel(s.logits, o.logits)
         print(f"seoul: 128 greedy picks identical, last-step score difference {worst:.3g}")
         assert worst <= TOL
+
+
+def test_q6k_word_table_steps_match_oracle():
+    """A model with the product's own Q6_K word table (lookup of given and greedy tokens, word scores, the pick):
+    prefill, single steps and a riding step against the oracle (itself pinned to the reference's own Q6_K code), bit
+    for bit."""
+    path = synth.cached_gguf("tiny_q6k")
+    o, e = oracle.Oracle(path, n_ctx=96), nb.Engine(path, n_ctx=96)
+    g, g2 = e.new_state(), e.new_state()
+    ids = synth.random_ids(24, e.n_vocab, 11)
+    o.step_batch(tokens=ids[:16], want_logits=True)
+    g.step_batch(tokens=ids[:16], want_logits=True)
+    assert np.array_equal(bits(g.logits), bits(o.logits))
+    for t in ids[16:]:
+        o.step(int(t))
+        g.step(int(t))
+        assert np.array_equal(bits(g.hidden), bits(o.hidden)) and np.array_equal(bits(g.logits), bits(o.logits))
+        assert g.argmax()[0] == int(np.argmax(o.logits))
+    # greedy on the device: each step reads its own previous pick
+    picks = nb.greedy([g], 4)[:, 0]   # picks[k]: the pick step k makes after reading the previous one
+    for k in range(4):
+        o.step(int(np.argmax(o.logits)))
+        assert int(picks[k]) == int(np.argmax(o.logits))
+    assert np.array_equal(bits(g.logits), bits(o.logits))
+    # riding: a second conversation beside the first, each with the numbers of its own step
+    o2 = o.new_state()
+    for t in ids[:3]:
+        o2.step(int(t), want_logits=True)
+        g2.step(int(t))
+    nb.step2(g, int(ids[0]), None, True, g2, int(ids[1]), None, True)
+    o.step(int(ids[0]))
+    o2.step(int(ids[1]), want_logits=True)
+    assert np.array_equal(bits(g.logits), bits(o.logits)) and np.array_equal(bits(g2.logits), bits(o2.logits))
