@@ -480,35 +480,49 @@ __global__ void __launch_bounds__(256) k_q6k_head(const __grid_constant__ Q6Head
     const int rl = tid >> 3, m = tid & 7, warp = tid >> 5, lane = tid & 31;
     const bool act = rl < nr;
     const uint8_t *row = tile + (size_t) (act ? rl : 0) * rb;
-    for (int c = 0; c < nc; c++) {
-        const int8_t *x0 = xs + (size_t) c * 256 * nb;
-        const float *xd = a.xd + (size_t) c * nb;
-        const int16_t *xb = a.xb + (size_t) c * 16 * nb;
-        float acc = 0.0f;
-        for (int i = 0; i < nb; i++) {
-            const uint8_t *b = row + (size_t) i * 210;
-            const int8_t *sc = (const int8_t *) (b + 192);
+    // every block's codes unpacked once and used for all the columns (each column its own integer lane and chain)
+    float acc[MV_MAX_COLS];
+#pragma unroll
+    for (int c = 0; c < MV_MAX_COLS; c++) acc[c] = 0.0f;
+    for (int i = 0; i < nb; i++) {
+        const uint8_t *b = row + (size_t) i * 210;
+        const int8_t *sc = (const int8_t *) (b + 192);
+        uint32_t codes[8];
+        int scl[8];
+#pragma unroll
+        for (int n = 0; n < 2; n++) {
+            const uint8_t *qh = b + 128 + 32 * n + 4 * m;
+            const uint32_t qh4 = (uint32_t) qh[0] | ((uint32_t) qh[1] << 8) | ((uint32_t) qh[2] << 16) | ((uint32_t) qh[3] << 24);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const uint8_t *ql = b + 64 * n + (k & 1) * 32 + 4 * m;
+                const uint32_t ql4 = (uint32_t) ql[0] | ((uint32_t) ql[1] << 8) | ((uint32_t) ql[2] << 16) | ((uint32_t) ql[3] << 24);
+                codes[4 * n + k] = ((k < 2 ? ql4 : ql4 >> 4) & 0x0f0f0f0fu) | (((qh4 >> (2 * k)) & 0x03030303u) << 4);
+                scl[4 * n + k] = sc[8 * n + 2 * k + (m >= 4)];
+            }
+        }
+        const float dblk = h2f((uint16_t) (b[208] | (b[209] << 8)));
+        const int s2m = sc[2 * m], s2m1 = sc[2 * m + 1];
+#pragma unroll
+        for (int c = 0; c < MV_MAX_COLS; c++) {
+            if (c >= nc) break;
+            const int8_t *x0 = xs + (size_t) c * 256 * nb + 256 * i;
             int lanesum = 0;
 #pragma unroll
-            for (int n = 0; n < 2; n++) {
-                const uint8_t *qh = b + 128 + 32 * n + 4 * m;
-                const uint32_t qh4 = (uint32_t) qh[0] | ((uint32_t) qh[1] << 8) | ((uint32_t) qh[2] << 16) | ((uint32_t) qh[3] << 24);
-#pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    const uint8_t *ql = b + 64 * n + (k & 1) * 32 + 4 * m;
-                    const uint32_t ql4 = (uint32_t) ql[0] | ((uint32_t) ql[1] << 8) | ((uint32_t) ql[2] << 16) | ((uint32_t) ql[3] << 24);
-                    const uint32_t lo = (k < 2 ? ql4 : ql4 >> 4) & 0x0f0f0f0fu;
-                    const uint32_t codes = lo | (((qh4 >> (2 * k)) & 0x03030303u) << 4);
-                    const int x4 = *(const int *) (x0 + 256 * i + 128 * n + 32 * k + 4 * m);
-                    lanesum += __dp4a((int) codes, x4, 0) * (int) sc[8 * n + 2 * k + (m >= 4)];
-                }
+            for (int g = 0; g < 8; g++) {
+                const int x4 = *(const int *) (x0 + 128 * (g >> 2) + 32 * (g & 3) + 4 * m);
+                lanesum += __dp4a((int) codes[g], x4, 0) * scl[g];   // codes <= 63: signed is exact
             }
-            const int16_t *bs = xb + 16 * i;
-            lanesum -= 32 * ((int) sc[2 * m] * bs[2 * m] + (int) sc[2 * m + 1] * bs[2 * m + 1]);
-            const float s = __fmul_rn(h2f((uint16_t) (b[208] | (b[209] << 8))), xd[i]);
-            acc = __fmaf_rn(s, __int2float_rn(lanesum), acc);
+            const int16_t *bs = a.xb + (size_t) c * 16 * nb + 16 * i;
+            lanesum -= 32 * (s2m * bs[2 * m] + s2m1 * bs[2 * m + 1]);
+            const float s = __fmul_rn(dblk, a.xd[(size_t) c * nb + i]);
+            acc[c] = __fmaf_rn(s, __int2float_rn(lanesum), acc[c]);
         }
-        const float r4 = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
+    }
+#pragma unroll
+    for (int c = 0; c < MV_MAX_COLS; c++) {
+        if (c >= nc) break;
+        const float r4 = __fadd_rn(acc[c], __shfl_down_sync(0xffffffffu, acc[c], 4));
         const float r2 = __fadd_rn(r4, __shfl_down_sync(0xffffffffu, r4, 2));
         const float r1 = __fadd_rn(r2, __shfl_down_sync(0xffffffffu, r2, 1));
         unsigned long long key = 0ull;

@@ -16,7 +16,7 @@ from __future__ import annotations
 
 import os
 import struct
-from dataclasses import dataclass, field
+from dataclasses import dataclass, replace, field
 
 import numpy as np
 
@@ -70,7 +70,11 @@ WIDE_HEADS = Shape(n_embd=1024, n_layer=4, attn_layers=(1, 2, 3), n_head=8, n_he
 TINY_Q6K = Shape(n_embd=512, n_layer=4, attn_layers=(1, 3), n_head=8, n_head_kv=2, head_dim=64, n_ff=1024,
                  n_vocab=1003, word_q6k=True)
 
-SHAPES = {"seoul": SEOUL, "tiny": TINY, "small": SMALL, "wide_heads": WIDE_HEADS, "tiny_q6k": TINY_Q6K}
+# the Seoul shape with the product's own Q6_K word table
+SEOUL_Q6K = replace(SEOUL, word_q6k=True)
+
+SHAPES = {"seoul": SEOUL, "tiny": TINY, "small": SMALL, "wide_heads": WIDE_HEADS, "tiny_q6k": TINY_Q6K,
+          "seoul_q6k": SEOUL_Q6K}
 
 
 def _q4_0(rng: np.random.Generator, rows: int, cols: int) -> np.ndarray:
