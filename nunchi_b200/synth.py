@@ -21,7 +21,7 @@ from dataclasses import dataclass, replace, field
 import numpy as np
 
 # ggml type ids used here
-GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q6_K = 0, 1, 2, 14
+GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q4_1, GGML_Q6_K = 0, 1, 2, 3, 14
 # gguf value types
 _U32, _I32, _F32, _BOOL, _STR, _ARR, _U64 = 4, 5, 6, 7, 8, 9, 10
 ALIGN = 32
@@ -44,6 +44,7 @@ class Shape:
     swa_layers: tuple = ()                        # attention layers that use the window
     rope_freqs: bool = False                      # write a rope_freqs.weight table
     word_q6k: bool = False                        # the word table in Q6_K (the product's own format) instead of Q4_0
+    tables_q41: bool = False                      # the layer tables in Q4_1 (d and m per block) instead of Q4_0
 
     @property
     def kvd(self) -> int:
@@ -70,11 +71,14 @@ WIDE_HEADS = Shape(n_embd=1024, n_layer=4, attn_layers=(1, 2, 3), n_head=8, n_he
 TINY_Q6K = Shape(n_embd=512, n_layer=4, attn_layers=(1, 3), n_head=8, n_head_kv=2, head_dim=64, n_ff=1024,
                  n_vocab=1003, word_q6k=True)
 
+# TINY with Q4_1 layer tables (a per-block minimum besides the scale)
+TINY_Q41 = Shape(n_embd=512, n_layer=4, attn_layers=(1, 3), n_head=8, n_head_kv=2, head_dim=64, n_ff=1024,
+                 n_vocab=1003, tables_q41=True)
 # the Seoul shape with the product's own Q6_K word table
 SEOUL_Q6K = replace(SEOUL, word_q6k=True)
 
 SHAPES = {"seoul": SEOUL, "tiny": TINY, "small": SMALL, "wide_heads": WIDE_HEADS, "tiny_q6k": TINY_Q6K,
-          "seoul_q6k": SEOUL_Q6K}
+          "seoul_q6k": SEOUL_Q6K, "tiny_q41": TINY_Q41}
 
 
 def _q4_0(rng: np.random.Generator, rows: int, cols: int) -> np.ndarray:
@@ -99,6 +103,19 @@ def _q6k(rng: np.random.Generator, rows: int, cols: int) -> np.ndarray:
     return out
 
 
+def _q4_1(rng: np.random.Generator, rows: int, cols: int) -> np.ndarray:
+    """A Q4_1 table [rows][cols/32 blocks] of 20-byte blocks: fp16 d, fp16 m (about -8 d: values d*code + m centred),
+    16 bytes of packed codes."""
+    assert cols % 32 == 0
+    nblk = rows * (cols // 32)
+    out = np.empty((nblk, 20), np.uint8)
+    d = rng.uniform(0.002, 0.01, nblk).astype(np.float32)
+    out[:, :2] = d.astype(np.float16).view(np.uint8).reshape(nblk, 2)
+    out[:, 2:4] = (-8.0 * d * rng.uniform(0.8, 1.2, nblk)).astype(np.float16).view(np.uint8).reshape(nblk, 2)
+    out[:, 4:] = rng.integers(0, 256, (nblk, 16), dtype=np.uint8)
+    return out
+
+
 def _norm(rng, n):
     return (1.0 + 0.1 * rng.standard_normal(n)).astype(np.float32)
 
@@ -107,6 +124,7 @@ def tensors(shape: Shape, seed: int = 0):
     """Yield (name, ggml_type, ne (fastest first), bytes) in file order, drawing from one seeded generator."""
     rng = np.random.default_rng(seed)
     E, F = shape.n_embd, shape.n_ff
+    QT, qt = (GGML_Q4_1, _q4_1) if shape.tables_q41 else (GGML_Q4_0, _q4_0)   # the layer tables' format
     if shape.word_q6k:
         yield "token_embd.weight", GGML_Q6_K, (E, shape.n_vocab), _q6k(rng, shape.n_vocab, E)
     else:
@@ -120,24 +138,24 @@ def tensors(shape: Shape, seed: int = 0):
         yield p + "attn_norm.weight", GGML_F32, (E,), _norm(rng, E)
         if shape.is_attn(il):
             H, D, kvd = shape.n_head, shape.head_dim, shape.kvd
-            yield p + "attn_q.weight", GGML_Q4_0, (E, H * D), _q4_0(rng, H * D, E)
-            yield p + "attn_k.weight", GGML_Q4_0, (E, kvd), _q4_0(rng, kvd, E)
-            yield p + "attn_v.weight", GGML_Q4_0, (E, kvd), _q4_0(rng, kvd, E)
-            yield p + "attn_gate.weight", GGML_Q4_0, (E, H), _q4_0(rng, H, E)
-            yield p + "attn_output.weight", GGML_Q4_0, (H * D, E), _q4_0(rng, E, H * D)
+            yield p + "attn_q.weight", QT, (E, H * D), qt(rng, H * D, E)
+            yield p + "attn_k.weight", QT, (E, kvd), qt(rng, kvd, E)
+            yield p + "attn_v.weight", QT, (E, kvd), qt(rng, kvd, E)
+            yield p + "attn_gate.weight", QT, (E, H), qt(rng, H, E)
+            yield p + "attn_output.weight", QT, (H * D, E), qt(rng, E, H * D)
             yield p + "attn_q_norm.weight", GGML_F32, (D,), _norm(rng, D)
             yield p + "attn_k_norm.weight", GGML_F32, (D,), _norm(rng, D)
         else:
             K = shape.l_cache
             taps = (0.1 * rng.standard_normal((E, K))).astype(np.float32)   # [channel][tap]
             yield p + "shortconv.conv.weight", GGML_F32, (K, E), taps
-            yield p + "shortconv.in_proj.weight", GGML_Q4_0, (E, 3 * E), _q4_0(rng, 3 * E, E)
-            yield p + "shortconv.out_proj.weight", GGML_Q4_0, (E, E), _q4_0(rng, E, E)
+            yield p + "shortconv.in_proj.weight", QT, (E, 3 * E), qt(rng, 3 * E, E)
+            yield p + "shortconv.out_proj.weight", QT, (E, E), qt(rng, E, E)
         yield p + "post_attention_norm.weight", GGML_F32, (E,), _norm(rng, E)
         yield p + "ffn_norm.weight", GGML_F32, (E,), _norm(rng, E)
-        yield p + "ffn_gate.weight", GGML_Q4_0, (E, F), _q4_0(rng, F, E)
-        yield p + "ffn_up.weight", GGML_Q4_0, (E, F), _q4_0(rng, F, E)
-        yield p + "ffn_down.weight", GGML_Q4_0, (F, E), _q4_0(rng, E, F)
+        yield p + "ffn_gate.weight", QT, (E, F), qt(rng, F, E)
+        yield p + "ffn_up.weight", QT, (E, F), qt(rng, F, E)
+        yield p + "ffn_down.weight", QT, (F, E), qt(rng, E, F)
         yield p + "post_ffw_norm.weight", GGML_F32, (E,), _norm(rng, E)
 
 

@@ -15,7 +15,7 @@
 static char g_err[256];
 const char *or_error(void) { return g_err; }
 
-typedef struct { const uint8_t *w; int rows, cols; size_t row_bytes; } or_table;   /* GGUF Q4_0 rows */
+typedef struct { const uint8_t *w; int rows, cols; size_t row_bytes; int has_m; } or_table;   /* GGUF Q4_0 / Q4_1 rows */
 
 typedef struct {
     const float *attn_norm, *post_attn_norm, *ffn_norm, *post_ffn_norm, *conv_w, *q_norm, *k_norm;
@@ -134,10 +134,24 @@ static float row_dot(const uint8_t *row, int nb, const int8_t *xq, const float *
     }
     return fmaf(-8.0f, cor, acc);
 }
+/* one row of group_avx2<true> (Q4_1 blocks: d, m, 16 code bytes): the same acc chain, cor = fma(m, s_j, cor), and
+ * acc + cor with one rounding (tables.cpp:136-142) */
+static float row_dot_m(const uint8_t *row, int nb, const int8_t *xq, const float *xd, const float *xs) {
+    float acc = 0.0f, cor = 0.0f;
+    for (int j = 0; j < nb; j++) {
+        const uint8_t *blk = row + 20 * (size_t) j;
+        uint16_t dh, mh; memcpy(&dh, blk, 2); memcpy(&mh, blk + 2, 2);
+        acc = fmaf((float) block_dot(blk + 2, xq + 32 * j), or_h2f(dh) * xd[j], acc);   /* codes at blk + 4 */
+        cor = fmaf(or_h2f(mh), xs[j], cor);
+    }
+    return acc + cor;
+}
 static void matvec(const or_table *W, const q8v *x, float *out, int nt) {
     const int nb = W->cols / 32;
     #pragma omp parallel for num_threads(nt) schedule(static)
-    for (int r = 0; r < W->rows; r++) out[r] = row_dot(W->w + (size_t) r * W->row_bytes, nb, x->q, x->d, x->s);
+    for (int r = 0; r < W->rows; r++)
+        out[r] = W->has_m ? row_dot_m(W->w + (size_t) r * W->row_bytes, nb, x->q, x->d, x->s)
+                          : row_dot(W->w + (size_t) r * W->row_bytes, nb, x->q, x->d, x->s);
 }
 void or_block_dots(const uint8_t *q4, int rows, int cols, const int8_t *xq, int32_t *s) {
     const int nb = cols / 32;
@@ -190,8 +204,12 @@ static inline float silu(float x) { return x / (1.0f + expf(-x)); }   /* seoul.c
 static int table(const gm_file *f, const char *name, or_table *t) {
     const gm_tensor *g = gm_find(f, name);
     if (!g) { snprintf(g_err, sizeof g_err, "missing tensor %s", name); return -1; }
-    if (g->type != GM_T_Q4_0) { snprintf(g_err, sizeof g_err, "%s: only Q4_0 tables are read here", name); return -1; }
+    if (g->type != GM_T_Q4_0 && g->type != GM_T_Q4_1) {
+        snprintf(g_err, sizeof g_err, "%s: only Q4_0 / Q4_1 tables are read here", name);
+        return -1;
+    }
     t->w = g->data; t->cols = (int) g->ne[0]; t->rows = (int) g->ne[1]; t->row_bytes = g->row_bytes;
+    t->has_m = g->type == GM_T_Q4_1;
     return 0;
 }
 static const float *f32(const gm_file *f, const char *name, int required) {

@@ -213,3 +213,19 @@ def test_q6k_word_table_steps_match_reference_live():
         o.step(int(t))
         r.step(int(t))
         assert np.array_equal(bits(o.hidden), bits(r.hidden)) and np.array_equal(bits(o.logits), bits(r.logits))
+
+
+@needs_ref
+def test_q41_layer_tables_steps_match_reference_live():
+    """Q4_1 layer tables (a minimum m per block: out = acc + cor with cor = fma(m, s_j, cor), group_avx2<true>,
+    tables.cpp:127-143): the oracle's prefill and steps against the reference's own code, bit for bit."""
+    path = synth.cached_gguf("tiny_q41")
+    o, r = oracle.Oracle(path, n_ctx=96), oracle.Reference(path, n_ctx=96)
+    ids = synth.random_ids(24, o.n_vocab, 7)
+    o.step_batch(tokens=ids[:16], want_logits=True)
+    r.step_batch(tokens=ids[:16], want_logits=True)
+    assert np.array_equal(bits(o.logits), bits(r.logits))
+    for t in ids[16:]:
+        o.step(int(t))
+        r.step(int(t))
+        assert np.array_equal(bits(o.hidden), bits(r.hidden)) and np.array_equal(bits(o.logits), bits(r.logits))
