@@ -77,6 +77,7 @@ struct MvArgs {
     const uint8_t *emb;        // word table (same row layout) for P_EMBED_NORM
     int emb_row_bytes;
     int emb_q6k;               // 1: the word table is Q6_K (rows of 210-byte blocks per 256 values, as in the file)
+    int has_m;                 // 1: Q4_1 rows (codes | scales | minimums); the result is acc + cor, cor over the minimums
     const float *conv_w;       // [d_conv+1][n_embd]
     int d_conv, conv_layer, n_embd;
     int ring_layer;            // >= 0: write the conv memory slots of this layer from ring_src (bcx rows); in P_CONV
@@ -163,7 +164,8 @@ struct MvPlan {
     int stage, bar, xq, xd, xs, fs, dd, vb, vo, ab, pc, red, total;
 };
 __host__ __device__ inline int align_up(int x, int a) { return (x + a - 1) / a * a; }
-__host__ __device__ inline MvPlan mv_plan(int cols, int sr, int nc, int vb_len, int ab_len, int ns) {
+// hm: Q4_1 rows (a minimum per block besides the scale): the scale buffers hold the minimums in a second half
+__host__ __device__ inline MvPlan mv_plan(int cols, int sr, int nc, int vb_len, int ab_len, int ns, int hm = 0) {
     MvPlan p;
     const int nb = cols / 32, ld = nb + 4;   // row strides: 16-byte aligned, conflict-free for vector loads
     int o = 0;
@@ -175,7 +177,7 @@ __host__ __device__ inline MvPlan mv_plan(int cols, int sr, int nc, int vb_len, 
     // the prologue's vectors (vb) are dead before the first block dot is stored: they share the dot buffers' space
     const int u = o;
     p.fs = o;    o = align_up(o + MV_NBUF * 4 * nc * sr * ld, 16);
-    p.dd = o;    o = align_up(o + MV_NBUF * 2 * sr * ld, 16);
+    p.dd = o;    o = align_up(o + (hm ? 2 : 1) * MV_NBUF * 2 * sr * ld, 16);
     p.vo = o;
     p.vb = u;    o = o > align_up(u + 4 * nc * vb_len, 16) ? o : align_up(u + 4 * nc * vb_len, 16);
     p.ab = o;    o = align_up(o + 4 * nc * ab_len, 16);

@@ -46,6 +46,7 @@ constexpr int BATCH_GROUP = 64;   // step_batch checks the context per 64 positi
 struct TableRef {
     size_t off = 0;
     int rows = 0, cols = 0, row_bytes = 0;
+    bool has_m = false;   // Q4_1 rows: a minimum per block after the scales
 };
 struct LayerRef {
     bool conv = false, swa = false;
@@ -138,20 +139,28 @@ imi_cuda_engine::~imi_cuda_engine() {
 // ---------------------------------------------------------------------------------------------------------------
 namespace {
 
-// rows of Q4_0 tables, in order, into the engine's row layout: [cols/2 code bytes | cols/32 fp16 scales]. The code
-// bytes of block j keep the file's order (byte i: column i in the low nibble, column 16+i in the high one).
+// bytes of one table row in the engine's layout: Q4_0 [cols/2 code bytes | cols/32 fp16 scales], Q4_1 the same
+// followed by [cols/32 fp16 minimums]
+size_t engine_row_bytes(const gguf_tensor *t) { return (size_t) (t->ne[0] / 32) * (t->type == T_Q4_1 ? 20 : 18); }
+
+// rows of Q4_0 / Q4_1 tables, in order, into the engine's row layout. The code bytes of block j keep the file's order
+// (byte i: column i in the low nibble, column 16+i in the high one). File blocks: Q4_0 [d | 16 code bytes], Q4_1
+// [d | m | 16 code bytes] (ggml's block_q4_0 / block_q4_1).
 void repack_rows(uint8_t *dst, const std::vector<std::pair<const gguf_tensor *, int>> &rows) {
     for (size_t r = 0; r < rows.size(); r++) {
         const gguf_tensor *t = rows[r].first;
-        const int nb = (int) (t->ne[0] / 32);
+        const int nb = (int) (t->ne[0] / 32), hm = t->type == T_Q4_1, fb = hm ? 20 : 18;
         const uint8_t *src = t->data + (size_t) rows[r].second * t->row_bytes;
-        uint8_t *codes = dst + r * (size_t) nb * 18, *scales = codes + (size_t) nb * 16;
+        uint8_t *codes = dst + r * (size_t) nb * fb, *scales = codes + (size_t) nb * 16, *mins = scales + (size_t) nb * 2;
         for (int j = 0; j < nb; j++) {
-            memcpy(scales + 2 * j, src + 18 * j, 2);
-            memcpy(codes + 16 * j, src + 18 * j + 2, 16);
+            memcpy(scales + 2 * j, src + fb * j, 2);
+            if (hm) memcpy(mins + 2 * j, src + fb * j + 2, 2);
+            memcpy(codes + 16 * j, src + fb * j + 2 + 2 * hm, 16);
         }
     }
 }
+
+constexpr int T_Q4_ANY = -1;   // Loader::need: a layer table, Q4_0 or Q4_1
 
 struct Loader {
     const gguf_file &f;
@@ -169,7 +178,8 @@ struct Loader {
     const gguf_tensor *need(const std::string &name, int type) {
         const gguf_tensor *t = f.tensor(name);
         if (!t) { if (err.empty()) err = "missing tensor " + name; return nullptr; }
-        if (t->type != type || !t->data) {
+        const bool ok = type == T_Q4_ANY ? (t->type == T_Q4_0 || t->type == T_Q4_1) : t->type == type;
+        if (!ok || !t->data) {
             if (err.empty()) err = name + ": type " + std::to_string(t->type) + " is not read by this engine";
             return nullptr;
         }
@@ -188,10 +198,13 @@ struct Loader {
         const int cols = (int) rows[0].first->ne[0];
         for (auto &r : rows)
             if (r.first->ne[0] != cols) { err = r.first->name + ": widths of a stacked table differ"; return false; }
+        for (auto &r : rows)   // one layout per table: stacked tables share the rows' format
+            if (r.first->type != rows[0].first->type) { err = r.first->name + ": types of a stacked table differ"; return false; }
         if (cols % 256) { err = rows[0].first->name + ": width must be a multiple of 256"; return false; }
         tr.rows = (int) rows.size();
         tr.cols = cols;
-        tr.row_bytes = cols / 32 * 18;
+        tr.has_m = rows[0].first->type == T_Q4_1;
+        tr.row_bytes = (int) engine_row_bytes(rows[0].first);
         if (2 * tr.row_bytes > MV_STAGE_BYTES) { err = rows[0].first->name + ": rows too wide"; return false; }
         tr.off = take((size_t) tr.rows * tr.row_bytes);
         tables.push_back({ tr.off, rows });
@@ -272,7 +285,7 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
             if (cw->ne[0] != e->d_conv + 1 || cw->ne[1] != E) return fail(IMI_E_FORMAT, p + "shortconv.conv.weight: bad shape");
             Lr.conv_w = L.take((size_t) (e->d_conv + 1) * E * 4);
             L.convs.push_back({ Lr.conv_w, cw });
-            const gguf_tensor *ip = L.need(p + "shortconv.in_proj.weight", T_Q4_0), *op = L.need(p + "shortconv.out_proj.weight", T_Q4_0);
+            const gguf_tensor *ip = L.need(p + "shortconv.in_proj.weight", T_Q4_ANY), *op = L.need(p + "shortconv.out_proj.weight", T_Q4_ANY);
             if (!ip || !op) return fail(IMI_E_FORMAT, L.err);
             if (ip->ne[0] != E || ip->ne[1] != 3 * E || op->ne[0] != E || op->ne[1] != E) return fail(IMI_E_FORMAT, p + "shortconv: bad shapes");
             Loader::all_rows(rows, ip);
@@ -281,9 +294,9 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
             Loader::all_rows(rows, op);
             if (!L.table(Lr.out_proj, rows)) return fail(IMI_E_FORMAT, L.err);
         } else {
-            const gguf_tensor *q = L.need(p + "attn_q.weight", T_Q4_0), *k = L.need(p + "attn_k.weight", T_Q4_0),
-                              *v = L.need(p + "attn_v.weight", T_Q4_0), *g = L.need(p + "attn_gate.weight", T_Q4_0),
-                              *o = L.need(p + "attn_output.weight", T_Q4_0);
+            const gguf_tensor *q = L.need(p + "attn_q.weight", T_Q4_ANY), *k = L.need(p + "attn_k.weight", T_Q4_ANY),
+                              *v = L.need(p + "attn_v.weight", T_Q4_ANY), *g = L.need(p + "attn_gate.weight", T_Q4_ANY),
+                              *o = L.need(p + "attn_output.weight", T_Q4_ANY);
             if (!q || !k || !v || !g || !o) return fail(IMI_E_FORMAT, L.err);
             const int D = e->head_dim;
             e->n_head_kv = (int) (k->ne[1] / D);   // seoul.cpp:153
@@ -302,8 +315,8 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
                      swa_pat->arr[il] != 0;
             Lr.ai = e->n_attn++;
         }
-        const gguf_tensor *fg = L.need(p + "ffn_gate.weight", T_Q4_0), *fu = L.need(p + "ffn_up.weight", T_Q4_0),
-                          *fd = L.need(p + "ffn_down.weight", T_Q4_0);
+        const gguf_tensor *fg = L.need(p + "ffn_gate.weight", T_Q4_ANY), *fu = L.need(p + "ffn_up.weight", T_Q4_ANY),
+                          *fd = L.need(p + "ffn_down.weight", T_Q4_ANY);
         if (!fg || !fu || !fd) return fail(IMI_E_FORMAT, L.err);
         e->n_ff = (int) fg->ne[1];
         if (fu->ne[1] != e->n_ff || fg->ne[0] != E || fu->ne[0] != E || fd->ne[0] != e->n_ff || fd->ne[1] != E)
@@ -325,15 +338,14 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
 
     // upload: tables through a pinned staging buffer, small vectors directly
     size_t stage_max = 0;
-    for (auto &t : L.tables) stage_max = std::max(stage_max, t.second.size() * (size_t) (t.second[0].first->ne[0] / 32 * 18));
+    for (auto &t : L.tables) stage_max = std::max(stage_max, t.second.size() * engine_row_bytes(t.second[0].first));
     for (auto &c : L.convs) stage_max = std::max(stage_max, (size_t) (c.second->ne[0] * c.second->ne[1] * 4));
     uint8_t *stg = nullptr;
     CK(cudaMallocHost(&stg, stage_max));
     std::unique_ptr<uint8_t, decltype(&cudaFreeHost)> stg_guard(stg, cudaFreeHost);
     for (auto &t : L.tables) {
         repack_rows(stg, t.second);
-        CK(cudaMemcpy(e->w + t.first, stg, t.second.size() * (size_t) (t.second[0].first->ne[0] / 32 * 18),
-                      cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(e->w + t.first, stg, t.second.size() * engine_row_bytes(t.second[0].first), cudaMemcpyHostToDevice));
     }
     for (auto &c : L.convs) {   // file [channel][tap] -> [tap][channel] (seoul.cpp:136-141)
         const int K = (int) c.second->ne[0], C = (int) c.second->ne[1];
@@ -428,7 +440,7 @@ void plan_stages(MvArgs &a, int pro, int gran, int grid) {
     for (int sr = full; sr >= gran; sr -= gran) {
         const int nst = std::max(1, (rows_cta + sr - 1) / sr);
         for (int ns = std::min(MV_MAX_STAGES, nst); ns >= std::min(2, nst); ns--)
-            if (table_smem(pro, a.cols, sr, a.ncol, a.n_embd, a.ab_len, a.d_conv, ns) <= (size_t) MV_SMEM_BUDGET) {
+            if (table_smem(pro, a.cols, sr, a.ncol, a.n_embd, a.ab_len, a.d_conv, ns, a.has_m) <= (size_t) MV_SMEM_BUDGET) {
                 a.sr = sr;
                 a.nstage = ns;
                 return;
@@ -445,6 +457,7 @@ cudaError_t table_launch(imi_cuda_engine *e, const TableRef &t, int pro, int epi
     a.rows = t.rows;
     a.cols = t.cols;
     a.row_bytes = t.row_bytes;
+    a.has_m = t.has_m ? 1 : 0;
     const int gran = epi == E_SILU ? 2 : 1;
     a.unit = epi == E_SILU ? 64 : 1;
     const int units = t.rows / a.unit;
@@ -1252,6 +1265,7 @@ imi_cuda_status imi_cuda_trace_table(imi_cuda_engine *e, int layer, int which, i
     CK(cudaMemsetAsync(d, 0, (size_t) g * MV_TRACE * 8, e->stream));
     a.trace = d;
     a.W = e->w + t->off; a.rows = t->rows; a.cols = t->cols; a.row_bytes = t->row_bytes;
+    a.has_m = t->has_m ? 1 : 0;
     a.unit = epi == E_SILU ? 2 : 1;
     plan_stages(a, P_Q8IN, 1, g);
     cudaError_t r = launch_table(P_Q8IN, epi, a, g, e->stream, false);

@@ -5,7 +5,7 @@
 namespace imi {
 // one table read; `pro` / `epi` pick the input preparation and the output stage (common.cuh: Pro, Epi)
 cudaError_t launch_table(int pro, int epi, const MvArgs &a, int grid, cudaStream_t st, bool pdl);
-size_t table_smem(int pro, int cols, int sr, int ncol, int n_embd, int ab_len, int d_conv, int nstage);
+size_t table_smem(int pro, int cols, int sr, int ncol, int n_embd, int ab_len, int d_conv, int nstage, int has_m = 0);
 int table_nc_slot(int ncol);
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st, bool pdl);
 bool attn_supported(int head_dim, int grp, int n_ctx);

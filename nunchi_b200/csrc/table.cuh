@@ -408,14 +408,40 @@ __device__ __forceinline__ float row_chain(const float *f, const uint16_t *d, co
     return __fmaf_rn(-8.0f, cor, acc);
 }
 
-template <int PRO, int EPI, int NC>
+// the Q4_1 chains of one (input, row) (group_avx2<true>, tables.cpp:127-143): acc as for Q4_0, cor = fma(m_j, s_j,
+// cor) over the blocks' minimums, result acc + cor with one rounding; blocks in order
+__device__ __noinline__ float row_chain_m(const float *f, const uint16_t *d, const uint16_t *mn, const float *xdc,
+                                          const float *xsc, int nb) {
+    float acc = 0.0f, cor = 0.0f;
+#pragma unroll 4
+    for (int j = 0; j < nb; j += 4) {
+        const float4 fv = *(const float4 *) (f + j), xv = *(const float4 *) (xdc + j), sv = *(const float4 *) (xsc + j);
+        const uint2 dv = *(const uint2 *) (d + j), mv = *(const uint2 *) (mn + j);
+        const float d0 = h2f((uint16_t) (dv.x & 0xffff)), d1 = h2f((uint16_t) (dv.x >> 16)),
+                    d2 = h2f((uint16_t) (dv.y & 0xffff)), d3 = h2f((uint16_t) (dv.y >> 16));
+        const float m0 = h2f((uint16_t) (mv.x & 0xffff)), m1 = h2f((uint16_t) (mv.x >> 16)),
+                    m2 = h2f((uint16_t) (mv.y & 0xffff)), m3 = h2f((uint16_t) (mv.y >> 16));
+        acc = __fmaf_rn(fv.x, __fmul_rn(d0, xv.x), acc);
+        cor = __fmaf_rn(m0, sv.x, cor);
+        acc = __fmaf_rn(fv.y, __fmul_rn(d1, xv.y), acc);
+        cor = __fmaf_rn(m1, sv.y, cor);
+        acc = __fmaf_rn(fv.z, __fmul_rn(d2, xv.z), acc);
+        cor = __fmaf_rn(m2, sv.z, cor);
+        acc = __fmaf_rn(fv.w, __fmul_rn(d3, xv.w), acc);
+        cor = __fmaf_rn(m3, sv.w, cor);
+    }
+    return __fadd_rn(acc, cor);
+}
+
+// HM: Q4_1 rows (minimums beside the scales); a compile-time switch, so the Q4_0 instances carry none of it
+template <int PRO, int EPI, int NC, int HM>
 __global__ void __launch_bounds__(MV_THREADS, 1) k_table(const __grid_constant__ MvArgs a) {
     extern __shared__ __align__(128) uint8_t sm[];
     __shared__ int abort_flag, last_cta;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, K = a.cols, nb = K / 32, ld = nb + 4,
               nc = a.ncol, sr = a.sr;
     const int NS = a.nstage;
-    const MvPlan P = mv_plan(K, sr, NC, mv_vb_len(PRO, K, a.n_embd, NC, a.d_conv), a.ab_len, NS);
+    const MvPlan P = mv_plan(K, sr, NC, mv_vb_len(PRO, K, a.n_embd, NC, a.d_conv), a.ab_len, NS, HM);
     uint8_t *stage = sm + P.stage;
     uint64_t *bar = (uint64_t *) (sm + P.bar);
     const int8_t *xq = (const int8_t *) (sm + P.xq);
@@ -509,6 +535,14 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_table(const __grid_constant__
                     const int r = idx / nchunk, k = idx - r * nchunk;
                     *(uint2 *) (dq + r * ld + 4 * k) = *(const uint2 *) (sb + (size_t) r * a.row_bytes + K / 2 + 8 * k);
                 }
+                if (HM) {   // Q4_1: the rows' minimums, after the scales in the row and in the second half here
+                    uint16_t *mq = dq + MV_NBUF * sr * ld;
+                    for (int idx = it; idx < nr * nchunk; idx += MV_ITHREADS) {
+                        const int r = idx / nchunk, k = idx - r * nchunk;
+                        *(uint2 *) (mq + r * ld + 4 * k) =
+                            *(const uint2 *) (sb + (size_t) r * a.row_bytes + K / 2 + 2 * nb + 8 * k);
+                    }
+                }
                 auto one = [&](int r, int j, bool cached) {
                     const uint4 code = *(const uint4 *) (sb + (size_t) r * a.row_bytes + 16 * j);
 #pragma unroll
@@ -593,7 +627,10 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_table(const __grid_constant__
                 const bool act = t < nc * nr;
                 const int c = act ? t / nr : 0, r = act ? t - c * nr : 0;
                 float v = 0.0f;
-                if (act) v = row_chain(f + (c * sr + r) * ld, dq + r * ld, xd + c * nb, xs + c * nb, nb);
+                if (act)
+                    v = HM ? row_chain_m(f + (c * sr + r) * ld, dq + r * ld, dq + MV_NBUF * sr * ld + r * ld,
+                                              xd + c * nb, xs + c * nb, nb)
+                                : row_chain(f + (c * sr + r) * ld, dq + r * ld, xd + c * nb, xs + c * nb, nb);
                 if (EPI == E_STORE) {
                     if (act) a.out[(size_t) c * a.out_stride + r0 + rb + r] = v;
                 } else if (EPI == E_SILU) {   // rows (2i, 2i+1) are (gate_i, up_i): act_i = silu(gate) * up (seoul.cpp:384-391)

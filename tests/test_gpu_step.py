@@ -267,3 +267,33 @@ def test_q6k_word_table_steps_match_oracle():
     o.step(int(ids[0]))
     o2.step(int(ids[1]), want_logits=True)
     assert np.array_equal(bits(g.logits), bits(o.logits)) and np.array_equal(bits(g2.logits), bits(o2.logits))
+
+
+def test_q41_layer_tables_steps_match_oracle():
+    """A model whose layer tables are Q4_1 (a minimum per block: out = acc + cor, cor = fma(m, s_j, cor) over the
+    blocks in order): prefill, single steps, greedy and a riding step against the oracle (itself pinned to the
+    reference's own Q4_1 code), bit for bit."""
+    path = synth.cached_gguf("tiny_q41")
+    o, e = oracle.Oracle(path, n_ctx=96), nb.Engine(path, n_ctx=96)
+    g, g2 = e.new_state(), e.new_state()
+    ids = synth.random_ids(24, e.n_vocab, 12)
+    o.step_batch(tokens=ids[:16], want_logits=True)
+    g.step_batch(tokens=ids[:16], want_logits=True)
+    assert np.array_equal(bits(g.logits), bits(o.logits))
+    for t in ids[16:]:
+        o.step(int(t))
+        g.step(int(t))
+        assert np.array_equal(bits(g.hidden), bits(o.hidden)) and np.array_equal(bits(g.logits), bits(o.logits))
+    picks = nb.greedy([g], 4)[:, 0]
+    for k in range(4):
+        o.step(int(np.argmax(o.logits)))
+        assert int(picks[k]) == int(np.argmax(o.logits))
+    assert np.array_equal(bits(g.logits), bits(o.logits))
+    o2 = o.new_state()
+    for t in ids[:3]:
+        o2.step(int(t), want_logits=True)
+        g2.step(int(t))
+    nb.step2(g, int(ids[0]), None, True, g2, int(ids[1]), None, True)
+    o.step(int(ids[0]))
+    o2.step(int(ids[1]), want_logits=True)
+    assert np.array_equal(bits(g.logits), bits(o.logits)) and np.array_equal(bits(g2.logits), bits(o2.logits))
