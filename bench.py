@@ -1,13 +1,16 @@
 #!/usr/bin/env python
 """Benchmark of the B200 decode engine for imi's brain token loop.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload ride2|b1]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload ride2|b1|prefill|multi64]
 
 Workload (the batch-2 "riding" step): the Seoul-shaped synthetic backbone (seed 0);
 conversation A prefilled with 1024 random ids (seed 1), conversation B with 256 (seed 2); then every timed step is
 one step2 (imi_seoul::step2, seoul.cpp:208): both conversations advance one greedy position on one read of every
 table. `--workload b1` runs configs[0] instead (32-token prompt, one conversation). Under torchrun each rank runs
 the same workload on its own GPU (whole conversations per GPU, no collective): weak scaling.
+`--workload prefill` runs configs[2] (one step = one fresh conversation reading 400 input vectors and 16 ids in
+chunks of 128, the last position's word scores; positions/s) and `--workload multi64` configs[3] (64 conversations
+per GPU with contexts drawn from 256..2048, every step one greedy position for all 64; tok/s, default 256 steps).
 
 One JSON line on rank 0: `value` = tokens/s of the whole job with everything resident on the device (CUDA events on
 the engine's stream, max over ranks); `e2e` = the same through the public step2 + argmax calls with host token input
@@ -37,14 +40,17 @@ KV_BYTES_PER_POS = None   # filled from the engine shape
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--steps", type=int, default=0, help="timed steps (0 = the workload's default)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["ride2", "b1"], default="ride2")
+    ap.add_argument("--workload", choices=["ride2", "b1", "prefill", "multi64"], default="ride2")
     ap.add_argument("--cpu-steps", type=int, default=0, help="reference CPU sample size in steps (0 = auto)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    return ap.parse_args()
+    a = ap.parse_args()
+    if not a.steps:
+        a.steps = {"prefill": 5, "multi64": 256}.get(a.workload, 128)
+    return a
 
 
 class Ranks:
@@ -147,11 +153,32 @@ def peaks() -> dict:
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d.get("bf16_tflops"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+PREFILL_VECS, PREFILL_IDS, PREFILL_CHUNK = 400, 16, 128
+MULTI_N, MULTI_CTX = 64, (256, 2048)
+
+
+def multi_contexts(rank: int) -> list:
+    """each session's context length, uniform in 256..2048 (seed 4 + the GPU's rank)."""
+    rng = np.random.default_rng(4 + rank)
+    return [int(x) for x in rng.integers(MULTI_CTX[0], MULTI_CTX[1] + 1, MULTI_N)]
 
 
 def workload_desc(args) -> dict:
+    if args.workload == "prefill":
+        return {"workload": f"configs[2] prefill: Seoul-shaped Q4_0 backbone (seed 0), a fresh conversation reads "
+                            f"{PREFILL_VECS} input vectors N(0,1)*0.5 (seed 3) then {PREFILL_IDS} random ids (seed 3) "
+                            f"in chunks of {PREFILL_CHUNK} (step_batch calls of 128, 128, 128, 16 vectors and 16 ids), "
+                            "word scores of the last position; host inputs copied inside the timed region (the API "
+                            "takes host vectors)", "tokens_per_step": PREFILL_VECS + PREFILL_IDS, "prompts": []}
+    if args.workload == "multi64":
+        return {"workload": f"configs[3] {MULTI_N} sessions per GPU: contexts uniform in {MULTI_CTX[0]}..{MULTI_CTX[1]} "
+                            "(seed 4 + rank) read beforehand (not timed), then greedy steps of all sessions, 8 "
+                            "conversations per table read (the timed region runs the 8 groups one after another, "
+                            "each for all its steps)", "tokens_per_step": MULTI_N, "prompts": []}
     if args.workload == "ride2":
         return {"workload": "configs[1] riding step2: Seoul-shaped Q4_0 backbone (seed 0), conversation A after a "
                             f"{A_PROMPT}-id prompt, B after {B_PROMPT} ids, greedy, one table read per step for both",
@@ -238,11 +265,151 @@ def run_ours(args, ranks: Ranks) -> dict:
     return out
 
 
+def prefill_inputs(n_embd: int, n_vocab: int):
+    from nunchi_b200 import synth
+    rng = np.random.default_rng(3)
+    vecs = (rng.standard_normal((PREFILL_VECS, n_embd)) * 0.5).astype(np.float32)
+    return vecs, synth.random_ids(PREFILL_IDS, n_vocab, 3)
+
+
+def prefill_calls(s, vecs, ids):
+    """configs[2]'s reads of one conversation: the vectors in chunks of 128, then the ids with the word scores."""
+    for a in range(0, len(vecs), PREFILL_CHUNK):
+        s.step_batch(embd=vecs[a:a + PREFILL_CHUNK], want_logits=False)
+    s.step_batch(ids, want_logits=True)
+
+
+def run_prefill(args, ranks: Ranks) -> dict:
+    import torch
+    import nunchi_b200 as nb
+    from nunchi_b200 import synth
+    torch.cuda.set_device(ranks.local)
+    eng = nb.Engine(synth.cached_gguf("seoul", 0), device=ranks.local, n_ctx=512, max_batch=8)
+    info = eng.info
+    s = eng.new_state()
+    vecs, ids = prefill_inputs(info.n_embd, info.n_vocab)
+    st = torch.cuda.ExternalStream(eng.stream)
+    ev = lambda: torch.cuda.Event(enable_timing=True)   # noqa: E731
+    for _ in range(args.warmup):
+        s.reset()
+        prefill_calls(s, vecs, ids)
+    torch.cuda.synchronize()
+    ranks.barrier()
+    clocks = Clocks(ranks.local)
+    clocks.start()
+    e0, e1 = ev(), ev()
+    t0 = time.perf_counter()
+    e0.record(st)
+    picks = []
+    for _ in range(args.steps):
+        s.reset()
+        prefill_calls(s, vecs, ids)
+        picks.append(s.argmax()[0])   # the host read of the prefill's result (the first greedy word)
+    e1.record(st)
+    e1.synchronize()
+    wall = time.perf_counter() - t0
+    clk = clocks.stop()
+    ranks.barrier()
+    ms, ms_wall = ranks.max(e0.elapsed_time(e1)), ranks.max(wall * 1e3)
+    assert len(set(picks)) == 1, "prefills of the same inputs gave different picks"
+    n_pos = PREFILL_VECS + PREFILL_IDS
+    groups = sum(-(-min(PREFILL_CHUNK, PREFILL_VECS - a) // 8) for a in range(0, PREFILL_VECS, PREFILL_CHUNK))
+    groups += -(-PREFILL_IDS // 8)
+    out = {"ms": ms, "value": ranks.world * n_pos * args.steps / (ms / 1e3), "clocks": clk, "info": info, "ncol": 8}
+    out["launches"] = (groups * (eng.launches_per_step(1, 0) + info.n_attn) + 1) * args.steps
+    out["e2e"] = {"value": ranks.world * n_pos * args.steps / (ms_wall / 1e3), "unit": "positions/s",
+                  "h2d_bytes_per_step": int(vecs.nbytes + ids.nbytes), "d2h_bytes_per_step": 8,
+                  "ms_per_step": ms_wall / args.steps, "clock": "host wall clock around the same calls"}
+    t_ms, t_bytes = eng.bench_tables(ncol=8, reps=20)
+    out["tables"] = {"ms": t_ms, "bytes": t_bytes}
+    # what this design reads: every layer table once per group of 8 positions, plus the word table once
+    out["step_bytes"] = int(groups * t_bytes + table_bytes_word(info))
+    # the contraction (2 flops per weight per position; Q4_0 holds 32 weights in 18 bytes) + the last word scores
+    out["flops_per_step"] = 2 * (t_bytes * 16 // 9) * n_pos + 2 * info.n_vocab * info.n_embd
+    s.close()
+    eng.close()
+    return out
+
+
+def table_bytes_word(info) -> int:
+    """Bytes of the Q4_0 word table (the word table is read once per step with word scores)."""
+    return info.n_vocab * info.n_embd // 32 * 18
+
+
+def run_multi(args, ranks: Ranks) -> dict:
+    import torch
+    import nunchi_b200 as nb
+    from nunchi_b200 import synth
+    torch.cuda.set_device(ranks.local)
+    ctx = multi_contexts(ranks.rank)
+    n_ctx = MULTI_CTX[1] + args.warmup + 2 * args.steps + 8   # warm-up, timed steps, end-to-end steps
+    eng = nb.Engine(synth.cached_gguf("seoul", 0), device=ranks.local, n_ctx=n_ctx, max_batch=MULTI_N)
+    info = eng.info
+    states = [eng.new_state() for _ in range(MULTI_N)]
+    t0 = time.perf_counter()
+    for i, (s, n) in enumerate(zip(states, ctx)):
+        s.step_batch(synth.random_ids(n, info.n_vocab, 100 * ranks.rank + i), want_logits=True)
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+    st = torch.cuda.ExternalStream(eng.stream)
+    ev = lambda: torch.cuda.Event(enable_timing=True)   # noqa: E731
+    groups = [states[g:g + 8] for g in range(0, MULTI_N, 8)]   # device greedy runs 8 conversations per call
+    for g in groups:
+        nb.greedy(g, args.warmup)
+    torch.cuda.synchronize()
+    ranks.barrier()
+    pos0 = [s.pos for s in states]
+    clocks = Clocks(ranks.local)
+    clocks.start()
+    e0, e1 = ev(), ev()
+    e0.record(st)
+    for g in groups:   # each group's steps read every table once for its 8 conversations
+        nb.greedy(g, args.steps)
+    e1.record(st)
+    e1.synchronize()
+    clk = clocks.stop()
+    ranks.barrier()
+    ms = ranks.max(e0.elapsed_time(e1))
+    out = {"ms": ms, "value": ranks.world * MULTI_N * args.steps / (ms / 1e3), "clocks": clk, "info": info,
+           "ncol": 8, "prefill_s": prefill_s}
+    mid = [p + args.steps // 2 for p in pos0]
+    # every table once per group of 8 conversations, plus each conversation's own K/V and conv memory
+    out["step_bytes"] = int((len(groups) - 1) * info.weight_bytes + step_bytes(info, mid))
+    out["launches"] = eng.launches_per_step(MULTI_N, 1) * args.steps
+    if not args.no_e2e:   # host ids in, one step of all, host read of every pick, each step
+        picks = np.array([s.argmax()[0] for s in states], np.int32)
+        e2, e3 = ev(), ev()
+        torch.cuda.synchronize()
+        e2.record(st)
+        for _ in range(args.steps):
+            nb.step_multi(states, picks)
+            picks = np.array([s.argmax()[0] for s in states], np.int32)
+        e3.record(st)
+        e3.synchronize()
+        ms_e2e = ranks.max(e2.elapsed_time(e3))
+        out["e2e"] = {"value": ranks.world * MULTI_N * args.steps / (ms_e2e / 1e3), "unit": "tok/s",
+                      "h2d_bytes_per_step": 80 * MULTI_N, "d2h_bytes_per_step": 28 * MULTI_N,
+                      "ms_per_step": ms_e2e / args.steps}
+    t_ms, t_bytes = eng.bench_tables(ncol=8, reps=20)
+    out["tables"] = {"ms": t_ms, "bytes": t_bytes}
+    for s in states:
+        s.close()
+    eng.close()
+    return out
+
+
+MULTI_CPU_SESSIONS = 4
+
+
 def run_reference_cpu(args, steps: int) -> dict:
     """The reference's own CPU path (imi/core/seoul.cpp + tables.cpp compiled from the reference tree into
     oracle/_ref) on this host's cores: the same workload, `steps` timed positions after the same prompts."""
     import oracle
     from nunchi_b200 import synth
+    if args.workload == "prefill":
+        return run_reference_prefill(steps)
+    if args.workload == "multi64":
+        return run_reference_multi(steps)
     wl = workload_desc(args)
     prompts = wl["prompts"]
     threads = os.cpu_count() or 1
@@ -275,19 +442,82 @@ def run_reference_cpu(args, steps: int) -> dict:
                       f"AVX2, {threads} threads", "ms_per_step": dt / steps * 1e3}
 
 
+def reference_threads() -> int:
+    return os.cpu_count() or 1
+
+
+def run_reference_prefill(steps: int) -> dict:
+    """configs[2] on the reference's CPU path: `steps` fresh conversations each reading the same 416 positions
+    (imi_seoul::reset + step_batch, seoul.cpp:188-191,490-517), every host thread."""
+    import oracle
+    from nunchi_b200 import synth
+    if not oracle.reference_available():
+        raise RuntimeError("oracle/_ref/libimi_ref.so is not built")
+    threads = reference_threads()
+    r = oracle.Reference(synth.cached_gguf("seoul", 0), n_ctx=512, threads=threads)
+    vecs, ids = prefill_inputs(r.n_embd, r.n_vocab)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        r.reset()
+        prefill_calls(r, vecs, ids)
+        int(np.argmax(r.logits))
+    dt = time.perf_counter() - t0
+    n = (PREFILL_VECS + PREFILL_IDS) * steps
+    return {"value": n / dt, "unit": "positions/s", "cores": threads, "kind": "reference",
+            "sample": f"{steps} prefills of the same 416 positions; imi_seoul from the reference's seoul.cpp/tables.cpp, "
+                      f"AVX2, {threads} threads", "ms_per_step": dt / steps * 1e3}
+
+
+def run_reference_multi(steps: int) -> dict:
+    """configs[3] on the reference's CPU path, a bounded sample: the first sessions of rank 0's draw, their contexts
+    read beforehand (not timed), then `steps` greedy positions of each, the sessions one after another through
+    swap_state (the reference runs one conversation at a time; no CPU batching is invented)."""
+    import oracle
+    from nunchi_b200 import synth
+    if not oracle.reference_available():
+        raise RuntimeError("oracle/_ref/libimi_ref.so is not built")
+    threads = reference_threads()
+    ctx = multi_contexts(0)[:MULTI_CPU_SESSIONS]
+    r = oracle.Reference(synth.cached_gguf("seoul", 0), n_ctx=MULTI_CTX[1] + steps + 8, threads=threads)
+    parked = []
+    for i, n in enumerate(ctx):
+        r.reset()
+        r.step_batch(synth.random_ids(n, r.n_vocab, i), want_logits=True)
+        s = r.new_state()
+        r.swap_state(s)   # the session's memory parks in s; the brain's own becomes a fresh one
+        parked.append(s)
+    picks = [int(np.argmax(s.logits)) for s in parked]
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        for i, s in enumerate(parked):
+            r.swap_state(s)
+            r.step(picks[i])
+            picks[i] = int(np.argmax(r.logits))
+            r.swap_state(s)
+    dt = time.perf_counter() - t0
+    n = len(parked) * steps
+    return {"value": n / dt, "unit": "tok/s", "cores": threads, "kind": "reference",
+            "sample": f"{len(parked)} of the 64 sessions (contexts {ctx}, read beforehand, not timed), {steps} greedy "
+                      f"steps each, one session at a time via swap_state; imi_seoul from the reference's "
+                      f"seoul.cpp/tables.cpp, AVX2, {threads} threads", "ms_per_step": dt / steps * 1e3}
+
+
 def cpu_steps(args) -> int:
     if args.cpu_steps:
         return args.cpu_steps
-    return 64 if args.workload == "ride2" else 128
+    return {"ride2": 64, "prefill": 3, "multi64": 16}.get(args.workload, 128)
 
 
 def main():
     args = parse()
     ranks = Ranks()
     wl = workload_desc(args)
-    metric = ("decode tok/s, batch-2 riding step (step2), Seoul-shaped Q4_0 backbone" if args.workload == "ride2"
-              else "decode tok/s, batch-1 greedy step, Seoul-shaped Q4_0 backbone")
-    base = {"metric": metric, "unit": "tok/s", "n_gpus": ranks.world, "steps": args.steps, "warmup": args.warmup,
+    metric = {"ride2": "decode tok/s, batch-2 riding step (step2), Seoul-shaped Q4_0 backbone",
+              "b1": "decode tok/s, batch-1 greedy step, Seoul-shaped Q4_0 backbone",
+              "prefill": "prefill positions/s, 400 input vectors + 16 ids, Seoul-shaped Q4_0 backbone",
+              "multi64": "decode tok/s, 64 sessions per GPU, Seoul-shaped Q4_0 backbone"}[args.workload]
+    unit = "positions/s" if args.workload == "prefill" else "tok/s"
+    base = {"metric": metric, "unit": unit, "n_gpus": ranks.world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int4 x int8 -> int32 block dots, fp32 scale and accumulate", "data": "synthetic",
             "config": {"workload": wl["workload"], "parallelism": f"whole conversations per GPU x{ranks.world}, "
@@ -299,11 +529,11 @@ def main():
         ref = run_reference_cpu(args, args.steps)
         line = dict(base, impl="reference", value=ref["value"], ms_per_step=ref["ms_per_step"], n_gpus=ranks.world,
                     cpu_baseline={k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")},
-                    e2e={"value": ref["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
+                    e2e={"value": ref["value"], "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
         print(json.dumps(line), flush=True)
         ranks.close()
         return
-    r = run_ours(args, ranks)
+    r = {"prefill": run_prefill, "multi64": run_multi}.get(args.workload, run_ours)(args, ranks)
     pk = peaks()
     t_gbs = r["tables"]["bytes"] / (r["tables"]["ms"] / 1e3) / 1e9
     step_ms = r["ms"] / args.steps
@@ -311,11 +541,20 @@ def main():
     line["roofline"] = {
         "kernel": "k_table (every layer table of a step, read back to back: imi_seoul::bench_tables)",
         "bound": "hbm", "achieved": t_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": t_gbs / pk["hbm_gbs"],
-        "peak_source": pk["source"], "traffic": table_traffic(len(r["mid_positions"])),
+        "peak_source": pk["source"], "traffic": table_traffic(r.get("ncol") or len(r["mid_positions"])),
+        "ncol": r.get("ncol") or len(r["mid_positions"]),
         "algorithmic_bytes_per_launch": r["tables"]["bytes"], "launch_ms": r["tables"]["ms"]}
     sb = r["step_bytes"]
     line["step_roofline"] = {"bytes_per_step": sb, "achieved_gbs": sb / (step_ms / 1e3) / 1e9,
                              "frac": sb / (step_ms / 1e3) / 1e9 / pk["hbm_gbs"], "peak_source": pk["source"]}
+    if "flops_per_step" in r:   # prefill is a contraction: its tensor-pipe roofline, which this design does not use
+        tf = r["flops_per_step"] / (step_ms / 1e3) / 1e12
+        line["flops_roofline"] = {"flops_per_step": r["flops_per_step"], "achieved_tflops": tf,
+                                  "peak_tflops": pk.get("bf16_tflops"), "unit": "TFLOP/s",
+                                  "frac": tf / pk["bf16_tflops"] if pk.get("bf16_tflops") else None,
+                                  "note": "int8 block dots on the integer pipes (dp4a), 8 positions per table read"}
+    if "prefill_s" in r:
+        line["config"]["prefill_s"] = r["prefill_s"]
     if "e2e" in r:
         line["e2e"] = r["e2e"]
     if ranks.rank == 0 and ranks.world == 1 and not args.no_cpu_baseline:
