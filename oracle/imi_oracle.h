@@ -3,7 +3,7 @@
  *
  * Every float operation follows the order of imi's AVX2 path (imi/core/vec.h, imi/core/tables.cpp,
  * imi/core/seoul.cpp) so that, built with -ffp-contract=off, its results are bit-identical to the reference's own
- * code compiled from /root/reference (oracle/_ref). Pinned against that build by tests/test_oracle_pin.py. */
+ * code compiled unmodified from the reference tree (oracle/_ref). Pinned against that build by tests/test_oracle.py. */
 #ifndef IMI_ORACLE_H
 #define IMI_ORACLE_H
 #include <stdint.h>
