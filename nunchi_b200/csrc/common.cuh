@@ -161,7 +161,7 @@ struct PreCol {
     int pos, off, tok, pad;
 };
 struct MvPlan {
-    int stage, bar, xq, xd, xs, fs, dd, vb, vo, ab, pc, red, total;
+    int stage, sstride, bar, xq, xd, xs, fs, dd, vb, vo, ab, pc, red, total;
 };
 __host__ __device__ inline int align_up(int x, int a) { return (x + a - 1) / a * a; }
 // hm: Q4_1 rows (a minimum per block besides the scale): the scale buffers hold the minimums in a second half
@@ -169,7 +169,10 @@ __host__ __device__ inline MvPlan mv_plan(int cols, int sr, int nc, int vb_len, 
     MvPlan p;
     const int nb = cols / 32, ld = nb + 4;   // row strides: 16-byte aligned, conflict-free for vector loads
     int o = 0;
-    p.stage = o; o += ns * MV_STAGE_BYTES;
+    // weight stages sized to their rows (a stage holds sr rows of at most MV_STAGE_BYTES): where the block-dot buffers
+    // leave few rows per stage (8 inputs), more stages stay in flight
+    p.sstride = align_up(sr * (cols / 32) * (hm ? 20 : 18), 128);
+    p.stage = o; o += ns * p.sstride;
     p.bar = o;   o = align_up(o + 8 * MV_MAX_STAGES, 16);
     p.xq = o;    o = align_up(o + nc * cols, 16);
     p.xd = o;    o = align_up(o + 4 * nc * nb, 16);

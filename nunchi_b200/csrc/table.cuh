@@ -473,7 +473,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_table(const __grid_constant__
         const uint32_t bytes = (uint32_t) n * (uint32_t) a.row_bytes;
         uint64_t *b = &bar[st % NS];
         mbar_expect_tx(b, bytes);
-        bulk_g2s(stage + (st % NS) * MV_STAGE_BYTES, a.W + (size_t) (r0 + rr) * a.row_bytes, bytes, b);
+        bulk_g2s(stage + (st % NS) * P.sstride, a.W + (size_t) (r0 + rr) * a.row_bytes, bytes, b);
     };
     constexpr bool late = PRO == P_RESID_NORM || PRO == P_FINAL;
     // by one thread: the first stages (later ones are issued as their slots free up; an L2 bulk prefetch of the rest
@@ -528,7 +528,7 @@ __global__ void __launch_bounds__(MV_THREADS, 1) k_table(const __grid_constant__
             if (st >= MV_NBUF) nbar_sync(NB_FREE + b, NB_PAIR);   // chain warp b is done with buffer b
             if (ok) {
                 const int rb = st * sr, nr = min(sr, nrows - rb);
-                const uint8_t *sb = stage + (st % NS) * MV_STAGE_BYTES;
+                const uint8_t *sb = stage + (st % NS) * P.sstride;
                 float *f = fs + b * NC * sr * ld;
                 uint16_t *dq = dd + b * sr * ld;
                 for (int idx = it; idx < nr * nchunk; idx += MV_ITHREADS) {   // the rows' scales
