@@ -43,9 +43,12 @@ typedef struct {
 const char *imi_cuda_error(void);
 
 /* Load a GGUF model onto CUDA device `device` (replaces imi_seoul::load(path, threads, ctx_len), seoul.cpp:93).
- * n_ctx: positions per conversation; max_batch: most conversations stepped together by imi_cuda_step_multi
- * (and prefill chunk width of imi_cuda_step_batch is fixed at 128 independent of it). An engine and its states are
- * used by one host thread at a time: they share the engine's stream, its staging buffers and its read-back buffer. */
+ * n_ctx: positions per conversation; max_batch: most conversations stepped together by imi_cuda_step_multi.
+ * An engine and its states are used by one host thread at a time: they share the engine's stream, its staging
+ * buffers and its read-back buffer.
+ * Device memory budget: when the environment variable IMI_CUDA_MAX_DEVICE_BYTES is set (bytes), the engine and all
+ * its states together allocate at most that much; a load or a new state beyond it fails with IMI_E_NOMEM (for a GPU
+ * shared with other work). */
 imi_cuda_status imi_cuda_load(const char *gguf_path, int device, int n_ctx, int max_batch, imi_cuda_engine **out);
 void imi_cuda_free(imi_cuda_engine *e);                                     /* ~imi_seoul, seoul.cpp:687-689 */
 imi_cuda_status imi_cuda_get_info(const imi_cuda_engine *e, imi_cuda_info *out);
@@ -125,6 +128,12 @@ imi_cuda_status imi_cuda_trace_table(imi_cuda_engine *e, int layer, int which, i
  * norm; grids[launch]: CTAs. *n receives the number of launches (at most max_launches). */
 imi_cuda_status imi_cuda_trace_step(imi_cuda_state *s, int32_t token, int want_logits, unsigned long long *out,
                                     int max_launches, int *kinds, int *grids, int *n);
+
+/* Diagnostics: the failure path of the engine's bounded device waits (every wait on a weight stage gives up after
+ * about one second and reports IMI_E_TIMEOUT instead of hanging). One CTA waits on an mbarrier that nothing completes,
+ * with a limit of limit_ms milliseconds at the device's clock; the wait gives up, the kernel sets the error flag and
+ * returns. Returns IMI_E_TIMEOUT when the wait gave up as designed (the context stays usable), IMI_OK never. */
+imi_cuda_status imi_cuda_check_wait_timeout(int device, double limit_ms);
 
 /* ---- kernel level (known-answer tests and the isolated table sweep) ---- */
 

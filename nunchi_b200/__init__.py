@@ -76,6 +76,7 @@ def lib():
         L.imi_cuda_q6k_scores.argtypes = [C.c_int, _vp, C.c_int, C.c_int, _fp, _fp, _vp, _fp, _vp]
         L.imi_cuda_q4_matvec.argtypes = [C.c_int, _vp, C.c_int, C.c_int, _vp, _fp, _fp, C.c_int, _fp, _ip]
         L.imi_cuda_q4_matvec_static.argtypes = [C.c_int, _vp, C.c_int, C.c_int, _vp, _vp, _vp, C.c_int, _vp, _vp]
+        L.imi_cuda_check_wait_timeout.argtypes = [C.c_int, C.c_double]
         _L = L
     return _L
 

@@ -335,11 +335,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *b, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// bounded wait (about one second at the boost clock): false if the phase never completed
-__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity) {
+// bounded wait (by default about one second at the boost clock): false if the phase never completed
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, long long limit = 2000000000LL) {
     const long long t0 = clock64();
     while (!mbar_try_wait(b, parity))
-        if (clock64() - t0 > 2000000000LL) return false;
+        if (clock64() - t0 > limit) return false;
     return true;
 }
 // global -> shared bulk copy completing on an mbarrier (addresses 16-byte aligned, bytes a multiple of 16)

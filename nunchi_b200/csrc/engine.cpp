@@ -13,6 +13,8 @@
 #include "launch.h"
 
 #include <cmath>
+#include <cstdint>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -36,6 +38,19 @@ static imi_cuda_status fail(imi_cuda_status st, const std::string &msg) {
         cudaError_t e_ = (x);                                                                                 \
         if (e_ != cudaSuccess) return fail(e_ == cudaErrorMemoryAllocation ? IMI_E_NOMEM : IMI_E_CUDA,        \
                                            std::string(#x) + ": " + cudaGetErrorString(e_));                  \
+    } while (0)
+
+// a device allocation counted against the engine's budget (IMI_CUDA_MAX_DEVICE_BYTES)
+#define DALLOC(e, ptr, n)                                                                                     \
+    do {                                                                                                      \
+        const size_t n_ = (n);                                                                                \
+        if ((e)->dev_used + n_ > (e)->dev_budget)                                                             \
+            return fail(IMI_E_NOMEM, "device memory budget (IMI_CUDA_MAX_DEVICE_BYTES = " +                  \
+                                         std::to_string((e)->dev_budget) + ") exceeded: " +                   \
+                                         std::to_string((e)->dev_used) + " bytes held, " + std::to_string(n_) + \
+                                         " more asked");                                                      \
+        CK(cudaMalloc((void **) &(ptr), n_));                                                                 \
+        (e)->dev_used += n_;                                                                                  \
     } while (0)
 
 namespace {
@@ -92,6 +107,7 @@ struct imi_cuda_engine {
     cudaEvent_t staged = nullptr;   // the last host->device copy of the staging buffers has run
     std::map<int, cudaGraphExec_t> graphs;
     size_t state_bytes = 0;
+    size_t dev_budget = SIZE_MAX, dev_used = 0;   // IMI_CUDA_MAX_DEVICE_BYTES and what the engine + states hold
     uint8_t *qbuf = nullptr;
     // diagnostics: when trace_buf is set, every launch enqueued gets its own [grid][MV_TRACE] slice
     unsigned long long *trace_buf = nullptr;
@@ -110,6 +126,7 @@ struct imi_cuda_engine {
 struct imi_cuda_state {
     imi_cuda_engine *e = nullptr;
     void *mem = nullptr;
+    size_t mem_bytes = 0;
     SessDev *s = nullptr;
     __half *kc = nullptr, *vc = nullptr;
     float *ring = nullptr, *hidden = nullptr, *logits = nullptr;
@@ -334,7 +351,8 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
                                       std::to_string(n_ctx) + ") not supported");
     if ((e->n_head * e->head_dim) % 256) return fail(IMI_E_FORMAT, "n_head * head_dim must be a multiple of 256");
     e->w_bytes = L.off;
-    CK(cudaMalloc(&e->w, e->w_bytes));
+    if (const char *cap = getenv("IMI_CUDA_MAX_DEVICE_BYTES")) e->dev_budget = (size_t) strtoull(cap, nullptr, 10);
+    DALLOC(e, e->w, e->w_bytes);
 
     // upload: tables through a pinned staging buffer, small vectors directly
     size_t stage_max = 0;
@@ -364,7 +382,7 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
         std::vector<float> cs(2 * per), sn(2 * per);
         imi::rope_table(n_ctx, D, e->rope_base, rf ? (const float *) rf->data : nullptr, cs.data(), sn.data());
         imi::rope_table(n_ctx, D, e->rope_base_swa, nullptr, cs.data() + per, sn.data() + per);
-        CK(cudaMalloc(&e->rope_cs, 4 * per * 4));
+        DALLOC(e, e->rope_cs, 4 * per * 4);
         e->rope_sn = e->rope_cs + 2 * per;
         CK(cudaMemcpy(e->rope_cs, cs.data(), 2 * per * 4, cudaMemcpyHostToDevice));
         CK(cudaMemcpy(e->rope_sn, sn.data(), 2 * per * 4, cudaMemcpyHostToDevice));
@@ -374,7 +392,7 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
     const int HD = e->n_head * e->head_dim, kvd = e->n_head_kv * e->head_dim;
     e->big_n = std::max(3 * E, HD + 2 * kvd + e->n_head);
     const size_t per_col = (size_t) 2 * E + e->big_n + E + HD + e->n_ff + E + E + E;
-    CK(cudaMalloc(&e->X, per_col * STEP_COLS * 4));
+    DALLOC(e, e->X, per_col * STEP_COLS * 4);
     e->big = e->X + (size_t) 2 * E * STEP_COLS;
     e->y = e->big + (size_t) e->big_n * STEP_COLS;
     e->att = e->y + (size_t) E * STEP_COLS;
@@ -385,7 +403,7 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
     {
         const size_t na = (size_t) STEP_COLS * e->n_ff, nt = (size_t) STEP_COLS * HD;
         uint8_t *q = nullptr;
-        CK(cudaMalloc(&q, na + nt + 4 * 2 * (na / 32 + nt / 32) + 1024));
+        DALLOC(e, q, na + nt + 4 * 2 * (na / 32 + nt / 32) + 1024);
         e->qbuf = q;
         e->qa_q = (int8_t *) q;
         e->qt_q = (int8_t *) (q + na);
@@ -399,12 +417,12 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
         if (q6k_head_ctas(e->n_vocab, E / 256, STEP_COLS) <= 0) return fail(IMI_E_FORMAT, "Q6_K word table too wide");
         uint8_t *q = nullptr;
         const size_t nq = (size_t) STEP_COLS * E, nd = (size_t) STEP_COLS * (E / 256), nbs = (size_t) STEP_COLS * (E / 16);
-        CK(cudaMalloc(&q, nq + 4 * nd + 2 * nbs + 64));
+        DALLOC(e, q, nq + 4 * nd + 2 * nbs + 64);
         e->q8k_q = (int8_t *) q;
         e->q8k_d = (float *) (q + nq);
         e->q8k_b = (int16_t *) (q + nq + 4 * nd);
     }
-    CK(cudaMalloc(&e->cols_d, sizeof(Col) * STEP_COLS + 64));
+    DALLOC(e, e->cols_d, sizeof(Col) * STEP_COLS + 64);
     e->done = (unsigned *) (e->cols_d + STEP_COLS);
     e->err = (int *) (e->done + 4);
     CK(cudaMemset(e->cols_d, 0, sizeof(Col) * STEP_COLS + 64));
@@ -767,7 +785,8 @@ imi_cuda_status imi_cuda_state_new(imi_cuda_engine *e, imi_cuda_state **out) {
                  o_v = take((size_t) e->n_attn * e->n_ctx * kvd * 2),
                  o_r = take((size_t) e->n_conv * (e->d_conv + 1) * E * 4), o_h = take((size_t) E * 4),
                  o_l = take((size_t) e->n_vocab * 4), o_p = take((size_t) e->n_ctx * 4);
-    CK(cudaMalloc(&s->mem, o));
+    DALLOC(e, s->mem, o);
+    s->mem_bytes = o;
     uint8_t *m = (uint8_t *) s->mem;
     s->s = (SessDev *) (m + o_s);
     s->kc = (__half *) (m + o_k);
@@ -788,6 +807,7 @@ void imi_cuda_state_free(imi_cuda_state *s) {
     cudaSetDevice(s->e->device);
     cudaStreamSynchronize(s->e->stream);
     cudaFree(s->mem);
+    s->e->dev_used -= s->mem_bytes;
     delete s;
 }
 
@@ -1184,6 +1204,25 @@ imi_cuda_status imi_cuda_q4_matvec_static(int device, const uint8_t *q4, int row
     if (r != cudaSuccess) return fail(IMI_E_CUDA, std::string("q4_matvec_static: ") + cudaGetErrorString(r));
     if (herr) return fail(IMI_E_TIMEOUT, "q4_matvec_static: a device-side wait gave up");
     return IMI_OK;
+}
+
+imi_cuda_status imi_cuda_check_wait_timeout(int device, double limit_ms) {
+    if (!(limit_ms > 0.0) || limit_ms > 10000.0) return fail(IMI_E_ARG, "limit_ms must be in (0, 10000]");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) return fail(IMI_E_NODEV, "no CUDA device");
+    CK(cudaSetDevice(device));
+    int khz = 0;
+    CK(cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, device));
+    int *err = nullptr;
+    CK(cudaMalloc(&err, 4));
+    cudaError_t r = cudaMemset(err, 0, 4);
+    if (r == cudaSuccess) r = launch_wait_check((long long) (limit_ms * khz), err, 0);
+    int h = 0;
+    if (r == cudaSuccess) r = cudaMemcpy(&h, err, 4, cudaMemcpyDeviceToHost);
+    cudaFree(err);
+    if (r != cudaSuccess) return fail(IMI_E_CUDA, std::string("check_wait_timeout: ") + cudaGetErrorString(r));
+    if (h) return fail(IMI_E_TIMEOUT, "a device-side wait gave up (code " + std::to_string(h) + ")");
+    return fail(IMI_E_CUDA, "check_wait_timeout: a wait that nothing completes completed");
 }
 
 void *imi_cuda_stream(const imi_cuda_engine *e) { return e ? (void *) e->stream : nullptr; }

@@ -370,6 +370,21 @@ __global__ void __launch_bounds__(ATT_NT) k_attn(const __grid_constant__ AttnArg
 __host__ __device__ inline size_t attn_smem_bytes(int D, int n_ctx) { return attn_plan(D, n_ctx).total; }
 
 // ---------------------------------------------------------------------------------------------------------------
+// the failure path of the bounded device waits: a wait on an mbarrier no thread ever arrives at (a flag nothing
+// sets), with a short limit, gives up, reports IMI_E_TIMEOUT's code in the error flag and returns; no copy is in
+// flight, so the CTA exits cleanly and the context stays usable
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void k_wait_check(long long limit, int *err) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (!mbar_wait(&bar, 0, limit) && threadIdx.x == 0) atomicExch(err, 7);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // known-answer helper: the 8-bit cut of a vector
 // ---------------------------------------------------------------------------------------------------------------
 __global__ void k_q8_cut(const float *x, int n, int8_t *q, float *d, float *s) {

@@ -210,9 +210,10 @@ def metadata(shape: Shape) -> list:
     return kv
 
 
-def write_gguf(path: str, shape: Shape = SEOUL, seed: int = 0) -> str:
-    """Write the seeded synthetic model to `path` (GGUF v3). Returns the path."""
-    ts = list(tensors(shape, seed))
+def write_gguf(path: str, shape: Shape = SEOUL, seed: int = 0, override: dict | None = None) -> str:
+    """Write the seeded synthetic model to `path` (GGUF v3). Returns the path. `override` maps tensor names to
+    (ggml type, ne, array) written in their place (files the engine must refuse, in the failure tests)."""
+    ts = [(n, *override[n]) if override and n in override else (n, t, ne, d) for n, t, ne, d in tensors(shape, seed)]
     kv = metadata(shape)
     infos, off = [], 0
     for name, typ, ne, data in ts:

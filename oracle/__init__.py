@@ -62,6 +62,7 @@ class Oracle:
             for f in ("or_k_cache", "or_v_cache"):
                 getattr(L, f).restype = C.POINTER(C.c_uint16)
                 getattr(L, f).argtypes = [C.c_void_p, C.c_int]
+            L.or_state_import.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]
             L.or_step.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_int]
             L.or_step_batch.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
             L.or_rms_scale.restype = C.c_float
@@ -179,6 +180,14 @@ class OracleState:
 
     def conv_state(self, il):
         return np.ctypeslib.as_array(self.L.or_conv_state(self.h, il), (self.m.d_conv, self.m.n_embd)).copy()
+
+    def import_memory(self, pos, k, v, conv):
+        """Start from another implementation's memory: position, K/V caches [n_attn][pos][kvd] (fp16 bits) and conv
+        memory [n_conv][d_conv][n_embd] (oldest tap first), e.g. the engine's checkpoint (nunchi_b200 State.unpack)."""
+        k, v = np.ascontiguousarray(k, np.uint16), np.ascontiguousarray(v, np.uint16)
+        conv = np.ascontiguousarray(conv, np.float32)
+        if self.L.or_state_import(self.m.h, self.h, int(pos), _ptr(k), _ptr(v), _ptr(conv)):
+            raise ValueError("position beyond the oracle's n_ctx")
 
 
 # ---- kernel-level pieces (module functions over the C restatement) ----

@@ -345,6 +345,23 @@ const uint16_t *or_k_cache(const or_state *s, int ai) { return s->k[ai]; }
 const uint16_t *or_v_cache(const or_state *s, int ai) { return s->v[ai]; }
 const float *or_conv_state(const or_state *s, int il) { return s->conv[il]; }
 
+/* test harness: start from another implementation's memory (k, v [n_attn][pos][kvd] fp16 bits; conv
+ * [n_conv][d_conv][n_embd] fp32 per conv layer in layer order, oldest tap first; imi's layout, seoul.h:43-47), so one
+ * step here and one step of the engine read identical memory. -1 if pos does not fit n_ctx. */
+int or_state_import(const or_model *m, or_state *s, int pos, const uint16_t *k, const uint16_t *v, const float *conv) {
+    if (pos < 0 || pos > m->n_ctx) return -1;
+    const size_t kvd = (size_t) m->n_head_kv * m->head_dim, E = (size_t) m->n_embd;
+    for (int a = 0; a < m->n_attn; a++) {
+        memcpy(s->k[a], k + (size_t) a * pos * kvd, (size_t) pos * kvd * 2);
+        memcpy(s->v[a], v + (size_t) a * pos * kvd, (size_t) pos * kvd * 2);
+    }
+    int ci = 0;
+    for (int il = 0; il < m->n_layer; il++)
+        if (s->conv[il]) memcpy(s->conv[il], conv + (size_t) (ci++) * m->d_conv * E, (size_t) m->d_conv * E * 4);
+    s->pos = pos;
+    return 0;
+}
+
 /* ---------------- one position (seoul.cpp:359-488) ---------------- */
 
 /* the word scores of the hidden state: Q6_K (seoul.cpp:479-487 with imi_q8k / imi_q6k_row) or the Q4_0 adapter */

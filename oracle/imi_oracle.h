@@ -32,6 +32,9 @@ const float *or_logits(const or_state *s);
 const uint16_t *or_k_cache(const or_state *s, int ai);
 const uint16_t *or_v_cache(const or_state *s, int ai);
 const float *or_conv_state(const or_state *s, int il);
+/* test harness: overwrite position, K/V of positions 0..pos-1 ([n_attn][pos][kvd]) and conv memory
+ * ([n_conv][d_conv][n_embd], conv layers in order) with another implementation's; -1 if pos > n_ctx */
+int or_state_import(const or_model *m, or_state *s, int pos, const uint16_t *k, const uint16_t *v, const float *conv);
 
 /* one position: token >= 0, or embd[n_embd]. 0 ok, 1 context full (state unchanged), as seoul.cpp:352-357 */
 int or_step(const or_model *m, or_state *s, int32_t token, const float *embd, int want_logits);

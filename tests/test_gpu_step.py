@@ -1,13 +1,13 @@
 """Step-level parity on the GPU (B200) against the oracle (the C restatement of imi's step, itself pinned bit-exact to
 the reference's own code).
 
-Float tolerances:
-  * error budget (north star): against the reference's fp64 truth key (committed golden), the engine's relative L2
-    error of the word scores is within 1e-3 of imi's own error at every position (test_error_budget_vs_truth_key);
+Float tolerances (tests/parity.py):
+  * error budget (north star): against the reference's fp64 truth key (committed golden), the engine's word scores
+    are within 1e-3 (max-abs, relative to max|truth|) of imi's own error at every position
+    (test_error_budget_vs_truth_key);
   * direct comparison: the engine keeps imi's float order everywhere, so most steps are bit-identical; the one
     operation that can differ is expf (correctly rounded on the device; glibc's agrees on all but ~0.06% of inputs).
-    A 1-ulp difference there can move one 8-bit activation code by one step (1/127 of its block's maximum), and that
-    change stays in the attention cache, so direct comparisons allow TOL = 1e-2 of max|score|;
+    Direct comparisons allow TOL = 1e-3 of max|value|;
   * greedy picks are identical except where the oracle's top two scores are within 1e-4 of max|score| (logged).
 """
 import numpy as np
@@ -16,45 +16,17 @@ import pytest
 import nunchi_b200 as nb
 import oracle
 from nunchi_b200 import synth
+from parity import TOL, bits, follow_greedy, is_tie, record, rel
 
 pytestmark = pytest.mark.gpu
-TOL = 1e-2
 BUDGET = 1e-3
-
-
-def bits(a):
-    return np.ascontiguousarray(a, np.float32).view(np.uint32)
-
-
-def rel(a, b):
-    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
-
-
-def follow_greedy(o, ids):
-    """Run the oracle's greedy loop beside the device's picks: step k reads the previous pick (the first step reads
-    the pick after the prompt) and ids[k] is the pick step k makes. Every pick must match unless the oracle's top two
-    scores are within 1e-4 of max|score| there (a tie: logged, and the comparison stops, the paths part).
-    Returns how many picks matched."""
-    t = int(np.argmax(o.logits))
-    for k, got in enumerate(ids):
-        o.step(t)
-        lo = o.logits
-        t = int(np.argmax(lo))
-        if int(got) != t:
-            top2 = np.sort(lo)[-2:]
-            assert top2[1] - top2[0] <= 1e-4 * np.abs(lo).max(), f"greedy pick {k}: device {got} oracle {t}"
-            print(f"greedy pick {k}: near-tie ({top2[1] - top2[0]:.3g}), paths part here")
-            return k
-    return len(ids)
 
 
 def close_scores(lg, lo, log, where):
     r = rel(lg, lo)
     assert r <= TOL, f"{where}: scores differ by {r:.3g} of max"
-    top2 = np.sort(lo)[-2:]
-    tie = (top2[1] - top2[0]) <= 1e-4 * np.abs(lo).max()
     if int(np.argmax(lg)) != int(np.argmax(lo)):
-        assert tie, f"{where}: greedy pick differs without a tie"
+        assert is_tie(lo), f"{where}: greedy pick differs without a tie"
         log.append(where)
     return r
 
@@ -64,40 +36,50 @@ def test_steps_match_oracle(name, n):
     path = synth.cached_gguf(name)
     o = oracle.Oracle(path, n_ctx=128)
     g = nb.Seoul(path, ctx_len=128)
-    exact, ties = 0, []
+    exact, ties, worst = 0, [], 0.0
     for i, t in enumerate(synth.random_ids(n, o.n_vocab, 3)):
         o.step(int(t))
         g.step(int(t))
         ho, hg, lo, lg = o.hidden, g.hidden, o.logits, g.logits
         assert rel(hg, ho) <= TOL, f"hidden at {i}"
-        close_scores(lg, lo, ties, f"{name} position {i}")
+        worst = max(worst, close_scores(lg, lo, ties, f"{name} position {i}"))
         assert g.state.argmax()[0] == int(np.argmax(lg)), "device pick is not the first maximum of its scores"
         exact += np.array_equal(bits(hg), bits(ho)) and np.array_equal(bits(lg), bits(lo))
-    print(f"{name}: {exact}/{n} steps bit-identical, ties {ties}")
+    record(f"steps_{name}", steps=n, bit_identical=int(exact), rel_scores_max=worst, ties=ties)
     assert exact >= n // 2
 
 
 @pytest.mark.parametrize("name", ["tiny", "wide_heads", "seoul"])
 def test_error_budget_vs_truth_key(name):
-    """The reference's fp64 truth key (imi/ref/ref_exact.py, committed in tests/golden): the engine's score error is
-    imi's own error within 1e-3 (metric of imi/ref/compare.py: relative L2 per position)."""
+    """The reference's fp64 truth key (imi/ref/ref_exact.py, committed in tests/golden; 32 positions): at every
+    position the engine's max-abs error (relative to max|truth|) of the word scores and of the hidden state is imi's
+    own error within 1e-3. imi's own scores come from the oracle (pinned bit for bit to the reference; its hidden
+    states are checked against the committed reference outputs here too)."""
     import os
     gd = os.path.join(os.path.dirname(__file__), "golden")
     ref, truth = np.load(os.path.join(gd, f"ref_{name}.npz")), np.load(os.path.join(gd, f"truth_{name}.npz"))
-    g = nb.Seoul(synth.cached_gguf(name), ctx_len=64)
+    path = synth.cached_gguf(name)
+    g = nb.Seoul(path, ctx_len=64)
+    o = oracle.Oracle(path, n_ctx=64)
+    n_full = len(truth["logits_full"])
+    assert n_full >= 32 or name != "seoul"
+    worst = 0.0
     for i, t in enumerate(ref["tokens"]):
         g.step(int(t))
+        o.step(int(t))
+        assert np.array_equal(bits(o.hidden), bits(ref["hidden"][i])), "oracle no longer the reference"
         th = truth["hidden"][i]
-        e_imi = np.linalg.norm(ref["hidden"][i] - th) / np.linalg.norm(th)
-        e_gpu = np.linalg.norm(g.hidden - th) / np.linalg.norm(th)
-        assert abs(e_gpu - e_imi) <= BUDGET, f"hidden error at {i}: engine {e_gpu:.4g} imi {e_imi:.4g}"
-        if i < len(truth["logits_full"]):
+        e_imi, e_gpu = rel(ref["hidden"][i], th), rel(g.hidden, th)
+        assert e_gpu - e_imi <= BUDGET, f"hidden error at {i}: engine {e_gpu:.4g} imi {e_imi:.4g}"
+        if i < n_full:
             tl = truth["logits_full"][i]
-            e_imi = np.linalg.norm(ref["logits_full"][i] - tl) / np.linalg.norm(tl)
-            e_gpu = np.linalg.norm(g.logits - tl) / np.linalg.norm(tl)
-            assert abs(e_gpu - e_imi) <= BUDGET, f"score error at {i}: engine {e_gpu:.4g} imi {e_imi:.4g}"
+            e_imi, e_gpu = rel(o.logits, tl), rel(g.logits, tl)
+            worst = max(worst, e_gpu - e_imi)
+            assert e_gpu - e_imi <= BUDGET, f"score error at {i}: engine {e_gpu:.4g} imi {e_imi:.4g}"
         assert int(np.argmax(g.logits)) == int(ref["logits_top_ids"][i][0]) or \
             ref["logits_top_vals"][i][0] - ref["logits_top_vals"][i][1] <= 1e-4 * np.abs(ref["logits_top_vals"][i]).max()
+    record(f"truth_budget_{name}", positions=len(ref["tokens"]), full_score_positions=n_full,
+           worst_excess_over_imi=worst)
 
 
 def test_embedding_input_and_hidden_only(tiny_path):
@@ -188,7 +170,7 @@ def test_step_batch_matches_oracle(name):
     assert rel(g.logits, o.logits) <= TOL
 
 
-def test_greedy_on_device_matches_oracle(small_path):
+def test_greedy_on_device_matches_oracle(small_path, record_property):
     o = oracle.Oracle(small_path, n_ctx=128)
     e = nb.Engine(small_path, n_ctx=128)
     s = e.new_state()
@@ -196,7 +178,8 @@ def test_greedy_on_device_matches_oracle(small_path):
     s.step_batch(prompt, want_logits=True)
     o.step_batch(tokens=prompt, want_logits=True)
     ids = nb.greedy([s], 40)[:, 0]
-    assert follow_greedy(o, ids) >= 0
+    n, tie = follow_greedy(o, ids, "small greedy 40", record_property)
+    assert n == 40 or tie is not None
 
 
 def test_context_full_and_reset(tiny_path):
@@ -219,8 +202,10 @@ def test_context_full_and_reset(tiny_path):
         s.step(e.n_vocab)   # token out of range
 
 
-def test_seoul_greedy_128_steps(seoul_path):
-    """32-id prompt, then 128 greedy steps, against the oracle running the same greedy loop."""
+def test_seoul_greedy_128_steps(seoul_path, record_property):
+    """32-id prompt, then 128 greedy steps, against the oracle running the same greedy loop: every pick
+    identical, or identical up to a logged near-tie (the number of identical picks and the tie position are recorded
+    as test properties, in IMI_PARITY_LOG and as a warning)."""
     o = oracle.Oracle(seoul_path, n_ctx=192)
     e = nb.Engine(seoul_path, n_ctx=192)
     s = e.new_state()
@@ -229,11 +214,10 @@ def test_seoul_greedy_128_steps(seoul_path):
     o.step_batch(tokens=prompt, want_logits=True)
     assert rel(s.logits, o.logits) <= TOL
     ids = nb.greedy([s], 128)[:, 0]
-    k = follow_greedy(o, ids)
-    if k == 128:
-        worst = rel(s.logits, o.logits)
-        print(f"seoul: 128 greedy picks identical, last-step score difference {worst:.3g}")
-        assert worst <= TOL
+    k, tie = follow_greedy(o, ids, "seoul configs[0] greedy 128", record_property)
+    assert k == 128 or tie is not None
+    if tie is None:
+        assert rel(s.logits, o.logits) <= TOL
 
 
 def test_q6k_word_table_steps_match_oracle():

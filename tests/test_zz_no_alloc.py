@@ -1,7 +1,8 @@
 """The table read that allocates nothing (imi_cuda_q4_matvec_static) against the allocating entry point
-(imi_cuda_q4_matvec) on the same inputs, through the C-ABI on device buffers. Two calls in a row with different
-shapes share the one static scratch; each must match. The kernels keep imi's accumulation order, so the results
-agree bit for bit; the float tolerance below is the stated bound should that ever not hold (rel 1e-6).
+(imi_cuda_q4_matvec) and against the oracle (imi_q4_group's per-row result restated in C) on the same inputs,
+through the C-ABI on device buffers. Two calls in a row with different shapes share the one static scratch; each
+must match. The kernels keep imi's accumulation order, so the results agree bit for bit; the float tolerance below
+is the stated bound should that ever not hold (rel 1e-6).
 
 This file is collected last on purpose: it must pass after the other tests have used the device, and alone."""
 import ctypes as C
@@ -50,11 +51,14 @@ def test_static_matches_allocating_entry_two_calls_in_a_row():
     for rows, cols, ncol, seed in [(2048, 2048, 2, 11), (300, 8192, 1, 12)]:
         q4, cq, cd, cs = _case(rows, cols, ncol, seed)
         want = nb.q4_matvec(q4, rows, cols, cq, cd, cs)
+        truth = np.asarray(oracle.q4_matvec(q4, rows, cols, cq, cd, cs), np.float32).reshape(want.shape)
         st, got = _static(torch, q4, rows, cols, cq, cd, cs, stream)
         assert st == 0, nb.lib().imi_cuda_error().decode()
         assert np.isfinite(got).all()
         np.testing.assert_allclose(got, want, rtol=RTOL, atol=0)
+        np.testing.assert_allclose(got, truth, rtol=RTOL, atol=0)
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+        assert np.array_equal(got.view(np.uint32), truth.view(np.uint32))
 
 
 def test_static_largest_table_and_refusal_beyond_it():
@@ -67,6 +71,8 @@ def test_static_largest_table_and_refusal_beyond_it():
     st, got = _static(torch, q4, rows, cols, cq, cd, cs, stream)
     assert st == 0, nb.lib().imi_cuda_error().decode()
     np.testing.assert_allclose(got, want, rtol=RTOL, atol=0)
+    truth = np.asarray(oracle.q4_matvec(q4, rows, cols, cq, cd, cs), np.float32).reshape(got.shape)
+    np.testing.assert_allclose(got, truth, rtol=RTOL, atol=0)
     # one more row passes the limit: refused before any device work, with the limit in the message
     st, _ = _static(torch, np.zeros((rows + 1) * (cols // 32) * 18, np.uint8), rows + 1, cols,
                     np.zeros(cols, np.int8), np.zeros(cols // 32, np.float32), np.zeros(cols // 32, np.float32), stream)
