@@ -156,6 +156,14 @@ imi_cuda_status imi_cuda_q6k_scores(int device, const uint8_t *q6k, int rows, in
 imi_cuda_status imi_cuda_q4_matvec(int device, const uint8_t *q4, int rows, int cols, const int8_t *xq,
                                    const float *xd, const float *xs, int ncol, float *out, int32_t *block_dots);
 
+/* The isolated table read timed on the device (the configs[4] sweep; imi/kernels/q4x2_bench.cpp's measurement): a
+ * rows x cols Q4_0 table (random codes and scales, the engine's row layout) times ncol 8-bit inputs, `reps` reads after
+ * one untimed read, CUDA events on one stream. The table is replicated in device memory until the copies pass 256 MB
+ * and the reads rotate through them, so every read comes from HBM (L2 holds 126 MB). *ms = mean milliseconds per
+ * read of all ncol inputs; *bytes = algorithmic bytes per read: the table once, the inputs' codes and scales, the
+ * outputs. ncol 1..256; cols a multiple of 256. */
+imi_cuda_status imi_cuda_bench_matvec(int device, int rows, int cols, int ncol, int reps, float *ms, size_t *bytes);
+
 /* ---- without allocation ---- */
 
 /* No counterpart in the reference (imi's own path has no device memory): imi_cuda_q4_matvec on device buffers that

@@ -77,6 +77,8 @@ def lib():
         L.imi_cuda_q4_matvec.argtypes = [C.c_int, _vp, C.c_int, C.c_int, _vp, _fp, _fp, C.c_int, _fp, _ip]
         L.imi_cuda_q4_matvec_static.argtypes = [C.c_int, _vp, C.c_int, C.c_int, _vp, _vp, _vp, C.c_int, _vp, _vp]
         L.imi_cuda_check_wait_timeout.argtypes = [C.c_int, C.c_double]
+        L.imi_cuda_bench_matvec.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_float),
+                                            C.POINTER(C.c_size_t)]
         _L = L
     return _L
 
@@ -303,6 +305,13 @@ def q4_matvec(q4, rows: int, cols: int, xq, xd, xs, dots: bool = False, device: 
     _check(lib().imi_cuda_q4_matvec(device, _ptr(q4), rows, cols, _ptr(xq), _ptr(xd), _ptr(xs), ncol, _ptr(out),
                                     _ptr(dd)))
     return (out, dd) if dots else out
+
+
+def bench_matvec(rows: int, cols: int, ncol: int, reps: int = 20, device: int = 0):
+    """The isolated table read timed on the device (imi_cuda_bench_matvec): (mean ms per read, algorithmic bytes)."""
+    ms, b = C.c_float(), C.c_size_t()
+    _check(lib().imi_cuda_bench_matvec(device, rows, cols, ncol, reps, C.byref(ms), C.byref(b)))
+    return float(ms.value), int(b.value)
 
 
 class Seoul:

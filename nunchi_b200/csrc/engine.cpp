@@ -1113,6 +1113,101 @@ imi_cuda_status imi_cuda_q4_matvec(int device, const uint8_t *q4, int rows, int 
     return IMI_OK;
 }
 
+imi_cuda_status imi_cuda_bench_matvec(int device, int rows, int cols, int ncol, int reps, float *ms, size_t *bytes) {
+    if (rows <= 0 || cols <= 0 || cols % 256 || ncol < 1 || ncol > 256 || reps < 1 || !ms)
+        return fail(IMI_E_ARG, "bad bench_matvec arguments (cols a multiple of 256, 1..256 inputs)");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) return fail(IMI_E_NODEV, "no CUDA device");
+    CK(cudaSetDevice(device));
+    CK(prepare_kernels());
+    int sms = 148;
+    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+    const int nb = cols / 32, row_bytes = nb * 18;
+    const size_t tb = (size_t) rows * row_bytes, tstride = (tb + 255) / 256 * 256, rot = (size_t) 256 << 20;
+    const int copies = (int) std::max<size_t>(1, (rot + tb - 1) / tb);
+    // the table (engine layout: codes, then fp16 scales) and the inputs, from a fixed xorshift sequence
+    std::vector<uint8_t> host(tb);
+    uint64_t x = 0x9E3779B97F4A7C15ull;
+    auto next = [&]() { x ^= x << 13; x ^= x >> 7; x ^= x << 17; return x; };
+    for (int r = 0; r < rows; r++) {
+        uint8_t *row = host.data() + (size_t) r * row_bytes;
+        for (int i = 0; i < nb * 16; i += 8) { const uint64_t v = next(); memcpy(row + i, &v, 8); }
+        for (int j = 0; j < nb; j++) {   // fp16 scales in [2^-9, 2^-7): exponent 6..7, random mantissa
+            const uint16_t h = (uint16_t) (((6 + (next() & 1)) << 10) | (next() & 0x3ff));
+            memcpy(row + nb * 16 + 2 * j, &h, 2);
+        }
+    }
+    std::vector<int8_t> hq((size_t) ncol * cols);
+    for (auto &q : hq) q = (int8_t) ((int) (next() % 255) - 127);
+    std::vector<float> hd((size_t) ncol * nb, 0.01f), hs((size_t) ncol * nb, 0.5f);
+    auto al = [](size_t n) { return (n + 255) / 256 * 256; };
+    const size_t o_q = (size_t) copies * tstride, o_d = o_q + al(hq.size()), o_s = o_d + al(hd.size() * 4),
+                 o_o = o_s + al(hs.size() * 4), o_c = o_o + al((size_t) ncol * rows * 4),
+                 total = o_c + al(sizeof(Col) * MV_MAX_COLS) + 256;
+    uint8_t *m = nullptr;
+    CK(cudaMalloc(&m, total));
+    cudaStream_t st = nullptr;
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    cudaError_t r = cudaMemcpy(m, host.data(), tb, cudaMemcpyHostToDevice);
+    for (int c = 1; c < copies && r == cudaSuccess; c++) r = cudaMemcpy(m + c * tstride, m, tb, cudaMemcpyDeviceToDevice);
+    if (r == cudaSuccess) r = cudaMemcpy(m + o_q, hq.data(), hq.size(), cudaMemcpyHostToDevice);
+    if (r == cudaSuccess) r = cudaMemcpy(m + o_d, hd.data(), hd.size() * 4, cudaMemcpyHostToDevice);
+    if (r == cudaSuccess) r = cudaMemcpy(m + o_s, hs.data(), hs.size() * 4, cudaMemcpyHostToDevice);
+    if (r == cudaSuccess) r = cudaMemset(m + o_c, 0, al(sizeof(Col) * MV_MAX_COLS) + 256);
+    if (r == cudaSuccess) r = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+    // one read of all inputs from table copy k: groups of up to 8 inputs per read of the table (the small-batch
+    // kernel), programmatic dependent launches one after another as the engine's step runs them
+    auto read = [&](int k) -> cudaError_t {
+        for (int c0 = 0; c0 < ncol; c0 += MV_MAX_COLS) {
+            MvArgs a = {};
+            a.W = m + (size_t) (k % copies) * tstride; a.rows = rows; a.cols = cols; a.row_bytes = row_bytes; a.unit = 1;
+            a.cols_d = (const Col *) (m + o_c); a.ncol = std::min(MV_MAX_COLS, ncol - c0);
+            a.q8_q = (const int8_t *) (m + o_q) + (size_t) c0 * cols;
+            a.q8_d = (const float *) (m + o_d) + (size_t) c0 * nb;
+            a.q8_s = (const float *) (m + o_s) + (size_t) c0 * nb;
+            a.out = (float *) (m + o_o) + (size_t) c0 * rows; a.out_stride = rows;
+            a.err = (int *) (m + o_c + al(sizeof(Col) * MV_MAX_COLS)); a.ring_layer = -1;
+            const int grid = std::max(1, std::min(sms, rows));
+            plan_stages(a, P_Q8IN, 1, grid);
+            const cudaError_t e = launch_table(P_Q8IN, E_STORE, a, grid, st, true);
+            if (e != cudaSuccess) return e;
+        }
+        return cudaSuccess;
+    };
+    if (r == cudaSuccess) r = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+    if (r == cudaSuccess) {
+        cudaError_t rc = cudaSuccess;
+        for (int i = 0; i < reps && rc == cudaSuccess; i++) rc = read(i);
+        r = cudaStreamEndCapture(st, &g);
+        if (rc != cudaSuccess) r = rc;
+    }
+    if (r == cudaSuccess) r = cudaGraphInstantiate(&ge, g, 0);
+    if (r == cudaSuccess) r = cudaEventCreate(&e0);
+    if (r == cudaSuccess) r = cudaEventCreate(&e1);
+    if (r == cudaSuccess) r = cudaGraphLaunch(ge, st);   // untimed: first touch, code and parameters warm
+    if (r == cudaSuccess) r = cudaEventRecord(e0, st);
+    if (r == cudaSuccess) r = cudaGraphLaunch(ge, st);
+    if (r == cudaSuccess) r = cudaEventRecord(e1, st);
+    if (r == cudaSuccess) r = cudaEventSynchronize(e1);
+    float t = 0;
+    if (r == cudaSuccess) r = cudaEventElapsedTime(&t, e0, e1);
+    int herr = 0;
+    if (r == cudaSuccess) r = cudaMemcpy(&herr, m + o_c + al(sizeof(Col) * MV_MAX_COLS), 4, cudaMemcpyDeviceToHost);
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    if (ge) cudaGraphExecDestroy(ge);
+    if (g) cudaGraphDestroy(g);
+    if (st) cudaStreamDestroy(st);
+    cudaFree(m);
+    if (r != cudaSuccess) return fail(IMI_E_CUDA, std::string("bench_matvec: ") + cudaGetErrorString(r));
+    if (herr) return fail(IMI_E_TIMEOUT, "bench_matvec: a device-side wait gave up");
+    *ms = t / reps;
+    if (bytes) *bytes = tb + hq.size() + 8 * (size_t) ncol * nb + 4 * (size_t) ncol * rows;
+    return IMI_OK;
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // the same table read without allocating (imi_cuda_q4_matvec_static)
 // ---------------------------------------------------------------------------------------------------------------

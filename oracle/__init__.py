@@ -36,14 +36,15 @@ def _ptr(a):
 
 
 class Oracle:
-    """imi's step restated in C (liboracle.so)."""
+    """imi's step restated in C (liboracle.so). exp="cr": the build whose exponential is correctly rounded
+    (liboracle_cr.so) in place of the C library's expf, the only operation in which the engine may differ from imi."""
 
-    _L = None
+    _libs = {}
 
     @classmethod
-    def lib(cls):
-        if cls._L is None:
-            L = _lib("liboracle.so")
+    def lib(cls, exp: str = "libc"):
+        if exp not in cls._libs:
+            L = _lib({"libc": "liboracle.so", "cr": "liboracle_cr.so"}[exp])
             L.or_load.restype = C.c_void_p
             L.or_load.argtypes = [C.c_char_p, C.c_int, C.c_int]
             L.or_error.restype = C.c_char_p
@@ -76,11 +77,11 @@ class Oracle:
             L.or_h2f.restype = C.c_float
             L.or_h2f.argtypes = [C.c_uint16]
             L.or_rope_angles.argtypes = [C.c_int, C.c_int, C.c_float, C.c_void_p, C.c_void_p, C.c_void_p]
-            cls._L = L
-        return cls._L
+            cls._libs[exp] = L
+        return cls._libs[exp]
 
-    def __init__(self, path: str, n_ctx: int = 512, threads: int = 0):
-        L = self.lib()
+    def __init__(self, path: str, n_ctx: int = 512, threads: int = 0, exp: str = "libc"):
+        self.L = L = self.lib(exp)
         self.h = L.or_load(path.encode(), n_ctx, threads or os.cpu_count() or 1)
         if not self.h:
             raise RuntimeError(f"oracle load failed: {L.or_error().decode()}")
@@ -96,7 +97,7 @@ class Oracle:
     def __del__(self):
         try:
             self.state = None
-            self.lib().or_free(self.h)
+            self.L.or_free(self.h)
         except Exception:
             pass
 
@@ -133,7 +134,7 @@ class Oracle:
 
 class OracleState:
     def __init__(self, m: Oracle):
-        self.m, self.L = m, m.lib()
+        self.m, self.L = m, m.L
         self.h = self.L.or_state_new(m.h)
 
     def __del__(self):

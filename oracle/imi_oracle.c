@@ -197,7 +197,15 @@ static float dot_h(const float *q, const uint16_t *k, int n) {   /* seoul.cpp:29
     const float r0 = a[0] + a[4], r1 = a[1] + a[5], r2 = a[2] + a[6], r3 = a[3] + a[7];
     return (r0 + r2) + (r1 + r3);
 }
-static inline float silu(float x) { return x / (1.0f + expf(-x)); }   /* seoul.cpp:48 */
+/* imi calls the C library's expf (seoul.cpp:48,446,451). Built with -DOR_EXPF_CR (liboracle_cr.so) the oracle uses
+ * the correctly rounded exponential instead, the one the engine computes on the device: the two builds differ only
+ * there, which lets the tests tell expf's own rounding apart from everything else. */
+#ifdef OR_EXPF_CR
+static inline float or_expf(float x) { return (float) exp((double) x); }
+#else
+static inline float or_expf(float x) { return expf(x); }
+#endif
+static inline float silu(float x) { return x / (1.0f + or_expf(-x)); }   /* seoul.cpp:48 */
 
 /* ---------------- load (seoul.cpp:93-186 with a Q4_0 tied word table) ---------------- */
 
@@ -449,7 +457,7 @@ static void run(const or_model *m, or_state *S, int32_t token, const float *embd
                         mx = mx < sc[t] ? sc[t] : mx;
                     }
                     double sum = 0;
-                    for (int t = 0; t < nk; t++) { sc[t] = expf(sc[t] - mx); sum += sc[t]; }
+                    for (int t = 0; t < nk; t++) { sc[t] = or_expf(sc[t] - mx); sum += sc[t]; }
                     const float inv = (float) (1.0 / sum);
                     for (int i = 0; i < D; i++) o[i] = 0.0f;
                     for (int t = 0; t < nk; t++) {
@@ -457,7 +465,7 @@ static void run(const or_model *m, or_state *S, int32_t token, const float *embd
                         const uint16_t *vr = vc + (size_t) (s0 + t) * kvd + g * D;
                         for (int i = 0; i < D; i++) o[i] = fmaf(p, or_h2f(vr[i]), o[i]);
                     }
-                    const float gate = 1.0f / (1.0f + expf(-qkv[H * D + 2 * kvd + h]));
+                    const float gate = 1.0f / (1.0f + or_expf(-qkv[H * D + 2 * kvd + h]));
                     for (int i = 0; i < D; i++) S->att[h * D + i] = o[i] * gate;
                 }
             }

@@ -41,6 +41,6 @@ def seoul_path():
 def _built():
     """The oracle and the engine library are built in-tree (build() does both); build here if missing."""
     import subprocess
-    if not os.path.exists(os.path.join(ROOT, "oracle", "liboracle.so")):
+    if not all(os.path.exists(os.path.join(ROOT, "oracle", f)) for f in ("liboracle.so", "liboracle_cr.so")):
         subprocess.run(["make", "-C", os.path.join(ROOT, "oracle")], check=True, capture_output=True)
     yield

@@ -1,11 +1,18 @@
 """Shared checks of the parity tests (engine on the GPU against the oracle, the C restatement of imi's step that
 tests/test_oracle.py pins bit for bit to the reference's own code).
 
-Tolerance (north star): word scores and hidden states within TOL = 1e-3 of max|value| (max-abs relative). The engine
-keeps imi's float order everywhere, so most steps are bit-identical; the one operation that can differ is expf
-(correctly rounded on the device, glibc's differs on ~0.06% of inputs). A 1-ulp difference there can move one 8-bit
-activation code by one step (1/127 of its block's maximum), which then stays in the attention cache.
-Greedy picks are identical except at logged ties (oracle's top two scores within TIE = 1e-4 of max|score|)."""
+The engine keeps imi's float order everywhere. The one operation whose rounding it does not share is expf: imi calls
+the C library's expf, the engine computes the correctly rounded exponential (they differ on ~0.06% of inputs). The
+oracle comes in two builds (oracle.Oracle(exp=...)): "libc" calls the C library's expf and is the reference bit for bit;
+"cr" uses the correctly rounded exponential and is otherwise the same code. Hence:
+  * against the "cr" oracle the engine is bit-exact: every step from identical memory (paired_step: the oracle is given
+    the engine's K/V caches, conv memory and position from its checkpoint image) and whole free-running sequences;
+  * against the "libc" oracle (= imi) a 1-ulp expf difference can move one 8-bit activation code by one step (1/127 of
+    its block's maximum), which then stays in the attention cache and the conv memory. That difference is imi's own
+    expf against the correctly rounded one; it is recorded per step, and the north star's bound holds at every
+    position: against the reference's fp64 truth key the engine's max-abs error (relative to max|truth|) is at most
+    imi's own plus TOL = 1e-3; greedy picks are identical except at logged ties (the top two scores within TIE = 1e-4
+    of max|score|)."""
 from __future__ import annotations
 
 import json
@@ -82,3 +89,22 @@ def import_memory(state, o_state):
     m = state.unpack()
     o_state.import_memory(m["pos"], m["k"], m["v"], m["conv"])
     return m["pos"]
+
+
+def paired_step(g, o_state, token=-1, embd=None, want_logits=True, where="step", libc=None):
+    """One step of the engine state g and the "cr" oracle state o_state from identical memory (the engine's, imported
+    into the oracle first): hidden state and (when wanted) scores bit for bit. With libc (a "libc" oracle state, i.e.
+    imi's own float results) the same step is taken there too and its max-abs relative difference recorded.
+    Returns (rel hidden vs libc, rel scores vs libc) (zeros without libc)."""
+    import_memory(g, o_state)
+    if libc is not None:
+        import_memory(g, libc)
+    g.step(int(token), embd, want_logits)
+    o_state.step(int(token), embd, want_logits)
+    assert same_bits(g.hidden, o_state.hidden), f"{where}: hidden state differs ({rel(g.hidden, o_state.hidden):.3g})"
+    if want_logits:
+        assert same_bits(g.logits, o_state.logits), f"{where}: scores differ ({rel(g.logits, o_state.logits):.3g})"
+    if libc is None:
+        return 0.0, 0.0
+    libc.step(int(token), embd, want_logits)
+    return rel(g.hidden, libc.hidden), (rel(g.logits, libc.logits) if want_logits else 0.0)

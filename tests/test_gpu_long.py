@@ -3,35 +3,24 @@
 * Long-context attention: the engine's attention stages cached V rows in shared-memory tiles of 512 positions
   (head_dim 64) or 256 (head_dim 128), two tiles in flight; lengths just below, at and above a tile edge and several
   tiles long exercise the refill and the alternating tile buffers. At each length the oracle is given exactly the
-  engine's memory (checkpoint image: K/V caches, conv memory, position) and both take one step, so the comparison
-  isolates the step at that length from drift accumulated before it (seoul.cpp:425-456, 589-621).
+  engine's memory (checkpoint image: K/V caches, conv memory, position) and both take one step, bit for bit with the
+  "cr" oracle (tests/parity.py), imi's own numbers ("libc") recorded (seoul.cpp:425-456, 589-621).
 * configs[1] (BASELINE): the Seoul shape, conversation A after 1024 ids (seed 1), B after 256 (seed 2), 128 greedy
-  steps riding (one table read for both): tokens, scores, hidden states and memory byte-identical to running each
-  alone; steps at positions 1024+ checked against the oracle from imported memory.
+  steps riding (one table read for both): picks, scores, hidden states and memory byte-identical to running each
+  alone; A's steps at positions 1024+ bit for bit the oracle's from its memory.
 * sessions at contexts 1500-2048 stepped together equal stepping each alone, byte for byte, and one of them
-  against the oracle."""
+  the oracle's from its memory."""
 import numpy as np
 import pytest
 
 import nunchi_b200 as nb
 import oracle
 from nunchi_b200 import synth
-from parity import TOL, bits, close, follow_greedy, import_memory, record, rel, same_bits
+from parity import follow_greedy, import_memory, paired_step, record, same_bits
 
 pytestmark = pytest.mark.gpu
 
 LENGTHS = (511, 512, 513, 1025, 2047)
-
-
-def step_both(g, o, token, where):
-    """one step of the engine state g and the oracle state o (same memory beforehand); returns (rel hidden, rel
-    scores, bit-identical)"""
-    g.step(int(token))
-    o.step(int(token))
-    hg, ho, lg, lo = g.hidden, o.hidden, g.logits, o.logits
-    rh = close(hg, ho, where + " hidden")
-    rl = close(lg, lo, where + " scores")
-    return rh, rl, same_bits(hg, ho) and same_bits(lg, lo)
 
 
 @pytest.mark.parametrize("name", ["tiny", "wide_heads"])
@@ -41,36 +30,33 @@ def test_long_context_step_vs_oracle(name):
     path = synth.cached_gguf(name)
     n_ctx = 2304
     e = nb.Engine(path, n_ctx=n_ctx)
-    o = oracle.Oracle(path, n_ctx=n_ctx)
+    cr, lc = oracle.Oracle(path, n_ctx=n_ctx, exp="cr"), oracle.Oracle(path, n_ctx=n_ctx)
     g = e.new_state()
     ids = synth.random_ids(n_ctx, e.n_vocab, 31)
-    exact = 0
     for L in LENGTHS:
-        g.step_batch(tokens=ids[g.pos:L], want_logits=False)
+        if L > g.pos:
+            g.step_batch(tokens=ids[g.pos:L], want_logits=False)
         assert g.pos == L
-        assert import_memory(g, o.state) == L
-        rh, rl, same = step_both(g, o.state, ids[L], f"{name} cached length {L}")
-        exact += same
-        record(f"long_context_{name}", cached=L, rel_hidden=rh, rel_scores=rl, bit_identical=bool(same))
-    assert exact >= len(LENGTHS) - 1, f"only {exact} of {len(LENGTHS)} long-context steps bit-identical"
+        rh, rl = paired_step(g, cr.state, ids[L], where=f"{name} cached length {L}", libc=lc.state)
+        record(f"long_context_{name}", cached=L, bit_exact_vs_cr=True, libc_rel_hidden=rh, libc_rel_scores=rl)
 
 
 @pytest.mark.parametrize("name", ["tiny", "wide_heads"])
-def test_long_context_prefill_chunk_vs_oracle(name):
-    """a prefill chunk whose positions straddle a V tile edge (the batched read writes K/V before its attention)"""
+def test_long_context_prefill_chunk(name):
+    """a batched read whose positions straddle a V tile edge (the batched read writes K/V before its attention): bit
+    for bit the oracle's batched read from the same memory"""
     path = synth.cached_gguf(name)
     e = nb.Engine(path, n_ctx=1100)
-    o = oracle.Oracle(path, n_ctx=1100)
+    cr = oracle.Oracle(path, n_ctx=1100, exp="cr")
     g = e.new_state()
     ids = synth.random_ids(1040, e.n_vocab, 32)
     g.step_batch(tokens=ids[:1020], want_logits=False)
-    import_memory(g, o.state)
+    import_memory(g, cr.state)
     hg = g.step_batch(tokens=ids[1020:], want_logits=True, hidden_all=True)
-    ho = o.state.step_batch(tokens=ids[1020:], want_logits=True, hidden_all=True)
-    worst = max(rel(hg[i], ho[i]) for i in range(len(hg)))
-    record(f"long_prefill_{name}", rel_hidden=worst, rel_scores=rel(g.logits, o.state.logits))
-    assert worst <= TOL
-    close(g.logits, o.state.logits, f"{name} prefill chunk at 1020..1039 scores")
+    ho = cr.state.step_batch(tokens=ids[1020:], want_logits=True, hidden_all=True)
+    assert np.array_equal(hg.view(np.uint32), ho.view(np.uint32))
+    assert same_bits(g.logits, cr.state.logits)
+    record(f"long_prefill_{name}", bit_exact_vs_cr=True)
 
 
 def test_configs1_riding_equals_alone_seoul(seoul_path, record_property):
@@ -83,7 +69,7 @@ def test_configs1_riding_equals_alone_seoul(seoul_path, record_property):
     a1.load(a.save())
     b1.load(b.save())
     # the oracle from A's memory at position 1024: its first greedy steps against the riding engine's
-    o = oracle.Oracle(seoul_path, n_ctx=1024 + 16)
+    o = oracle.Oracle(seoul_path, n_ctx=1024 + 16, exp="cr")
     import_memory(a, o.state)
     o.state.step(int(a.argmax()[0]))   # the oracle's own step at position 1024 needs the prompt's last pick
     ride = nb.greedy([a, b], 128)
@@ -95,30 +81,26 @@ def test_configs1_riding_equals_alone_seoul(seoul_path, record_property):
         assert same_bits(x.logits, y.logits) and same_bits(x.hidden, y.hidden)
         assert x.save() == y.save(), "riding and alone left different memory"
     record("configs1_riding_vs_alone", steps=128, identical=True)
-    # the oracle's scores at position 1024 against the engine's first riding step (a's pick there is ride[0, 0])
-    lo = o.state.logits
-    assert int(np.argmax(lo)) == int(ride[0, 0]) or np.sort(lo)[-1] - np.sort(lo)[-2] <= 1e-4 * np.abs(lo).max()
-    record_property("configs1_first_pick_oracle", int(np.argmax(lo)))
+    # the oracle's pick at position 1024 against the engine's first riding step's (a's pick there is ride[0, 0])
+    assert int(np.argmax(o.state.logits)) == int(ride[0, 0])
+    record_property("configs1_first_pick_oracle", int(np.argmax(o.state.logits)))
 
 
 def test_configs1_steps_vs_oracle_seoul(seoul_path, record_property):
-    """configs[1]'s conversation A at positions 1024..1031 against the oracle given its memory, then 8 greedy picks
-    of the oracle's own loop beside the device's."""
+    """configs[1]'s conversation A at positions 1024..1027 against the oracle given its memory, bit for bit ("cr"),
+    imi's own numbers recorded ("libc"); then 8 greedy picks of the oracle's own loop beside the device's."""
     e = nb.Engine(seoul_path, n_ctx=1024 + 32)
     a = e.new_state()
     a.step_batch(synth.random_ids(1024, e.n_vocab, 1), want_logits=True)
-    o = oracle.Oracle(seoul_path, n_ctx=1024 + 32)
-    import_memory(a, o.state)
-    worst = 0.0
-    toks = synth.random_ids(4, e.n_vocab, 41)
-    for k, t in enumerate(toks):
-        rh, rl, _ = step_both(a, o.state, t, f"seoul configs[1] A position {1024 + k}")
-        worst = max(worst, rl)
+    cr, lc = oracle.Oracle(seoul_path, n_ctx=1024 + 32, exp="cr"), oracle.Oracle(seoul_path, n_ctx=1024 + 32)
+    worst_h, worst_s = 0.0, 0.0
+    for k, t in enumerate(synth.random_ids(4, e.n_vocab, 41)):
+        rh, rl = paired_step(a, cr.state, t, where=f"seoul configs[1] A position {1024 + k}", libc=lc.state)
+        worst_h, worst_s = max(worst_h, rh), max(worst_s, rl)
     ids = nb.greedy([a], 8)[:, 0]
-    n, tie = follow_greedy(o.state, ids, "seoul configs[1] A greedy from 1028", record_property)
-    record("configs1_A_vs_oracle", rel_scores_max=worst, greedy_identical=n, tie=tie)
-    if tie is None:
-        close(a.logits, o.state.logits, "seoul configs[1] A after 8 greedy steps")
+    n, _ = follow_greedy(cr.state, ids, "seoul configs[1] A greedy from 1028 vs cr", record_property)
+    assert n == 8 and same_bits(a.logits, cr.state.logits)
+    record("configs1_A_vs_oracle", bit_exact_vs_cr=True, libc_rel_hidden_max=worst_h, libc_rel_scores_max=worst_s)
 
 
 def test_configs3_long_sessions_multi_equals_alone(seoul_path):
@@ -135,7 +117,7 @@ def test_configs3_long_sessions_multi_equals_alone(seoul_path):
         c = e.new_state()
         c.load(s.save())
         alone.append(c)
-    o = oracle.Oracle(seoul_path, n_ctx=2048 + 8)
+    o = oracle.Oracle(seoul_path, n_ctx=2048 + 8, exp="cr")
     import_memory(multi[0], o.state)
     for k in range(4):
         toks = np.array([s.argmax()[0] for s in multi], np.int32)
@@ -144,9 +126,8 @@ def test_configs3_long_sessions_multi_equals_alone(seoul_path):
             s.step(int(t))
         if k == 0:
             o.state.step(int(toks[0]))
-            r = close(multi[0].logits, o.state.logits, f"configs[3] session at {lens[0]} scores")
-            record("configs3_session_vs_oracle", cached=lens[0], rel_scores=r,
-                   bit_identical=same_bits(multi[0].logits, o.state.logits))
+            assert same_bits(multi[0].logits, o.state.logits) and same_bits(multi[0].hidden, o.state.hidden)
+            record("configs3_session_vs_oracle", cached=lens[0], bit_exact_vs_cr=True)
     for m, a in zip(multi, alone):
         assert m.pos == a.pos
         assert same_bits(m.logits, a.logits) and same_bits(m.hidden, a.hidden)

@@ -250,3 +250,23 @@ def test_oracle_memory_import_continues_identically(tiny_path):
         assert np.array_equal(bits(s.logits), bits(t.logits)) and np.array_equal(bits(s.hidden), bits(t.hidden))
     with pytest.raises(ValueError):
         t.import_memory(65, np.zeros((2, 65, 128), np.uint16), np.zeros((2, 65, 128), np.uint16), conv)
+
+
+def test_oracle_builds_differ_only_in_the_exponential(tiny_path):
+    """liboracle_cr.so (correctly rounded exponential, as the engine computes it) against liboracle.so (the C library's
+    expf, as imi): the same code otherwise, so steps without any exponential in play agree bit for bit and steps with
+    it differ at most by what a few 1-ulp expf differences do."""
+    a, b = oracle.Oracle(tiny_path, n_ctx=32), oracle.Oracle(tiny_path, n_ctx=32, exp="cr")
+    assert a.L is not b.L
+    diff = 0.0
+    for t in synth.random_ids(8, a.n_vocab, 3):
+        a.step(int(t))
+        b.step(int(t))
+        diff = max(diff, float(np.abs(a.logits - b.logits).max() / np.abs(a.logits).max()))
+    assert diff < 1e-2
+    x = np.random.default_rng(1).standard_normal(512).astype(np.float32)
+    qa = [np.asarray(v) for v in oracle.cut(x)]
+    L = oracle.Oracle.lib("cr")
+    q, d, s = np.zeros(512, np.int8), np.zeros(16, np.float32), np.zeros(16, np.float32)
+    L.or_cut(x.ctypes.data, 512, q.ctypes.data, d.ctypes.data, s.ctypes.data)
+    assert np.array_equal(q, qa[0]) and np.array_equal(bits(d), bits(qa[1])) and np.array_equal(bits(s), bits(qa[2]))
