@@ -1,21 +1,28 @@
 #!/usr/bin/env python
 """Benchmark of the B200 decode engine for imi's brain token loop.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload ride2|b1|prefill|multi64]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload ride2|b1|prefill|multi64|sweep] [--no-extra]
 
-Workload (the batch-2 "riding" step): the Seoul-shaped synthetic backbone (seed 0);
+Headline (the batch-2 "riding" step): the Seoul-shaped synthetic backbone (seed 0);
 conversation A prefilled with 1024 random ids (seed 1), conversation B with 256 (seed 2); then every timed step is
 one step2 (imi_seoul::step2, seoul.cpp:208): both conversations advance one greedy position on one read of every
-table. `--workload b1` runs configs[0] instead (32-token prompt, one conversation). Under torchrun each rank runs
-the same workload on its own GPU (whole conversations per GPU, no collective): weak scaling.
+table. Under torchrun each rank runs the same workload on its own GPU (whole conversations per GPU, no collective):
+weak scaling.
+
+The default line also carries, unless --no-extra: `b1` (configs[0]: batch-1 greedy decode after a 32-id prompt),
+`multi64` (configs[3]: 64 conversations per GPU with contexts drawn from 256..2048, one greedy position of all 64 per
+step; box tokens/s summed over the ranks) and, on one GPU, `sweep` (configs[4]: the isolated table read, N x K in
+{2048x2048, 8192x2048, 2048x8192, 97,496x2048} x B in {1, 2, 8, 32, 128}, GB/s). `--workload X` makes X the headline.
 `--workload prefill` runs configs[2] (one step = one fresh conversation reading 400 input vectors and 16 ids in
-chunks of 128, the last position's word scores; positions/s) and `--workload multi64` configs[3] (64 conversations
-per GPU with contexts drawn from 256..2048, every step one greedy position for all 64; tok/s, default 256 steps).
+chunks of 128, the last position's word scores; positions/s).
 
 One JSON line on rank 0: `value` = tokens/s of the whole job with everything resident on the device (CUDA events on
-the engine's stream, max over ranks); `e2e` = the same through the public step2 + argmax calls with host token input
-and a host read of both picks every step; `roofline` = the table-read kernel's bandwidth against the measured HBM
-peak; `cpu_baseline` = the reference's own CPU code (oracle/_ref) on this host.
+the engine's stream, max over ranks); `e2e` = the same through the public calls with host token input and a host read
+of every pick every step; `roofline` = the table-read kernel's bandwidth against the measured HBM peak;
+`step_roofline` = the whole step's algorithmic bytes (every weight once per step, each conversation's K/V and conv
+memory) over its time; `cpu_baseline` = the reference's own CPU code (oracle/_ref) on this host at all cores and at 4
+threads pinned to cores 0-3, with the CPU model.
 """
 from __future__ import annotations
 
@@ -34,7 +41,6 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 A_PROMPT, B_PROMPT, B1_PROMPT = 1024, 256, 32
-KV_BYTES_PER_POS = None   # filled from the engine shape
 
 
 def parse():
@@ -43,13 +49,14 @@ def parse():
     ap.add_argument("--steps", type=int, default=0, help="timed steps (0 = the workload's default)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["ride2", "b1", "prefill", "multi64"], default="ride2")
-    ap.add_argument("--cpu-steps", type=int, default=0, help="reference CPU sample size in steps (0 = auto)")
+    ap.add_argument("--workload", choices=["ride2", "b1", "prefill", "multi64", "sweep"], default="ride2")
+    ap.add_argument("--no-extra", action="store_true", help="headline only (no b1 / multi64 / sweep sub-objects)")
+    ap.add_argument("--extra-steps", type=int, default=64, help="timed steps of the multi64 sub-object")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     a = ap.parse_args()
     if not a.steps:
-        a.steps = {"prefill": 5, "multi64": 256}.get(a.workload, 128)
+        a.steps = {"prefill": 5, "multi64": 256, "sweep": 1}.get(a.workload, 128)
     return a
 
 
@@ -167,19 +174,23 @@ def multi_contexts(rank: int) -> list:
     return [int(x) for x in rng.integers(MULTI_CTX[0], MULTI_CTX[1] + 1, MULTI_N)]
 
 
-def workload_desc(args) -> dict:
-    if args.workload == "prefill":
+def workload_desc(workload: str) -> dict:
+    if workload == "prefill":
         return {"workload": f"configs[2] prefill: Seoul-shaped Q4_0 backbone (seed 0), a fresh conversation reads "
                             f"{PREFILL_VECS} input vectors N(0,1)*0.5 (seed 3) then {PREFILL_IDS} random ids (seed 3) "
                             f"in chunks of {PREFILL_CHUNK} (step_batch calls of 128, 128, 128, 16 vectors and 16 ids), "
                             "word scores of the last position; host inputs copied inside the timed region (the API "
                             "takes host vectors)", "tokens_per_step": PREFILL_VECS + PREFILL_IDS, "prompts": []}
-    if args.workload == "multi64":
+    if workload == "multi64":
         return {"workload": f"configs[3] {MULTI_N} sessions per GPU: contexts uniform in {MULTI_CTX[0]}..{MULTI_CTX[1]} "
-                            "(seed 4 + rank) read beforehand (not timed), then greedy steps of all sessions, 8 "
-                            "conversations per table read (the timed region runs the 8 groups one after another, "
-                            "each for all its steps)", "tokens_per_step": MULTI_N, "prompts": []}
-    if args.workload == "ride2":
+                            "(seed 4 + rank) read beforehand (not timed), then greedy steps of all sessions",
+                "tokens_per_step": MULTI_N, "prompts": []}
+    if workload == "sweep":
+        return {"workload": "configs[4] isolated Q4_0 x Q8 table read: N x K in " +
+                            ", ".join(f"{r}x{c}" for r, c in SWEEP_SHAPES) + f"; B in {list(SWEEP_B)}; random codes "
+                            "and fp16 scales, table copies rotated through more than 256 MB so every read comes from "
+                            "HBM", "tokens_per_step": 0, "prompts": []}
+    if workload == "ride2":
         return {"workload": "configs[1] riding step2: Seoul-shaped Q4_0 backbone (seed 0), conversation A after a "
                             f"{A_PROMPT}-id prompt, B after {B_PROMPT} ids, greedy, one table read per step for both",
                 "tokens_per_step": 2, "prompts": [A_PROMPT, B_PROMPT]}
@@ -188,22 +199,32 @@ def workload_desc(args) -> dict:
 
 
 def step_bytes(info, positions) -> int:
-    """Algorithmic HBM bytes of one step: every weight byte once, plus each conversation's K/V read over its
-    positions and written at the new one, plus the conv memory read and written."""
+    """Algorithmic HBM bytes of one decode step of conversations at `positions`: every weight byte once (layer tables,
+    word table, small parameters), plus each conversation's K/V read over its positions and written at the new one,
+    plus its conv memory read and written. Activations are negligible."""
     kvd = info.n_head_kv * info.head_dim
     kv = sum((p + 1) * info.n_attn * kvd * 2 * 2 + info.n_attn * kvd * 2 * 2 for p in positions)
     conv = len(positions) * (info.n_layer - info.n_attn) * 2 * info.d_conv * info.n_embd * 4
     return int(info.weight_bytes + kv + conv)
 
 
-def run_ours(args, ranks: Ranks) -> dict:
+def step_roofline(bytes_per_step: int, ms_per_step: float, pk: dict) -> dict:
+    gbs = bytes_per_step / (ms_per_step / 1e3) / 1e9
+    return {"bytes_per_step": int(bytes_per_step), "achieved_gbs": gbs, "frac": gbs / pk["hbm_gbs"],
+            "peak_gbs": pk["hbm_gbs"], "peak_source": pk["source"],
+            "bytes": "algorithmic: every weight once per step + each conversation's K/V and conv memory"}
+
+
+def run_ours(args, ranks: Ranks, workload: str, steps: int, e2e: bool = True) -> dict:
+    """configs[1] (ride2) or configs[0] (b1): the conversations' prompts read, then `steps` greedy steps replayed on
+    the device (CUDA events), then as many through the public step calls (e2e)."""
     import torch
     import nunchi_b200 as nb
     from nunchi_b200 import synth
     torch.cuda.set_device(ranks.local)
-    wl = workload_desc(args)
+    wl = workload_desc(workload)
     prompts = wl["prompts"]
-    n_ctx = max(prompts) + args.warmup + 2 * args.steps + 16
+    n_ctx = max(prompts) + args.warmup + 2 * steps + 16
     path = synth.cached_gguf("seoul", 0)
     eng = nb.Engine(path, device=ranks.local, n_ctx=n_ctx, max_batch=8)
     info = eng.info
@@ -220,7 +241,7 @@ def run_ours(args, ranks: Ranks) -> dict:
     clocks.start()
     e0, e1 = ev(), ev()
     e0.record(st)
-    nb.greedy(states, args.steps)
+    nb.greedy(states, steps)
     e1.record(st)
     e1.synchronize()
     torch.cuda.synchronize()
@@ -228,19 +249,19 @@ def run_ours(args, ranks: Ranks) -> dict:
     ranks.barrier()
     ms = ranks.max(e0.elapsed_time(e1))
     tps = wl["tokens_per_step"]
-    value = ranks.world * tps * args.steps / (ms / 1e3)
-    mid = [p + args.steps // 2 for p in pos0]
-    out = {"ms": ms, "value": value, "clocks": clk, "info": info, "mid_positions": mid}
+    value = ranks.world * tps * steps / (ms / 1e3)
+    mid = [p + steps // 2 for p in pos0]
+    out = {"ms": ms, "value": value, "clocks": clk, "info": info, "mid_positions": mid, "ncol": len(states)}
     out["step_bytes"] = step_bytes(info, mid)
-    out["launches"] = eng.launches_per_step(len(states)) * args.steps
+    out["launches"] = eng.launches_per_step(len(states)) * steps
     # end to end through the public API: host token in, step, host read of the pick, every step
-    if not args.no_e2e:
+    if e2e and not args.no_e2e:
         picks = [s.argmax()[0] for s in states]
         ranks.barrier()
         e2, e3 = ev(), ev()
         torch.cuda.synchronize()
         e2.record(st)
-        for _ in range(args.steps):
+        for _ in range(steps):
             if len(states) == 2:
                 nb.step2(states[0], picks[0], None, True, states[1], picks[1], None, True)
             else:
@@ -250,9 +271,9 @@ def run_ours(args, ranks: Ranks) -> dict:
         e3.synchronize()
         ms_e2e = ranks.max(e2.elapsed_time(e3))
         col_bytes, sess_bytes = 80, 24
-        out["e2e"] = {"value": ranks.world * tps * args.steps / (ms_e2e / 1e3), "unit": "tok/s",
+        out["e2e"] = {"value": ranks.world * tps * steps / (ms_e2e / 1e3), "unit": "tok/s",
                       "h2d_bytes_per_step": col_bytes * len(states), "d2h_bytes_per_step": (sess_bytes + 4) * len(states),
-                      "ms_per_step": ms_e2e / args.steps}
+                      "ms_per_step": ms_e2e / steps}
     # the table-read kernel alone: every layer table back to back (imi_seoul::bench_tables); the NVTX range lets a
     # profiler select exactly these launches (ncu --nvtx --nvtx-include "bench_tables/")
     torch.cuda.nvtx.range_push("bench_tables")
@@ -279,7 +300,12 @@ def prefill_calls(s, vecs, ids):
     s.step_batch(ids, want_logits=True)
 
 
-def run_prefill(args, ranks: Ranks) -> dict:
+def prefill_reads() -> int:
+    """step_batch calls of one configs[2] prefill: the vector chunks, then the ids"""
+    return -(-PREFILL_VECS // PREFILL_CHUNK) + 1
+
+
+def run_prefill(args, ranks: Ranks, steps: int) -> dict:
     import torch
     import nunchi_b200 as nb
     from nunchi_b200 import synth
@@ -301,7 +327,7 @@ def run_prefill(args, ranks: Ranks) -> dict:
     t0 = time.perf_counter()
     e0.record(st)
     picks = []
-    for _ in range(args.steps):
+    for _ in range(steps):
         s.reset()
         prefill_calls(s, vecs, ids)
         picks.append(s.argmax()[0])   # the host read of the prefill's result (the first greedy word)
@@ -313,17 +339,18 @@ def run_prefill(args, ranks: Ranks) -> dict:
     ms, ms_wall = ranks.max(e0.elapsed_time(e1)), ranks.max(wall * 1e3)
     assert len(set(picks)) == 1, "prefills of the same inputs gave different picks"
     n_pos = PREFILL_VECS + PREFILL_IDS
-    groups = sum(-(-min(PREFILL_CHUNK, PREFILL_VECS - a) // 8) for a in range(0, PREFILL_VECS, PREFILL_CHUNK))
-    groups += -(-PREFILL_IDS // 8)
-    out = {"ms": ms, "value": ranks.world * n_pos * args.steps / (ms / 1e3), "clocks": clk, "info": info, "ncol": 8}
-    out["launches"] = (groups * (eng.launches_per_step(1, 0) + info.n_attn) + 1) * args.steps
-    out["e2e"] = {"value": ranks.world * n_pos * args.steps / (ms_wall / 1e3), "unit": "positions/s",
+    out = {"ms": ms, "value": ranks.world * n_pos * steps / (ms / 1e3), "clocks": clk, "info": info, "ncol": 8}
+    out["launches"] = eng.prefill_launches(PREFILL_VECS, PREFILL_CHUNK, PREFILL_IDS) * steps
+    out["e2e"] = {"value": ranks.world * n_pos * steps / (ms_wall / 1e3), "unit": "positions/s",
                   "h2d_bytes_per_step": int(vecs.nbytes + ids.nbytes), "d2h_bytes_per_step": 8,
-                  "ms_per_step": ms_wall / args.steps, "clock": "host wall clock around the same calls"}
+                  "ms_per_step": ms_wall / steps, "clock": "host wall clock around the same calls"}
     t_ms, t_bytes = eng.bench_tables(ncol=8, reps=20)
     out["tables"] = {"ms": t_ms, "bytes": t_bytes}
-    # what this design reads: every layer table once per group of 8 positions, plus the word table once
-    out["step_bytes"] = int(groups * t_bytes + table_bytes_word(info))
+    # algorithmic: every weight once per step_batch call (the configuration's chunks), K/V of the positions written
+    # once and read by the later ones; the word table once (the last position's scores)
+    kvd = info.n_head_kv * info.head_dim
+    out["step_bytes"] = int(prefill_reads() * (info.weight_bytes - table_bytes_word(info)) + table_bytes_word(info)
+                            + info.n_attn * kvd * 4 * n_pos * (n_pos + 1) // 2)
     # the contraction (2 flops per weight per position; Q4_0 holds 32 weights in 18 bytes) + the last word scores
     out["flops_per_step"] = 2 * (t_bytes * 16 // 9) * n_pos + 2 * info.n_vocab * info.n_embd
     s.close()
@@ -336,13 +363,14 @@ def table_bytes_word(info) -> int:
     return info.n_vocab * info.n_embd // 32 * 18
 
 
-def run_multi(args, ranks: Ranks) -> dict:
+def run_multi(args, ranks: Ranks, steps: int, e2e: bool = True) -> dict:
+    """64 sessions per GPU, contexts read beforehand (not timed), then `steps` greedy steps of all."""
     import torch
     import nunchi_b200 as nb
     from nunchi_b200 import synth
     torch.cuda.set_device(ranks.local)
     ctx = multi_contexts(ranks.rank)
-    n_ctx = MULTI_CTX[1] + args.warmup + 2 * args.steps + 8   # warm-up, timed steps, end-to-end steps
+    n_ctx = MULTI_CTX[1] + args.warmup + 2 * steps + 8   # warm-up, timed steps, end-to-end steps
     eng = nb.Engine(synth.cached_gguf("seoul", 0), device=ranks.local, n_ctx=n_ctx, max_batch=MULTI_N)
     info = eng.info
     states = [eng.new_state() for _ in range(MULTI_N)]
@@ -353,9 +381,7 @@ def run_multi(args, ranks: Ranks) -> dict:
     prefill_s = time.perf_counter() - t0
     st = torch.cuda.ExternalStream(eng.stream)
     ev = lambda: torch.cuda.Event(enable_timing=True)   # noqa: E731
-    groups = [states[g:g + 8] for g in range(0, MULTI_N, 8)]   # device greedy runs 8 conversations per call
-    for g in groups:
-        nb.greedy(g, args.warmup)
+    nb.greedy(states, args.warmup)
     torch.cuda.synchronize()
     ranks.barrier()
     pos0 = [s.pos for s in states]
@@ -363,33 +389,31 @@ def run_multi(args, ranks: Ranks) -> dict:
     clocks.start()
     e0, e1 = ev(), ev()
     e0.record(st)
-    for g in groups:   # each group's steps read every table once for its 8 conversations
-        nb.greedy(g, args.steps)
+    nb.greedy(states, steps)
     e1.record(st)
     e1.synchronize()
     clk = clocks.stop()
     ranks.barrier()
     ms = ranks.max(e0.elapsed_time(e1))
-    out = {"ms": ms, "value": ranks.world * MULTI_N * args.steps / (ms / 1e3), "clocks": clk, "info": info,
-           "ncol": 8, "prefill_s": prefill_s}
-    mid = [p + args.steps // 2 for p in pos0]
-    # every table once per group of 8 conversations, plus each conversation's own K/V and conv memory
-    out["step_bytes"] = int((len(groups) - 1) * info.weight_bytes + step_bytes(info, mid))
-    out["launches"] = eng.launches_per_step(MULTI_N, 1) * args.steps
-    if not args.no_e2e:   # host ids in, one step of all, host read of every pick, each step
+    out = {"ms": ms, "value": ranks.world * MULTI_N * steps / (ms / 1e3), "clocks": clk, "info": info,
+           "ncol": 8, "prefill_s": prefill_s, "reads_per_step": -(-MULTI_N // 8)}
+    mid = [p + steps // 2 for p in pos0]
+    out["step_bytes"] = step_bytes(info, mid)   # every weight once per step of all 64, plus each one's K/V
+    out["launches"] = eng.launches_per_step(MULTI_N, 1) * steps
+    if e2e and not args.no_e2e:   # host ids in, one step of all, host read of every pick, each step
         picks = np.array([s.argmax()[0] for s in states], np.int32)
         e2, e3 = ev(), ev()
         torch.cuda.synchronize()
         e2.record(st)
-        for _ in range(args.steps):
+        for _ in range(steps):
             nb.step_multi(states, picks)
             picks = np.array([s.argmax()[0] for s in states], np.int32)
         e3.record(st)
         e3.synchronize()
         ms_e2e = ranks.max(e2.elapsed_time(e3))
-        out["e2e"] = {"value": ranks.world * MULTI_N * args.steps / (ms_e2e / 1e3), "unit": "tok/s",
+        out["e2e"] = {"value": ranks.world * MULTI_N * steps / (ms_e2e / 1e3), "unit": "tok/s",
                       "h2d_bytes_per_step": 80 * MULTI_N, "d2h_bytes_per_step": 28 * MULTI_N,
-                      "ms_per_step": ms_e2e / args.steps}
+                      "ms_per_step": ms_e2e / steps}
     t_ms, t_bytes = eng.bench_tables(ncol=8, reps=20)
     out["tables"] = {"ms": t_ms, "bytes": t_bytes}
     for s in states:
@@ -398,21 +422,71 @@ def run_multi(args, ranks: Ranks) -> dict:
     return out
 
 
+SWEEP_SHAPES = ((2048, 2048), (8192, 2048), (2048, 8192), (97496, 2048))
+SWEEP_B = (1, 2, 8, 32, 128)
+
+
+def run_sweep(args, ranks: Ranks, pk: dict) -> dict:
+    """the isolated table read (imi_cuda_bench_matvec) for every shape and batch, GB/s of its algorithmic
+    bytes (table once, inputs' codes and scales, outputs) and, for the batches read as a contraction, TFLOP/s."""
+    import torch
+    import nunchi_b200 as nb
+    torch.cuda.set_device(ranks.local)
+    rows = []
+    for n, k in SWEEP_SHAPES:
+        for b in SWEEP_B:
+            ms, byts = nb.bench_matvec(n, k, b, reps=20, device=ranks.local)
+            gbs = byts / (ms / 1e3) / 1e9
+            tf = 2.0 * b * n * k / (ms / 1e3) / 1e12
+            rows.append({"N": n, "K": k, "B": b, "ms": ms, "bytes": byts, "gbs": gbs, "hbm_frac": gbs / pk["hbm_gbs"],
+                         "tflops": tf, "tensor_frac": tf / pk["bf16_tflops"] if pk.get("bf16_tflops") else None})
+    return {"rows": rows, "peak_gbs": pk["hbm_gbs"], "peak_tflops": pk.get("bf16_tflops"), "peak_source": pk["source"],
+            "note": "one read = every input once against the table; inputs above 8 per read are read as groups of 8 "
+                    "per table read by the small-batch kernel unless the tensor-core path runs them"}
+
+
 MULTI_CPU_SESSIONS = 4
 
 
-def run_reference_cpu(args, steps: int) -> dict:
-    """The reference's own CPU path (imi/core/seoul.cpp + tables.cpp compiled from the reference tree into
-    oracle/_ref) on this host's cores: the same workload, `steps` timed positions after the same prompts."""
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+class Pinned:
+    """Run the reference's CPU code on a fixed set of cores: the affinity is set before its thread team starts (the
+    workers inherit it) and restored afterwards (taskset -c 0-3, as the reference's 4-thread figures, README.md)."""
+
+    def __init__(self, cpus):
+        self.cpus = set(cpus) if cpus else None
+
+    def __enter__(self):
+        self.old = os.sched_getaffinity(0)
+        if self.cpus:
+            os.sched_setaffinity(0, self.cpus)
+        return self
+
+    def __exit__(self, *exc):
+        os.sched_setaffinity(0, self.old)
+
+
+def reference_threads() -> int:
+    return len(os.sched_getaffinity(0)) or os.cpu_count() or 1
+
+
+def run_reference_decode(workload: str, steps: int, threads: int) -> dict:
+    """configs[0] / configs[1] on the reference's own CPU path (imi/core/seoul.cpp + tables.cpp compiled from the
+    reference tree into oracle/_ref): `steps` timed positions after the same prompts."""
     import oracle
     from nunchi_b200 import synth
-    if args.workload == "prefill":
-        return run_reference_prefill(steps)
-    if args.workload == "multi64":
-        return run_reference_multi(steps)
-    wl = workload_desc(args)
+    wl = workload_desc(workload)
     prompts = wl["prompts"]
-    threads = os.cpu_count() or 1
     if not oracle.reference_available():
         raise RuntimeError("oracle/_ref/libimi_ref.so is not built")
     n_ctx = max(prompts) + steps + 8
@@ -442,18 +516,13 @@ def run_reference_cpu(args, steps: int) -> dict:
                       f"AVX2, {threads} threads", "ms_per_step": dt / steps * 1e3}
 
 
-def reference_threads() -> int:
-    return os.cpu_count() or 1
-
-
-def run_reference_prefill(steps: int) -> dict:
+def run_reference_prefill(steps: int, threads: int) -> dict:
     """configs[2] on the reference's CPU path: `steps` fresh conversations each reading the same 416 positions
-    (imi_seoul::reset + step_batch, seoul.cpp:188-191,490-517), every host thread."""
+    (imi_seoul::reset + step_batch, seoul.cpp:188-191,490-517)."""
     import oracle
     from nunchi_b200 import synth
     if not oracle.reference_available():
         raise RuntimeError("oracle/_ref/libimi_ref.so is not built")
-    threads = reference_threads()
     r = oracle.Reference(synth.cached_gguf("seoul", 0), n_ctx=512, threads=threads)
     vecs, ids = prefill_inputs(r.n_embd, r.n_vocab)
     t0 = time.perf_counter()
@@ -468,7 +537,7 @@ def run_reference_prefill(steps: int) -> dict:
                       f"AVX2, {threads} threads", "ms_per_step": dt / steps * 1e3}
 
 
-def run_reference_multi(steps: int) -> dict:
+def run_reference_multi(steps: int, threads: int) -> dict:
     """configs[3] on the reference's CPU path, a bounded sample: the first sessions of rank 0's draw, their contexts
     read beforehand (not timed), then `steps` greedy positions of each, the sessions one after another through
     swap_state (the reference runs one conversation at a time; no CPU batching is invented)."""
@@ -476,7 +545,6 @@ def run_reference_multi(steps: int) -> dict:
     from nunchi_b200 import synth
     if not oracle.reference_available():
         raise RuntimeError("oracle/_ref/libimi_ref.so is not built")
-    threads = reference_threads()
     ctx = multi_contexts(0)[:MULTI_CPU_SESSIONS]
     r = oracle.Reference(synth.cached_gguf("seoul", 0), n_ctx=MULTI_CTX[1] + steps + 8, threads=threads)
     parked = []
@@ -502,23 +570,91 @@ def run_reference_multi(steps: int) -> dict:
                       f"seoul.cpp/tables.cpp, AVX2, {threads} threads", "ms_per_step": dt / steps * 1e3}
 
 
-def cpu_steps(args) -> int:
-    if args.cpu_steps:
-        return args.cpu_steps
-    return {"ride2": 64, "prefill": 3, "multi64": 16}.get(args.workload, 128)
+def run_reference_tables(ncol: int, threads: int) -> dict:
+    """the reference's own table reads alone (imi_seoul::bench_tables, seoul.cpp:657-685: every layer table back to
+    back, 1 or 2 inputs riding each read): CPU GB/s of the layer tables"""
+    import oracle
+    from nunchi_b200 import synth
+    r = oracle.Reference(synth.cached_gguf("seoul", 0), n_ctx=16, threads=threads)
+    ms = r.bench_tables(ncol=ncol, reps=5)
+    return {"ms": ms, "gbs": TABLE_BYTES / (ms / 1e3) / 1e9, "B": ncol, "cores": threads}
+
+
+TABLE_BYTES = 582967296   # the Seoul shape's layer tables (SURVEY 8(d)), one pass
+
+
+def run_reference(workload: str, steps: int, threads: int) -> dict:
+    if workload == "prefill":
+        return run_reference_prefill(steps, threads)
+    if workload == "multi64":
+        return run_reference_multi(steps, threads)
+    if workload == "sweep":
+        rows = [run_reference_tables(b, threads) for b in (1, 2)]
+        return {"value": rows[0]["gbs"], "unit": "GB/s", "cores": threads, "kind": "reference", "rows": rows,
+                "sample": "imi_seoul::bench_tables (every layer table back to back, 5 passes, best) at 1 and 2 inputs; "
+                          f"the reference's batched read (imi_q4_group_batch) is not timed alone; {threads} threads",
+                "ms_per_step": rows[0]["ms"]}
+    return run_reference_decode(workload, steps, threads)
+
+
+def cpu_steps(workload: str) -> int:
+    return {"ride2": 64, "prefill": 3, "multi64": 16, "sweep": 1}.get(workload, 128)
+
+
+def cpu_baseline(workload: str, steps: int) -> dict:
+    """The reference's CPU path at all of this host's cores and at 4 threads pinned to cores 0-3."""
+    allc = reference_threads()
+    try:
+        with Pinned(None):
+            full = run_reference(workload, steps, allc)
+        four = None
+        if len(os.sched_getaffinity(0)) >= 4:
+            with Pinned(sorted(os.sched_getaffinity(0))[:4]):
+                four = run_reference(workload, steps, 4)
+    except Exception as ex:   # the reference build is missing: say so, keep the GPU line
+        return {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {ex}"}
+    out = {k: full[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    out["cpu_model"] = cpu_model()
+    if "rows" in full:
+        out["rows"] = full["rows"]
+    if four is not None:
+        out["at_4_threads"] = {"value": four["value"], "unit": four["unit"], "cores": 4,
+                               "pinned": "the first 4 cores of this process's affinity (taskset -c 0-3 equivalent)"}
+    return out
+
+
+METRIC = {"ride2": "decode tok/s, batch-2 riding step (step2), Seoul-shaped Q4_0 backbone",
+          "b1": "decode tok/s, batch-1 greedy step, Seoul-shaped Q4_0 backbone",
+          "prefill": "prefill positions/s, 400 input vectors + 16 ids, Seoul-shaped Q4_0 backbone",
+          "multi64": "decode tok/s, 64 sessions per GPU, Seoul-shaped Q4_0 backbone",
+          "sweep": "isolated Q4_0 x Q8 table read GB/s (97,496 x 2048, B=1)"}
+
+
+def sub_line(r: dict, steps: int, workload: str, pk: dict, cpu: dict = None) -> dict:
+    """a sub-object of the default line: one more configuration, measured the same way"""
+    ms_step = r["ms"] / steps
+    o = {"workload": workload_desc(workload)["workload"], "value": r["value"], "unit": "tok/s", "steps": steps,
+         "ms_per_step": ms_step, "step_roofline": step_roofline(r["step_bytes"], ms_step, pk),
+         "gpu_launches": r["launches"], "clocks": r["clocks"]}
+    for k in ("e2e", "prefill_s", "reads_per_step"):
+        if k in r:
+            o[k] = r[k]
+    if "tables" in r:
+        t_gbs = r["tables"]["bytes"] / (r["tables"]["ms"] / 1e3) / 1e9
+        o["tables_roofline"] = {"ncol": r["ncol"], "achieved": t_gbs, "peak": pk["hbm_gbs"], "frac": t_gbs / pk["hbm_gbs"],
+                                "launch_ms": r["tables"]["ms"]}
+    if cpu:
+        o["cpu_baseline"] = cpu
+    return o
 
 
 def main():
     args = parse()
     ranks = Ranks()
-    wl = workload_desc(args)
-    metric = {"ride2": "decode tok/s, batch-2 riding step (step2), Seoul-shaped Q4_0 backbone",
-              "b1": "decode tok/s, batch-1 greedy step, Seoul-shaped Q4_0 backbone",
-              "prefill": "prefill positions/s, 400 input vectors + 16 ids, Seoul-shaped Q4_0 backbone",
-              "multi64": "decode tok/s, 64 sessions per GPU, Seoul-shaped Q4_0 backbone"}[args.workload]
-    unit = "positions/s" if args.workload == "prefill" else "tok/s"
-    base = {"metric": metric, "unit": unit, "n_gpus": ranks.world, "steps": args.steps, "warmup": args.warmup,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+    wl = workload_desc(args.workload)
+    unit = {"prefill": "positions/s", "sweep": "GB/s"}.get(args.workload, "tok/s")
+    base = {"metric": METRIC[args.workload], "unit": unit, "n_gpus": ranks.world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int4 x int8 -> int32 block dots, fp32 scale and accumulate", "data": "synthetic",
             "config": {"workload": wl["workload"], "parallelism": f"whole conversations per GPU x{ranks.world}, "
                        "no collective", "l2": "no flush: every step reads ~696 MB of weights (> 126 MB L2)"}}
@@ -526,44 +662,66 @@ def main():
         if ranks.rank != 0:
             ranks.close()
             return
-        ref = run_reference_cpu(args, args.steps)
+        ref = run_reference(args.workload, args.steps if args.workload != "sweep" else 1, reference_threads())
         line = dict(base, impl="reference", value=ref["value"], ms_per_step=ref["ms_per_step"], n_gpus=ranks.world,
-                    cpu_baseline={k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                    cpu_baseline=dict({k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                                      cpu_model=cpu_model()),
                     e2e={"value": ref["value"], "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
         print(json.dumps(line), flush=True)
         ranks.close()
         return
-    r = {"prefill": run_prefill, "multi64": run_multi}.get(args.workload, run_ours)(args, ranks)
     pk = peaks()
+    if args.workload == "sweep":
+        sw = run_sweep(args, ranks, pk)
+        top = [r for r in sw["rows"] if r["N"] == 97496 and r["B"] == 1][0]
+        line = dict(base, value=top["gbs"], ms_per_step=top["ms"], gpu_launches=None, sweep=sw,
+                    roofline={"kernel": "k_table (isolated read)", "bound": "hbm", "achieved": top["gbs"],
+                              "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": top["hbm_frac"], "peak_source": pk["source"],
+                              "traffic": None})
+        if ranks.rank == 0 and ranks.world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline("sweep", 1)
+        if ranks.rank == 0:
+            print(json.dumps(line), flush=True)
+        ranks.close()
+        return
+    if args.workload == "prefill":
+        r = run_prefill(args, ranks, args.steps)
+    elif args.workload == "multi64":
+        r = run_multi(args, ranks, args.steps)
+    else:
+        r = run_ours(args, ranks, args.workload, args.steps)
     t_gbs = r["tables"]["bytes"] / (r["tables"]["ms"] / 1e3) / 1e9
     step_ms = r["ms"] / args.steps
     line = dict(base, value=r["value"], ms_per_step=step_ms, gpu_launches=r["launches"], clocks=r["clocks"])
     line["roofline"] = {
         "kernel": "k_table (every layer table of a step, read back to back: imi_seoul::bench_tables)",
         "bound": "hbm", "achieved": t_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": t_gbs / pk["hbm_gbs"],
-        "peak_source": pk["source"], "traffic": table_traffic(r.get("ncol") or len(r["mid_positions"])),
-        "ncol": r.get("ncol") or len(r["mid_positions"]),
+        "peak_source": pk["source"], "traffic": table_traffic(r["ncol"]), "ncol": r["ncol"],
         "algorithmic_bytes_per_launch": r["tables"]["bytes"], "launch_ms": r["tables"]["ms"]}
-    sb = r["step_bytes"]
-    line["step_roofline"] = {"bytes_per_step": sb, "achieved_gbs": sb / (step_ms / 1e3) / 1e9,
-                             "frac": sb / (step_ms / 1e3) / 1e9 / pk["hbm_gbs"], "peak_source": pk["source"]}
-    if "flops_per_step" in r:   # prefill is a contraction: its tensor-pipe roofline, which this design does not use
+    line["step_roofline"] = step_roofline(r["step_bytes"], step_ms, pk)
+    if "flops_per_step" in r:   # prefill is a contraction: its tensor-pipe roofline
         tf = r["flops_per_step"] / (step_ms / 1e3) / 1e12
         line["flops_roofline"] = {"flops_per_step": r["flops_per_step"], "achieved_tflops": tf,
                                   "peak_tflops": pk.get("bf16_tflops"), "unit": "TFLOP/s",
-                                  "frac": tf / pk["bf16_tflops"] if pk.get("bf16_tflops") else None,
-                                  "note": "int8 block dots on the integer pipes (dp4a), 8 positions per table read"}
+                                  "frac": tf / pk["bf16_tflops"] if pk.get("bf16_tflops") else None}
     if "prefill_s" in r:
         line["config"]["prefill_s"] = r["prefill_s"]
     if "e2e" in r:
         line["e2e"] = r["e2e"]
-    if ranks.rank == 0 and ranks.world == 1 and not args.no_cpu_baseline:
-        try:
-            ref = run_reference_cpu(args, cpu_steps(args))
-            line["cpu_baseline"] = {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")}
-        except Exception as ex:   # the reference build is missing: say so, keep the GPU line
-            line["cpu_baseline"] = {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference",
-                                    "sample": f"unavailable: {ex}"}
+    cpu_here = ranks.rank == 0 and ranks.world == 1 and not args.no_cpu_baseline
+    if cpu_here:
+        line["cpu_baseline"] = cpu_baseline(args.workload, cpu_steps(args.workload))
+    if args.workload == "ride2" and not args.no_extra:
+        b1 = run_ours(args, ranks, "b1", args.steps)
+        line["b1"] = sub_line(b1, args.steps, "b1", pk, cpu_baseline("b1", cpu_steps("b1")) if cpu_here else None)
+        m = run_multi(args, ranks, args.extra_steps)
+        line["multi64"] = sub_line(m, args.extra_steps, "multi64", pk,
+                                   cpu_baseline("multi64", cpu_steps("multi64")) if cpu_here else None)
+        line["multi64"]["box_tok_s"] = m["value"]
+        if ranks.world == 1:
+            line["sweep"] = run_sweep(args, ranks, pk)
+            if cpu_here:
+                line["sweep"]["cpu_baseline"] = cpu_baseline("sweep", 1)
     if ranks.rank == 0:
         print(json.dumps(line), flush=True)
     ranks.close()

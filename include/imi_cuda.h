@@ -82,10 +82,10 @@ imi_cuda_status imi_cuda_step_multi(imi_cuda_state *const *s, int n, const int32
 imi_cuda_status imi_cuda_step_batch(imi_cuda_state *s, const int32_t *tokens, const float *embd, int n,
                                     int want_logits, float *hidden_all);
 
-/* Greedy decode on the device: `steps` positions for each of n conversations, each step's input being the previous
- * step's pick (the caller loop of imi/core/hear.cpp:65-72 without a stop word). The first step reads tokens[i]
- * (or, when tokens is NULL, each conversation's last pick). ids[steps][n] receives every pick. Logits of the last
- * step stay readable. */
+/* Greedy decode on the device: `steps` positions for each of n conversations (n <= max(max_batch, 8)), each step's
+ * input being the previous step's pick (the caller loop of imi/core/hear.cpp:65-72 without a stop word). The first
+ * step reads tokens[i] (or, when tokens is NULL, each conversation's last pick). ids[steps][n] receives every pick.
+ * Logits of the last step stay readable. */
 imi_cuda_status imi_cuda_greedy(imi_cuda_state *const *s, int n, const int32_t *tokens, int steps, int32_t *ids);
 
 /* Checkpoint / resume of one conversation (the content of imi_seoul_state, seoul.h:21-26) as a host byte image:
@@ -110,6 +110,8 @@ imi_cuda_status imi_cuda_get_argmax(const imi_cuda_state *s, int32_t *id, float 
 void *imi_cuda_stream(const imi_cuda_engine *e);
 /* Kernel launches of one step of n conversations (with or without word scores). */
 int imi_cuda_launches_per_step(const imi_cuda_engine *e, int n, int want_logits);
+/* Kernel launches of one imi_cuda_step_batch of n positions (with or without the last position's word scores). */
+int imi_cuda_launches_per_batch(const imi_cuda_engine *e, int n, int want_logits);
 /* Every layer table read back to back with ncol (1..8) inputs riding each read, as imi_seoul::bench_tables
  * (seoul.cpp:657-685): *ms = mean milliseconds per pass over `reps` passes (after one untimed pass), *bytes = table
  * bytes read per pass. */
@@ -158,8 +160,9 @@ imi_cuda_status imi_cuda_q4_matvec(int device, const uint8_t *q4, int rows, int 
 
 /* The isolated table read timed on the device (the configs[4] sweep; imi/kernels/q4x2_bench.cpp's measurement): a
  * rows x cols Q4_0 table (random codes and scales, the engine's row layout) times ncol 8-bit inputs, `reps` reads after
- * one untimed read, CUDA events on one stream. The table is replicated in device memory until the copies pass 256 MB
- * and the reads rotate through them, so every read comes from HBM (L2 holds 126 MB). *ms = mean milliseconds per
+ * one untimed pass, CUDA events on one stream. The table is replicated in device memory until the copies pass 256 MB
+ * and the reads rotate through all of them (at least `reps` reads, at least one per copy), so every read comes from
+ * HBM (L2 holds 126 MB). *ms = mean milliseconds per
  * read of all ncol inputs; *bytes = algorithmic bytes per read: the table once, the inputs' codes and scales, the
  * outputs. ncol 1..256; cols a multiple of 256. */
 imi_cuda_status imi_cuda_bench_matvec(int device, int rows, int cols, int ncol, int reps, float *ms, size_t *bytes);

@@ -67,6 +67,7 @@ def lib():
         L.imi_cuda_stream.restype = _vp
         L.imi_cuda_stream.argtypes = [_vp]
         L.imi_cuda_launches_per_step.argtypes = [_vp, C.c_int, C.c_int]
+        L.imi_cuda_launches_per_batch.argtypes = [_vp, C.c_int, C.c_int]
         L.imi_cuda_bench_tables.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(C.c_float), C.POINTER(C.c_size_t)]
         L.imi_cuda_trace_table.argtypes = [_vp, C.c_int, C.c_int, C.c_int, _vp, C.POINTER(C.c_int)]
         L.imi_cuda_state_save.argtypes = [_vp, _vp, C.c_size_t, C.POINTER(C.c_size_t)]
@@ -131,6 +132,14 @@ class Engine:
 
     def launches_per_step(self, n: int = 1, want_logits: bool = True) -> int:
         return lib().imi_cuda_launches_per_step(self.h, n, int(bool(want_logits)))
+
+    def launches_per_batch(self, n: int, want_logits: bool = True) -> int:
+        return lib().imi_cuda_launches_per_batch(self.h, n, int(bool(want_logits)))
+
+    def prefill_launches(self, n_vecs: int, chunk: int, n_ids: int) -> int:
+        """launches of configs[2]'s reads: the vectors in chunks of `chunk`, then the ids with the word scores"""
+        k = sum(self.launches_per_batch(min(chunk, n_vecs - a), False) for a in range(0, n_vecs, chunk))
+        return k + self.launches_per_batch(n_ids, True)
 
     def bench_tables(self, ncol: int = 1, reps: int = 20):
         """imi_seoul::bench_tables: all layer tables back to back; (mean ms per pass, table bytes per pass)."""

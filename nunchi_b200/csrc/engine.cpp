@@ -924,7 +924,22 @@ imi_cuda_status imi_cuda_step_batch(imi_cuda_state *s, const int32_t *tokens, co
 imi_cuda_status imi_cuda_greedy(imi_cuda_state *const *s, int n, const int32_t *tokens, int steps, int32_t *ids) {
     if (!s || n <= 0 || steps <= 0) return fail(IMI_E_ARG, "bad greedy arguments");
     imi_cuda_engine *e = s[0]->e;
-    if (n > STEP_COLS) return fail(IMI_E_ARG, "greedy runs at most 8 conversations per call");
+    if (n > e->max_batch && n > STEP_COLS) return fail(IMI_E_ARG, "more conversations than max_batch");
+    if (n > STEP_COLS) {   // groups of STEP_COLS conversations, each group all its steps (conversations are independent)
+        for (int i = 0; i < n; i++)
+            for (int j = 0; j < i; j++) if (s[j] == s[i]) return fail(IMI_E_ARG, "a state appears twice");
+        std::vector<int32_t> part((size_t) steps * STEP_COLS);
+        for (int g0 = 0; g0 < n; g0 += STEP_COLS) {
+            const int m = std::min(STEP_COLS, n - g0);
+            const imi_cuda_status st = imi_cuda_greedy(s + g0, m, tokens ? tokens + g0 : nullptr, steps,
+                                                       ids ? part.data() : nullptr);
+            if (st != IMI_OK) return st;
+            if (ids)
+                for (int k = 0; k < steps; k++)
+                    for (int c = 0; c < m; c++) ids[(size_t) k * n + g0 + c] = part[(size_t) k * m + c];
+        }
+        return IMI_OK;
+    }
     for (int i = 0; i < n; i++) {
         if (!s[i] || s[i]->e != e) return fail(IMI_E_ARG, "states of another engine");
         for (int j = 0; j < i; j++) if (s[j] == s[i]) return fail(IMI_E_ARG, "a state appears twice");
@@ -1176,10 +1191,12 @@ imi_cuda_status imi_cuda_bench_matvec(int device, int rows, int cols, int ncol, 
         }
         return cudaSuccess;
     };
+    // every copy at least once per timed graph, so no read finds its table still in L2 from the previous pass
+    const int nreads = std::max(reps, copies);
     if (r == cudaSuccess) r = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
     if (r == cudaSuccess) {
         cudaError_t rc = cudaSuccess;
-        for (int i = 0; i < reps && rc == cudaSuccess; i++) rc = read(i);
+        for (int i = 0; i < nreads && rc == cudaSuccess; i++) rc = read(i);
         r = cudaStreamEndCapture(st, &g);
         if (rc != cudaSuccess) r = rc;
     }
@@ -1203,7 +1220,7 @@ imi_cuda_status imi_cuda_bench_matvec(int device, int rows, int cols, int ncol, 
     cudaFree(m);
     if (r != cudaSuccess) return fail(IMI_E_CUDA, std::string("bench_matvec: ") + cudaGetErrorString(r));
     if (herr) return fail(IMI_E_TIMEOUT, "bench_matvec: a device-side wait gave up");
-    *ms = t / reps;
+    *ms = t / nreads;
     if (bytes) *bytes = tb + hq.size() + 8 * (size_t) ncol * nb + 4 * (size_t) ncol * rows;
     return IMI_OK;
 }
@@ -1329,6 +1346,15 @@ int imi_cuda_launches_per_step(const imi_cuda_engine *e, int n, int want_logits)
     for (auto &L : e->layers) per += L.conv ? 4 : 5;
     // + the word table (or the final norm without scores); a Q6_K word table takes the final norm and its own read
     return groups * (per + 1 + (e->tok_q6k && want_logits ? 1 : 0));
+}
+
+int imi_cuda_launches_per_batch(const imi_cuda_engine *e, int n, int want_logits) {
+    if (!e || n <= 0) return 0;
+    int per = 1;   // a read of up to STEP_COLS positions: its layers, then the final norm
+    for (auto &L : e->layers) per += L.conv ? 4 : 6;   // attention: K/V write, attention, and the tables around it
+    int reads = 0;
+    for (int g0 = 0; g0 < n; g0 += BATCH_GROUP) reads += (std::min(BATCH_GROUP, n - g0) + STEP_COLS - 1) / STEP_COLS;
+    return reads * per + (want_logits ? (e->tok_q6k ? 2 : 1) : 0);
 }
 
 imi_cuda_status imi_cuda_bench_tables(imi_cuda_engine *e, int ncol, int reps, float *ms, size_t *bytes) {
