@@ -158,6 +158,12 @@ imi_cuda_status imi_cuda_q6k_scores(int device, const uint8_t *q6k, int rows, in
 imi_cuda_status imi_cuda_q4_matvec(int device, const uint8_t *q4, int rows, int cols, const int8_t *xq,
                                    const float *xd, const float *xs, int ncol, float *out, int32_t *block_dots);
 
+/* The same table read for many inputs on the tensor cores (the batched read of imi_q8b + imi_q4_group_batch,
+ * tables.cpp:405-477): ncol 1..256 inputs, each block's integer dot by a tcgen05 MMA (fp16 codes, exact), imi's float
+ * chains per (row, input) in block order; results as imi_cuda_q4_matvec gives them. Host pointers. */
+imi_cuda_status imi_cuda_q4_matmul(int device, const uint8_t *q4, int rows, int cols, const int8_t *xq,
+                                   const float *xd, const float *xs, int ncol, float *out);
+
 /* The isolated table read timed on the device (the configs[4] sweep; imi/kernels/q4x2_bench.cpp's measurement): a
  * rows x cols Q4_0 table (random codes and scales, the engine's row layout) times ncol 8-bit inputs, `reps` reads after
  * one untimed pass, CUDA events on one stream. The table is replicated in device memory until the copies pass 256 MB

@@ -78,6 +78,7 @@ def lib():
         L.imi_cuda_q4_matvec.argtypes = [C.c_int, _vp, C.c_int, C.c_int, _vp, _fp, _fp, C.c_int, _fp, _ip]
         L.imi_cuda_q4_matvec_static.argtypes = [C.c_int, _vp, C.c_int, C.c_int, _vp, _vp, _vp, C.c_int, _vp, _vp]
         L.imi_cuda_check_wait_timeout.argtypes = [C.c_int, C.c_double]
+        L.imi_cuda_q4_matmul.argtypes = [C.c_int, _vp, C.c_int, C.c_int, _vp, _fp, _fp, C.c_int, _fp]
         L.imi_cuda_bench_matvec.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_float),
                                             C.POINTER(C.c_size_t)]
         _L = L
@@ -314,6 +315,17 @@ def q4_matvec(q4, rows: int, cols: int, xq, xd, xs, dots: bool = False, device: 
     _check(lib().imi_cuda_q4_matvec(device, _ptr(q4), rows, cols, _ptr(xq), _ptr(xd), _ptr(xs), ncol, _ptr(out),
                                     _ptr(dd)))
     return (out, dd) if dots else out
+
+
+def q4_matmul(q4, rows: int, cols: int, xq, xd, xs, device: int = 0):
+    """The same as q4_matvec for many inputs on the tensor cores (imi_cuda_q4_matmul): out[ncol][rows]."""
+    q4 = np.ascontiguousarray(q4, dtype=np.uint8)
+    xq = np.ascontiguousarray(xq, dtype=np.int8)
+    xd, xs = _f32(xd), _f32(xs)
+    ncol = xq.size // cols
+    out = np.zeros((ncol, rows), np.float32)
+    _check(lib().imi_cuda_q4_matmul(device, _ptr(q4), rows, cols, _ptr(xq), _ptr(xd), _ptr(xs), ncol, _ptr(out)))
+    return out
 
 
 def bench_matvec(rows: int, cols: int, ncol: int, reps: int = 20, device: int = 0):

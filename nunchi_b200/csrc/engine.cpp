@@ -12,6 +12,8 @@
 #include "gguf_file.h"
 #include "launch.h"
 
+#include <cudaTypedefs.h>
+
 #include <cmath>
 #include <cstdint>
 #include <cstdlib>
@@ -440,6 +442,72 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
     *out = e.release();
     return IMI_OK;
 }
+
+// ---------------------------------------------------------------------------------------------------------------
+// the tensor-core batched read: tensor maps of a table, the columns' operands in the MMA's layout
+// ---------------------------------------------------------------------------------------------------------------
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::mutex g_encode_mu;
+
+// the two TMA views of a table's rows ([rows][row_bytes] bytes): codes in boxes of TC_RAW_W bytes, scales in 16
+cudaError_t tc_tensor_maps(TcArgs &a, const uint8_t *W, int rows, int row_bytes) {
+    {
+        std::lock_guard<std::mutex> g(g_encode_mu);
+        if (!g_encode) {
+            void *fn = nullptr;
+            cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+            const cudaError_t r = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q);
+            if (r != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+            g_encode = (PFN_cuTensorMapEncodeTiled_v12000) fn;
+        }
+    }
+    cuuint64_t dims[2] = { (cuuint64_t) row_bytes, (cuuint64_t) rows }, strides[1] = { (cuuint64_t) row_bytes };
+    cuuint32_t box[2] = { (cuuint32_t) TC_RAW_W, (cuuint32_t) TC_M }, es[2] = { 1, 1 };
+    CUresult c = g_encode(&a.tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *) W, dims, strides, box, es,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (c != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    box[0] = 16;
+    c = g_encode(&a.tm_scales, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *) W, dims, strides, box, es,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return c == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// columns per group of the batched read: 64, or all of them rounded up to 16
+int tc_group(int ncol) { return ncol >= 64 ? 64 : std::max(16, (ncol + 15) / 16 * 16); }
+
+// an integer |v| <= 2048 as fp16 bits (exact)
+uint16_t int_half(int v) {
+    if (v == 0) return 0;
+    const uint16_t sg = v < 0 ? 0x8000 : 0;
+    unsigned m = (unsigned) (v < 0 ? -v : v);
+    int e = 0;
+    while ((m >> (e + 1)) != 0) e++;
+    return (uint16_t) (sg | ((e + 15) << 10) | ((m << (10 - e)) & 0x3FF));
+}
+
+// the columns' 8-bit codes, scales and scale * code sums ([ncol][cols], [ncol][cols/32]) in the batched read's layout:
+// xh [group][cols/8][G][8] fp16, xds [group][cols/32][2][G] (zeros for the padding columns)
+void tc_operands_host(const int8_t *xq, const float *xd, const float *xs, int ncol, int cols, int G,
+                      std::vector<uint16_t> &xh, std::vector<float> &xds) {
+    const int groups = (ncol + G - 1) / G, nq = cols / 8, nb = cols / 32;
+    xh.assign((size_t) groups * nq * G * 8, 0);
+    xds.assign((size_t) groups * nb * 2 * G, 0.0f);
+    for (int c = 0; c < ncol; c++) {
+        const int g = c / G, cg = c - g * G;
+        for (int k = 0; k < cols; k++)
+            xh[(((size_t) g * nq + k / 8) * G + cg) * 8 + (k & 7)] = int_half(xq[(size_t) c * cols + k]);
+        for (int j = 0; j < nb; j++) {
+            xds[(((size_t) g * nb + j) * 2 + 0) * G + cg] = xd[(size_t) c * nb + j];
+            xds[(((size_t) g * nb + j) * 2 + 1) * G + cg] = xs[(size_t) c * nb + j];
+        }
+    }
+}
+
+}  // namespace
 
 // ---------------------------------------------------------------------------------------------------------------
 // the step schedule
@@ -1222,6 +1290,56 @@ imi_cuda_status imi_cuda_bench_matvec(int device, int rows, int cols, int ncol, 
     if (herr) return fail(IMI_E_TIMEOUT, "bench_matvec: a device-side wait gave up");
     *ms = t / nreads;
     if (bytes) *bytes = tb + hq.size() + 8 * (size_t) ncol * nb + 4 * (size_t) ncol * rows;
+    return IMI_OK;
+}
+
+imi_cuda_status imi_cuda_q4_matmul(int device, const uint8_t *q4, int rows, int cols, const int8_t *xq, const float *xd,
+                                   const float *xs, int ncol, float *out) {
+    if (!q4 || !xq || !xd || !xs || !out || rows <= 0 || cols <= 0 || cols % 256 || ncol < 1 || ncol > 256)
+        return fail(IMI_E_ARG, "bad q4_matmul arguments (cols a multiple of 256, 1..256 inputs)");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) return fail(IMI_E_NODEV, "no CUDA device");
+    CK(cudaSetDevice(device));
+    CK(prepare_kernels());
+    const int nb = cols / 32, row_bytes = nb * 18, G = tc_group(ncol), groups = (ncol + G - 1) / G;
+    std::vector<uint8_t> packed((size_t) rows * row_bytes);
+    for (int r = 0; r < rows; r++)
+        for (int j = 0; j < nb; j++) {
+            const uint8_t *src = q4 + ((size_t) r * nb + j) * 18;
+            uint8_t *row = packed.data() + (size_t) r * row_bytes;
+            memcpy(row + (size_t) nb * 16 + 2 * j, src, 2);
+            memcpy(row + 16 * j, src + 2, 16);
+        }
+    std::vector<uint16_t> xh;
+    std::vector<float> xds;
+    tc_operands_host(xq, xd, xs, ncol, cols, G, xh, xds);
+    auto al = [](size_t x) { return (x + 255) / 256 * 256; };
+    const size_t b_w = packed.size(), b_h = xh.size() * 2, b_x = xds.size() * 4, b_o = (size_t) ncol * rows * 4;
+    uint8_t *m = nullptr;
+    CK(cudaMalloc(&m, al(b_w) + al(b_h) + al(b_x) + al(b_o) + 256));
+    uint8_t *dW = m, *dh = m + al(b_w);
+    float *dx = (float *) (dh + al(b_h)), *dout = (float *) ((uint8_t *) dx + al(b_x));
+    int *derr = (int *) ((uint8_t *) dout + al(b_o));
+    TcArgs a = {};
+    cudaError_t r = cudaMemcpy(dW, packed.data(), b_w, cudaMemcpyHostToDevice);
+    if (r == cudaSuccess) r = cudaMemcpy(dh, xh.data(), b_h, cudaMemcpyHostToDevice);
+    if (r == cudaSuccess) r = cudaMemcpy(dx, xds.data(), b_x, cudaMemcpyHostToDevice);
+    if (r == cudaSuccess) r = cudaMemset(derr, 0, 4);
+    if (r == cudaSuccess) r = tc_tensor_maps(a, dW, rows, row_bytes);
+    if (r == cudaSuccess) {
+        a.rows = rows; a.cols = cols; a.row_bytes = row_bytes; a.ncol = ncol; a.G = G; a.groups = groups;
+        a.xh = dh; a.xds = dx; a.out = dout; a.out_stride = rows; a.epi = TE_STORE; a.err = derr;
+        int sms = 148;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+        const int units = (rows + TC_M - 1) / TC_M * groups;
+        r = launch_tc_table(a, std::min(sms, units), 0, false);
+    }
+    if (r == cudaSuccess) r = cudaMemcpy(out, dout, b_o, cudaMemcpyDeviceToHost);
+    int herr = 0;
+    if (r == cudaSuccess) r = cudaMemcpy(&herr, derr, 4, cudaMemcpyDeviceToHost);
+    cudaFree(m);
+    if (r != cudaSuccess) return fail(IMI_E_CUDA, std::string("q4_matmul: ") + cudaGetErrorString(r));
+    if (herr) return fail(IMI_E_TIMEOUT, "q4_matmul: a device-side wait gave up");
     return IMI_OK;
 }
 

@@ -5,6 +5,7 @@
 //   softmax, P.V and the sigmoid gate, in the float order of seoul.cpp:425-453.
 #include "common.cuh"
 #include "table.cuh"
+#include "tc_table.cuh"
 
 namespace imi {
 

@@ -1,0 +1,369 @@
+// k_tc_table: one 4-bit table times many inputs (16..256 columns) on the 5th-generation tensor cores: the batched
+// read of imi_q8b + imi_q4_group_batch (imi/core/tables.cpp:405-477), used where a step reads a table for dozens of
+// conversations or prefill positions at once.
+//
+// The exact numbers allow tensor cores because imi's per-block integer dots are exact: for a 32-value block j the dot
+// sum_i code_ri * x_ci of 4-bit codes (0..15) and 8-bit input codes (-127..127) is an integer below 2^16 in
+// magnitude, which an fp16 x fp16 -> fp32 tensor-core product computes exactly (every product and every partial sum is
+// an integer that fp32 holds exactly). imi scales each block's dot before it accumulates, so the MMA must not sum over
+// blocks: every block gets its own TMEM columns (D_j[row][col] = dot of block j), and the epilogue runs imi's two
+// float chains per (row, column) in block order (group_avx2<false>, tables.cpp:127-143):
+//     acc = fma(dot_j, d_rj * dx_cj, acc),  cor = fma(d_rj, s_cj, cor),  out = acc - 8 cor (one rounding).
+//
+// Work unit: a tile of 128 rows x a group of G columns (G = 16, 32 or 64). K is read in stages of 128 values (4
+// blocks). Warp roles (448 threads, one CTA per SM, persistent over units):
+//   warp 0      producer: TMA of the tile's 4-bit codes (128 rows x 80 bytes, 64 used: a padded shared-memory row
+//               stride keeps the unpack's reads free of bank conflicts) and fp16 scales, bulk copies of the columns'
+//               fp16 codes (already in the MMA's K-major layout) and their scales and sums;
+//   warp 1      TMEM owner (512 columns) and MMA issuer: per block two tcgen05.mma kind::f16 (K = 16 each) into the
+//               block's own TMEM slot, committed to the slot's barrier;
+//   warps 2-5   unpack: 4-bit codes -> fp16 in the MMA's canonical K-major layout (8-row x 16-byte core matrices),
+//               the rows' block scales handed to the epilogue;
+//   warps 6-13  epilogue: per TMEM slot a tcgen05.ld of the block's dots (warp w reads lanes 32 (w % 4) ..), the two
+//               fma chains for G/2 columns per thread (packed f32x2 operations, each lane rounded as imi's scalar
+//               chain), the result stored at the end of the unit.
+// Every wait on an mbarrier is bounded (about one second); a wait that gives up sets the error flag, the CTA stops
+// issuing work, waits (bounded) for its copies and MMAs in flight, frees its TMEM and returns.
+#pragma once
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace imi {
+
+constexpr int TC_M = 128;              // rows per tile (the MMA's M; TMEM lanes)
+constexpr int TC_KS = 128;             // values per K stage
+constexpr int TC_BPS = TC_KS / 32;     // blocks per stage
+constexpr int TC_RAW_W = 80;           // bytes per row of a raw code stage in shared memory (64 used)
+constexpr int TC_NR = 3, TC_NS = 3, TC_NE = 4;   // rings: raw TMA stages, MMA operand stages, epilogue stages
+constexpr int TC_THREADS = 448;
+constexpr int TC_WARP_PROD = 0, TC_WARP_MMA = 1, TC_WARP_UNP = 2, TC_WARP_EPI = 6;
+constexpr int TC_TMEM_COLS = 512;
+
+enum TcEpi : int { TE_STORE = 0 };
+
+struct TcArgs {
+    CUtensorMap tm_codes;     // the table's rows as bytes [rows][row_bytes], box {TC_RAW_W, 128}
+    CUtensorMap tm_scales;    // the same rows, box {16, 128} (8 fp16 scales of two stages)
+    int rows, cols, row_bytes;
+    int ncol, G, groups;      // columns, columns per group, groups (units = tiles * groups)
+    const uint8_t *xh;        // the columns' 8-bit codes as fp16, [group][cols / 8][G][8]
+    const float *xds;         // per group and block: G scales then G scale * code sums, [group][cols / 32][2][G]
+    float *out;               // out[c * out_stride + row]
+    int out_stride;
+    int epi;
+    int *err;
+};
+
+struct TcPlan {
+    int raw, op, epi, bar, tptr, total;
+    int raw_bytes, a_bytes, b_bytes, op_bytes, xds_bytes, epi_bytes, nslot;
+};
+__host__ __device__ inline TcPlan tc_plan(int G) {
+    TcPlan p;
+    p.raw_bytes = TC_M * TC_RAW_W + TC_M * 16;            // codes + scales of one stage
+    p.a_bytes = (TC_KS / 8) * TC_M * 16;                  // fp16 codes of 128 rows, 16 chunks of 8 values
+    p.b_bytes = (TC_KS / 8) * G * 16;                     // fp16 codes of G columns
+    p.op_bytes = p.a_bytes + p.b_bytes;
+    p.xds_bytes = TC_BPS * 2 * G * 4;
+    p.epi_bytes = align_up(p.xds_bytes + TC_M * 8, 128);  // + the rows' 4 block scales (fp16)
+    p.nslot = TC_TMEM_COLS / G;
+    int o = 0;
+    p.raw = o;  o += TC_NR * align_up(p.raw_bytes, 128);
+    p.op = o;   o += TC_NS * align_up(p.op_bytes, 128);
+    p.epi = o;  o += TC_NE * p.epi_bytes;
+    p.bar = o;  o += 8 * (2 * TC_NR + 3 * TC_NS + 3 * TC_NE + 2 * 32 + 1);
+    p.tptr = o; o += 16;
+    p.total = align_up(o, 128) + 128;                     // + slack to align the base to 128 bytes
+    return p;
+}
+
+#ifdef __CUDACC__
+// ---- tcgen05 / TMA wrappers ----
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_u32(dst)), "l"(tm), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint64_t *b) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(b))
+                 : "memory");
+}
+// D[tmem] (+)= A[smem] . B[smem]^T, kind::f16 (fp16 inputs, fp32 accumulate)
+__device__ __forceinline__ void tc_mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, int acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+// shared-memory matrix descriptor, K-major, no swizzle: 8-row x 16-byte core matrices, lbo between the two 16-byte K
+// chunks of an MMA, sbo between 8-row groups (tcgen05 descriptor: start >> 4, lbo >> 4 at bit 16, sbo >> 4 at bit 32,
+// version 1 at bit 46, layout 0 = no swizzle at bits 61-63)
+__device__ __forceinline__ uint64_t tc_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t) ((saddr >> 4) & 0x3FFF) | ((uint64_t) ((lbo >> 4) & 0x3FFF) << 16) |
+           ((uint64_t) ((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46);
+}
+// instruction descriptor: D f32 (bit 4), A and B f16 (format 0), both K-major, N >> 3 at bit 17, M >> 4 at bit 24
+__host__ __device__ constexpr uint32_t tc_idesc_f16(int n, int m) {
+    return (1u << 4) | ((uint32_t) (n >> 3) << 17) | ((uint32_t) (m >> 4) << 24);
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&v)[N]);
+template <>
+__device__ __forceinline__ void tmem_ld<8>(uint32_t t, uint32_t (&v)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(t));
+}
+template <>
+__device__ __forceinline__ void tmem_ld<16>(uint32_t t, uint32_t (&v)[16]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                   "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+                 : "r"(t));
+}
+template <>
+__device__ __forceinline__ void tmem_ld<32>(uint32_t t, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(t));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 8 values (low or high nibbles of 8 code bytes w0, w1) as fp16: (0x6400 | v) is 1024 + v in fp16; minus 1024 exactly
+__device__ __forceinline__ uint32_t nib2h(uint32_t t, int hi) {
+    const uint32_t m = ((hi ? t >> 4 : t) & 0x000F000Fu) | 0x64006400u;
+    const __half2 r = __hsub2(*reinterpret_cast<const __half2 *>(&m), __half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400)));
+    return *reinterpret_cast<const uint32_t *>(&r);
+}
+__device__ __forceinline__ uint4 nib8(uint32_t w0, uint32_t w1, int hi) {
+    return make_uint4(nib2h(__byte_perm(w0, 0, 0x4140), hi), nib2h(__byte_perm(w0, 0, 0x4342), hi),
+                      nib2h(__byte_perm(w1, 0, 0x4140), hi), nib2h(__byte_perm(w1, 0, 0x4342), hi));
+}
+
+template <int G>
+__global__ void __launch_bounds__(TC_THREADS, 1) k_tc_table(const __grid_constant__ TcArgs a) {
+    extern __shared__ __align__(128) uint8_t smt[];
+    constexpr int CH = G / 2;                              // columns per epilogue thread
+    const TcPlan P = tc_plan(G);
+    uint8_t *sm = smt + ((128 - (smem_u32(smt) & 127)) & 127);
+    uint64_t *bars = (uint64_t *) (sm + P.bar);
+    // raw_full / b_full / x_full: a TMA or bulk copy landed (1 arrival + bytes); raw_empty, a_full, s_full: the 4
+    // unpack warps; op_empty, tm_full, fin: tcgen05.commit; epi_empty, tm_empty: the 8 epilogue warps
+    uint64_t *raw_full = bars, *raw_empty = raw_full + TC_NR, *a_full = raw_empty + TC_NR, *b_full = a_full + TC_NS,
+             *op_empty = b_full + TC_NS, *x_full = op_empty + TC_NS, *s_full = x_full + TC_NE,
+             *epi_empty = s_full + TC_NE, *tm_full = epi_empty + TC_NE, *tm_empty = tm_full + 32,
+             *fin = tm_empty + 32;
+    uint32_t *tptr = (uint32_t *) (sm + P.tptr);
+    __shared__ int abort_flag;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int K = a.cols, nst = K / TC_KS, tiles = (a.rows + TC_M - 1) / TC_M, units = tiles * a.groups;
+    const int nslot = P.nslot;
+
+    if (tid == 0) {
+        for (int i = 0; i < TC_NR; i++) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 4); }
+        for (int i = 0; i < TC_NS; i++) { mbar_init(&a_full[i], 4); mbar_init(&b_full[i], 1); mbar_init(&op_empty[i], 1); }
+        for (int i = 0; i < TC_NE; i++) { mbar_init(&x_full[i], 1); mbar_init(&s_full[i], 4); mbar_init(&epi_empty[i], 8); }
+        for (int i = 0; i < nslot; i++) { mbar_init(&tm_full[i], 1); mbar_init(&tm_empty[i], 8); }
+        mbar_init(fin, 1);
+        abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == TC_WARP_MMA) {   // the whole warp allocates the 512 TMEM columns
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tptr)),
+                     "r"(TC_TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tptr;
+    pdl_trigger();
+    pdl_wait();
+
+    auto fail = [&]() {
+        abort_flag = 1;
+        atomicExch(a.err, 7);
+    };
+    auto wait = [&](uint64_t *b, uint32_t parity) -> bool {
+        if (*(volatile int *) &abort_flag) return false;
+        if (mbar_wait(b, parity)) return true;
+        fail();
+        return false;
+    };
+
+    if (warp == TC_WARP_PROD) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            int i = 0, nr = 0, nb = 0, nx = 0;   // stages issued per ring
+            bool ok = true;
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+                const int tile = u / a.groups, g = u - tile * a.groups;
+                const uint8_t *xh = a.xh + (size_t) g * (K / 8) * G * 16;
+                const float *xds = a.xds + (size_t) g * (K / 32) * 2 * G;
+                for (int s = 0; s < nst; s++, i++) {
+                    const int r = i % TC_NR, o = i % TC_NS, e = i % TC_NE;
+                    if (!(ok = wait(&raw_empty[r], ((i / TC_NR) & 1) ^ 1))) break;
+                    uint8_t *raw = sm + P.raw + r * align_up(P.raw_bytes, 128);
+                    mbar_expect_tx(&raw_full[r], (uint32_t) P.raw_bytes);
+                    tma_load_2d(raw, &a.tm_codes, s * (TC_KS / 2), tile * TC_M, &raw_full[r]);
+                    tma_load_2d(raw + TC_M * TC_RAW_W, &a.tm_scales, K / 2 + 16 * (s / 2), tile * TC_M, &raw_full[r]);
+                    nr++;
+                    if (!(ok = wait(&op_empty[o], ((i / TC_NS) & 1) ^ 1))) break;
+                    uint8_t *op = sm + P.op + o * align_up(P.op_bytes, 128);
+                    mbar_expect_tx(&b_full[o], (uint32_t) P.b_bytes);
+                    bulk_g2s(op + P.a_bytes, xh + (size_t) s * (TC_KS / 8) * G * 16, (uint32_t) P.b_bytes, &b_full[o]);
+                    nb++;
+                    if (!(ok = wait(&epi_empty[e], ((i / TC_NE) & 1) ^ 1))) break;
+                    uint8_t *ep = sm + P.epi + e * P.epi_bytes;
+                    mbar_expect_tx(&x_full[e], (uint32_t) P.xds_bytes);
+                    bulk_g2s(ep, xds + (size_t) s * TC_BPS * 2 * G, (uint32_t) P.xds_bytes, &x_full[e]);
+                    nx++;
+                }
+            }
+            if (!ok) {   // the copies in flight land before the CTA exits (bounded waits on the last stages issued)
+                for (int k = nr > TC_NR ? nr - TC_NR : 0; k < nr; k++) mbar_wait(&raw_full[k % TC_NR], (k / TC_NR) & 1);
+                for (int k = nb > TC_NS ? nb - TC_NS : 0; k < nb; k++) mbar_wait(&b_full[k % TC_NS], (k / TC_NS) & 1);
+                for (int k = nx > TC_NE ? nx - TC_NE : 0; k < nx; k++) mbar_wait(&x_full[k % TC_NE], (k / TC_NE) & 1);
+            }
+        }
+    } else if (warp == TC_WARP_MMA) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint32_t idesc = tc_idesc_f16(G, TC_M);
+            int i = 0, b = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+                for (int s = 0; s < nst && ok; s++, i++) {
+                    const int o = i % TC_NS;
+                    if (!(ok = wait(&a_full[o], (i / TC_NS) & 1) && wait(&b_full[o], (i / TC_NS) & 1))) break;
+                    tc_fence_after();
+                    const uint32_t abase = smem_u32(sm + P.op + o * align_up(P.op_bytes, 128)), bbase = abase + P.a_bytes;
+                    for (int jj = 0; jj < TC_BPS; jj++, b++) {
+                        const int slot = b % nslot;
+                        if (!(ok = wait(&tm_empty[slot], ((b / nslot) & 1) ^ 1))) break;
+                        tc_fence_after();
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {   // K = 16 per MMA: chunks 4jj + 2h, 4jj + 2h + 1
+                            const int q = 4 * jj + 2 * h;
+                            tc_mma_f16(tmem + slot * G, tc_desc(abase + q * TC_M * 16, TC_M * 16, 128),
+                                       tc_desc(bbase + q * G * 16, G * 16, 128), idesc, h);
+                        }
+                        tc_commit(&tm_full[slot]);
+                    }
+                    if (ok) tc_commit(&op_empty[o]);
+                }
+            }
+            if (!ok) {   // the MMAs issued complete before TMEM is freed
+                tc_commit(fin);
+                mbar_wait(fin, 0);
+            }
+        }
+    } else if (warp < TC_WARP_EPI) {
+        // ---------------- unpack: 4-bit codes -> fp16, canonical K-major layout ----------------
+        const int row = tid - TC_WARP_UNP * 32;   // 0..127: this thread's row of the tile
+        int i = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+            for (int s = 0; s < nst; s++, i++) {
+                const int r = i % TC_NR, o = i % TC_NS, e = i % TC_NE;
+                if (!(ok = wait(&raw_full[r], (i / TC_NR) & 1) && wait(&op_empty[o], ((i / TC_NS) & 1) ^ 1) &&
+                           wait(&epi_empty[e], ((i / TC_NE) & 1) ^ 1)))
+                    break;
+                const uint8_t *raw = sm + P.raw + r * align_up(P.raw_bytes, 128);
+                uint8_t *A = sm + P.op + o * align_up(P.op_bytes, 128);
+#pragma unroll
+                for (int p = 0; p < TC_BPS; p++) {   // block p of the stage: 16 code bytes -> 4 chunks of 8 fp16
+                    const uint4 c = *(const uint4 *) (raw + row * TC_RAW_W + 16 * p);
+                    *(uint4 *) (A + ((4 * p + 0) * TC_M + row) * 16) = nib8(c.x, c.y, 0);   // values 0..7
+                    *(uint4 *) (A + ((4 * p + 1) * TC_M + row) * 16) = nib8(c.z, c.w, 0);   // 8..15
+                    *(uint4 *) (A + ((4 * p + 2) * TC_M + row) * 16) = nib8(c.x, c.y, 1);   // 16..23
+                    *(uint4 *) (A + ((4 * p + 3) * TC_M + row) * 16) = nib8(c.z, c.w, 1);   // 24..31
+                }
+                // the row's 4 block scales of this stage (8 bytes of the 16-byte scale box)
+                const uint2 sc = *(const uint2 *) (raw + TC_M * TC_RAW_W + row * 16 + 8 * (s & 1));
+                *(uint2 *) (sm + P.epi + e * P.epi_bytes + P.xds_bytes + row * 8) = sc;
+                fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&a_full[o]);
+                    mbar_arrive(&raw_empty[r]);
+                    mbar_arrive(&s_full[e]);
+                }
+            }
+        }
+    } else {
+        // ---------------- epilogue: imi's float chains per (row, column) ----------------
+        const int qd = warp & 3, h = (warp - TC_WARP_EPI) >> 2, row = qd * 32 + lane;
+        const uint32_t tl = tmem + ((uint32_t) (qd * 32) << 16) + h * CH;
+        int i = 0, b = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+            const int tile = u / a.groups, g = u - tile * a.groups;
+            float2 acc[CH / 2], cor[CH / 2];
+#pragma unroll
+            for (int k = 0; k < CH / 2; k++) acc[k] = cor[k] = make_float2(0.0f, 0.0f);
+            for (int s = 0; s < nst && ok; s++, i++) {
+                const int e = i % TC_NE;
+                if (!(ok = wait(&x_full[e], (i / TC_NE) & 1) && wait(&s_full[e], (i / TC_NE) & 1))) break;
+                const uint8_t *ep = sm + P.epi + e * P.epi_bytes;
+                const uint16_t *dsc = (const uint16_t *) (ep + P.xds_bytes + row * 8);
+                for (int jj = 0; jj < TC_BPS; jj++, b++) {
+                    const int slot = b % nslot;
+                    if (!(ok = wait(&tm_full[slot], (b / nslot) & 1))) break;
+                    tc_fence_after();
+                    uint32_t f[CH];
+                    tmem_ld<CH>(tl + slot * G, f);
+                    tmem_ld_wait();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tm_empty[slot]);
+                    const float d = h2f(dsc[jj]);
+                    const float2 dd = make_float2(d, d);
+                    const float *xd = (const float *) ep + jj * 2 * G + h * CH, *xs = xd + G;
+#pragma unroll
+                    for (int k = 0; k < CH / 2; k++) {
+                        const float2 dx = *(const float2 *) (xd + 2 * k), sx = *(const float2 *) (xs + 2 * k);
+                        const float2 fv = make_float2(__uint_as_float(f[2 * k]), __uint_as_float(f[2 * k + 1]));
+                        acc[k] = __ffma2_rn(fv, __fmul2_rn(dd, dx), acc[k]);
+                        cor[k] = __ffma2_rn(dd, sx, cor[k]);
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&epi_empty[e]);
+            }
+            if (!ok) break;
+            const int grow = tile * TC_M + row;
+            if (grow < a.rows) {
+#pragma unroll
+                for (int k = 0; k < CH / 2; k++) {
+                    const int c0 = g * G + h * CH + 2 * k;
+                    if (c0 < a.ncol) a.out[(size_t) c0 * a.out_stride + grow] = __fmaf_rn(-8.0f, cor[k].x, acc[k].x);
+                    if (c0 + 1 < a.ncol) a.out[(size_t) (c0 + 1) * a.out_stride + grow] = __fmaf_rn(-8.0f, cor[k].y, acc[k].y);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == TC_WARP_MMA) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS) : "memory");
+    }
+}
+#endif
+
+}  // namespace imi

@@ -80,3 +80,23 @@ def test_q6k_word_scores_bit_exact(rows, cols, seed):
         assert np.array_equal(mine, want)
     want = oracle.q6k_rows(W, x)
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+# ---- the tensor-core batched read (tcgen05, fp16 codes, exact block dots; imi's chains per (row, input)) ----
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("rows,cols,ncol", [(128, 256, 16), (2048, 2048, 64), (300, 8192, 32), (1003, 512, 48),
+                                            (2048, 2048, 128), (3104, 2048, 40), (97496, 2048, 64), (16384, 2048, 64),
+                                            (2048, 8192, 64), (77, 1024, 1), (129, 256, 256)])
+def test_tc_table_bit_exact(rows, cols, ncol):
+    """imi_cuda_q4_matmul against the oracle (imi_q4_group's per-row result for each input), bit for bit: block dots
+    from fp16 x fp16 -> fp32 MMAs are exact, and the epilogue keeps the per-row fma order"""
+    rng = np.random.default_rng(rows + 3 * cols + 7 * ncol)
+    q4 = synth._q4_0(rng, rows, cols).reshape(-1)
+    x = rng.standard_normal((ncol, cols)).astype(np.float32) * rng.uniform(0.1, 4.0, (ncol, 1)).astype(np.float32)
+    x[0, :64] = 0.0                                      # zero blocks: scale 0
+    cuts = [oracle.cut(v) for v in x]
+    cq, cd, cs = (np.concatenate([c[k] for c in cuts]) for k in range(3))
+    want = np.asarray(oracle.q4_matvec(q4, rows, cols, cq, cd, cs), np.float32).reshape(ncol, rows)
+    got = nb.q4_matmul(q4, rows, cols, cq, cd, cs)
+    assert np.array_equal(bits(got), bits(want)), f"max rel {np.abs(got - want).max() / np.abs(want).max():.3g}"
