@@ -476,8 +476,8 @@ cudaError_t tc_tensor_maps(TcArgs &a, const uint8_t *W, int rows, int row_bytes)
     return c == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-// columns per group of the batched read: 64, or all of them rounded up to 16
-int tc_group(int ncol) { return ncol >= 64 ? 64 : std::max(16, (ncol + 15) / 16 * 16); }
+// columns per group of the batched read (the kernel's instances: 16, 32, 64)
+int tc_group(int ncol) { return ncol <= 16 ? 16 : ncol <= 32 ? 32 : 64; }
 
 // an integer |v| <= 2048 as fp16 bits (exact)
 uint16_t int_half(int v) {
@@ -1224,9 +1224,16 @@ imi_cuda_status imi_cuda_bench_matvec(int device, int rows, int cols, int ncol, 
     for (auto &q : hq) q = (int8_t) ((int) (next() % 255) - 127);
     std::vector<float> hd((size_t) ncol * nb, 0.01f), hs((size_t) ncol * nb, 0.5f);
     auto al = [](size_t n) { return (n + 255) / 256 * 256; };
+    // more than 8 inputs: the tensor-core read, its operands in the MMA's layout
+    const bool tc = ncol > MV_MAX_COLS;
+    const int G = tc_group(ncol), groups = (ncol + G - 1) / G;
+    std::vector<uint16_t> th;
+    std::vector<float> tx;
+    if (tc) tc_operands_host(hq.data(), hd.data(), hs.data(), ncol, cols, G, th, tx);
     const size_t o_q = (size_t) copies * tstride, o_d = o_q + al(hq.size()), o_s = o_d + al(hd.size() * 4),
                  o_o = o_s + al(hs.size() * 4), o_c = o_o + al((size_t) ncol * rows * 4),
-                 total = o_c + al(sizeof(Col) * MV_MAX_COLS) + 256;
+                 o_th = o_c + al(sizeof(Col) * MV_MAX_COLS) + 256, o_tx = o_th + al(th.size() * 2),
+                 total = o_tx + al(tx.size() * 4);
     uint8_t *m = nullptr;
     CK(cudaMalloc(&m, total));
     cudaStream_t st = nullptr;
@@ -1239,10 +1246,24 @@ imi_cuda_status imi_cuda_bench_matvec(int device, int rows, int cols, int ncol, 
     if (r == cudaSuccess) r = cudaMemcpy(m + o_d, hd.data(), hd.size() * 4, cudaMemcpyHostToDevice);
     if (r == cudaSuccess) r = cudaMemcpy(m + o_s, hs.data(), hs.size() * 4, cudaMemcpyHostToDevice);
     if (r == cudaSuccess) r = cudaMemset(m + o_c, 0, al(sizeof(Col) * MV_MAX_COLS) + 256);
+    if (r == cudaSuccess && tc) r = cudaMemcpy(m + o_th, th.data(), th.size() * 2, cudaMemcpyHostToDevice);
+    if (r == cudaSuccess && tc) r = cudaMemcpy(m + o_tx, tx.data(), tx.size() * 4, cudaMemcpyHostToDevice);
+    std::vector<TcArgs> tca(tc ? copies : 0);
+    for (int c = 0; c < (int) tca.size() && r == cudaSuccess; c++) {
+        TcArgs &t = tca[c];
+        r = tc_tensor_maps(t, m + (size_t) c * tstride, rows, row_bytes);
+        t.rows = rows; t.cols = cols; t.row_bytes = row_bytes; t.ncol = ncol; t.G = G; t.groups = groups;
+        t.xh = m + o_th; t.xds = (const float *) (m + o_tx); t.out = (float *) (m + o_o); t.out_stride = rows;
+        t.epi = TE_STORE; t.err = (int *) (m + o_c + al(sizeof(Col) * MV_MAX_COLS));
+    }
     if (r == cudaSuccess) r = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
     // one read of all inputs from table copy k: groups of up to 8 inputs per read of the table (the small-batch
     // kernel), programmatic dependent launches one after another as the engine's step runs them
     auto read = [&](int k) -> cudaError_t {
+        if (tc) {
+            const int units = (rows + TC_M - 1) / TC_M * groups;
+            return launch_tc_table(tca[k % copies], std::min(sms, units), st, true);
+        }
         for (int c0 = 0; c0 < ncol; c0 += MV_MAX_COLS) {
             MvArgs a = {};
             a.W = m + (size_t) (k % copies) * tstride; a.rows = rows; a.cols = cols; a.row_bytes = row_bytes; a.unit = 1;
