@@ -12,13 +12,15 @@
 //
 // Work unit: a tile of 128 rows x a group of G columns (G = 16, 32 or 64). K is read in stages of 128 values (4
 // blocks). Warp roles (448 threads, one CTA per SM, persistent over units):
-//   warp 0      producer: TMA of the tile's 4-bit codes (128 rows x 80 bytes, 64 used: a padded shared-memory row
-//               stride keeps the unpack's reads free of bank conflicts) and fp16 scales, bulk copies of the columns'
-//               fp16 codes (already in the MMA's K-major layout) and their scales and sums;
+//   warp 0      producer: per stage one barrier for four copies into a ring slot: TMA of the tile's 4-bit codes
+//               (128 rows x 80 bytes, 64 used: a padded shared-memory row stride keeps the unpack's reads free of
+//               bank conflicts) and fp16 scales, bulk copies of the columns' fp16 codes (already in the MMA's K-major
+//               layout, read by the MMA where they land) and of their scales and sums; it waits only for the slot, so
+//               weight bytes stream several stages ahead of the math;
 //   warp 1      TMEM owner (512 columns) and MMA issuer: per block two tcgen05.mma kind::f16 (K = 16 each) into the
 //               block's own TMEM slot, committed to the slot's barrier;
 //   warps 2-5   unpack: 4-bit codes -> fp16 in the MMA's canonical K-major layout (8-row x 16-byte core matrices),
-//               the rows' block scales handed to the epilogue;
+//               the rows' block scales and the columns' scales and sums handed to the epilogue;
 //   warps 6-13  epilogue: per TMEM slot a tcgen05.ld of the block's dots (warp w reads lanes 32 (w % 4) ..), the two
 //               fma chains for G/2 columns per thread (packed f32x2 operations, each lane rounded as imi's scalar
 //               chain), the result stored at the end of the unit.
@@ -35,7 +37,7 @@ constexpr int TC_M = 128;              // rows per tile (the MMA's M; TMEM lanes
 constexpr int TC_KS = 128;             // values per K stage
 constexpr int TC_BPS = TC_KS / 32;     // blocks per stage
 constexpr int TC_RAW_W = 80;           // bytes per row of a raw code stage in shared memory (64 used)
-constexpr int TC_NR = 3, TC_NS = 3, TC_NE = 4;   // rings: raw TMA stages, MMA operand stages, epilogue stages
+constexpr int TC_NR = 4, TC_NA = 2, TC_NE = 4;   // rings: copied stages, unpacked weight stages, epilogue stages
 constexpr int TC_THREADS = 448;
 constexpr int TC_WARP_PROD = 0, TC_WARP_MMA = 1, TC_WARP_UNP = 2, TC_WARP_EPI = 6;
 constexpr int TC_TMEM_COLS = 512;
@@ -56,23 +58,26 @@ struct TcArgs {
 };
 
 struct TcPlan {
-    int raw, op, epi, bar, tptr, total;
-    int raw_bytes, a_bytes, b_bytes, op_bytes, xds_bytes, epi_bytes, nslot;
+    int raw, a, epi, bar, tptr, total;
+    int raw_bytes, raw_stride, b_off, x_off, a_bytes, b_bytes, xds_bytes, epi_bytes, nslot;
 };
+// a copied stage: [codes 128 x TC_RAW_W | scales 128 x 16 | columns' fp16 codes | columns' scales and sums]
 __host__ __device__ inline TcPlan tc_plan(int G) {
     TcPlan p;
-    p.raw_bytes = TC_M * TC_RAW_W + TC_M * 16;            // codes + scales of one stage
-    p.a_bytes = (TC_KS / 8) * TC_M * 16;                  // fp16 codes of 128 rows, 16 chunks of 8 values
     p.b_bytes = (TC_KS / 8) * G * 16;                     // fp16 codes of G columns
-    p.op_bytes = p.a_bytes + p.b_bytes;
     p.xds_bytes = TC_BPS * 2 * G * 4;
-    p.epi_bytes = align_up(p.xds_bytes + TC_M * 8, 128);  // + the rows' 4 block scales (fp16)
+    p.b_off = TC_M * TC_RAW_W + TC_M * 16;
+    p.x_off = p.b_off + p.b_bytes;
+    p.raw_bytes = p.x_off + p.xds_bytes;
+    p.raw_stride = align_up(p.raw_bytes, 128);
+    p.a_bytes = (TC_KS / 8) * TC_M * 16;                  // fp16 codes of 128 rows, 16 chunks of 8 values
+    p.epi_bytes = align_up(p.xds_bytes + TC_M * 8, 128);  // the columns' scales and sums + the rows' 4 block scales
     p.nslot = TC_TMEM_COLS / G;
     int o = 0;
-    p.raw = o;  o += TC_NR * align_up(p.raw_bytes, 128);
-    p.op = o;   o += TC_NS * align_up(p.op_bytes, 128);
+    p.raw = o;  o += TC_NR * p.raw_stride;
+    p.a = o;    o += TC_NA * p.a_bytes;
     p.epi = o;  o += TC_NE * p.epi_bytes;
-    p.bar = o;  o += 8 * (2 * TC_NR + 3 * TC_NS + 3 * TC_NE + 2 * 32 + 1);
+    p.bar = o;  o += 8 * (2 * TC_NR + 2 * TC_NA + 2 * TC_NE + 2 * 32 + 1);
     p.tptr = o; o += 16;
     p.total = align_up(o, 128) + 128;                     // + slack to align the base to 128 bytes
     return p;
@@ -161,11 +166,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_table(const __grid_constan
     const TcPlan P = tc_plan(G);
     uint8_t *sm = smt + ((128 - (smem_u32(smt) & 127)) & 127);
     uint64_t *bars = (uint64_t *) (sm + P.bar);
-    // raw_full / b_full / x_full: a TMA or bulk copy landed (1 arrival + bytes); raw_empty, a_full, s_full: the 4
-    // unpack warps; op_empty, tm_full, fin: tcgen05.commit; epi_empty, tm_empty: the 8 epilogue warps
-    uint64_t *raw_full = bars, *raw_empty = raw_full + TC_NR, *a_full = raw_empty + TC_NR, *b_full = a_full + TC_NS,
-             *op_empty = b_full + TC_NS, *x_full = op_empty + TC_NS, *s_full = x_full + TC_NE,
-             *epi_empty = s_full + TC_NE, *tm_full = epi_empty + TC_NE, *tm_empty = tm_full + 32,
+    // raw_full: the four copies of a stage landed (1 arrival + bytes); raw_empty: unpacked (4 warps) and read by the
+    // MMAs (1 commit); a_full / e_full: the 4 unpack warps; a_empty, tm_full, fin: tcgen05.commit; e_empty, tm_empty:
+    // the 8 epilogue warps
+    uint64_t *raw_full = bars, *raw_empty = raw_full + TC_NR, *a_full = raw_empty + TC_NR, *a_empty = a_full + TC_NA,
+             *e_full = a_empty + TC_NA, *e_empty = e_full + TC_NE, *tm_full = e_empty + TC_NE, *tm_empty = tm_full + 32,
              *fin = tm_empty + 32;
     uint32_t *tptr = (uint32_t *) (sm + P.tptr);
     __shared__ int abort_flag;
@@ -174,9 +179,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_table(const __grid_constan
     const int nslot = P.nslot;
 
     if (tid == 0) {
-        for (int i = 0; i < TC_NR; i++) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 4); }
-        for (int i = 0; i < TC_NS; i++) { mbar_init(&a_full[i], 4); mbar_init(&b_full[i], 1); mbar_init(&op_empty[i], 1); }
-        for (int i = 0; i < TC_NE; i++) { mbar_init(&x_full[i], 1); mbar_init(&s_full[i], 4); mbar_init(&epi_empty[i], 8); }
+        for (int i = 0; i < TC_NR; i++) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 5); }
+        for (int i = 0; i < TC_NA; i++) { mbar_init(&a_full[i], 4); mbar_init(&a_empty[i], 1); }
+        for (int i = 0; i < TC_NE; i++) { mbar_init(&e_full[i], 4); mbar_init(&e_empty[i], 8); }
         for (int i = 0; i < nslot; i++) { mbar_init(&tm_full[i], 1); mbar_init(&tm_empty[i], 8); }
         mbar_init(fin, 1);
         abort_flag = 0;
@@ -204,41 +209,30 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_table(const __grid_constan
         fail();
         return false;
     };
+    auto raw_at = [&](int r) { return sm + P.raw + r * P.raw_stride; };
 
     if (warp == TC_WARP_PROD) {
         // ---------------- producer ----------------
         if (lane == 0) {
-            int i = 0, nr = 0, nb = 0, nx = 0;   // stages issued per ring
+            int i = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
                 const int tile = u / a.groups, g = u - tile * a.groups;
                 const uint8_t *xh = a.xh + (size_t) g * (K / 8) * G * 16;
                 const float *xds = a.xds + (size_t) g * (K / 32) * 2 * G;
                 for (int s = 0; s < nst; s++, i++) {
-                    const int r = i % TC_NR, o = i % TC_NS, e = i % TC_NE;
+                    const int r = i % TC_NR;
                     if (!(ok = wait(&raw_empty[r], ((i / TC_NR) & 1) ^ 1))) break;
-                    uint8_t *raw = sm + P.raw + r * align_up(P.raw_bytes, 128);
+                    uint8_t *raw = raw_at(r);
                     mbar_expect_tx(&raw_full[r], (uint32_t) P.raw_bytes);
                     tma_load_2d(raw, &a.tm_codes, s * (TC_KS / 2), tile * TC_M, &raw_full[r]);
                     tma_load_2d(raw + TC_M * TC_RAW_W, &a.tm_scales, K / 2 + 16 * (s / 2), tile * TC_M, &raw_full[r]);
-                    nr++;
-                    if (!(ok = wait(&op_empty[o], ((i / TC_NS) & 1) ^ 1))) break;
-                    uint8_t *op = sm + P.op + o * align_up(P.op_bytes, 128);
-                    mbar_expect_tx(&b_full[o], (uint32_t) P.b_bytes);
-                    bulk_g2s(op + P.a_bytes, xh + (size_t) s * (TC_KS / 8) * G * 16, (uint32_t) P.b_bytes, &b_full[o]);
-                    nb++;
-                    if (!(ok = wait(&epi_empty[e], ((i / TC_NE) & 1) ^ 1))) break;
-                    uint8_t *ep = sm + P.epi + e * P.epi_bytes;
-                    mbar_expect_tx(&x_full[e], (uint32_t) P.xds_bytes);
-                    bulk_g2s(ep, xds + (size_t) s * TC_BPS * 2 * G, (uint32_t) P.xds_bytes, &x_full[e]);
-                    nx++;
+                    bulk_g2s(raw + P.b_off, xh + (size_t) s * (TC_KS / 8) * G * 16, (uint32_t) P.b_bytes, &raw_full[r]);
+                    bulk_g2s(raw + P.x_off, xds + (size_t) s * TC_BPS * 2 * G, (uint32_t) P.xds_bytes, &raw_full[r]);
                 }
             }
-            if (!ok) {   // the copies in flight land before the CTA exits (bounded waits on the last stages issued)
-                for (int k = nr > TC_NR ? nr - TC_NR : 0; k < nr; k++) mbar_wait(&raw_full[k % TC_NR], (k / TC_NR) & 1);
-                for (int k = nb > TC_NS ? nb - TC_NS : 0; k < nb; k++) mbar_wait(&b_full[k % TC_NS], (k / TC_NS) & 1);
-                for (int k = nx > TC_NE ? nx - TC_NE : 0; k < nx; k++) mbar_wait(&x_full[k % TC_NE], (k / TC_NE) & 1);
-            }
+            if (!ok)   // the copies in flight land before the CTA exits (bounded waits on the last stages issued)
+                for (int k = i > TC_NR ? i - TC_NR : 0; k < i; k++) mbar_wait(&raw_full[k % TC_NR], (k / TC_NR) & 1);
         }
     } else if (warp == TC_WARP_MMA) {
         // ---------------- MMA issuer ----------------
@@ -248,10 +242,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_table(const __grid_constan
             bool ok = true;
             for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
                 for (int s = 0; s < nst && ok; s++, i++) {
-                    const int o = i % TC_NS;
-                    if (!(ok = wait(&a_full[o], (i / TC_NS) & 1) && wait(&b_full[o], (i / TC_NS) & 1))) break;
+                    const int r = i % TC_NR, o = i % TC_NA;
+                    if (!(ok = wait(&a_full[o], (i / TC_NA) & 1) && wait(&raw_full[r], (i / TC_NR) & 1))) break;
                     tc_fence_after();
-                    const uint32_t abase = smem_u32(sm + P.op + o * align_up(P.op_bytes, 128)), bbase = abase + P.a_bytes;
+                    const uint32_t abase = smem_u32(sm + P.a + o * P.a_bytes), bbase = smem_u32(raw_at(r) + P.b_off);
                     for (int jj = 0; jj < TC_BPS; jj++, b++) {
                         const int slot = b % nslot;
                         if (!(ok = wait(&tm_empty[slot], ((b / nslot) & 1) ^ 1))) break;
@@ -264,7 +258,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_table(const __grid_constan
                         }
                         tc_commit(&tm_full[slot]);
                     }
-                    if (ok) tc_commit(&op_empty[o]);
+                    if (ok) {
+                        tc_commit(&a_empty[o]);
+                        tc_commit(&raw_empty[r]);
+                    }
                 }
             }
             if (!ok) {   // the MMAs issued complete before TMEM is freed
@@ -279,12 +276,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_table(const __grid_constan
         bool ok = true;
         for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
             for (int s = 0; s < nst; s++, i++) {
-                const int r = i % TC_NR, o = i % TC_NS, e = i % TC_NE;
-                if (!(ok = wait(&raw_full[r], (i / TC_NR) & 1) && wait(&op_empty[o], ((i / TC_NS) & 1) ^ 1) &&
-                           wait(&epi_empty[e], ((i / TC_NE) & 1) ^ 1)))
+                const int r = i % TC_NR, o = i % TC_NA, e = i % TC_NE;
+                if (!(ok = wait(&raw_full[r], (i / TC_NR) & 1) && wait(&a_empty[o], ((i / TC_NA) & 1) ^ 1) &&
+                           wait(&e_empty[e], ((i / TC_NE) & 1) ^ 1)))
                     break;
-                const uint8_t *raw = sm + P.raw + r * align_up(P.raw_bytes, 128);
-                uint8_t *A = sm + P.op + o * align_up(P.op_bytes, 128);
+                const uint8_t *raw = raw_at(r);
+                uint8_t *A = sm + P.a + o * P.a_bytes, *ep = sm + P.epi + e * P.epi_bytes;
 #pragma unroll
                 for (int p = 0; p < TC_BPS; p++) {   // block p of the stage: 16 code bytes -> 4 chunks of 8 fp16
                     const uint4 c = *(const uint4 *) (raw + row * TC_RAW_W + 16 * p);
@@ -293,15 +290,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_table(const __grid_constan
                     *(uint4 *) (A + ((4 * p + 2) * TC_M + row) * 16) = nib8(c.x, c.y, 1);   // 16..23
                     *(uint4 *) (A + ((4 * p + 3) * TC_M + row) * 16) = nib8(c.z, c.w, 1);   // 24..31
                 }
-                // the row's 4 block scales of this stage (8 bytes of the 16-byte scale box)
-                const uint2 sc = *(const uint2 *) (raw + TC_M * TC_RAW_W + row * 16 + 8 * (s & 1));
-                *(uint2 *) (sm + P.epi + e * P.epi_bytes + P.xds_bytes + row * 8) = sc;
+                // the row's 4 block scales of this stage (8 bytes of the 16-byte scale box), the columns' scales/sums
+                *(uint2 *) (ep + P.xds_bytes + row * 8) = *(const uint2 *) (raw + TC_M * TC_RAW_W + row * 16 + 8 * (s & 1));
+                if (row < P.xds_bytes / 16) *(uint4 *) (ep + 16 * row) = *(const uint4 *) (raw + P.x_off + 16 * row);
                 fence_proxy_async();
                 __syncwarp();
                 if (lane == 0) {
                     mbar_arrive(&a_full[o]);
                     mbar_arrive(&raw_empty[r]);
-                    mbar_arrive(&s_full[e]);
+                    mbar_arrive(&e_full[e]);
                 }
             }
         }
@@ -318,7 +315,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_table(const __grid_constan
             for (int k = 0; k < CH / 2; k++) acc[k] = cor[k] = make_float2(0.0f, 0.0f);
             for (int s = 0; s < nst && ok; s++, i++) {
                 const int e = i % TC_NE;
-                if (!(ok = wait(&x_full[e], (i / TC_NE) & 1) && wait(&s_full[e], (i / TC_NE) & 1))) break;
+                if (!(ok = wait(&e_full[e], (i / TC_NE) & 1))) break;
                 const uint8_t *ep = sm + P.epi + e * P.epi_bytes;
                 const uint16_t *dsc = (const uint16_t *) (ep + P.xds_bytes + row * 8);
                 for (int jj = 0; jj < TC_BPS; jj++, b++) {
@@ -343,7 +340,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_table(const __grid_constan
                     }
                 }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&epi_empty[e]);
+                if (lane == 0) mbar_arrive(&e_empty[e]);
             }
             if (!ok) break;
             const int grow = tile * TC_M + row;
