@@ -164,6 +164,13 @@ imi_cuda_status imi_cuda_q4_matvec(int device, const uint8_t *q4, int rows, int 
 imi_cuda_status imi_cuda_q4_matmul(int device, const uint8_t *q4, int rows, int cols, const int8_t *xq,
                                    const float *xd, const float *xs, int ncol, float *out);
 
+/* Diagnostics: imi_cuda_q4_matmul with CTA 0's timeline of the tensor-core read in ns, trace[7][64]: 0 stage copies
+ * issued, 1 stage copies seen by the unpack warps, 2 stage unpacked, 3 block's MMAs issued, 4 block's dots seen by the
+ * epilogue, 5 block's chains done, 6 block's dots in registers (stages and blocks counted from the CTA's first unit);
+ * trace holds 7 * 64 values. */
+imi_cuda_status imi_cuda_trace_tc(int device, const uint8_t *q4, int rows, int cols, const int8_t *xq, const float *xd,
+                                  const float *xs, int ncol, float *out, unsigned long long *trace);
+
 /* The isolated table read timed on the device (the configs[4] sweep; imi/kernels/q4x2_bench.cpp's measurement): a
  * rows x cols Q4_0 table (random codes and scales, the engine's row layout) times ncol 8-bit inputs, `reps` reads after
  * one untimed pass, CUDA events on one stream. The table is replicated in device memory until the copies pass 256 MB

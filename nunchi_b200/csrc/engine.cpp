@@ -14,6 +14,7 @@
 
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstdlib>
@@ -57,13 +58,15 @@ static imi_cuda_status fail(imi_cuda_status st, const std::string &msg) {
 
 namespace {
 
-constexpr int STEP_COLS = 8;      // columns per launch (the small-batch table kernel's limit)
+constexpr int STEP_COLS = 8;      // columns per launch of the small-batch table kernel
+constexpr int TC_CHUNK = 128;     // prefill positions per batched read (tensor-core path)
 constexpr int BATCH_GROUP = 64;   // step_batch checks the context per 64 positions, as seoul.cpp:496-498
 
 struct TableRef {
     size_t off = 0;
     int rows = 0, cols = 0, row_bytes = 0;
     bool has_m = false;   // Q4_1 rows: a minimum per block after the scales
+    TcArgs tc = {};       // the tensor-core batched read of this table: its TMA views (Q4_0 tables)
 };
 struct LayerRef {
     bool conv = false, swa = false;
@@ -97,13 +100,20 @@ struct imi_cuda_engine {
     float *qa_d = nullptr, *qa_s = nullptr, *qt_d = nullptr, *qt_s = nullptr;
     Col *cols_d = nullptr, *cols_h = nullptr;
     float *embd_h = nullptr;
-    // pinned: what the host reads back after a step (session records at 32-byte slots from 0, the error word at 256),
-    // so the read is a small DMA into page-locked memory instead of a staged copy into pageable memory. One read
-    // brings every conversation of the last step; it stays valid until anything changes a session (gen moves on).
+    // columns one launch takes at most: 8 in the small-batch table kernel; up to ncmax (the larger of max_batch and
+    // a prefill chunk) in the tensor-core batched read, when every table is Q4_0 (tc_batch)
+    int ncmax = STEP_COLS;
+    bool tc_batch = false;
+    uint8_t *tc_xh = nullptr;   // the batched read's column operand and the columns' block scales and sums
+    float *tc_xds = nullptr;
+    SessDev *reply_d = nullptr;   // the last step's conversation records gathered for one read-back
+    // pinned: what the host reads back after a step (session records at 32-byte slots from 0, the error word after
+    // them), so the read is one small DMA into page-locked memory instead of staged copies into pageable memory. One
+    // read brings every conversation of the last step; it stays valid until anything changes a session (gen moves on).
     uint8_t *reply_h = nullptr;
     uint64_t gen = 1, reply_gen = 0;
     int last_n = 0, reply_n = 0;
-    const SessDev *last_s[STEP_COLS] = {}, *reply_src[STEP_COLS] = {};
+    std::vector<const SessDev *> last_s, reply_src;
     unsigned *done = nullptr;
     int *err = nullptr;
     cudaEvent_t staged = nullptr;   // the last host->device copy of the staging buffers has run
@@ -146,6 +156,7 @@ imi_cuda_engine::~imi_cuda_engine() {
     cudaFree(qbuf);
     cudaFree(q8k_q);
     cudaFree(cols_d);
+    cudaFree(tc_xh);
     cudaFreeHost(cols_h);
     cudaFreeHost(embd_h);
     cudaFreeHost(reply_h);
@@ -233,6 +244,72 @@ struct Loader {
         for (int r = 0; r < t->ne[1]; r++) o.push_back({ t, r });
     }
 };
+
+}  // namespace
+
+// ---------------------------------------------------------------------------------------------------------------
+// the tensor-core batched read: tensor maps of a table, the columns' operands in the MMA's layout
+// ---------------------------------------------------------------------------------------------------------------
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::mutex g_encode_mu;
+
+// the two TMA views of a table's rows ([rows][row_bytes] bytes): codes in boxes of TC_RAW_W bytes, scales in 16
+cudaError_t tc_tensor_maps(TcArgs &a, const uint8_t *W, int rows, int row_bytes) {
+    {
+        std::lock_guard<std::mutex> g(g_encode_mu);
+        if (!g_encode) {
+            void *fn = nullptr;
+            cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+            const cudaError_t r = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q);
+            if (r != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+            g_encode = (PFN_cuTensorMapEncodeTiled_v12000) fn;
+        }
+    }
+    cuuint64_t dims[2] = { (cuuint64_t) row_bytes, (cuuint64_t) rows }, strides[1] = { (cuuint64_t) row_bytes };
+    cuuint32_t box[2] = { (cuuint32_t) TC_RAW_W, (cuuint32_t) TC_M }, es[2] = { 1, 1 };
+    CUresult c = g_encode(&a.tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *) W, dims, strides, box, es,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (c != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    box[0] = 16;
+    c = g_encode(&a.tm_scales, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *) W, dims, strides, box, es,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return c == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// columns per group of the batched read (the kernel's instances: 16, 32, 64)
+int tc_group(int ncol) { return ncol <= 16 ? 16 : ncol <= 32 ? 32 : 64; }
+
+// an integer |v| <= 2048 as fp16 bits (exact)
+uint16_t int_half(int v) {
+    if (v == 0) return 0;
+    const uint16_t sg = v < 0 ? 0x8000 : 0;
+    unsigned m = (unsigned) (v < 0 ? -v : v);
+    int e = 0;
+    while ((m >> (e + 1)) != 0) e++;
+    return (uint16_t) (sg | ((e + 15) << 10) | ((m << (10 - e)) & 0x3FF));
+}
+
+// the columns' 8-bit codes, scales and scale * code sums ([ncol][cols], [ncol][cols/32]) in the batched read's layout:
+// xh [group][cols/8][G][8] fp16, xds [group][cols/32][2][G] (zeros for the padding columns)
+void tc_operands_host(const int8_t *xq, const float *xd, const float *xs, int ncol, int cols, int G,
+                      std::vector<uint16_t> &xh, std::vector<float> &xds) {
+    const int groups = (ncol + G - 1) / G, nq = cols / 8, nb = cols / 32;
+    xh.assign((size_t) groups * nq * G * 8, 0);
+    xds.assign((size_t) groups * nb * 2 * G, 0.0f);
+    for (int c = 0; c < ncol; c++) {
+        const int g = c / G, cg = c - g * G;
+        for (int k = 0; k < cols; k++)
+            xh[(((size_t) g * nq + k / 8) * G + cg) * 8 + (k & 7)] = int_half(xq[(size_t) c * cols + k]);
+        for (int j = 0; j < nb; j++) {
+            xds[(((size_t) g * nb + j) * 2 + 0) * G + cg] = xd[(size_t) c * nb + j];
+            xds[(((size_t) g * nb + j) * 2 + 1) * G + cg] = xs[(size_t) c * nb + j];
+        }
+    }
+}
 
 }  // namespace
 
@@ -390,20 +467,30 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
         CK(cudaMemcpy(e->rope_sn, sn.data(), 2 * per * 4, cudaMemcpyHostToDevice));
     }
 
-    // per-column scratch
+    // the tensor-core batched read takes every Q4_0 layer table and a Q4_0 word table (a Q4_1 table or a Q6_K word
+    // table keeps the small-batch kernel, 8 columns per read)
     const int HD = e->n_head * e->head_dim, kvd = e->n_head_kv * e->head_dim;
+    e->tc_batch = !e->tok_q6k && !e->tok.has_m;
+    for (auto &Lr : e->layers)
+        for (const TableRef *t : { &Lr.in_proj, &Lr.out_proj, &Lr.qkvg, &Lr.o, &Lr.gate_up, &Lr.down })
+            if (t->rows && t->has_m) e->tc_batch = false;
+    if ((HD % 256) || (e->n_ff % 256)) e->tc_batch = false;
+    e->ncmax = e->tc_batch ? std::max({ STEP_COLS, max_batch, TC_CHUNK }) : STEP_COLS;
+    if (e->ncmax > 256) return fail(IMI_E_ARG, "max_batch above 256");
+    const int NC = e->ncmax;
+    // per-column scratch
     e->big_n = std::max(3 * E, HD + 2 * kvd + e->n_head);
     const size_t per_col = (size_t) 2 * E + e->big_n + E + HD + e->n_ff + E + E + E;
-    DALLOC(e, e->X, per_col * STEP_COLS * 4);
-    e->big = e->X + (size_t) 2 * E * STEP_COLS;
-    e->y = e->big + (size_t) e->big_n * STEP_COLS;
-    e->att = e->y + (size_t) E * STEP_COLS;
-    e->act = e->att + (size_t) HD * STEP_COLS;
-    e->fo = e->act + (size_t) e->n_ff * STEP_COLS;
-    e->embd = e->fo + (size_t) E * STEP_COLS;
-    e->hid = e->embd + (size_t) E * STEP_COLS;
+    DALLOC(e, e->X, per_col * NC * 4);
+    e->big = e->X + (size_t) 2 * E * NC;
+    e->y = e->big + (size_t) e->big_n * NC;
+    e->att = e->y + (size_t) E * NC;
+    e->act = e->att + (size_t) HD * NC;
+    e->fo = e->act + (size_t) e->n_ff * NC;
+    e->embd = e->fo + (size_t) E * NC;
+    e->hid = e->embd + (size_t) E * NC;
     {
-        const size_t na = (size_t) STEP_COLS * e->n_ff, nt = (size_t) STEP_COLS * HD;
+        const size_t na = (size_t) STEP_COLS * e->n_ff, nt = (size_t) NC * HD;
         uint8_t *q = nullptr;
         DALLOC(e, q, na + nt + 4 * 2 * (na / 32 + nt / 32) + 1024);
         e->qbuf = q;
@@ -424,14 +511,32 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
         e->q8k_d = (float *) (q + nq);
         e->q8k_b = (int16_t *) (q + nq + 4 * nd);
     }
-    DALLOC(e, e->cols_d, sizeof(Col) * STEP_COLS + 64);
-    e->done = (unsigned *) (e->cols_d + STEP_COLS);
+    DALLOC(e, e->cols_d, sizeof(Col) * NC + 64 + 32 * NC);
+    e->done = (unsigned *) (e->cols_d + NC);
     e->err = (int *) (e->done + 4);
-    CK(cudaMemset(e->cols_d, 0, sizeof(Col) * STEP_COLS + 64));
-    CK(cudaMallocHost(&e->cols_h, sizeof(Col) * STEP_COLS));
-    CK(cudaMallocHost(&e->embd_h, (size_t) E * 4 * STEP_COLS));
-    CK(cudaMallocHost(&e->reply_h, 512));
-    memset(e->cols_h, 0, sizeof(Col) * STEP_COLS);
+    e->reply_d = (SessDev *) ((uint8_t *) e->cols_d + sizeof(Col) * NC + 64);
+    CK(cudaMemset(e->cols_d, 0, sizeof(Col) * NC + 64 + 32 * NC));
+    CK(cudaMallocHost(&e->cols_h, sizeof(Col) * NC));
+    CK(cudaMallocHost(&e->embd_h, (size_t) E * 4 * NC));
+    CK(cudaMallocHost(&e->reply_h, (size_t) 32 * NC + 64));
+    memset(e->cols_h, 0, sizeof(Col) * NC);
+    e->last_s.assign(NC, nullptr);
+    e->reply_src.assign(NC, nullptr);
+    if (e->tc_batch) {   // the batched read's operand buffers and every table's TMA views
+        const int ncp = (NC + 63) / 64 * 64, kmax = std::max(std::max(E, HD), e->n_ff);
+        const size_t bh = (size_t) kmax * ncp * 2, bx = (size_t) (kmax / 32) * 2 * ncp * 4;
+        DALLOC(e, e->tc_xh, bh + bx);
+        e->tc_xds = (float *) (e->tc_xh + bh);
+        auto maps = [&](TableRef &t) -> cudaError_t {
+            t.tc = {};
+            t.tc.rows = t.rows; t.tc.cols = t.cols; t.tc.row_bytes = t.row_bytes; t.tc.err = e->err;
+            return tc_tensor_maps(t.tc, e->w + t.off, t.rows, t.row_bytes);
+        };
+        for (auto &Lr : e->layers)
+            for (TableRef *t : { &Lr.in_proj, &Lr.out_proj, &Lr.qkvg, &Lr.o, &Lr.gate_up, &Lr.down })
+                if (t->rows) CK(maps(*t));
+        CK(maps(e->tok));
+    }
     CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
     CK(cudaEventCreateWithFlags(&e->staged, cudaEventDisableTiming));
     CK(prepare_kernels());
@@ -442,72 +547,6 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
     *out = e.release();
     return IMI_OK;
 }
-
-// ---------------------------------------------------------------------------------------------------------------
-// the tensor-core batched read: tensor maps of a table, the columns' operands in the MMA's layout
-// ---------------------------------------------------------------------------------------------------------------
-namespace {
-
-PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
-std::mutex g_encode_mu;
-
-// the two TMA views of a table's rows ([rows][row_bytes] bytes): codes in boxes of TC_RAW_W bytes, scales in 16
-cudaError_t tc_tensor_maps(TcArgs &a, const uint8_t *W, int rows, int row_bytes) {
-    {
-        std::lock_guard<std::mutex> g(g_encode_mu);
-        if (!g_encode) {
-            void *fn = nullptr;
-            cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
-            const cudaError_t r = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q);
-            if (r != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
-            g_encode = (PFN_cuTensorMapEncodeTiled_v12000) fn;
-        }
-    }
-    cuuint64_t dims[2] = { (cuuint64_t) row_bytes, (cuuint64_t) rows }, strides[1] = { (cuuint64_t) row_bytes };
-    cuuint32_t box[2] = { (cuuint32_t) TC_RAW_W, (cuuint32_t) TC_M }, es[2] = { 1, 1 };
-    CUresult c = g_encode(&a.tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *) W, dims, strides, box, es,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (c != CUDA_SUCCESS) return cudaErrorInvalidValue;
-    box[0] = 16;
-    c = g_encode(&a.tm_scales, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *) W, dims, strides, box, es,
-                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return c == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
-}
-
-// columns per group of the batched read (the kernel's instances: 16, 32, 64)
-int tc_group(int ncol) { return ncol <= 16 ? 16 : ncol <= 32 ? 32 : 64; }
-
-// an integer |v| <= 2048 as fp16 bits (exact)
-uint16_t int_half(int v) {
-    if (v == 0) return 0;
-    const uint16_t sg = v < 0 ? 0x8000 : 0;
-    unsigned m = (unsigned) (v < 0 ? -v : v);
-    int e = 0;
-    while ((m >> (e + 1)) != 0) e++;
-    return (uint16_t) (sg | ((e + 15) << 10) | ((m << (10 - e)) & 0x3FF));
-}
-
-// the columns' 8-bit codes, scales and scale * code sums ([ncol][cols], [ncol][cols/32]) in the batched read's layout:
-// xh [group][cols/8][G][8] fp16, xds [group][cols/32][2][G] (zeros for the padding columns)
-void tc_operands_host(const int8_t *xq, const float *xd, const float *xs, int ncol, int cols, int G,
-                      std::vector<uint16_t> &xh, std::vector<float> &xds) {
-    const int groups = (ncol + G - 1) / G, nq = cols / 8, nb = cols / 32;
-    xh.assign((size_t) groups * nq * G * 8, 0);
-    xds.assign((size_t) groups * nb * 2 * G, 0.0f);
-    for (int c = 0; c < ncol; c++) {
-        const int g = c / G, cg = c - g * G;
-        for (int k = 0; k < cols; k++)
-            xh[(((size_t) g * nq + k / 8) * G + cg) * 8 + (k & 7)] = int_half(xq[(size_t) c * cols + k]);
-        for (int j = 0; j < nb; j++) {
-            xds[(((size_t) g * nb + j) * 2 + 0) * G + cg] = xd[(size_t) c * nb + j];
-            xds[(((size_t) g * nb + j) * 2 + 1) * G + cg] = xs[(size_t) c * nb + j];
-        }
-    }
-}
-
-}  // namespace
 
 // ---------------------------------------------------------------------------------------------------------------
 // the step schedule
@@ -723,9 +762,166 @@ cudaError_t enqueue_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind)
     return launch_final(fa, e->stream, true);
 }
 
+// one read of table t by the tensor-core batched path for the columns prepared in tc_xh / tc_xds
+cudaError_t tc_read(imi_cuda_engine *e, const TableRef &t, int ncol, int epi, float *out, int out_stride) {
+    TcArgs a = t.tc;
+    a.ncol = ncol;
+    a.G = tc_group(ncol);
+    a.groups = (ncol + a.G - 1) / a.G;
+    a.xh = e->tc_xh;
+    a.xds = e->tc_xds;
+    a.out = out;
+    a.out_stride = out_stride;
+    a.epi = epi;
+    a.cols_d = e->cols_d;
+    a.done = e->done;
+    a.err = e->err;
+    const int units = (t.rows + TC_M - 1) / TC_M * a.groups;
+    return launch_tc_table(a, std::min(e->sm_count, units), e->stream, true);
+}
+
+// the step schedule of the tensor-core batched path (more than 8 columns): before every table read one launch
+// prepares the columns' inputs (k_tc_prep, one CTA per column), then the read (k_tc_table); attention as in the
+// small-batch schedule. Same float order as enqueue_step's schedule, column by column.
+cudaError_t enqueue_batch(imi_cuda_engine *e, int ncol, bool head, StepKind kind) {
+    const int E = e->n_embd, HD = e->n_head * e->head_dim, G = tc_group(ncol);
+    TcPrepArgs p0 = {};
+    p0.cols_d = e->cols_d;
+    p0.ncol = ncol;
+    p0.G = G;
+    p0.xh = e->tc_xh;
+    p0.xds = e->tc_xds;
+    p0.eps = e->eps;
+    p0.n_embd = E;
+    p0.d_conv = e->d_conv;
+    p0.emb = e->w + e->tok.off;
+    p0.emb_row_bytes = e->tok.row_bytes;
+    p0.emb_q6k = 0;
+    p0.x_stride = 2 * E;
+    p0.ring_layer = -1;
+    float *X0 = e->X, *X1 = e->X + E;
+    cudaError_t r;
+    auto prep = [&](TcPrepArgs p, int K) {
+        p.K = K;
+        return launch_tc_prep(p, e->stream, true);
+    };
+    if (kind == K_HEAD_ONLY) {   // word scores of a hidden state already computed (seoul.cpp:507-516)
+        TcPrepArgs p = p0;
+        p.pro = TP_CUT;
+        p.in = e->hid;
+        p.in_stride = E;
+        if ((r = prep(p, E)) != cudaSuccess) return r;
+        return tc_read(e, e->tok, ncol, TE_HEAD, nullptr, 0);
+    }
+    for (int il = 0; il < e->n_layer; il++) {
+        const LayerRef &L = e->layers[il];
+        TcPrepArgs p = p0;
+        p.pro = il > 0 ? TP_RESID_NORM : TP_EMBED_NORM;
+        p.in = e->fo;
+        p.in_stride = E;
+        p.xin = X1;
+        p.xout = X0;
+        p.wpost = il > 0 ? e->f32(e->layers[il - 1].post_ffn_norm) : nullptr;
+        p.wpre = e->f32(L.attn_norm);
+        if ((r = prep(p, E)) != cudaSuccess) return r;
+        if ((r = tc_read(e, L.conv ? L.in_proj : L.qkvg, ncol, TE_STORE, e->big, e->big_n)) != cudaSuccess) return r;
+        if (L.conv) {
+            p = p0;
+            p.pro = TP_CONV;
+            p.in = e->big;
+            p.in_stride = e->big_n;
+            p.conv_w = e->f32(L.conv_w);
+            p.conv_layer = L.ci;
+            p.ring_conv = kind == K_DECODE;   // distinct conversations: the conv's own input goes to memory here
+            if ((r = prep(p, E)) != cudaSuccess) return r;
+            if ((r = tc_read(e, L.out_proj, ncol, TE_STORE, e->y, E)) != cudaSuccess) return r;
+        } else {
+            AttnArgs t = {};
+            t.cols_d = e->cols_d;
+            t.ncol = ncol;
+            t.qkv = e->big;
+            t.qkv_stride = e->big_n;
+            t.att = e->att;
+            t.att_stride = HD;
+            t.q_norm = e->f32(L.q_norm);
+            t.k_norm = e->f32(L.k_norm);
+            t.eps = e->eps;
+            t.scale = 1.0f / sqrtf((float) e->head_dim);   // seoul.cpp:432
+            const size_t per = (size_t) e->n_ctx * (e->head_dim / 2);
+            t.rope_cs = e->rope_cs + (L.swa ? per : 0);
+            t.rope_sn = e->rope_sn + (L.swa ? per : 0);
+            t.ai = L.ai;
+            t.n_head = e->n_head;
+            t.n_head_kv = e->n_head_kv;
+            t.head_dim = e->head_dim;
+            t.n_ctx = e->n_ctx;
+            t.window = (L.swa && e->n_swa > 0) ? e->n_swa : 0;   // seoul.cpp:431
+            t.err = e->err;
+            t.kv_fused = kind == K_DECODE;
+            t.q8o_q = e->qt_q;
+            t.q8o_d = e->qt_d;
+            t.q8o_s = e->qt_s;
+            if (kind == K_PREFILL && (r = launch_kvwrite(t, e->stream, true)) != cudaSuccess) return r;
+            if ((r = launch_attn(t, e->stream, true)) != cudaSuccess) return r;
+            p = p0;
+            p.pro = TP_Q8;
+            p.q8_q = e->qt_q;
+            p.q8_d = e->qt_d;
+            p.q8_s = e->qt_s;
+            if ((r = prep(p, HD)) != cudaSuccess) return r;
+            if ((r = tc_read(e, L.o, ncol, TE_STORE, e->y, E)) != cudaSuccess) return r;
+        }
+        p = p0;
+        p.pro = TP_RESID_NORM;
+        p.in = e->y;
+        p.in_stride = E;
+        p.xin = X0;
+        p.xout = X1;
+        p.wpost = e->f32(L.post_attn_norm);
+        p.wpre = e->f32(L.ffn_norm);
+        if (L.conv && kind != K_DECODE) {   // a prefill chunk's conv memory, one launch after the conv read it
+            p.ring_layer = L.ci;
+            p.ring_src = e->big;
+            p.ring_src_stride = e->big_n;
+        }
+        if ((r = prep(p, E)) != cudaSuccess) return r;
+        if ((r = tc_read(e, L.gate_up, ncol, TE_SILU, e->act, e->n_ff)) != cudaSuccess) return r;
+        p = p0;
+        p.pro = TP_CUT;
+        p.in = e->act;
+        p.in_stride = e->n_ff;
+        if ((r = prep(p, e->n_ff)) != cudaSuccess) return r;
+        if ((r = tc_read(e, L.down, ncol, TE_STORE, e->fo, E)) != cudaSuccess) return r;
+    }
+    const LayerRef &last = e->layers.back();
+    if (head) {
+        TcPrepArgs p = p0;
+        p.pro = TP_FINAL;
+        p.in = e->fo;
+        p.in_stride = E;
+        p.xin = X1;
+        p.wpost = e->f32(last.post_ffn_norm);
+        p.wpre = e->f32(e->out_norm);
+        if ((r = prep(p, E)) != cudaSuccess) return r;
+        return tc_read(e, e->tok, ncol, TE_HEAD, nullptr, 0);
+    }
+    FinalArgs fa = {};
+    fa.cols_d = e->cols_d;
+    fa.ncol = ncol;
+    fa.in = e->fo;
+    fa.in_stride = E;
+    fa.xin = X1;
+    fa.x_stride = 2 * E;
+    fa.wpost = e->f32(last.post_ffn_norm);
+    fa.out_norm = e->f32(e->out_norm);
+    fa.eps = e->eps;
+    fa.n_embd = E;
+    return launch_final(fa, e->stream, true);
+}
+
 imi_cuda_status run_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind, bool copy_cols) {
     e->gen++;
-    e->last_n = std::min(ncol, STEP_COLS);
+    e->last_n = ncol;
     for (int c = 0; c < e->last_n; c++) e->last_s[c] = e->cols_h[c].s;
     if (copy_cols) {
         CK(cudaMemcpyAsync(e->cols_d, e->cols_h, sizeof(Col) * ncol, cudaMemcpyHostToDevice, e->stream));
@@ -736,7 +932,7 @@ imi_cuda_status run_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind,
     if (it == e->graphs.end()) {
         cudaGraph_t g = nullptr;
         CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
-        const cudaError_t r = enqueue_step(e, ncol, head, kind);
+        const cudaError_t r = ncol > STEP_COLS ? enqueue_batch(e, ncol, head, kind) : enqueue_step(e, ncol, head, kind);
         const cudaError_t r2 = cudaStreamEndCapture(e->stream, &g);
         if (r != cudaSuccess || r2 != cudaSuccess) {
             if (g) cudaGraphDestroy(g);
@@ -777,7 +973,7 @@ Col decode_col(imi_cuda_state *s, int32_t token, bool has_embd, int c, bool want
 
 static_assert(sizeof(SessDev) <= 32, "a session record fits its slot of the reply buffer");
 imi_cuda_status check_err(imi_cuda_engine *e) {
-    int *hp = (int *) (e->reply_h + 256);
+    int *hp = (int *) (e->reply_h + 32 * e->ncmax);
     CK(cudaMemcpyAsync(hp, e->err, 4, cudaMemcpyDeviceToHost, e->stream));
     CK(cudaStreamSynchronize(e->stream));
     const int h = *hp;
@@ -932,8 +1128,8 @@ imi_cuda_status imi_cuda_step_multi(imi_cuda_state *const *s, int n, const int32
         if (s[i]->pos >= e->n_ctx) return fail(IMI_E_CTX_FULL, "context full (" + std::to_string(e->n_ctx) + ")");
     }
     CK(cudaSetDevice(e->device));
-    for (int i0 = 0; i0 < n; i0 += STEP_COLS) {
-        const int m = std::min(STEP_COLS, n - i0);
+    for (int i0 = 0; i0 < n; i0 += e->ncmax) {   // all of them in one read when the batched path runs them
+        const int m = std::min(e->ncmax, n - i0);
         std::vector<int32_t> t(m);
         for (int c = 0; c < m; c++) t[c] = tokens ? tokens[i0 + c] : -1;
         imi_cuda_status st = step_group(s + i0, m, t.data(), embd ? embd + (size_t) i0 * e->n_embd : nullptr,
@@ -949,11 +1145,17 @@ imi_cuda_status imi_cuda_step_batch(imi_cuda_state *s, const int32_t *tokens, co
     imi_cuda_engine *e = s->e;
     const int E = e->n_embd;
     CK(cudaSetDevice(e->device));
+    // imi checks the context per 64 positions and steps every group before the first that would pass n_ctx
+    // (seoul.cpp:496-498); the positions of those groups are read here in chunks of up to ncmax (one table read each)
+    int n_ok = 0;
     for (int g0 = 0; g0 < n; g0 += BATCH_GROUP) {
         const int gn = std::min(BATCH_GROUP, n - g0);
-        if (s->pos + gn > e->n_ctx) return fail(IMI_E_CTX_FULL, "context full (" + std::to_string(e->n_ctx) + ")");
-        for (int i0 = g0; i0 < g0 + gn; i0 += STEP_COLS) {
-            const int m = std::min(STEP_COLS, g0 + gn - i0);
+        if (s->pos + g0 + gn > e->n_ctx) break;
+        n_ok = g0 + gn;
+    }
+    {
+        for (int i0 = 0; i0 < n_ok; i0 += e->ncmax) {
+            const int m = std::min(e->ncmax, n_ok - i0);
             imi_cuda_status st;
             if ((st = staging_wait(e)) != IMI_OK) return st;
             for (int c = 0; c < m; c++) {
@@ -976,6 +1178,7 @@ imi_cuda_status imi_cuda_step_batch(imi_cuda_state *s, const int32_t *tokens, co
             s->pos += m;
         }
     }
+    if (n_ok < n) return fail(IMI_E_CTX_FULL, "context full (" + std::to_string(e->n_ctx) + ")");
     if (want_logits) {   // the last position's word scores (seoul.cpp:507-516)
         imi_cuda_status st;
         if ((st = staging_wait(e)) != IMI_OK) return st;
@@ -993,12 +1196,12 @@ imi_cuda_status imi_cuda_greedy(imi_cuda_state *const *s, int n, const int32_t *
     if (!s || n <= 0 || steps <= 0) return fail(IMI_E_ARG, "bad greedy arguments");
     imi_cuda_engine *e = s[0]->e;
     if (n > e->max_batch && n > STEP_COLS) return fail(IMI_E_ARG, "more conversations than max_batch");
-    if (n > STEP_COLS) {   // groups of STEP_COLS conversations, each group all its steps (conversations are independent)
+    if (n > e->ncmax) {   // groups of ncmax conversations, each group all its steps (conversations are independent)
         for (int i = 0; i < n; i++)
             for (int j = 0; j < i; j++) if (s[j] == s[i]) return fail(IMI_E_ARG, "a state appears twice");
-        std::vector<int32_t> part((size_t) steps * STEP_COLS);
-        for (int g0 = 0; g0 < n; g0 += STEP_COLS) {
-            const int m = std::min(STEP_COLS, n - g0);
+        std::vector<int32_t> part((size_t) steps * e->ncmax);
+        for (int g0 = 0; g0 < n; g0 += e->ncmax) {
+            const int m = std::min(e->ncmax, n - g0);
             const imi_cuda_status st = imi_cuda_greedy(s + g0, m, tokens ? tokens + g0 : nullptr, steps,
                                                        ids ? part.data() : nullptr);
             if (st != IMI_OK) return st;
@@ -1066,9 +1269,12 @@ imi_cuda_status imi_cuda_get_argmax(const imi_cuda_state *s, int32_t *id, float 
         bool in_last = false;
         for (int c = 0; c < e->last_n; c++) in_last |= e->last_s[c] == s->s;
         e->reply_n = in_last ? e->last_n : 1;
-        for (int c = 0; c < e->reply_n; c++) {
-            e->reply_src[c] = in_last ? e->last_s[c] : s->s;
-            CK(cudaMemcpyAsync(e->reply_h + 32 * c, e->reply_src[c], sizeof(SessDev), cudaMemcpyDeviceToHost, e->stream));
+        for (int c = 0; c < e->reply_n; c++) e->reply_src[c] = in_last ? e->last_s[c] : s->s;
+        if (in_last && e->reply_n > 1) {   // the records gathered on the device (cols_d still holds the last step's)
+            CK(launch_gather_sess(e->cols_d, e->reply_n, (uint8_t *) e->reply_d, e->stream));
+            CK(cudaMemcpyAsync(e->reply_h, e->reply_d, (size_t) 32 * e->reply_n, cudaMemcpyDeviceToHost, e->stream));
+        } else {
+            CK(cudaMemcpyAsync(e->reply_h, s->s, sizeof(SessDev), cudaMemcpyDeviceToHost, e->stream));
         }
         const imi_cuda_status st = check_err(e);
         if (st != IMI_OK) return st;
@@ -1314,6 +1520,8 @@ imi_cuda_status imi_cuda_bench_matvec(int device, int rows, int cols, int ncol, 
     return IMI_OK;
 }
 
+static unsigned long long *g_tc_trace_host = nullptr;   // diagnostics: imi_cuda_trace_tc sets it for one call
+
 imi_cuda_status imi_cuda_q4_matmul(int device, const uint8_t *q4, int rows, int cols, const int8_t *xq, const float *xd,
                                    const float *xs, int ncol, float *out) {
     if (!q4 || !xq || !xd || !xs || !out || rows <= 0 || cols <= 0 || cols % 256 || ncol < 1 || ncol > 256)
@@ -1337,11 +1545,17 @@ imi_cuda_status imi_cuda_q4_matmul(int device, const uint8_t *q4, int rows, int 
     auto al = [](size_t x) { return (x + 255) / 256 * 256; };
     const size_t b_w = packed.size(), b_h = xh.size() * 2, b_x = xds.size() * 4, b_o = (size_t) ncol * rows * 4;
     uint8_t *m = nullptr;
-    CK(cudaMalloc(&m, al(b_w) + al(b_h) + al(b_x) + al(b_o) + 256));
+    const size_t b_t = (size_t) 7 * TC_TRACE * 8;
+    CK(cudaMalloc(&m, al(b_w) + al(b_h) + al(b_x) + al(b_o) + 256 + b_t));
     uint8_t *dW = m, *dh = m + al(b_w);
     float *dx = (float *) (dh + al(b_h)), *dout = (float *) ((uint8_t *) dx + al(b_x));
     int *derr = (int *) ((uint8_t *) dout + al(b_o));
+    unsigned long long *dtr = (unsigned long long *) ((uint8_t *) derr + 256);
     TcArgs a = {};
+    if (g_tc_trace_host) {
+        a.trace = dtr;
+        cudaMemset(dtr, 0, b_t);
+    }
     cudaError_t r = cudaMemcpy(dW, packed.data(), b_w, cudaMemcpyHostToDevice);
     if (r == cudaSuccess) r = cudaMemcpy(dh, xh.data(), b_h, cudaMemcpyHostToDevice);
     if (r == cudaSuccess) r = cudaMemcpy(dx, xds.data(), b_x, cudaMemcpyHostToDevice);
@@ -1356,12 +1570,22 @@ imi_cuda_status imi_cuda_q4_matmul(int device, const uint8_t *q4, int rows, int 
         r = launch_tc_table(a, std::min(sms, units), 0, false);
     }
     if (r == cudaSuccess) r = cudaMemcpy(out, dout, b_o, cudaMemcpyDeviceToHost);
+    if (r == cudaSuccess && g_tc_trace_host) r = cudaMemcpy(g_tc_trace_host, dtr, b_t, cudaMemcpyDeviceToHost);
     int herr = 0;
     if (r == cudaSuccess) r = cudaMemcpy(&herr, derr, 4, cudaMemcpyDeviceToHost);
     cudaFree(m);
     if (r != cudaSuccess) return fail(IMI_E_CUDA, std::string("q4_matmul: ") + cudaGetErrorString(r));
     if (herr) return fail(IMI_E_TIMEOUT, "q4_matmul: a device-side wait gave up");
     return IMI_OK;
+}
+
+imi_cuda_status imi_cuda_trace_tc(int device, const uint8_t *q4, int rows, int cols, const int8_t *xq, const float *xd,
+                                  const float *xs, int ncol, float *out, unsigned long long *trace) {
+    if (!trace) return fail(IMI_E_ARG, "trace is null");
+    g_tc_trace_host = trace;
+    const imi_cuda_status st = imi_cuda_q4_matmul(device, q4, rows, cols, xq, xd, xs, ncol, out);
+    g_tc_trace_host = nullptr;
+    return st;
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -1480,6 +1704,12 @@ void *imi_cuda_stream(const imi_cuda_engine *e) { return e ? (void *) e->stream 
 
 int imi_cuda_launches_per_step(const imi_cuda_engine *e, int n, int want_logits) {
     if (!e || n <= 0) return 0;
+    if (n > STEP_COLS && e->tc_batch) {   // the batched path: a preparation launch before every table read
+        const int groups = (n + e->ncmax - 1) / e->ncmax;
+        int per = 0;
+        for (auto &L : e->layers) per += L.conv ? 8 : 9;
+        return groups * (per + (want_logits ? 2 : 1));
+    }
     const int groups = (n + STEP_COLS - 1) / STEP_COLS;
     int per = 0;
     for (auto &L : e->layers) per += L.conv ? 4 : 5;
@@ -1489,11 +1719,19 @@ int imi_cuda_launches_per_step(const imi_cuda_engine *e, int n, int want_logits)
 
 int imi_cuda_launches_per_batch(const imi_cuda_engine *e, int n, int want_logits) {
     if (!e || n <= 0) return 0;
-    int per = 1;   // a read of up to STEP_COLS positions: its layers, then the final norm
-    for (auto &L : e->layers) per += L.conv ? 4 : 6;   // attention: K/V write, attention, and the tables around it
-    int reads = 0;
-    for (int g0 = 0; g0 < n; g0 += BATCH_GROUP) reads += (std::min(BATCH_GROUP, n - g0) + STEP_COLS - 1) / STEP_COLS;
-    return reads * per + (want_logits ? (e->tok_q6k ? 2 : 1) : 0);
+    int reads = 0, launches = 0;
+    for (int i0 = 0; i0 < n; i0 += e->ncmax) {
+        const int m = std::min(e->ncmax, n - i0);
+        int per = 1;   // one read of m positions: its layers, then the final norm
+        if (m > STEP_COLS)
+            for (auto &L : e->layers) per += L.conv ? 8 : 10;   // a preparation per table; K/V write and attention
+        else
+            for (auto &L : e->layers) per += L.conv ? 4 : 6;
+        launches += per;
+        reads++;
+    }
+    (void) reads;
+    return launches + (want_logits ? (e->tok_q6k ? 2 : 1) : 0);
 }
 
 imi_cuda_status imi_cuda_bench_tables(imi_cuda_engine *e, int ncol, int reps, float *ms, size_t *bytes) {

@@ -3,9 +3,11 @@
 // k_table (table.cuh): the 4-bit table reads with the small math of imi's step folded in.
 // k_attn: decode attention for one (query head, column): q/k RMSNorm, NEOX rotation, fp16 K/V write, scores,
 //   softmax, P.V and the sigmoid gate, in the float order of seoul.cpp:425-453.
+#define IMI_KERNELS 1
 #include "common.cuh"
 #include "table.cuh"
 #include "tc_table.cuh"
+#include "tc_prep.cuh"
 
 namespace imi {
 
@@ -383,6 +385,12 @@ __global__ void k_wait_check(long long limit, int *err) {
     }
     __syncthreads();
     if (!mbar_wait(&bar, 0, limit) && threadIdx.x == 0) atomicExch(err, 7);
+}
+
+// the conversation records of a step's columns into 32-byte slots (one read-back for all of them)
+__global__ void k_gather_sess(const Col *cols, int n, uint8_t *dst) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c < n) *(SessDev *) (dst + 32 * c) = *cols[c].s;
 }
 
 // ---------------------------------------------------------------------------------------------------------------

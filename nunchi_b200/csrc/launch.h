@@ -1,6 +1,7 @@
 // Host entry points of the kernels (kernels.cu).
 #pragma once
 #include "common.cuh"
+#include "tc_prep.cuh"
 #include "tc_table.cuh"
 
 namespace imi {
@@ -24,6 +25,10 @@ cudaError_t launch_q6k_head(const Q6HeadArgs &a, cudaStream_t st, bool pdl);
 int q6k_head_ctas(int rows, int nb, int nc);   // its grid (0: rows too wide)
 // the tensor-core batched table read (tc_table.cuh); a.G in {16, 32, 64}
 cudaError_t launch_tc_table(const TcArgs &a, int grid, cudaStream_t st, bool pdl);
+// the conversation records of a step's n columns into 32-byte slots of dst (device)
+cudaError_t launch_gather_sess(const Col *cols, int n, uint8_t *dst, cudaStream_t st);
+// the batched read's input preparation: one CTA per column
+cudaError_t launch_tc_prep(const TcPrepArgs &a, cudaStream_t st, bool pdl);
 // one CTA waiting on an mbarrier nothing completes, for at most `limit` clock cycles (the bounded waits' failure path)
 cudaError_t launch_wait_check(long long limit, int *err, cudaStream_t st);
 // GGUF Q4_0 rows (device) into the table kernel's row layout (device), on stream st

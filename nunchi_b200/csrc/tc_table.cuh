@@ -11,19 +11,20 @@
 //     acc = fma(dot_j, d_rj * dx_cj, acc),  cor = fma(d_rj, s_cj, cor),  out = acc - 8 cor (one rounding).
 //
 // Work unit: a tile of 128 rows x a group of G columns (G = 16, 32 or 64). K is read in stages of 128 values (4
-// blocks). Warp roles (448 threads, one CTA per SM, persistent over units):
+// blocks). Warp roles (one CTA per SM, persistent over units):
 //   warp 0      producer: per stage one barrier for four copies into a ring slot: TMA of the tile's 4-bit codes
 //               (128 rows x 80 bytes, 64 used: a padded shared-memory row stride keeps the unpack's reads free of
 //               bank conflicts) and fp16 scales, bulk copies of the columns' fp16 codes (already in the MMA's K-major
 //               layout, read by the MMA where they land) and of their scales and sums; it waits only for the slot, so
 //               weight bytes stream several stages ahead of the math;
 //   warp 1      TMEM owner (512 columns) and MMA issuer: per block two tcgen05.mma kind::f16 (K = 16 each) into the
-//               block's own TMEM slot, committed to the slot's barrier;
+//               block's own TMEM columns; the 4 blocks of a stage fill one TMEM stage slot, committed to its barrier
+//               once (a commit-to-wait hand-off costs about 0.3 us, so it is made per stage, not per block);
 //   warps 2-5   unpack: 4-bit codes -> fp16 in the MMA's canonical K-major layout (8-row x 16-byte core matrices),
 //               the rows' block scales and the columns' scales and sums handed to the epilogue;
-//   warps 6-13  epilogue: per TMEM slot a tcgen05.ld of the block's dots (warp w reads lanes 32 (w % 4) ..), the two
-//               fma chains for G/2 columns per thread (packed f32x2 operations, each lane rounded as imi's scalar
-//               chain), the result stored at the end of the unit.
+//   warps 6..   epilogue, 4 per 16 columns: per TMEM slot a tcgen05.ld of the block's dots (warp w reads lanes
+//               32 (w % 4) ..), the two fma chains for 16 columns per thread (packed f32x2 operations, each lane rounded
+//               as imi's scalar chain), the result stored at the end of the unit.
 // Every wait on an mbarrier is bounded (about one second); a wait that gives up sets the error flag, the CTA stops
 // issuing work, waits (bounded) for its copies and MMAs in flight, frees its TMEM and returns.
 #pragma once
@@ -38,11 +39,17 @@ constexpr int TC_KS = 128;             // values per K stage
 constexpr int TC_BPS = TC_KS / 32;     // blocks per stage
 constexpr int TC_RAW_W = 80;           // bytes per row of a raw code stage in shared memory (64 used)
 constexpr int TC_NR = 4, TC_NA = 2, TC_NE = 4;   // rings: copied stages, unpacked weight stages, epilogue stages
-constexpr int TC_THREADS = 448;
 constexpr int TC_WARP_PROD = 0, TC_WARP_MMA = 1, TC_WARP_UNP = 2, TC_WARP_EPI = 6;
+constexpr int TC_CH = 16;   // columns per epilogue thread
+// epilogue warps: 4 per 16 columns (one per TMEM lane quarter), so each thread runs 16 columns' chains
+__host__ __device__ constexpr int tc_epi_warps(int G) { return 4 * (G / TC_CH); }
+__host__ __device__ constexpr int tc_threads(int G) { return 32 * (TC_WARP_EPI + tc_epi_warps(G)); }
 constexpr int TC_TMEM_COLS = 512;
 
-enum TcEpi : int { TE_STORE = 0 };
+// output stage: TE_STORE out[c][row]; TE_SILU rows (2i, 2i+1) are (gate_i, up_i) of an interleaved gate/up table:
+// out[c][i] = silu(gate) * up (seoul.cpp:384-391); TE_HEAD word scores into each column's logits (when it has them)
+// and imi's greedy pick (first maximum, lowest id on ties), ending the step as the small-batch word-table read does
+enum TcEpi : int { TE_STORE = 0, TE_SILU = 1, TE_HEAD = 2 };
 
 struct TcArgs {
     CUtensorMap tm_codes;     // the table's rows as bytes [rows][row_bytes], box {TC_RAW_W, 128}
@@ -54,12 +61,16 @@ struct TcArgs {
     float *out;               // out[c * out_stride + row]
     int out_stride;
     int epi;
+    const Col *cols_d;        // TE_HEAD: the columns (logits, conversation records)
+    unsigned *done;           // TE_HEAD: CTAs finished (the last one picks and resets it)
     int *err;
+    unsigned long long *trace;   // optional (diagnostics): CTA 0's timeline, [7][64] ns (see k_tc_table)
 };
+constexpr int TC_TRACE = 64;
 
 struct TcPlan {
     int raw, a, epi, bar, tptr, total;
-    int raw_bytes, raw_stride, b_off, x_off, a_bytes, b_bytes, xds_bytes, epi_bytes, nslot;
+    int raw_bytes, raw_stride, b_off, x_off, a_bytes, b_bytes, xds_bytes, epi_bytes, nslot;   // nslot: TMEM stage slots
 };
 // a copied stage: [codes 128 x TC_RAW_W | scales 128 x 16 | columns' fp16 codes | columns' scales and sums]
 __host__ __device__ inline TcPlan tc_plan(int G) {
@@ -72,7 +83,7 @@ __host__ __device__ inline TcPlan tc_plan(int G) {
     p.raw_stride = align_up(p.raw_bytes, 128);
     p.a_bytes = (TC_KS / 8) * TC_M * 16;                  // fp16 codes of 128 rows, 16 chunks of 8 values
     p.epi_bytes = align_up(p.xds_bytes + TC_M * 8, 128);  // the columns' scales and sums + the rows' 4 block scales
-    p.nslot = TC_TMEM_COLS / G;
+    p.nslot = TC_TMEM_COLS / (G * TC_BPS);               // TMEM stage slots: a stage's 4 blocks, G columns each
     int o = 0;
     p.raw = o;  o += TC_NR * p.raw_stride;
     p.a = o;    o += TC_NA * p.a_bytes;
@@ -83,7 +94,7 @@ __host__ __device__ inline TcPlan tc_plan(int G) {
     return p;
 }
 
-#ifdef __CUDACC__
+#if defined(__CUDACC__) && defined(IMI_KERNELS)   // device code: compiled in kernels.cu only
 // ---- tcgen05 / TMA wrappers ----
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, int x, int y, uint64_t *bar) {
     asm volatile(
@@ -148,41 +159,45 @@ __device__ __forceinline__ void tmem_ld<32>(uint32_t t, uint32_t (&v)[32]) {
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// 8 values (low or high nibbles of 8 code bytes w0, w1) as fp16: (0x6400 | v) is 1024 + v in fp16; minus 1024 exactly
-__device__ __forceinline__ uint32_t nib2h(uint32_t t, int hi) {
-    const uint32_t m = ((hi ? t >> 4 : t) & 0x000F000Fu) | 0x64006400u;
+// 8 values (the low or the high nibbles of the 8 code bytes w0, w1) as fp16: every nibble spread into a 16-bit lane
+// under the byte 0x64, i.e. 0x6400 | v = 1024 + v in fp16, then minus 1024 (exact)
+__device__ __forceinline__ uint32_t h2sub1024(uint32_t m) {
     const __half2 r = __hsub2(*reinterpret_cast<const __half2 *>(&m), __half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400)));
     return *reinterpret_cast<const uint32_t *>(&r);
 }
 __device__ __forceinline__ uint4 nib8(uint32_t w0, uint32_t w1, int hi) {
-    return make_uint4(nib2h(__byte_perm(w0, 0, 0x4140), hi), nib2h(__byte_perm(w0, 0, 0x4342), hi),
-                      nib2h(__byte_perm(w1, 0, 0x4140), hi), nib2h(__byte_perm(w1, 0, 0x4342), hi));
+    const uint32_t n0 = (hi ? w0 >> 4 : w0) & 0x0F0F0F0Fu, n1 = (hi ? w1 >> 4 : w1) & 0x0F0F0F0Fu;
+    return make_uint4(h2sub1024(__byte_perm(n0, 0x64646464u, 0x7170)), h2sub1024(__byte_perm(n0, 0x64646464u, 0x7372)),
+                      h2sub1024(__byte_perm(n1, 0x64646464u, 0x7170)), h2sub1024(__byte_perm(n1, 0x64646464u, 0x7372)));
 }
 
 template <int G>
-__global__ void __launch_bounds__(TC_THREADS, 1) k_tc_table(const __grid_constant__ TcArgs a) {
+__global__ void __launch_bounds__(tc_threads(G), 1) k_tc_table(const __grid_constant__ TcArgs a) {
     extern __shared__ __align__(128) uint8_t smt[];
-    constexpr int CH = G / 2;                              // columns per epilogue thread
+    constexpr int CH = TC_CH, NEW = tc_epi_warps(G);
     const TcPlan P = tc_plan(G);
     uint8_t *sm = smt + ((128 - (smem_u32(smt) & 127)) & 127);
     uint64_t *bars = (uint64_t *) (sm + P.bar);
     // raw_full: the four copies of a stage landed (1 arrival + bytes); raw_empty: unpacked (4 warps) and read by the
     // MMAs (1 commit); a_full / e_full: the 4 unpack warps; a_empty, tm_full, fin: tcgen05.commit; e_empty, tm_empty:
-    // the 8 epilogue warps
+    // the epilogue warps
     uint64_t *raw_full = bars, *raw_empty = raw_full + TC_NR, *a_full = raw_empty + TC_NR, *a_empty = a_full + TC_NA,
              *e_full = a_empty + TC_NA, *e_empty = e_full + TC_NE, *tm_full = e_empty + TC_NE, *tm_empty = tm_full + 32,
              *fin = tm_empty + 32;
     uint32_t *tptr = (uint32_t *) (sm + P.tptr);
-    __shared__ int abort_flag;
+    __shared__ int abort_flag, last_cta;
+    __shared__ unsigned long long best[256];   // TE_HEAD: this CTA's best key per column
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (a.epi == TE_HEAD)
+        for (int k = tid; k < 256; k += blockDim.x) best[k] = 0ull;
     const int K = a.cols, nst = K / TC_KS, tiles = (a.rows + TC_M - 1) / TC_M, units = tiles * a.groups;
     const int nslot = P.nslot;
 
     if (tid == 0) {
         for (int i = 0; i < TC_NR; i++) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 5); }
         for (int i = 0; i < TC_NA; i++) { mbar_init(&a_full[i], 4); mbar_init(&a_empty[i], 1); }
-        for (int i = 0; i < TC_NE; i++) { mbar_init(&e_full[i], 4); mbar_init(&e_empty[i], 8); }
-        for (int i = 0; i < nslot; i++) { mbar_init(&tm_full[i], 1); mbar_init(&tm_empty[i], 8); }
+        for (int i = 0; i < TC_NE; i++) { mbar_init(&e_full[i], 4); mbar_init(&e_empty[i], NEW); }
+        for (int i = 0; i < nslot; i++) { mbar_init(&tm_full[i], 1); mbar_init(&tm_empty[i], NEW); }
         mbar_init(fin, 1);
         abort_flag = 0;
         fence_barrier_init();
@@ -229,6 +244,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_table(const __grid_constan
                     tma_load_2d(raw + TC_M * TC_RAW_W, &a.tm_scales, K / 2 + 16 * (s / 2), tile * TC_M, &raw_full[r]);
                     bulk_g2s(raw + P.b_off, xh + (size_t) s * (TC_KS / 8) * G * 16, (uint32_t) P.b_bytes, &raw_full[r]);
                     bulk_g2s(raw + P.x_off, xds + (size_t) s * TC_BPS * 2 * G, (uint32_t) P.xds_bytes, &raw_full[r]);
+                    if (a.trace && blockIdx.x == 0 && i < TC_TRACE) a.trace[0 * TC_TRACE + i] = global_ns();
                 }
             }
             if (!ok)   // the copies in flight land before the CTA exits (bounded waits on the last stages issued)
@@ -246,22 +262,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_table(const __grid_constan
                     if (!(ok = wait(&a_full[o], (i / TC_NA) & 1) && wait(&raw_full[r], (i / TC_NR) & 1))) break;
                     tc_fence_after();
                     const uint32_t abase = smem_u32(sm + P.a + o * P.a_bytes), bbase = smem_u32(raw_at(r) + P.b_off);
+                    const int slot = i % nslot;
+                    if (!(ok = wait(&tm_empty[slot], ((i / nslot) & 1) ^ 1))) break;
+                    tc_fence_after();
                     for (int jj = 0; jj < TC_BPS; jj++, b++) {
-                        const int slot = b % nslot;
-                        if (!(ok = wait(&tm_empty[slot], ((b / nslot) & 1) ^ 1))) break;
-                        tc_fence_after();
 #pragma unroll
                         for (int h = 0; h < 2; h++) {   // K = 16 per MMA: chunks 4jj + 2h, 4jj + 2h + 1
                             const int q = 4 * jj + 2 * h;
-                            tc_mma_f16(tmem + slot * G, tc_desc(abase + q * TC_M * 16, TC_M * 16, 128),
+                            tc_mma_f16(tmem + (slot * TC_BPS + jj) * G, tc_desc(abase + q * TC_M * 16, TC_M * 16, 128),
                                        tc_desc(bbase + q * G * 16, G * 16, 128), idesc, h);
                         }
-                        tc_commit(&tm_full[slot]);
+                        if (a.trace && blockIdx.x == 0 && b < TC_TRACE) a.trace[3 * TC_TRACE + b] = global_ns();
                     }
-                    if (ok) {
-                        tc_commit(&a_empty[o]);
-                        tc_commit(&raw_empty[r]);
-                    }
+                    tc_commit(&tm_full[slot]);
+                    tc_commit(&a_empty[o]);
+                    tc_commit(&raw_empty[r]);
                 }
             }
             if (!ok) {   // the MMAs issued complete before TMEM is freed
@@ -280,6 +295,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_table(const __grid_constan
                 if (!(ok = wait(&raw_full[r], (i / TC_NR) & 1) && wait(&a_empty[o], ((i / TC_NA) & 1) ^ 1) &&
                            wait(&e_empty[e], ((i / TC_NE) & 1) ^ 1)))
                     break;
+                if (a.trace && blockIdx.x == 0 && row == 0 && i < TC_TRACE) a.trace[1 * TC_TRACE + i] = global_ns();
                 const uint8_t *raw = raw_at(r);
                 uint8_t *A = sm + P.a + o * P.a_bytes, *ep = sm + P.epi + e * P.epi_bytes;
 #pragma unroll
@@ -300,6 +316,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_table(const __grid_constan
                     mbar_arrive(&raw_empty[r]);
                     mbar_arrive(&e_full[e]);
                 }
+                if (a.trace && blockIdx.x == 0 && row == 0 && i < TC_TRACE) a.trace[2 * TC_TRACE + i] = global_ns();
             }
         }
     } else {
@@ -314,42 +331,69 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_table(const __grid_constan
 #pragma unroll
             for (int k = 0; k < CH / 2; k++) acc[k] = cor[k] = make_float2(0.0f, 0.0f);
             for (int s = 0; s < nst && ok; s++, i++) {
-                const int e = i % TC_NE;
-                if (!(ok = wait(&e_full[e], (i / TC_NE) & 1))) break;
+                const int e = i % TC_NE, slot = i % nslot;
+                if (!(ok = wait(&e_full[e], (i / TC_NE) & 1) && wait(&tm_full[slot], (i / nslot) & 1))) break;
+                tc_fence_after();
                 const uint8_t *ep = sm + P.epi + e * P.epi_bytes;
                 const uint16_t *dsc = (const uint16_t *) (ep + P.xds_bytes + row * 8);
                 for (int jj = 0; jj < TC_BPS; jj++, b++) {
-                    const int slot = b % nslot;
-                    if (!(ok = wait(&tm_full[slot], (b / nslot) & 1))) break;
-                    tc_fence_after();
+                    const bool tr = a.trace && blockIdx.x == 0 && warp == TC_WARP_EPI && lane == 0 && b < TC_TRACE;
+                    if (tr) a.trace[4 * TC_TRACE + b] = global_ns();
                     uint32_t f[CH];
-                    tmem_ld<CH>(tl + slot * G, f);
+                    tmem_ld<CH>(tl + (slot * TC_BPS + jj) * G, f);
                     tmem_ld_wait();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&tm_empty[slot]);
+                    if (tr) a.trace[6 * TC_TRACE + b] = global_ns() + (unsigned long long) (f[0] & 0);
                     const float d = h2f(dsc[jj]);
                     const float2 dd = make_float2(d, d);
-                    const float *xd = (const float *) ep + jj * 2 * G + h * CH, *xs = xd + G;
+                    const float4 *xd = (const float4 *) ((const float *) ep + jj * 2 * G + h * CH),
+                                 *xs = (const float4 *) ((const float *) ep + jj * 2 * G + G + h * CH);
 #pragma unroll
-                    for (int k = 0; k < CH / 2; k++) {
-                        const float2 dx = *(const float2 *) (xd + 2 * k), sx = *(const float2 *) (xs + 2 * k);
-                        const float2 fv = make_float2(__uint_as_float(f[2 * k]), __uint_as_float(f[2 * k + 1]));
-                        acc[k] = __ffma2_rn(fv, __fmul2_rn(dd, dx), acc[k]);
-                        cor[k] = __ffma2_rn(dd, sx, cor[k]);
+                    for (int k = 0; k < CH / 4; k++) {   // 4 columns per pair of 16-byte loads
+                        const float4 dx = xd[k], sx = xs[k];
+                        const float2 f0 = make_float2(__uint_as_float(f[4 * k]), __uint_as_float(f[4 * k + 1])),
+                                     f1 = make_float2(__uint_as_float(f[4 * k + 2]), __uint_as_float(f[4 * k + 3]));
+                        acc[2 * k] = __ffma2_rn(f0, __fmul2_rn(dd, make_float2(dx.x, dx.y)), acc[2 * k]);
+                        acc[2 * k + 1] = __ffma2_rn(f1, __fmul2_rn(dd, make_float2(dx.z, dx.w)), acc[2 * k + 1]);
+                        cor[2 * k] = __ffma2_rn(dd, make_float2(sx.x, sx.y), cor[2 * k]);
+                        cor[2 * k + 1] = __ffma2_rn(dd, make_float2(sx.z, sx.w), cor[2 * k + 1]);
                     }
+                    if (tr) a.trace[5 * TC_TRACE + b] = global_ns() + (unsigned long long) (__float_as_uint(acc[0].x) & 0);
                 }
+                tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&e_empty[e]);
+                if (lane == 0) {
+                    mbar_arrive(&tm_empty[slot]);
+                    mbar_arrive(&e_empty[e]);
+                }
             }
             if (!ok) break;
             const int grow = tile * TC_M + row;
-            if (grow < a.rows) {
+            const bool live = grow < a.rows;
 #pragma unroll
-                for (int k = 0; k < CH / 2; k++) {
-                    const int c0 = g * G + h * CH + 2 * k;
-                    if (c0 < a.ncol) a.out[(size_t) c0 * a.out_stride + grow] = __fmaf_rn(-8.0f, cor[k].x, acc[k].x);
-                    if (c0 + 1 < a.ncol) a.out[(size_t) (c0 + 1) * a.out_stride + grow] = __fmaf_rn(-8.0f, cor[k].y, acc[k].y);
+            for (int k = 0; k < CH; k++) {
+                const int cc = g * G + h * CH + k;
+                const float v = (k & 1) ? __fmaf_rn(-8.0f, cor[k / 2].y, acc[k / 2].y) : __fmaf_rn(-8.0f, cor[k / 2].x, acc[k / 2].x);
+                if (a.epi == TE_STORE) {
+                    if (live && cc < a.ncol) a.out[(size_t) cc * a.out_stride + grow] = v;
+                } else if (a.epi == TE_SILU) {   // the up row is the next lane's
+                    const float up = __shfl_down_sync(0xffffffffu, v, 1);
+                    if (live && (grow & 1) == 0 && cc < a.ncol) {
+                        const float sl = __fdiv_rn(v, __fadd_rn(1.0f, exp_cr(-v)));
+                        a.out[(size_t) cc * a.out_stride + grow / 2] = __fmul_rn(sl, up);
+                    }
+                } else {   // TE_HEAD: word scores, and the running first maximum per column
+                    unsigned long long key = 0ull;
+                    if (live && cc < a.ncol) {
+                        float *lg = a.cols_d[cc].logits;
+                        if (lg) lg[grow] = v;
+                        key = amax_key(v, grow);
+                    }
+#pragma unroll
+                    for (int o = 16; o; o >>= 1) {
+                        const unsigned long long u2 = __shfl_xor_sync(0xffffffffu, key, o);
+                        key = u2 > key ? u2 : key;
+                    }
+                    if (lane == 0 && cc < a.ncol && key) atomicMax(&best[cc], key);
                 }
             }
         }
@@ -359,6 +403,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_table(const __grid_constan
     if (warp == TC_WARP_MMA) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS) : "memory");
+    }
+    if (a.epi == TE_HEAD) {   // the step ends here: pick, position, counters (one CTA, the last to finish)
+        if (tid < a.ncol && best[tid] && abort_flag == 0) atomicMax(&a.cols_d[tid].s->amax, best[tid]);
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) last_cta = atomicAdd(a.done, 1u) == gridDim.x - 1;
+        __syncthreads();
+        if (last_cta && tid < a.ncol) {
+            __threadfence();
+            const Col col = a.cols_d[tid];
+            const unsigned long long k = atomicExch(&col.s->amax, 0ull);
+            const int id = (int) (0xffffffffu - (uint32_t) (k & 0xffffffffu));
+            col.s->next_token = id;
+            col.s->amax_val = amax_val(k);
+            if (col.picks) col.picks[col.s->pos + col.off] = id;
+            if (col.pos_inc) atomicAdd(&col.s->pos, col.pos_inc);
+        }
+        if (last_cta && tid == 0) *a.done = 0;
     }
 }
 #endif
