@@ -339,12 +339,13 @@ def run_prefill(args, ranks: Ranks, steps: int) -> dict:
     ms, ms_wall = ranks.max(e0.elapsed_time(e1)), ranks.max(wall * 1e3)
     assert len(set(picks)) == 1, "prefills of the same inputs gave different picks"
     n_pos = PREFILL_VECS + PREFILL_IDS
-    out = {"ms": ms, "value": ranks.world * n_pos * steps / (ms / 1e3), "clocks": clk, "info": info, "ncol": 8}
+    out = {"ms": ms, "value": ranks.world * n_pos * steps / (ms / 1e3), "clocks": clk, "info": info,
+           "ncol": min(PREFILL_CHUNK, info.cols_per_read)}
     out["launches"] = eng.prefill_launches(PREFILL_VECS, PREFILL_CHUNK, PREFILL_IDS) * steps
     out["e2e"] = {"value": ranks.world * n_pos * steps / (ms_wall / 1e3), "unit": "positions/s",
                   "h2d_bytes_per_step": int(vecs.nbytes + ids.nbytes), "d2h_bytes_per_step": 8,
                   "ms_per_step": ms_wall / steps, "clock": "host wall clock around the same calls"}
-    t_ms, t_bytes = eng.bench_tables(ncol=8, reps=20)
+    t_ms, t_bytes = eng.bench_tables(ncol=out["ncol"], reps=20)
     out["tables"] = {"ms": t_ms, "bytes": t_bytes}
     # algorithmic: every weight once per step_batch call (the configuration's chunks), K/V of the positions written
     # once and read by the later ones; the word table once (the last position's scores)
@@ -395,8 +396,9 @@ def run_multi(args, ranks: Ranks, steps: int, e2e: bool = True) -> dict:
     clk = clocks.stop()
     ranks.barrier()
     ms = ranks.max(e0.elapsed_time(e1))
+    per_read = min(MULTI_N, info.cols_per_read)
     out = {"ms": ms, "value": ranks.world * MULTI_N * steps / (ms / 1e3), "clocks": clk, "info": info,
-           "ncol": 8, "prefill_s": prefill_s, "reads_per_step": -(-MULTI_N // 8)}
+           "ncol": per_read, "prefill_s": prefill_s, "reads_per_step": -(-MULTI_N // per_read)}
     mid = [p + steps // 2 for p in pos0]
     out["step_bytes"] = step_bytes(info, mid)   # every weight once per step of all 64, plus each one's K/V
     out["launches"] = eng.launches_per_step(MULTI_N, 1) * steps
@@ -414,7 +416,7 @@ def run_multi(args, ranks: Ranks, steps: int, e2e: bool = True) -> dict:
         out["e2e"] = {"value": ranks.world * MULTI_N * steps / (ms_e2e / 1e3), "unit": "tok/s",
                       "h2d_bytes_per_step": 80 * MULTI_N, "d2h_bytes_per_step": 28 * MULTI_N,
                       "ms_per_step": ms_e2e / steps}
-    t_ms, t_bytes = eng.bench_tables(ncol=8, reps=20)
+    t_ms, t_bytes = eng.bench_tables(ncol=per_read, reps=20)
     out["tables"] = {"ms": t_ms, "bytes": t_bytes}
     for s in states:
         s.close()

@@ -37,6 +37,9 @@ typedef struct {
     int n_embd, n_vocab, n_ctx, n_layer, n_attn, n_head, n_head_kv, head_dim, n_ff, d_conv, n_swa, max_batch;
     size_t weight_bytes;   /* bytes of layer tables + word table + small parameters on the device */
     size_t state_bytes;    /* device bytes of one conversation state */
+    int cols_per_read;     /* conversations (or prefill positions) one read of the tables serves at most: 8 on the
+                              small-batch kernel; up to 256 (max(max_batch, 128)) on the tensor cores, which every
+                              Q4_0 model uses above 8 */
 } imi_cuda_info;
 
 /* Last error message of this thread (never NULL). */
@@ -112,7 +115,7 @@ void *imi_cuda_stream(const imi_cuda_engine *e);
 int imi_cuda_launches_per_step(const imi_cuda_engine *e, int n, int want_logits);
 /* Kernel launches of one imi_cuda_step_batch of n positions (with or without the last position's word scores). */
 int imi_cuda_launches_per_batch(const imi_cuda_engine *e, int n, int want_logits);
-/* Every layer table read back to back with ncol (1..8) inputs riding each read, as imi_seoul::bench_tables
+/* Every layer table read back to back with ncol (1..cols_per_read) inputs riding each read, as imi_seoul::bench_tables
  * (seoul.cpp:657-685): *ms = mean milliseconds per pass over `reps` passes (after one untimed pass), *bytes = table
  * bytes read per pass. */
 imi_cuda_status imi_cuda_bench_tables(imi_cuda_engine *e, int ncol, int reps, float *ms, size_t *bytes);

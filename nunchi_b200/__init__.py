@@ -32,7 +32,7 @@ class ContextFull(ImiError):
 class Info(C.Structure):
     _fields_ = [(n, C.c_int) for n in ("n_embd", "n_vocab", "n_ctx", "n_layer", "n_attn", "n_head", "n_head_kv",
                                         "head_dim", "n_ff", "d_conv", "n_swa", "max_batch")] + \
-               [("weight_bytes", C.c_size_t), ("state_bytes", C.c_size_t)]
+               [("weight_bytes", C.c_size_t), ("state_bytes", C.c_size_t), ("cols_per_read", C.c_int)]
 
 
 _L = None

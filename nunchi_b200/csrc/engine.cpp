@@ -1033,6 +1033,7 @@ imi_cuda_status imi_cuda_get_info(const imi_cuda_engine *e, imi_cuda_info *o) {
     o->d_conv = e->d_conv; o->n_swa = e->n_swa; o->max_batch = e->max_batch;
     o->weight_bytes = e->w_bytes;
     o->state_bytes = e->state_bytes;
+    o->cols_per_read = e->ncmax;
     return IMI_OK;
 }
 
@@ -1735,7 +1736,7 @@ int imi_cuda_launches_per_batch(const imi_cuda_engine *e, int n, int want_logits
 }
 
 imi_cuda_status imi_cuda_bench_tables(imi_cuda_engine *e, int ncol, int reps, float *ms, size_t *bytes) {
-    if (!e || ncol < 1 || ncol > STEP_COLS || reps < 1 || !ms) return fail(IMI_E_ARG, "bad bench_tables arguments");
+    if (!e || ncol < 1 || ncol > e->ncmax || reps < 1 || !ms) return fail(IMI_E_ARG, "bad bench_tables arguments");
     CK(cudaSetDevice(e->device));
     std::vector<const TableRef *> ws;
     for (auto &L : e->layers)
@@ -1748,6 +1749,11 @@ imi_cuda_status imi_cuda_bench_tables(imi_cuda_engine *e, int ncol, int reps, fl
     CK(cudaMemsetAsync(e->X, 0, (size_t) (2 * e->n_embd + e->big_n + e->n_embd + e->n_head * e->head_dim + e->n_ff) * 4 * STEP_COLS, e->stream));
     auto pass = [&]() -> cudaError_t {
         for (auto *t : ws) {
+            if (ncol > STEP_COLS) {   // the tensor-core batched read (operands as left in its buffers; outputs to X)
+                const cudaError_t r = tc_read(e, *t, ncol, TE_STORE, e->X, t->rows);
+                if (r != cudaSuccess) return r;
+                continue;
+            }
             MvArgs a = {};
             a.cols_d = e->cols_d; a.ncol = ncol; a.eps = e->eps; a.n_embd = e->n_embd; a.ring_layer = -1;
             a.err = e->err; a.q8_q = e->qa_q; a.q8_d = e->qa_d; a.q8_s = e->qa_s; a.out = e->big; a.out_stride = 0;

@@ -197,8 +197,10 @@ __global__ void __launch_bounds__(TP_THREADS) k_tc_prep(const __grid_constant__ 
         tp_cut(a, c, q, h, act);
     }
     // conv memory of a prefill chunk: the slot of the column's position takes b*x (seoul.cpp:419-423), written one
-    // launch after the conv read it (no column of the chunk reads a slot this launch writes)
-    if (a.ring_layer >= 0) {
+    // launch after the conv read it (no column of the chunk reads a slot this launch writes). The columns are
+    // consecutive positions of one conversation and columns c and c + d_conv + 1 share a slot: only the last
+    // d_conv + 1 columns write, so the memory ends holding the chunk's last positions whatever order the CTAs run in
+    if (a.ring_layer >= 0 && c + a.d_conv + 1 >= a.ncol) {
         const int R = a.d_conv + 1, p = col.s->pos + col.off;
         const float4 *bcx = (const float4 *) (a.ring_src + (size_t) c * a.ring_src_stride);
         float4 *slot = (float4 *) (col.ring + ((size_t) a.ring_layer * R + p % R) * E);
