@@ -107,10 +107,35 @@ imi_cuda_status imi_cuda_get_logits(const imi_cuda_state *s, float *out /* n_voc
 /* The greedy pick of the latest step with logits: first maximum, lowest id on ties (imi/core/hear.cpp:67-68). */
 imi_cuda_status imi_cuda_get_argmax(const imi_cuda_state *s, int32_t *id, float *value);
 
+/* ---- the model file's keys and tensor headers (host only; imi_file, imi/model.h:17-36) ----
+ * The GGUF file memory-mapped by the library's own reader, for callers that read keys beside the brain (the
+ * tokenizer reads the word list from the same file: imi_words::load(brain.f), flow.cpp:49). Value types are GGUF's
+ * (4 u32, 5 i32, 6 f32, 7 bool, 8 string, 9 array, 10 u64, ...). Pointers stay valid until imi_cuda_file_close. */
+typedef struct imi_cuda_file imi_cuda_file;
+imi_cuda_status imi_cuda_file_open(const char *path, imi_cuda_file **out);
+void imi_cuda_file_close(imi_cuda_file *f);
+int64_t imi_cuda_file_find_key(const imi_cuda_file *f, const char *key);              /* -1 when absent */
+int64_t imi_cuda_file_n_keys(const imi_cuda_file *f);
+const char *imi_cuda_file_key_name(const imi_cuda_file *f, int64_t k);
+int imi_cuda_file_key_type(const imi_cuda_file *f, int64_t k);
+const void *imi_cuda_file_key_data(const imi_cuda_file *f, int64_t k);                  /* a scalar's bytes */
+const char *imi_cuda_file_key_str(const imi_cuda_file *f, int64_t k);                   /* a string (copy, 0-ended) */
+int imi_cuda_file_arr_type(const imi_cuda_file *f, int64_t k);
+uint64_t imi_cuda_file_arr_n(const imi_cuda_file *f, int64_t k);
+const void *imi_cuda_file_arr_data(const imi_cuda_file *f, int64_t k);                  /* fixed-size elements */
+const char *imi_cuda_file_arr_str(const imi_cuda_file *f, int64_t k, uint64_t i);       /* string element i */
+/* a tensor's header: 0 and its GGML type, shape (fastest first), bytes in the map; -1 when absent */
+int imi_cuda_file_tensor(const imi_cuda_file *f, const char *name, int *type, int64_t ne[4], const void **data,
+                         size_t *nbytes);
+
 /* ---- measurement ---- */
 
 /* The CUDA stream (cudaStream_t) every launch of this engine goes to, for callers that time on the device. */
 void *imi_cuda_stream(const imi_cuda_engine *e);
+/* Milliseconds on the device of the engine's last step (the last read of its tables with everything around it:
+ * every launch of one imi_cuda_step / step2 / step_multi group / step_batch chunk), waiting for it to finish; 0 if
+ * none ran. The C++ wrapper adds it to imi_seoul::t_tables after each step. */
+float imi_cuda_last_step_ms(const imi_cuda_engine *e);
 /* Kernel launches of one step of n conversations (with or without word scores). */
 int imi_cuda_launches_per_step(const imi_cuda_engine *e, int n, int want_logits);
 /* Kernel launches of one imi_cuda_step_batch of n positions (with or without the last position's word scores). */

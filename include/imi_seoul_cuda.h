@@ -6,9 +6,13 @@
 // message on stderr; a step past n_ctx prints "context full" and does nothing, seoul.cpp:209,353,498).
 // Differences, all deliberate: the thread count and shared team arguments are accepted and ignored (the GPU needs
 // no thread team); the device is chosen by IMI_CUDA_DEVICE (default 0); hidden / logits are copied back after each
-// step (logits only when asked for), so they stay valid until the next step as in imi.
+// step (logits only when asked for), so they stay valid until the next step as in imi. The model file `f` is the
+// library's own GGUF reader (imi_file_cuda.h: the same calls as imi/model.h). The research timers (seoul.h:54): a step
+// is one CUDA graph on the device, so t_tables receives each step's whole device time in ms (table reads, attention and
+// the small math together) and t_sync, t_attn stay 0 (no barrier waits; attention is not timed apart).
 #pragma once
 #include "imi_cuda.h"
+#include "imi_file_cuda.h"
 
 #include <cstdio>
 #include <cstdlib>
@@ -35,15 +39,22 @@ struct imi_seoul_state {
 };
 
 struct imi_seoul {
+    imi_file f;
     int n_embd = 0, n_vocab = 0, n_head = 0, n_head_kv = 0, head_dim = 0, n_ff = 0, d_conv = 0, n_swa = 0, n_ctx = 0;
+    float eps = 1e-5f, rope_base = 1e6f, rope_base_swa = 1e4f;
     int pos = 0, n_threads = 1;
     std::vector<float> hidden, logits;
+    double t_tables = 0, t_sync = 0, t_attn = 0;   // ms (see above)
     imi_cuda_engine *engine = nullptr;
 
     // seoul.cpp:93 load(path, threads, ctx_len, shared team): the last two steps of state fit on the device
     bool load(const std::string &path, int threads, int ctx_len, void *shared = nullptr) {
         (void) shared;
         n_threads = threads;
+        if (!f.load(path)) return false;
+        eps = f.key_f("lfm3.attention.layer_norm_rms_epsilon", 1e-5f);   // seoul.cpp:101-104
+        rope_base = f.key_f("lfm3.rope.freq_base", 1e6f);
+        rope_base_swa = f.key_f("lfm3.rope.freq_base_swa", 1e4f);
         const char *dev = getenv("IMI_CUDA_DEVICE");
         if (imi_cuda_load(path.c_str(), dev ? atoi(dev) : 0, ctx_len, 8, &engine) != IMI_OK) {
             fprintf(stderr, "imi-seoul: %s\n", imi_cuda_error());
@@ -68,6 +79,7 @@ struct imi_seoul {
     void step(int32_t token, const float *embd, bool want_logits) {   // seoul.cpp:352-357
         if (!ok(imi_cuda_step(own.s, token, embd, want_logits))) return;
         pos = imi_cuda_state_pos(own.s);
+        t_tables += imi_cuda_last_step_ms(engine);
         fetch(own.s, hidden, want_logits ? &logits : nullptr);
     }
     void step_batch(const int32_t *tokens, const float *embd, int n, bool want_logits, float *hidden_all = nullptr) {
@@ -94,6 +106,7 @@ struct imi_seoul {
                const float *embd_b, bool logits_b) {
         if (!ok(imi_cuda_step2(own.s, token_a, embd_a, logits_a, b.s, token_b, embd_b, logits_b))) return;
         pos = imi_cuda_state_pos(own.s);
+        t_tables += imi_cuda_last_step_ms(engine);
         b.pos = imi_cuda_state_pos(b.s);
         fetch(own.s, hidden, logits_a ? &logits : nullptr);
         fetch(b.s, b.hidden, logits_b ? &b.logits : nullptr);

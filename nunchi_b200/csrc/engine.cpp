@@ -117,6 +117,8 @@ struct imi_cuda_engine {
     unsigned *done = nullptr;
     int *err = nullptr;
     cudaEvent_t staged = nullptr;   // the last host->device copy of the staging buffers has run
+    cudaEvent_t t0 = nullptr, t1 = nullptr;   // around the last step's graph (imi_cuda_last_step_ms)
+    bool timed = false;
     std::map<int, cudaGraphExec_t> graphs;
     size_t state_bytes = 0;
     size_t dev_budget = SIZE_MAX, dev_used = 0;   // IMI_CUDA_MAX_DEVICE_BYTES and what the engine + states hold
@@ -161,6 +163,8 @@ imi_cuda_engine::~imi_cuda_engine() {
     cudaFreeHost(embd_h);
     cudaFreeHost(reply_h);
     if (staged) cudaEventDestroy(staged);
+    if (t0) cudaEventDestroy(t0);
+    if (t1) cudaEventDestroy(t1);
     if (stream) cudaStreamDestroy(stream);
 }
 
@@ -539,6 +543,8 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
     }
     CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
     CK(cudaEventCreateWithFlags(&e->staged, cudaEventDisableTiming));
+    CK(cudaEventCreate(&e->t0));
+    CK(cudaEventCreate(&e->t1));
     CK(prepare_kernels());
     e->state_bytes = sizeof(SessDev) + (size_t) 2 * e->n_attn * n_ctx * kvd * 2 +
                      (size_t) e->n_conv * (e->d_conv + 1) * E * 4 + (size_t) E * 4 + (size_t) e->n_vocab * 4 +
@@ -944,7 +950,10 @@ imi_cuda_status run_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind,
         if (r3 != cudaSuccess) return fail(IMI_E_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(r3));
         it = e->graphs.emplace(key, ge).first;
     }
+    CK(cudaEventRecord(e->t0, e->stream));
     CK(cudaGraphLaunch(it->second, e->stream));
+    CK(cudaEventRecord(e->t1, e->stream));
+    e->timed = true;
     return IMI_OK;
 }
 
@@ -1701,7 +1710,120 @@ imi_cuda_status imi_cuda_check_wait_timeout(int device, double limit_ms) {
     return fail(IMI_E_CUDA, "check_wait_timeout: a wait that nothing completes completed");
 }
 
+// ---- the model file's keys and tensor headers ----
+struct imi_cuda_file {
+    gguf_file f;
+    std::map<std::pair<int64_t, uint64_t>, std::string> strs;   // 0-ended copies of the strings asked for
+    std::map<int64_t, std::vector<const uint8_t *>> str_at;     // string arrays: where each element starts
+    std::mutex mu;
+};
+
+imi_cuda_status imi_cuda_file_open(const char *path, imi_cuda_file **out) {
+    if (!path || !out) return fail(IMI_E_ARG, "null argument");
+    *out = nullptr;
+    std::unique_ptr<imi_cuda_file> h(new imi_cuda_file);
+    if (!h->f.open(path)) return fail(IMI_E_FILE, h->f.error);
+    *out = h.release();
+    return IMI_OK;
+}
+void imi_cuda_file_close(imi_cuda_file *f) { delete f; }
+int64_t imi_cuda_file_find_key(const imi_cuda_file *f, const char *key) {
+    if (!f || !key) return -1;
+    for (size_t k = 0; k < f->f.values.size(); k++)
+        if (f->f.values[k].key == key) return (int64_t) k;
+    return -1;
+}
+int64_t imi_cuda_file_n_keys(const imi_cuda_file *f) { return f ? (int64_t) f->f.values.size() : 0; }
+static const gguf_value *file_value(const imi_cuda_file *f, int64_t k) {
+    return f && k >= 0 && k < (int64_t) f->f.values.size() ? &f->f.values[(size_t) k] : nullptr;
+}
+const char *imi_cuda_file_key_name(const imi_cuda_file *f, int64_t k) {
+    const gguf_value *v = file_value(f, k);
+    return v ? v->key.c_str() : nullptr;
+}
+int imi_cuda_file_key_type(const imi_cuda_file *f, int64_t k) {
+    const gguf_value *v = file_value(f, k);
+    return v ? v->type : -1;
+}
+const void *imi_cuda_file_key_data(const imi_cuda_file *f, int64_t k) {
+    const gguf_value *v = file_value(f, k);
+    return v && v->type != 8 && v->type != 9 ? v->val : nullptr;
+}
+// a GGUF string (u64 length, bytes) at p as a 0-ended copy kept with the file
+static const char *file_str(const imi_cuda_file *f, int64_t k, uint64_t i, const uint8_t *p) {
+    imi_cuda_file *m = const_cast<imi_cuda_file *>(f);
+    std::lock_guard<std::mutex> g(m->mu);
+    auto it = m->strs.find({ k, i });
+    if (it == m->strs.end()) {
+        uint64_t n;
+        memcpy(&n, p, 8);
+        it = m->strs.emplace(std::make_pair(k, i), std::string((const char *) p + 8, (size_t) n)).first;
+    }
+    return it->second.c_str();
+}
+const char *imi_cuda_file_key_str(const imi_cuda_file *f, int64_t k) {
+    const gguf_value *v = file_value(f, k);
+    return v && v->type == 8 ? file_str(f, k, UINT64_MAX, v->val) : nullptr;
+}
+int imi_cuda_file_arr_type(const imi_cuda_file *f, int64_t k) {
+    const gguf_value *v = file_value(f, k);
+    return v && v->type == 9 ? v->arr_type : -1;
+}
+uint64_t imi_cuda_file_arr_n(const imi_cuda_file *f, int64_t k) {
+    const gguf_value *v = file_value(f, k);
+    return v && v->type == 9 ? v->arr_n : 0;
+}
+const void *imi_cuda_file_arr_data(const imi_cuda_file *f, int64_t k) {
+    const gguf_value *v = file_value(f, k);
+    return v && v->type == 9 && v->arr_type != 8 ? v->arr : nullptr;
+}
+const char *imi_cuda_file_arr_str(const imi_cuda_file *f, int64_t k, uint64_t i) {
+    const gguf_value *v = file_value(f, k);
+    if (!v || v->type != 9 || v->arr_type != 8 || i >= v->arr_n) return nullptr;
+    const uint8_t *p = nullptr;
+    {   // strings lie one after another: index the array once
+        imi_cuda_file *m = const_cast<imi_cuda_file *>(f);
+        std::lock_guard<std::mutex> g(m->mu);
+        auto &at = m->str_at[k];
+        if (at.empty()) {
+            at.reserve(v->arr_n);
+            const uint8_t *q = v->arr;
+            for (uint64_t j = 0; j < v->arr_n; j++) {
+                at.push_back(q);
+                uint64_t n;
+                memcpy(&n, q, 8);
+                q += 8 + n;
+            }
+        }
+        p = at[i];
+    }
+    return file_str(f, k, i, p);
+}
+int imi_cuda_file_tensor(const imi_cuda_file *f, const char *name, int *type, int64_t ne[4], const void **data,
+                         size_t *nbytes) {
+    if (!f || !name) return -1;
+    const gguf_tensor *t = f->f.tensor(name);
+    if (!t) return -1;
+    if (type) *type = t->type;
+    if (ne)
+        for (int d = 0; d < 4; d++) ne[d] = t->ne[d];
+    if (data) *data = t->data;
+    if (nbytes) *nbytes = t->nbytes;
+    return 0;
+}
+
 void *imi_cuda_stream(const imi_cuda_engine *e) { return e ? (void *) e->stream : nullptr; }
+
+float imi_cuda_last_step_ms(const imi_cuda_engine *e) {
+    if (!e || !e->timed) return 0.0f;
+    cudaSetDevice(e->device);
+    float ms = 0.0f;
+    if (cudaEventSynchronize(e->t1) != cudaSuccess || cudaEventElapsedTime(&ms, e->t0, e->t1) != cudaSuccess) {
+        cudaGetLastError();
+        return 0.0f;
+    }
+    return ms;
+}
 
 int imi_cuda_launches_per_step(const imi_cuda_engine *e, int n, int want_logits) {
     if (!e || n <= 0) return 0;
