@@ -224,8 +224,8 @@ imi_cuda_status imi_cuda_bench_matvec(int device, int rows, int cols, int ncol, 
  * flag) on the stream itself, so nothing needs to be zero beforehand. A table above IMI_CUDA_STATIC_TABLE_BYTES
  * (rows * cols / 32 * 18 bytes) is refused with IMI_E_ARG.
  * The first call on a device looks the scratch address up (cudaGetSymbolAddress, with that device current) and sets
- * the kernels' shared-memory limits; a caller that captures CUDA work into a graph makes that first call before it
- * starts capturing. The scratch is shared: two calls on the same device that overlap in time (from two host threads,
+ * the kernels' shared-memory limits; both are kept for the life of the process, which assumes the device's primary
+ * context is not reset (cudaDeviceReset) in between. The scratch is shared: two calls on the same device that overlap in time (from two host threads,
  * or on two streams) race on it and corrupt each other's results; callers serialise them. */
 #define IMI_CUDA_STATIC_TABLE_BYTES 16777216u
 imi_cuda_status imi_cuda_q4_matvec_static(int device, const uint8_t *q4, int rows, int cols, const int8_t *xq,

@@ -199,6 +199,38 @@ __host__ __device__ inline int mv_vb_len(int pro, int cols, int n_embd, int nc, 
                                : pro == P_EMBED_NORM ? n_embd : pro == P_CONV ? (nc <= 2 ? d_conv : 0) * n_embd : 0;
 }
 
+// the column-count instance a launch of ncol inputs runs (1, 2, 4 or 8; 0: too many)
+__host__ __device__ inline int mv_nc_slot(int ncol) {
+    return ncol <= 1 ? 1 : ncol <= 2 ? 2 : ncol <= 4 ? 4 : ncol <= MV_MAX_COLS ? 8 : 0;
+}
+
+// rows per weight stage (a.sr) and stages in flight (a.nstage) of one table read of `grid` CTAs: full stages (at most
+// 64 rows of one MV_STAGE_BYTES stage) and as many of them as a CTA's slice needs (up to MV_MAX_STAGES), within one
+// CTA's shared memory (MV_SMEM_BUDGET); fewer stages first (down to 2), then fewer rows per stage. Stages hold a
+// multiple of `gran` rows. a.rows, cols, row_bytes, unit, ncol, n_embd, ab_len, d_conv and has_m must be set (the
+// engine's table_launch sets them). Returns the plan's shared-memory bytes (0: nothing fits; a.sr = gran and
+// a.nstage = 1 then, and the launch reports the excess).
+inline int mv_plan_stages(MvArgs &a, int pro, int gran, int grid) {
+    const int nc = mv_nc_slot(a.ncol), units = a.rows / a.unit, rows_cta = (units + grid - 1) / grid * a.unit;
+    const int cap = MV_STAGE_BYTES / a.row_bytes < 64 ? MV_STAGE_BYTES / a.row_bytes : 64;
+    const int full = cap / gran * gran > gran ? cap / gran * gran : gran;
+    const int vb = mv_vb_len(pro, a.cols, a.n_embd, nc, a.d_conv);
+    for (int sr = full; sr >= gran; sr -= gran) {
+        const int nst = (rows_cta + sr - 1) / sr > 1 ? (rows_cta + sr - 1) / sr : 1;
+        for (int ns = nst < MV_MAX_STAGES ? nst : MV_MAX_STAGES; ns >= (nst < 2 ? nst : 2); ns--) {
+            const int total = mv_plan(a.cols, sr, nc, vb, a.ab_len, ns, a.has_m).total;
+            if (total <= MV_SMEM_BUDGET) {
+                a.sr = sr;
+                a.nstage = ns;
+                return total;
+            }
+        }
+    }
+    a.sr = gran;
+    a.nstage = 1;
+    return 0;
+}
+
 #ifdef __CUDACC__
 // ---------------- exact scalar helpers ----------------
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }

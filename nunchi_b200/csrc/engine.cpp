@@ -561,25 +561,7 @@ namespace {
 
 enum StepKind { K_DECODE = 0, K_PREFILL = 1, K_HEAD_ONLY = 2 };
 
-// rows per weight stage (sr) and stages in flight (nstage) of one table read: full stages (at most 64 rows of one
-// MV_STAGE_BYTES stage) and as many of them as the CTA's slice needs (up to MV_MAX_STAGES), within one CTA's shared
-// memory; fewer stages first (down to 2), then fewer rows per stage. a.rows, cols, row_bytes, unit, ncol, n_embd,
-// ab_len and d_conv must be set.
-void plan_stages(MvArgs &a, int pro, int gran, int grid) {
-    const int units = a.rows / a.unit, rows_cta = (units + grid - 1) / grid * a.unit;
-    const int full = std::max(gran, (std::min(64, MV_STAGE_BYTES / a.row_bytes) / gran) * gran);
-    for (int sr = full; sr >= gran; sr -= gran) {
-        const int nst = std::max(1, (rows_cta + sr - 1) / sr);
-        for (int ns = std::min(MV_MAX_STAGES, nst); ns >= std::min(2, nst); ns--)
-            if (table_smem(pro, a.cols, sr, a.ncol, a.n_embd, a.ab_len, a.d_conv, ns, a.has_m) <= (size_t) MV_SMEM_BUDGET) {
-                a.sr = sr;
-                a.nstage = ns;
-                return;
-            }
-    }
-    a.sr = gran;   // nothing fits: the launch reports the shared-memory excess
-    a.nstage = 1;
-}
+void plan_stages(MvArgs &a, int pro, int gran, int grid) { mv_plan_stages(a, pro, gran, grid); }
 
 // one table read: CTAs take whole `unit`s of rows (64 for the SiLU stage, which cuts whole 32-value blocks of its
 // output; else 1), stages hold a multiple of `gran` rows (2 for the SiLU stage's (gate, up) pairs)
@@ -1614,7 +1596,10 @@ constexpr int STATIC_MAX_DEVICES = 64;
 static_assert(sizeof(Col) * MV_MAX_COLS <= STATIC_ERR, "column descriptors overflow the static head");
 __device__ __align__(256) uint8_t g_static_scratch[STATIC_HEAD + IMI_CUDA_STATIC_TABLE_BYTES];
 std::mutex g_static_mu;
-uint8_t *g_static_addr[STATIC_MAX_DEVICES];   // the scratch's device address, per device (null until looked up)
+// the scratch's device address, per device (null until looked up), kept for the life of the process together with the
+// kernels' shared-memory limits (prepare_kernels): both belong to the device's primary context, so this entry point
+// assumes that context is not reset (cudaDeviceReset) while the process uses it
+uint8_t *g_static_addr[STATIC_MAX_DEVICES];
 
 bool on_device(const void *p, int device) {
     cudaPointerAttributes at;

@@ -1,7 +1,8 @@
-// plan_check: the table read's shared-memory plan (mv_plan in common.cuh) for the Seoul tables at 1, 2, 4 and 8
-// inputs, with the stage choice the engine makes (the largest rows per stage, then the most stages, that fit one
-// CTA's budget). Host code only: prints one line per (table, inputs) with every region's offset, for the test to
-// check that regions are aligned, ordered and inside the budget.
+// plan_check: the table read's shared-memory plan for the Seoul tables at 1, 2, 4 and 8 inputs, made by the engine's
+// own stage choice (mv_plan_stages in common.cuh, called with the MvArgs fields the engine sets: the Seoul shape's
+// n_embd 2048 and d_conv 2, one CTA per SM of a 148-SM B200 at most). Host code only: prints one line per
+// (table, inputs) with every region's offset, for the test to check that regions are aligned, ordered and inside one
+// CTA's budget.
 #include "../nunchi_b200/csrc/common.cuh"
 
 #include <algorithm>
@@ -25,21 +26,17 @@ int main() {
             const int ab_len = t.epi == E_SILU ? (units + grid - 1) / grid * unit / 2 : 0;
             const int vb = mv_vb_len(t.pro, t.cols, 2048, nc, 2);
             const int full = std::max(gran, (std::min(64, MV_STAGE_BYTES / rb) / gran) * gran);
-            int sr = 0, ns = 0;
-            for (int s = full; s >= gran && !sr; s -= gran) {
-                const int nst = std::max(1, (rows_cta + s - 1) / s);
-                for (int n = std::min(MV_MAX_STAGES, nst); n >= std::min(2, nst); n--)
-                    if (mv_plan(t.cols, s, nc, vb, ab_len, n, t.hm).total <= MV_SMEM_BUDGET) {
-                        sr = s;
-                        ns = n;
-                        break;
-                    }
-            }
+            MvArgs a = {};
+            a.rows = t.rows; a.cols = t.cols; a.row_bytes = rb; a.unit = unit; a.ncol = nc; a.n_embd = 2048;
+            a.ab_len = ab_len; a.d_conv = 2; a.has_m = t.hm;
+            const int total = mv_plan_stages(a, t.pro, gran, grid);
+            const int sr = total ? a.sr : 0, ns = total ? a.nstage : 0;
+            const int budget = MV_SMEM_BUDGET;
             const MvPlan p = mv_plan(t.cols, sr ? sr : gran, nc, vb, ab_len, ns ? ns : 1, t.hm);
             printf("%s %d rb=%d full=%d rows_cta=%d sr=%d ns=%d stage=%d sstride=%d bar=%d xq=%d xd=%d xs=%d fs=%d dd=%d "
                    "vb=%d vo=%d ab=%d pc=%d red=%d total=%d budget=%d nc=%d nb=%d vb_len=%d ab_len=%d hm=%d\n",
                    t.name, nc, rb, full, rows_cta, sr, ns, p.stage, p.sstride, p.bar, p.xq, p.xd, p.xs, p.fs, p.dd,
-                   p.vb, p.vo, p.ab, p.pc, p.red, p.total, MV_SMEM_BUDGET, nc, t.cols / 32, vb, ab_len, t.hm);
+                   p.vb, p.vo, p.ab, p.pc, p.red, p.total, budget, nc, t.cols / 32, vb, ab_len, t.hm);
         }
     return 0;
 }

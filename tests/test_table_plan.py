@@ -1,7 +1,7 @@
 """The table read's shared-memory plan on the host (tests/plan_check.cu over mv_plan in common.cuh): for the Seoul
 tables (Q4_0 and Q4_1 rows) at 1, 2, 4 and 8 inputs, every region is aligned, the regions follow one another without
 overlap, the total fits one CTA's budget, weight stages hold their rows, and the decode plans (1 and 2 inputs) keep
-full stages."""
+full stages. The plans are the engine's own (mv_plan_stages)."""
 import os
 import shutil
 import subprocess
@@ -11,6 +11,7 @@ import pytest
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 MV_NBUF, MV_MAX_STAGES, MV_STAGE_BYTES = 4, 8, 36864
+MV_SMEM_BUDGET = 220 * 1024
 
 
 @pytest.fixture(scope="module")
