@@ -850,7 +850,9 @@ cudaError_t enqueue_batch(imi_cuda_engine *e, int ncol, bool head, StepKind kind
             t.q8o_d = e->qt_d;
             t.q8o_s = e->qt_s;
             if (kind == K_PREFILL && (r = launch_kvwrite(t, e->stream, true)) != cudaSuccess) return r;
-            if ((r = launch_attn(t, e->stream, true)) != cudaSuccess) return r;
+            // many columns: one CTA per (kv head, column) reads each cached row once for the heads sharing it
+            const bool grp = attn_grp_supported(e->head_dim, e->n_head / e->n_head_kv, e->n_ctx);
+            if ((r = (grp ? launch_attn_grp : launch_attn)(t, e->stream, true)) != cudaSuccess) return r;
             p = p0;
             p.pro = TP_Q8;
             p.q8_q = e->qt_q;

@@ -372,6 +372,275 @@ __global__ void __launch_bounds__(ATT_NT) k_attn(const __grid_constant__ AttnArg
 
 __host__ __device__ inline size_t attn_smem_bytes(int D, int n_ctx) { return attn_plan(D, n_ctx).total; }
 
+// k_attn_grp: the same attention for many columns, one CTA of ATG_NT threads per (kv head g, column c) computing the
+// GRP query heads g*GRP .. g*GRP+GRP-1 that share the kv head (GQA), so every cached K and V row of the group is read
+// once for all of them instead of once per query head. Per query head the float order is k_attn's: q RMSNorm +
+// rotation, scores by dot_h, the maximum, exp and the double sum, the normalised probabilities, the P.V chain over
+// positions in order, the sigmoid gate and the 8-bit cut of the head's output. Scores: one thread per position, its K
+// row converted once and dotted with the GRP queries; P.V: one thread per (query head, dimension), V rows in shared
+// memory tiles (ATG_NTILE in flight, cp.async) that serve all GRP heads.
+constexpr int ATG_NT = 256, ATG_NW = ATG_NT / 32, ATG_VT = 64, ATG_NTILE = 3;
+struct AttnGPlan {
+    size_t q, ktmp, tmp, kh, vh, rcs, rsn, y, red, vt, sc, total;
+};
+// floats per query head's score row: a multiple of 4, so every row starts 16-byte aligned (float4 reads of P.V)
+__host__ __device__ inline int attn_grp_sc_stride(int n_ctx) { return (n_ctx + 3) / 4 * 4; }
+__host__ __device__ inline AttnGPlan attn_grp_plan(int D, int grp, int n_ctx) {
+    AttnGPlan p;
+    size_t o = 0;
+    auto take = [&](size_t n) { const size_t r = o; o = (o + n + 15) / 16 * 16; return r; };
+    p.q = take(4 * (size_t) grp * D);
+    p.ktmp = take(4 * (size_t) D);
+    p.tmp = take(4 * (size_t) (grp + 1) * D);   // norm_rope scratch: warp 0 (this position's K), warps 1..grp (queries)
+    p.kh = take(2 * (size_t) D);
+    p.vh = take(2 * (size_t) D);
+    p.rcs = take(4 * (size_t) D / 2);
+    p.rsn = take(4 * (size_t) D / 2);
+    p.y = take(4 * (size_t) grp * D);
+    p.red = take(8 * (size_t) ATG_NW * grp + 4 * (size_t) ATG_NW * grp + 8 * (size_t) grp);
+    p.vt = take((size_t) ATG_NTILE * ATG_VT * D * 2);
+    p.sc = take(4 * (size_t) grp * attn_grp_sc_stride(n_ctx));
+    p.total = o;
+    return p;
+}
+
+template <int D, int GRP>
+__global__ void __launch_bounds__(ATG_NT, 2) k_attn_grp(const __grid_constant__ AttnArgs a) {
+    static_assert(GRP * D <= ATG_NT && GRP + 1 <= ATG_NW, "one thread per (query head, dimension); a warp per query");
+    extern __shared__ __align__(16) uint8_t sma[];
+    const AttnGPlan L = attn_grp_plan(D, GRP, a.n_ctx);
+    const int g = blockIdx.x, c = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    unsigned long long *trace = a.trace ? a.trace + (size_t) (blockIdx.y * gridDim.x + blockIdx.x) * MV_TRACE : nullptr;
+    if (trace && tid == 0) trace[0] = global_ns();
+    float *q = (float *) (sma + L.q), *ktmp = (float *) (sma + L.ktmp), *tmp = (float *) (sma + L.tmp);
+    float *y = (float *) (sma + L.y), *sc = (float *) (sma + L.sc);
+    uint16_t *kh = (uint16_t *) (sma + L.kh), *vh = (uint16_t *) (sma + L.vh), *vt = (uint16_t *) (sma + L.vt);
+    double *dsum = (double *) (sma + L.red);
+    float *wmax = (float *) (sma + L.red + 8 * ATG_NW * GRP), *inv = wmax + ATG_NW * GRP;
+    float *rcs = (float *) (sma + L.rcs), *rsn = (float *) (sma + L.rsn);
+    pdl_trigger();
+    const int H = a.n_head, kvd = a.n_head_kv * D, NC = a.n_ctx, SS = attn_grp_sc_stride(NC);
+    const Col col = a.cols_d[c];
+    const int pspec = ld_relaxed(&col.s->pos) + col.off;
+    for (int i = tid; i < D / 2; i += ATG_NT) {
+        rcs[i] = a.rope_cs[(size_t) pspec * (D / 2) + i];
+        rsn[i] = a.rope_sn[(size_t) pspec * (D / 2) + i];
+    }
+    if (tid == 0) {   // before the wait: this CTA's share of the column's cached K and V rows into L2 (a hint only)
+        const int pp = ld_relaxed(&col.s->pos) + col.off, ps = a.window > 0 ? max(0, pp - a.window + 1) : 0;
+        const size_t row = (size_t) kvd * 2, bytes = (size_t) max(pp - ps, 0) * row;
+        const size_t share = (bytes / a.n_head_kv + 15) / 16 * 16, b0 = (size_t) g * share, b1 = min(b0 + share, bytes);
+        const uint8_t *kb = (const uint8_t *) col.kc + ((size_t) a.ai * NC + ps) * row;
+        const uint8_t *vb0 = (const uint8_t *) col.vc + ((size_t) a.ai * NC + ps) * row;
+        for (size_t o = b0; o < b1; o += 65536) {
+            const uint32_t n = (uint32_t) min((size_t) 65536, b1 - o);
+            prefetch_l2(kb + o, n);
+            prefetch_l2(vb0 + o, n);
+        }
+    }
+    pdl_wait();
+    if (trace && tid == 0) trace[1] = global_ns();
+    const int p = ld_relaxed(&col.s->pos) + col.off;
+    const float *qkv = a.qkv + (size_t) c * a.qkv_stride;
+    const float *cs = rcs, *sn = rsn;
+    if (p != pspec) {
+        cs = a.rope_cs + (size_t) p * (D / 2);
+        sn = a.rope_sn + (size_t) p * (D / 2);
+    }
+    uint16_t *kc = (uint16_t *) col.kc + (size_t) a.ai * NC * kvd + g * D;
+    uint16_t *vc = (uint16_t *) col.vc + (size_t) a.ai * NC * kvd + g * D;
+    const int s0 = a.window > 0 ? max(0, p - a.window + 1) : 0, nk = p - s0 + 1;
+    const int ng = a.kv_fused ? nk - 1 : nk;   // positions whose V is read from the cache
+    const int ntile = (ng + ATG_VT - 1) / ATG_VT;
+    auto load_tile = [&](int k) {   // V rows of positions s0 + k*VT .. into buffer k % ATG_NTILE, by all threads
+        uint16_t *dst = vt + (size_t) (k % ATG_NTILE) * ATG_VT * D;
+        const int t0 = k * ATG_VT, n = min(ATG_VT, ng - t0);
+        for (int i = tid; i < n * (D / 8); i += ATG_NT) {
+            const int t = i / (D / 8), ch = i - t * (D / 8);
+            cp16(dst + (size_t) t * D + 8 * ch, vc + (size_t) (s0 + t0 + t) * kvd + 8 * ch);
+        }
+    };
+    __syncthreads();   // the rotary rows are in shared memory
+    for (int k = 0; k < ATG_NTILE - 1; k++) {   // the first V tiles load while the setup and the scores run
+        if (k < ntile) load_tile(k);
+        cp_commit();
+    }
+    // this position's K and V (warp 0) and the group's rotated queries (warp 1 + j for query head g*GRP + j)
+    if (a.kv_fused) kv_make<D>(a, qkv, g, p, ktmp, tmp, kh, vh);
+    if (warp >= 1 && warp <= GRP) {
+        const int j = warp - 1, h = g * GRP + j;
+        float *qj = q + j * D;
+        for (int i = lane; i < D; i += 32) qj[i] = qkv[h * D + i];
+        __syncwarp();
+        norm_rope<D>(qj, a.q_norm, cs, sn, a.eps, tmp + (j + 1) * D);
+    }
+    __syncthreads();
+    if (a.kv_fused && tid < D) {
+        kc[(size_t) p * kvd + tid] = kh[tid];
+        vc[(size_t) p * kvd + tid] = vh[tid];
+    }
+
+    // scores (seoul.cpp:445): one thread per position; the K row's halves converted once, dotted with every query in
+    // dot_h8's order (8 lane accumulators in steps of 8, then imi_hsum)
+    float lmax[GRP];
+#pragma unroll
+    for (int j = 0; j < GRP; j++) lmax[j] = -INFINITY;
+    constexpr int SB = GRP * D >= ATG_NT ? 1 : 2;   // K rows a thread loads together (registers allow one at full width)
+    for (int t0 = tid; t0 < nk; t0 += SB * ATG_NT) {
+        uint4 kr[SB][D / 8];
+#pragma unroll
+        for (int u = 0; u < SB; u++) {
+            const int t = t0 + u * ATG_NT, pt = s0 + t;
+            if (t < nk) {
+                const uint4 *src = (a.kv_fused && pt == p) ? (const uint4 *) kh : (const uint4 *) (kc + (size_t) pt * kvd);
+#pragma unroll
+                for (int w = 0; w < D / 8; w++) kr[u][w] = src[w];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < SB; u++) {
+            const int t = t0 + u * ATG_NT;
+            if (t < nk) {
+                float acc[GRP][8];
+#pragma unroll
+                for (int j = 0; j < GRP; j++)
+#pragma unroll
+                    for (int l = 0; l < 8; l++) acc[j][l] = 0.0f;
+#pragma unroll
+                for (int w = 0; w < D / 8; w++) {
+                    const uint32_t uu[4] = { kr[u][w].x, kr[u][w].y, kr[u][w].z, kr[u][w].w };
+                    float kf[8];
+#pragma unroll
+                    for (int hh = 0; hh < 4; hh++) {
+                        kf[2 * hh] = h2f((uint16_t) (uu[hh] & 0xffff));
+                        kf[2 * hh + 1] = h2f((uint16_t) (uu[hh] >> 16));
+                    }
+#pragma unroll
+                    for (int j = 0; j < GRP; j++) {
+                        const float4 qa = *(const float4 *) (q + j * D + 8 * w), qb = *(const float4 *) (q + j * D + 8 * w + 4);
+                        acc[j][0] = __fmaf_rn(qa.x, kf[0], acc[j][0]);
+                        acc[j][1] = __fmaf_rn(qa.y, kf[1], acc[j][1]);
+                        acc[j][2] = __fmaf_rn(qa.z, kf[2], acc[j][2]);
+                        acc[j][3] = __fmaf_rn(qa.w, kf[3], acc[j][3]);
+                        acc[j][4] = __fmaf_rn(qb.x, kf[4], acc[j][4]);
+                        acc[j][5] = __fmaf_rn(qb.y, kf[5], acc[j][5]);
+                        acc[j][6] = __fmaf_rn(qb.z, kf[6], acc[j][6]);
+                        acc[j][7] = __fmaf_rn(qb.w, kf[7], acc[j][7]);
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < GRP; j++) {
+                    const float r0 = __fadd_rn(acc[j][0], acc[j][4]), r1 = __fadd_rn(acc[j][1], acc[j][5]),
+                                r2 = __fadd_rn(acc[j][2], acc[j][6]), r3 = __fadd_rn(acc[j][3], acc[j][7]);
+                    const float v = __fmul_rn(__fadd_rn(__fadd_rn(r0, r2), __fadd_rn(r1, r3)), a.scale);
+                    sc[(size_t) j * SS + t] = v;
+                    lmax[j] = lmax[j] < v ? v : lmax[j];
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < GRP; j++) {
+        float m = lmax[j];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) wmax[warp * GRP + j] = m;
+    }
+    __syncthreads();
+    float m[GRP];
+#pragma unroll
+    for (int j = 0; j < GRP; j++) {
+        m[j] = wmax[j];
+        for (int w = 1; w < ATG_NW; w++) m[j] = fmaxf(m[j], wmax[w * GRP + j]);
+    }
+    // exp and the double sum (seoul.cpp:446-448), per query head
+    double ls[GRP];
+#pragma unroll
+    for (int j = 0; j < GRP; j++) ls[j] = 0.0;
+    for (int t = tid; t < nk; t += ATG_NT)
+#pragma unroll
+        for (int j = 0; j < GRP; j++) {
+            const float e = exp_cr(__fsub_rn(sc[(size_t) j * SS + t], m[j]));
+            sc[(size_t) j * SS + t] = e;
+            ls[j] += (double) e;
+        }
+#pragma unroll
+    for (int j = 0; j < GRP; j++) {
+        double v = ls[j];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) dsum[warp * GRP + j] = v;
+    }
+    __syncthreads();
+    if (tid < GRP) {
+        double t = 0.0;
+        for (int w = 0; w < ATG_NW; w++) t += dsum[w * GRP + tid];
+        inv[tid] = __double2float_rn(1.0 / t);
+    }
+    __syncthreads();
+    for (int t = tid; t < nk; t += ATG_NT)
+#pragma unroll
+        for (int j = 0; j < GRP; j++) sc[(size_t) j * SS + t] = __fmul_rn(sc[(size_t) j * SS + t], inv[j]);
+
+    // P.V (seoul.cpp:449-450): thread (j, i) runs o = fma(p_t, v_t,i, o) over positions in order for query head
+    // g*GRP + j, dimension i
+    const int j = tid / D, i = tid - (tid / D) * D;
+    const bool pv = j < GRP;
+    float o = 0.0f;
+    for (int k = 0; k < ntile; k++) {
+        if (k + ATG_NTILE - 1 < ntile) load_tile(k + ATG_NTILE - 1);   // into the buffer tile k - 1 left
+        cp_commit();
+        cp_wait_group<ATG_NTILE - 1>();   // tile k's group is complete
+        __syncthreads();
+        if (pv) {
+            const uint16_t *vb = vt + (size_t) (k % ATG_NTILE) * ATG_VT * D + i;
+            const float *pr = sc + (size_t) j * SS + (size_t) k * ATG_VT;
+            const int n = min(ATG_VT, ng - k * ATG_VT);
+            int t = 0;
+#pragma unroll 2
+            for (; t + 8 <= n; t += 8) {
+                uint16_t v8[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) v8[u] = vb[(size_t) (t + u) * D];
+                const float4 p0 = *(const float4 *) (pr + t), p1 = *(const float4 *) (pr + t + 4);
+                o = __fmaf_rn(p0.x, h2f(v8[0]), o);
+                o = __fmaf_rn(p0.y, h2f(v8[1]), o);
+                o = __fmaf_rn(p0.z, h2f(v8[2]), o);
+                o = __fmaf_rn(p0.w, h2f(v8[3]), o);
+                o = __fmaf_rn(p1.x, h2f(v8[4]), o);
+                o = __fmaf_rn(p1.y, h2f(v8[5]), o);
+                o = __fmaf_rn(p1.z, h2f(v8[6]), o);
+                o = __fmaf_rn(p1.w, h2f(v8[7]), o);
+            }
+            for (; t < n; t++) o = __fmaf_rn(pr[t], h2f(vb[(size_t) t * D]), o);
+        }
+        __syncthreads();   // the buffer is free for the tile issued two rounds on
+    }
+    cp_wait_group<0>();
+    if (pv) {
+        const int h = g * GRP + j;
+        if (ng < nk) o = __fmaf_rn(sc[(size_t) j * SS + nk - 1], h2f(vh[i]), o);   // this position's own V
+        const float gv = qkv[H * D + 2 * kvd + h];
+        const float gate = __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_cr(-gv)));   // seoul.cpp:451
+        const float yv = __fmul_rn(o, gate);
+        a.att[(size_t) c * a.att_stride + h * D + i] = yv;
+        y[j * D + i] = yv;
+    }
+    __syncthreads();
+    // the 8-bit cut of each query head's output blocks (imi_cut32 of seoul.cpp:457): warp j cuts head g*GRP + j
+    if (a.q8o_q && warp < GRP) {
+        const int HD = H * D, h = g * GRP + warp;
+        for (int q0 = 0; q0 < D / 4; q0 += 32) {
+            const int qi = q0 + lane;
+            const bool act = qi < D / 4;
+            const float4 v = act ? ((const float4 *) (y + warp * D))[qi] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            cut_chunk(v, act, qi, a.q8o_q + (size_t) c * HD + h * D, a.q8o_d + (size_t) c * (HD / 32) + h * D / 32,
+                      a.q8o_s + (size_t) c * (HD / 32) + h * D / 32);
+        }
+    }
+    if (trace && tid == 0) trace[14] = global_ns();
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // the failure path of the bounded device waits: a wait on an mbarrier no thread ever arrives at (a flag nothing
 // sets), with a short limit, gives up, reports IMI_E_TIMEOUT's code in the error flag and returns; no copy is in

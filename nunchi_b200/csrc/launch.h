@@ -11,6 +11,9 @@ size_t table_smem(int pro, int cols, int sr, int ncol, int n_embd, int ab_len, i
 int table_nc_slot(int ncol);
 cudaError_t launch_attn(const AttnArgs &a, cudaStream_t st, bool pdl);
 bool attn_supported(int head_dim, int grp, int n_ctx);
+// the same attention for many columns, one CTA per (kv head, column) for the query heads sharing it (GQA)
+cudaError_t launch_attn_grp(const AttnArgs &a, cudaStream_t st, bool pdl);
+bool attn_grp_supported(int head_dim, int grp, int n_ctx);
 cudaError_t launch_kvwrite(const AttnArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_final(const FinalArgs &a, cudaStream_t st, bool pdl);
 cudaError_t prepare_kernels();

@@ -132,7 +132,8 @@ def test_picks_read_back_after_riding_reset_load_and_free(tiny_path):
 
 @pytest.mark.parametrize("n", [3, 8, 11])
 def test_step_multi_is_byte_identical_to_alone(tiny_path, n):
-    e = nb.Engine(tiny_path, n_ctx=64, max_batch=16)
+    # a context length that is not a multiple of 4: the batched attention's per-head score rows are padded to it
+    e = nb.Engine(tiny_path, n_ctx=67, max_batch=16)
     multi = [e.new_state() for _ in range(n)]
     alone = [e.new_state() for _ in range(n)]
     toks = synth.random_ids(4 * n, e.n_vocab, 9).reshape(4, n)
@@ -149,8 +150,8 @@ def test_step_batch_matches_oracle(name):
     """batched reads of ids and of input vectors (across the 64-position context check) bit for bit the "cr" oracle's,
     at every position, and decoding continues from them alike; the "libc" oracle's free-running difference recorded"""
     path = synth.cached_gguf(name)
-    e = nb.Engine(path, n_ctx=256)
-    cr, lc = oracle.Oracle(path, n_ctx=256, exp="cr"), oracle.Oracle(path, n_ctx=256)
+    e = nb.Engine(path, n_ctx=259)   # not a multiple of 4 (the batched attention pads its per-head score rows)
+    cr, lc = oracle.Oracle(path, n_ctx=259, exp="cr"), oracle.Oracle(path, n_ctx=259)
     g = e.new_state()
     toks = synth.random_ids(77, e.n_vocab, 8)          # 64 + 13: crosses the 64-position context check
     emb = (0.5 * np.random.default_rng(3).standard_normal((19, e.n_embd))).astype(np.float32)
