@@ -187,15 +187,15 @@ imi_cuda_status imi_cuda_q4_matvec(int device, const uint8_t *q4, int rows, int 
                                    const float *xd, const float *xs, int ncol, float *out, int32_t *block_dots);
 
 /* The same table read for many inputs on the tensor cores (the batched read of imi_q8b + imi_q4_group_batch,
- * tables.cpp:405-477): ncol 1..256 inputs, each block's integer dot by a tcgen05 MMA (fp16 codes, exact), imi's float
+ * tables.cpp:405-477): ncol 1..256 inputs, each block's integer dot by a tcgen05 MMA (8-bit codes, int32, exact), imi's float
  * chains per (row, input) in block order; results as imi_cuda_q4_matvec gives them. Host pointers. */
 imi_cuda_status imi_cuda_q4_matmul(int device, const uint8_t *q4, int rows, int cols, const int8_t *xq,
                                    const float *xd, const float *xs, int ncol, float *out);
 
-/* Diagnostics: imi_cuda_q4_matmul with CTA 0's timeline of the tensor-core read in ns, trace[7][64]: 0 stage copies
- * issued, 1 stage copies seen by the unpack warps, 2 stage unpacked, 3 block's MMAs issued, 4 block's dots seen by the
- * epilogue, 5 block's chains done, 6 block's dots in registers (stages and blocks counted from the CTA's first unit);
- * trace holds 7 * 64 values. */
+/* Diagnostics: imi_cuda_q4_matmul with CTA 0's timeline of the tensor-core read in ns, trace[9][64]: 0 stage copies
+ * issued, 1 (unused, 0), 2 stage done by the last epilogue warp, 3 block's MMA issued, 4 block's dots awaited by the
+ * epilogue, 5 block's chains done, 6 block's dots in registers, 7 stage's copies seen by the MMA warp, 8 stage's TMEM
+ * slot free for the MMA warp (stages and blocks counted from the CTA's first unit); trace holds 9 * 64 values. */
 imi_cuda_status imi_cuda_trace_tc(int device, const uint8_t *q4, int rows, int cols, const int8_t *xq, const float *xd,
                                   const float *xs, int ncol, float *out, unsigned long long *trace);
 

@@ -12,7 +12,6 @@
 #include "gguf_file.h"
 #include "launch.h"
 
-#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <cmath>
@@ -104,6 +103,7 @@ struct imi_cuda_engine {
     // a prefill chunk) in the tensor-core batched read, when every table is Q4_0 (tc_batch)
     int ncmax = STEP_COLS;
     bool tc_batch = false;
+    uint8_t *tc_w = nullptr;    // every table's tiled copy for the batched read (k_tc_tile)
     uint8_t *tc_xh = nullptr;   // the batched read's column operand and the columns' block scales and sums
     float *tc_xds = nullptr;
     SessDev *reply_d = nullptr;   // the last step's conversation records gathered for one read-back
@@ -158,6 +158,7 @@ imi_cuda_engine::~imi_cuda_engine() {
     cudaFree(qbuf);
     cudaFree(q8k_q);
     cudaFree(cols_d);
+    cudaFree(tc_w);
     cudaFree(tc_xh);
     cudaFreeHost(cols_h);
     cudaFreeHost(embd_h);
@@ -252,62 +253,32 @@ struct Loader {
 }  // namespace
 
 // ---------------------------------------------------------------------------------------------------------------
-// the tensor-core batched read: tensor maps of a table, the columns' operands in the MMA's layout
+// the tensor-core batched read: column group width, the columns' operands in the MMA's layout
 // ---------------------------------------------------------------------------------------------------------------
 namespace {
 
-PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
-std::mutex g_encode_mu;
-
-// the two TMA views of a table's rows ([rows][row_bytes] bytes): codes in boxes of TC_RAW_W bytes, scales in 16
-cudaError_t tc_tensor_maps(TcArgs &a, const uint8_t *W, int rows, int row_bytes) {
-    {
-        std::lock_guard<std::mutex> g(g_encode_mu);
-        if (!g_encode) {
-            void *fn = nullptr;
-            cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
-            const cudaError_t r = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q);
-            if (r != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
-            g_encode = (PFN_cuTensorMapEncodeTiled_v12000) fn;
-        }
-    }
-    cuuint64_t dims[2] = { (cuuint64_t) row_bytes, (cuuint64_t) rows }, strides[1] = { (cuuint64_t) row_bytes };
-    cuuint32_t box[2] = { (cuuint32_t) TC_RAW_W, (cuuint32_t) TC_M }, es[2] = { 1, 1 };
-    CUresult c = g_encode(&a.tm_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *) W, dims, strides, box, es,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (c != CUDA_SUCCESS) return cudaErrorInvalidValue;
-    box[0] = 16;
-    c = g_encode(&a.tm_scales, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *) W, dims, strides, box, es,
-                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return c == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+// column group width (16, 32 or 64) of one batched read of a `rows`-row table for ncol columns: the narrowest whose
+// units (128-row tiles x column groups) still fit one wave of the SMs, so a short table spreads over more SMs (each
+// CTA's epilogue, the part that bounds a unit, runs G columns); a tall table keeps 64 (one group of 64 columns)
+int tc_group(int rows, int ncol, int sms) {
+    const int tiles = (rows + TC_M - 1) / TC_M;
+    for (int G = 16; G < 64; G *= 2)
+        if (G >= ncol || tiles * ((ncol + G - 1) / G) <= sms) return G;
+    return 64;
 }
-
-// columns per group of the batched read (the kernel's instances: 16, 32, 64)
-int tc_group(int ncol) { return ncol <= 16 ? 16 : ncol <= 32 ? 32 : 64; }
 
 // an integer |v| <= 2048 as fp16 bits (exact)
-uint16_t int_half(int v) {
-    if (v == 0) return 0;
-    const uint16_t sg = v < 0 ? 0x8000 : 0;
-    unsigned m = (unsigned) (v < 0 ? -v : v);
-    int e = 0;
-    while ((m >> (e + 1)) != 0) e++;
-    return (uint16_t) (sg | ((e + 15) << 10) | ((m << (10 - e)) & 0x3FF));
-}
-
 // the columns' 8-bit codes, scales and scale * code sums ([ncol][cols], [ncol][cols/32]) in the batched read's layout:
-// xh [group][cols/8][G][8] fp16, xds [group][cols/32][2][G] (zeros for the padding columns)
+// xh [group][cols/16][G][16] 8-bit, xds [group][cols/32][2][G] (zeros for the padding columns)
 void tc_operands_host(const int8_t *xq, const float *xd, const float *xs, int ncol, int cols, int G,
-                      std::vector<uint16_t> &xh, std::vector<float> &xds) {
-    const int groups = (ncol + G - 1) / G, nq = cols / 8, nb = cols / 32;
-    xh.assign((size_t) groups * nq * G * 8, 0);
+                      std::vector<int8_t> &xh, std::vector<float> &xds) {
+    const int groups = (ncol + G - 1) / G, nq = cols / 16, nb = cols / 32;
+    xh.assign((size_t) groups * nq * G * 16, 0);
     xds.assign((size_t) groups * nb * 2 * G, 0.0f);
     for (int c = 0; c < ncol; c++) {
         const int g = c / G, cg = c - g * G;
         for (int k = 0; k < cols; k++)
-            xh[(((size_t) g * nq + k / 8) * G + cg) * 8 + (k & 7)] = int_half(xq[(size_t) c * cols + k]);
+            xh[(((size_t) g * nq + k / 16) * G + cg) * 16 + (k & 15)] = xq[(size_t) c * cols + k];
         for (int j = 0; j < nb; j++) {
             xds[(((size_t) g * nb + j) * 2 + 0) * G + cg] = xd[(size_t) c * nb + j];
             xds[(((size_t) g * nb + j) * 2 + 1) * G + cg] = xs[(size_t) c * nb + j];
@@ -531,15 +502,22 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
         const size_t bh = (size_t) kmax * ncp * 2, bx = (size_t) (kmax / 32) * 2 * ncp * 4;
         DALLOC(e, e->tc_xh, bh + bx);
         e->tc_xds = (float *) (e->tc_xh + bh);
-        auto maps = [&](TableRef &t) -> cudaError_t {
-            t.tc = {};
-            t.tc.rows = t.rows; t.tc.cols = t.cols; t.tc.row_bytes = t.row_bytes; t.tc.err = e->err;
-            return tc_tensor_maps(t.tc, e->w + t.off, t.rows, t.row_bytes);
-        };
+        // every table's tiled copy (the weights as the tensor-core read streams them), made here on the device
+        std::vector<TableRef *> tcs;
         for (auto &Lr : e->layers)
             for (TableRef *t : { &Lr.in_proj, &Lr.out_proj, &Lr.qkvg, &Lr.o, &Lr.gate_up, &Lr.down })
-                if (t->rows) CK(maps(*t));
-        CK(maps(e->tok));
+                if (t->rows) tcs.push_back(t);
+        tcs.push_back(&e->tok);
+        size_t tb = 0;
+        for (TableRef *t : tcs) tb += (tc_tiled_bytes(t->rows, t->cols) + 255) / 256 * 256;
+        DALLOC(e, e->tc_w, tb);
+        size_t o = 0;
+        for (TableRef *t : tcs) {
+            t->tc = {};
+            t->tc.rows = t->rows; t->tc.cols = t->cols; t->tc.err = e->err; t->tc.wt = e->tc_w + o;
+            CK(launch_tc_tile(e->w + t->off, t->rows, t->cols, t->row_bytes, e->tc_w + o, nullptr));
+            o += (tc_tiled_bytes(t->rows, t->cols) + 255) / 256 * 256;
+        }
     }
     CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
     CK(cudaEventCreateWithFlags(&e->staged, cudaEventDisableTiming));
@@ -754,7 +732,7 @@ cudaError_t enqueue_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind)
 cudaError_t tc_read(imi_cuda_engine *e, const TableRef &t, int ncol, int epi, float *out, int out_stride) {
     TcArgs a = t.tc;
     a.ncol = ncol;
-    a.G = tc_group(ncol);
+    a.G = tc_group(t.rows, ncol, e->sm_count);
     a.groups = (ncol + a.G - 1) / a.G;
     a.xh = e->tc_xh;
     a.xds = e->tc_xds;
@@ -772,11 +750,10 @@ cudaError_t tc_read(imi_cuda_engine *e, const TableRef &t, int ncol, int epi, fl
 // prepares the columns' inputs (k_tc_prep, one CTA per column), then the read (k_tc_table); attention as in the
 // small-batch schedule. Same float order as enqueue_step's schedule, column by column.
 cudaError_t enqueue_batch(imi_cuda_engine *e, int ncol, bool head, StepKind kind) {
-    const int E = e->n_embd, HD = e->n_head * e->head_dim, G = tc_group(ncol);
+    const int E = e->n_embd, HD = e->n_head * e->head_dim;
     TcPrepArgs p0 = {};
     p0.cols_d = e->cols_d;
     p0.ncol = ncol;
-    p0.G = G;
     p0.xh = e->tc_xh;
     p0.xds = e->tc_xds;
     p0.eps = e->eps;
@@ -789,8 +766,10 @@ cudaError_t enqueue_batch(imi_cuda_engine *e, int ncol, bool head, StepKind kind
     p0.ring_layer = -1;
     float *X0 = e->X, *X1 = e->X + E;
     cudaError_t r;
-    auto prep = [&](TcPrepArgs p, int K) {
+    // the input preparation of the read of table t: the columns' operand in the layout of t's column group width
+    auto prep = [&](TcPrepArgs p, int K, const TableRef &t) {
         p.K = K;
+        p.G = tc_group(t.rows, ncol, e->sm_count);
         return launch_tc_prep(p, e->stream, true);
     };
     if (kind == K_HEAD_ONLY) {   // word scores of a hidden state already computed (seoul.cpp:507-516)
@@ -798,7 +777,7 @@ cudaError_t enqueue_batch(imi_cuda_engine *e, int ncol, bool head, StepKind kind
         p.pro = TP_CUT;
         p.in = e->hid;
         p.in_stride = E;
-        if ((r = prep(p, E)) != cudaSuccess) return r;
+        if ((r = prep(p, E, e->tok)) != cudaSuccess) return r;
         return tc_read(e, e->tok, ncol, TE_HEAD, nullptr, 0);
     }
     for (int il = 0; il < e->n_layer; il++) {
@@ -811,7 +790,7 @@ cudaError_t enqueue_batch(imi_cuda_engine *e, int ncol, bool head, StepKind kind
         p.xout = X0;
         p.wpost = il > 0 ? e->f32(e->layers[il - 1].post_ffn_norm) : nullptr;
         p.wpre = e->f32(L.attn_norm);
-        if ((r = prep(p, E)) != cudaSuccess) return r;
+        if ((r = prep(p, E, L.conv ? L.in_proj : L.qkvg)) != cudaSuccess) return r;
         if ((r = tc_read(e, L.conv ? L.in_proj : L.qkvg, ncol, TE_STORE, e->big, e->big_n)) != cudaSuccess) return r;
         if (L.conv) {
             p = p0;
@@ -821,7 +800,7 @@ cudaError_t enqueue_batch(imi_cuda_engine *e, int ncol, bool head, StepKind kind
             p.conv_w = e->f32(L.conv_w);
             p.conv_layer = L.ci;
             p.ring_conv = kind == K_DECODE;   // distinct conversations: the conv's own input goes to memory here
-            if ((r = prep(p, E)) != cudaSuccess) return r;
+            if ((r = prep(p, E, L.out_proj)) != cudaSuccess) return r;
             if ((r = tc_read(e, L.out_proj, ncol, TE_STORE, e->y, E)) != cudaSuccess) return r;
         } else {
             AttnArgs t = {};
@@ -858,7 +837,7 @@ cudaError_t enqueue_batch(imi_cuda_engine *e, int ncol, bool head, StepKind kind
             p.q8_q = e->qt_q;
             p.q8_d = e->qt_d;
             p.q8_s = e->qt_s;
-            if ((r = prep(p, HD)) != cudaSuccess) return r;
+            if ((r = prep(p, HD, L.o)) != cudaSuccess) return r;
             if ((r = tc_read(e, L.o, ncol, TE_STORE, e->y, E)) != cudaSuccess) return r;
         }
         p = p0;
@@ -874,13 +853,13 @@ cudaError_t enqueue_batch(imi_cuda_engine *e, int ncol, bool head, StepKind kind
             p.ring_src = e->big;
             p.ring_src_stride = e->big_n;
         }
-        if ((r = prep(p, E)) != cudaSuccess) return r;
+        if ((r = prep(p, E, L.gate_up)) != cudaSuccess) return r;
         if ((r = tc_read(e, L.gate_up, ncol, TE_SILU, e->act, e->n_ff)) != cudaSuccess) return r;
         p = p0;
         p.pro = TP_CUT;
         p.in = e->act;
         p.in_stride = e->n_ff;
-        if ((r = prep(p, e->n_ff)) != cudaSuccess) return r;
+        if ((r = prep(p, e->n_ff, L.down)) != cudaSuccess) return r;
         if ((r = tc_read(e, L.down, ncol, TE_STORE, e->fo, E)) != cudaSuccess) return r;
     }
     const LayerRef &last = e->layers.back();
@@ -892,7 +871,7 @@ cudaError_t enqueue_batch(imi_cuda_engine *e, int ncol, bool head, StepKind kind
         p.xin = X1;
         p.wpost = e->f32(last.post_ffn_norm);
         p.wpre = e->f32(e->out_norm);
-        if ((r = prep(p, E)) != cudaSuccess) return r;
+        if ((r = prep(p, E, e->tok)) != cudaSuccess) return r;
         return tc_read(e, e->tok, ncol, TE_HEAD, nullptr, 0);
     }
     FinalArgs fa = {};
@@ -1426,13 +1405,14 @@ imi_cuda_status imi_cuda_bench_matvec(int device, int rows, int cols, int ncol, 
     auto al = [](size_t n) { return (n + 255) / 256 * 256; };
     // more than 8 inputs: the tensor-core read, its operands in the MMA's layout
     const bool tc = ncol > MV_MAX_COLS;
-    const int G = tc_group(ncol), groups = (ncol + G - 1) / G;
-    std::vector<uint16_t> th;
+    const int G = tc_group(rows, ncol, sms), groups = (ncol + G - 1) / G;
+    std::vector<int8_t> th;
     std::vector<float> tx;
     if (tc) tc_operands_host(hq.data(), hd.data(), hs.data(), ncol, cols, G, th, tx);
-    const size_t o_q = (size_t) copies * tstride, o_d = o_q + al(hq.size()), o_s = o_d + al(hd.size() * 4),
+    const size_t tt = tc ? al(tc_tiled_bytes(rows, cols)) : 0, o_t = (size_t) copies * tstride;   // tiled copies
+    const size_t o_q = o_t + (size_t) copies * tt, o_d = o_q + al(hq.size()), o_s = o_d + al(hd.size() * 4),
                  o_o = o_s + al(hs.size() * 4), o_c = o_o + al((size_t) ncol * rows * 4),
-                 o_th = o_c + al(sizeof(Col) * MV_MAX_COLS) + 256, o_tx = o_th + al(th.size() * 2),
+                 o_th = o_c + al(sizeof(Col) * MV_MAX_COLS) + 256, o_tx = o_th + al(th.size()),
                  total = o_tx + al(tx.size() * 4);
     uint8_t *m = nullptr;
     CK(cudaMalloc(&m, total));
@@ -1446,16 +1426,18 @@ imi_cuda_status imi_cuda_bench_matvec(int device, int rows, int cols, int ncol, 
     if (r == cudaSuccess) r = cudaMemcpy(m + o_d, hd.data(), hd.size() * 4, cudaMemcpyHostToDevice);
     if (r == cudaSuccess) r = cudaMemcpy(m + o_s, hs.data(), hs.size() * 4, cudaMemcpyHostToDevice);
     if (r == cudaSuccess) r = cudaMemset(m + o_c, 0, al(sizeof(Col) * MV_MAX_COLS) + 256);
-    if (r == cudaSuccess && tc) r = cudaMemcpy(m + o_th, th.data(), th.size() * 2, cudaMemcpyHostToDevice);
+    if (r == cudaSuccess && tc) r = cudaMemcpy(m + o_th, th.data(), th.size(), cudaMemcpyHostToDevice);
     if (r == cudaSuccess && tc) r = cudaMemcpy(m + o_tx, tx.data(), tx.size() * 4, cudaMemcpyHostToDevice);
     std::vector<TcArgs> tca(tc ? copies : 0);
     for (int c = 0; c < (int) tca.size() && r == cudaSuccess; c++) {
         TcArgs &t = tca[c];
-        r = tc_tensor_maps(t, m + (size_t) c * tstride, rows, row_bytes);
-        t.rows = rows; t.cols = cols; t.row_bytes = row_bytes; t.ncol = ncol; t.G = G; t.groups = groups;
+        t.wt = m + o_t + (size_t) c * tt;
+        r = launch_tc_tile(m + (size_t) c * tstride, rows, cols, row_bytes, m + o_t + (size_t) c * tt, nullptr);
+        t.rows = rows; t.cols = cols; t.ncol = ncol; t.G = G; t.groups = groups;
         t.xh = m + o_th; t.xds = (const float *) (m + o_tx); t.out = (float *) (m + o_o); t.out_stride = rows;
         t.epi = TE_STORE; t.err = (int *) (m + o_c + al(sizeof(Col) * MV_MAX_COLS));
     }
+    if (r == cudaSuccess && tc) r = cudaDeviceSynchronize();   // the tiled copies (default stream) before the reads
     if (r == cudaSuccess) r = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
     // one read of all inputs from table copy k: groups of up to 8 inputs per read of the table (the small-batch
     // kernel), programmatic dependent launches one after another as the engine's step runs them
@@ -1524,7 +1506,9 @@ imi_cuda_status imi_cuda_q4_matmul(int device, const uint8_t *q4, int rows, int 
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) return fail(IMI_E_NODEV, "no CUDA device");
     CK(cudaSetDevice(device));
     CK(prepare_kernels());
-    const int nb = cols / 32, row_bytes = nb * 18, G = tc_group(ncol), groups = (ncol + G - 1) / G;
+    int sms = 148;
+    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+    const int nb = cols / 32, row_bytes = nb * 18, G = tc_group(rows, ncol, sms), groups = (ncol + G - 1) / G;
     std::vector<uint8_t> packed((size_t) rows * row_bytes);
     for (int r = 0; r < rows; r++)
         for (int j = 0; j < nb; j++) {
@@ -1533,18 +1517,19 @@ imi_cuda_status imi_cuda_q4_matmul(int device, const uint8_t *q4, int rows, int 
             memcpy(row + (size_t) nb * 16 + 2 * j, src, 2);
             memcpy(row + 16 * j, src + 2, 16);
         }
-    std::vector<uint16_t> xh;
+    std::vector<int8_t> xh;
     std::vector<float> xds;
     tc_operands_host(xq, xd, xs, ncol, cols, G, xh, xds);
     auto al = [](size_t x) { return (x + 255) / 256 * 256; };
-    const size_t b_w = packed.size(), b_h = xh.size() * 2, b_x = xds.size() * 4, b_o = (size_t) ncol * rows * 4;
+    const size_t b_w = packed.size(), b_h = xh.size(), b_x = xds.size() * 4, b_o = (size_t) ncol * rows * 4;
     uint8_t *m = nullptr;
-    const size_t b_t = (size_t) 7 * TC_TRACE * 8;
-    CK(cudaMalloc(&m, al(b_w) + al(b_h) + al(b_x) + al(b_o) + 256 + b_t));
+    const size_t b_t = (size_t) TC_TRACE_ROWS * TC_TRACE * 8, b_wt = tc_tiled_bytes(rows, cols);
+    CK(cudaMalloc(&m, al(b_w) + al(b_h) + al(b_x) + al(b_o) + 256 + b_t + al(b_wt)));
     uint8_t *dW = m, *dh = m + al(b_w);
     float *dx = (float *) (dh + al(b_h)), *dout = (float *) ((uint8_t *) dx + al(b_x));
     int *derr = (int *) ((uint8_t *) dout + al(b_o));
     unsigned long long *dtr = (unsigned long long *) ((uint8_t *) derr + 256);
+    uint8_t *dwt = (uint8_t *) dtr + b_t;   // the table's tiled copy
     TcArgs a = {};
     if (g_tc_trace_host) {
         a.trace = dtr;
@@ -1554,12 +1539,10 @@ imi_cuda_status imi_cuda_q4_matmul(int device, const uint8_t *q4, int rows, int 
     if (r == cudaSuccess) r = cudaMemcpy(dh, xh.data(), b_h, cudaMemcpyHostToDevice);
     if (r == cudaSuccess) r = cudaMemcpy(dx, xds.data(), b_x, cudaMemcpyHostToDevice);
     if (r == cudaSuccess) r = cudaMemset(derr, 0, 4);
-    if (r == cudaSuccess) r = tc_tensor_maps(a, dW, rows, row_bytes);
+    if (r == cudaSuccess) r = launch_tc_tile(dW, rows, cols, row_bytes, dwt, nullptr);
     if (r == cudaSuccess) {
-        a.rows = rows; a.cols = cols; a.row_bytes = row_bytes; a.ncol = ncol; a.G = G; a.groups = groups;
+        a.wt = dwt; a.rows = rows; a.cols = cols; a.ncol = ncol; a.G = G; a.groups = groups;
         a.xh = dh; a.xds = dx; a.out = dout; a.out_stride = rows; a.epi = TE_STORE; a.err = derr;
-        int sms = 148;
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
         const int units = (rows + TC_M - 1) / TC_M * groups;
         r = launch_tc_table(a, std::min(sms, units), 0, false);
     }

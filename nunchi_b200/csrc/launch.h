@@ -26,6 +26,8 @@ cudaError_t launch_q6k_scores(const uint8_t *W, int rows, int nb, const int8_t *
 // the Q6_K word table inside a step: word scores for ncol inputs, the greedy pick and the end of the step
 cudaError_t launch_q6k_head(const Q6HeadArgs &a, cudaStream_t st, bool pdl);
 int q6k_head_ctas(int rows, int nb, int nc);   // its grid (0: rows too wide)
+// a table's tiled copy for the tensor-core read (tc_table.cuh: k_tc_tile), tc_tiled_bytes(rows, cols) at dst
+cudaError_t launch_tc_tile(const uint8_t *W, int rows, int cols, int row_bytes, uint8_t *dst, cudaStream_t st);
 // the tensor-core batched table read (tc_table.cuh); a.G in {16, 32, 64}
 cudaError_t launch_tc_table(const TcArgs &a, int grid, cudaStream_t st, bool pdl);
 // the conversation records of a step's n columns into 32-byte slots of dst (device)

@@ -1,8 +1,8 @@
 // k_tc_prep: the small math imi's threads repeat before every table read (norms, residual adds, the short conv, the
 // 8-bit cut; seoul.cpp:402-474 and run_batch 562-623), for the tensor-core batched read: one CTA per column (a
 // conversation of a multi-session step or a position of a prefill chunk), imi's float order exactly as the
-// small-batch table kernel's input preparation (table.cuh: table_prologue), the cut codes written as fp16 straight
-// into the batched read's column operand ([group][K/8][G][8]) with the blocks' scales and scale * code sums
+// small-batch table kernel's input preparation (table.cuh: table_prologue), the cut codes written straight into the
+// batched read's column operand ([group][K/16][G][16], 8-bit) with the blocks' scales and scale * code sums
 // ([group][K/32][2][G]). The small-batch kernel prepares every column in every CTA (a few columns); with dozens of
 // columns that work would be repeated on every SM, so here it is done once, spread over the columns.
 #pragma once
@@ -25,7 +25,7 @@ struct TcPrepArgs {
     int ncol, pro;
     int K;                 // length of the prepared vector (the next table's width)
     int G;                 // columns per group of the batched read's operand
-    uint8_t *xh;           // operand out: [group][K/8][G][8] fp16 codes
+    uint8_t *xh;           // operand out: [group][K/16][G][16] 8-bit codes
     float *xds;            // [group][K/32][2][G]: scales, scale * code sums
     const float *in;       // per column: the previous table's output (RESID, FINAL), SiLU output (CUT), b|c|x (CONV)
     int in_stride;
@@ -47,18 +47,12 @@ struct TcPrepArgs {
 };
 
 #if defined(__CUDACC__) && defined(IMI_KERNELS)   // device code: compiled in kernels.cu only
-// the 4 codes of values 4q..4q+3 of column c (packed as cut32_g8 returns them) as fp16 into the operand; the block's
-// scale and scale * code sum by lane 8m of the block's group
+// the 4 codes of values 4q..4q+3 of column c (packed as cut32_g8 returns them: value 4q + u in byte u) into the
+// operand; the block's scale and scale * code sum by lane 8m of the block's group
 __device__ __forceinline__ void tp_put(const TcPrepArgs &a, int c, int q, uint32_t w, float d, int sum, bool act) {
     const int G = a.G, g = c / G, cg = c - g * G, K = a.K;
     if (!act) return;
-    uint32_t h[2];
-#pragma unroll
-    for (int u = 0; u < 2; u++) {
-        const int lo = (int) (int8_t) ((w >> (16 * u)) & 0xff), hi = (int) (int8_t) ((w >> (16 * u + 8)) & 0xff);
-        h[u] = (uint32_t) __half_as_ushort(__int2half_rn(lo)) | ((uint32_t) __half_as_ushort(__int2half_rn(hi)) << 16);
-    }
-    *(uint2 *) (a.xh + ((((size_t) g * (K / 8) + (q >> 1)) * G + cg) * 16 + 8 * (q & 1))) = make_uint2(h[0], h[1]);
+    *(uint32_t *) (a.xh + ((((size_t) g * (K / 16) + (q >> 2)) * G + cg) * 16 + 4 * (q & 3))) = w;
     if ((q & 7) == 0) {
         float *x = a.xds + (((size_t) g * (K / 32) + (q >> 3)) * 2) * G + cg;
         x[0] = d;
@@ -82,20 +76,14 @@ __global__ void __launch_bounds__(TP_THREADS) k_tc_prep(const __grid_constant__ 
     pdl_trigger();
     pdl_wait();
     const Col col = a.cols_d[c];
-    if (pro == TP_Q8) {   // codes made by the producer: repack as fp16, copy the blocks' scale and sum
+    if (pro == TP_Q8) {   // codes made by the producer: repack into the operand, copy the blocks' scale and sum
         const int nq = K / 4;
         for (int q0 = 0; q0 < nq; q0 += TP_THREADS) {
             const int q = q0 + tid;
             if (q < nq) {
                 const uint32_t w = *(const uint32_t *) (a.q8_q + (size_t) c * K + 4 * q);
                 const int G = a.G, g = c / G, cg = c - g * G;
-                uint32_t h[2];
-#pragma unroll
-                for (int u = 0; u < 2; u++) {
-                    const int lo = (int) (int8_t) ((w >> (16 * u)) & 0xff), hi = (int) (int8_t) ((w >> (16 * u + 8)) & 0xff);
-                    h[u] = (uint32_t) __half_as_ushort(__int2half_rn(lo)) | ((uint32_t) __half_as_ushort(__int2half_rn(hi)) << 16);
-                }
-                *(uint2 *) (a.xh + ((((size_t) g * (K / 8) + (q >> 1)) * G + cg) * 16 + 8 * (q & 1))) = make_uint2(h[0], h[1]);
+                *(uint32_t *) (a.xh + ((((size_t) g * (K / 16) + (q >> 2)) * G + cg) * 16 + 4 * (q & 3))) = w;
                 if ((q & 7) == 0) {
                     float *x = a.xds + (((size_t) g * (K / 32) + (q >> 3)) * 2) * G + cg;
                     x[0] = a.q8_d[(size_t) c * (K / 32) + (q >> 3)];

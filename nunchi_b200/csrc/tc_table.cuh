@@ -2,34 +2,36 @@
 // read of imi_q8b + imi_q4_group_batch (imi/core/tables.cpp:405-477), used where a step reads a table for dozens of
 // conversations or prefill positions at once.
 //
-// The exact numbers allow tensor cores because imi's per-block integer dots are exact: for a 32-value block j the dot
-// sum_i code_ri * x_ci of 4-bit codes (0..15) and 8-bit input codes (-127..127) is an integer below 2^16 in
-// magnitude, which an fp16 x fp16 -> fp32 tensor-core product computes exactly (every product and every partial sum is
-// an integer that fp32 holds exactly). imi scales each block's dot before it accumulates, so the MMA must not sum over
-// blocks: every block gets its own TMEM columns (D_j[row][col] = dot of block j), and the epilogue runs imi's two
-// float chains per (row, column) in block order (group_avx2<false>, tables.cpp:127-143):
+// The tensor cores compute imi's per-block integer dots exactly: for a 32-value block j the dot sum_i code_ri * x_ci
+// of 4-bit codes (0..15) and 8-bit input codes (-127..127) is an integer below 2^16 in magnitude, and the int8 MMA
+// (kind::i8, both operands s8, int32 accumulator) forms it with one instruction per block (K = 32). imi scales each
+// block's dot before it accumulates, so the MMA must not sum over blocks: every block gets its own TMEM columns
+// (D_j[row][col] = dot of block j), and the epilogue runs imi's two float chains per (row, column) in block order
+// (group_avx2<false>, tables.cpp:127-143):
 //     acc = fma(dot_j, d_rj * dx_cj, acc),  cor = fma(d_rj, s_cj, cor),  out = acc - 8 cor (one rounding).
 //
-// Work unit: a tile of 128 rows x a group of G columns (G = 16, 32 or 64). K is read in stages of 128 values (4
-// blocks). Warp roles (one CTA per SM, persistent over units):
-//   warp 0      producer: per stage one barrier for four copies into a ring slot: TMA of the tile's 4-bit codes
-//               (128 rows x 80 bytes, 64 used: a padded shared-memory row stride keeps the unpack's reads free of
-//               bank conflicts) and fp16 scales, bulk copies of the columns' fp16 codes (already in the MMA's K-major
-//               layout, read by the MMA where they land) and of their scales and sums; it waits only for the slot, so
-//               weight bytes stream several stages ahead of the math;
-//   warp 1      TMEM owner (512 columns) and MMA issuer: per block two tcgen05.mma kind::f16 (K = 16 each) into the
-//               block's own TMEM columns; the 4 blocks of a stage fill one TMEM stage slot, committed to its barrier
-//               once (a commit-to-wait hand-off costs about 0.3 us, so it is made per stage, not per block);
-//   warps 2-5   unpack: 4-bit codes -> fp16 in the MMA's canonical K-major layout (8-row x 16-byte core matrices),
-//               the rows' block scales and the columns' scales and sums handed to the epilogue;
-//   warps 6..   epilogue, 4 per 16 columns: per TMEM slot a tcgen05.ld of the block's dots (warp w reads lanes
-//               32 (w % 4) ..), the two fma chains for 16 columns per thread (packed f32x2 operations, each lane rounded
-//               as imi's scalar chain), the result stored at the end of the unit.
+// The weights come from the table's tiled copy (made once at load by k_tc_tile): for every tile of 128 rows and stage
+// of 128 values one contiguous TC_WSTAGE-byte block holding the codes already as 8-bit values in the MMA's canonical
+// K-major layout (8-row x 16-byte core matrices; chunk 2p of block p holds its values 0..15, chunk 2p+1 its values
+// 16..31) and then the rows' fp16 block scales. A stage is thus one bulk copy that the MMA reads where it lands (a
+// row-wise tensor copy of the row-major table moved only ~14 GB/s per SM: 128 separate 80-byte rows per stage).
+//
+// Work unit: a tile of 128 rows x a group of G columns (G = 16, 32 or 64). Warp roles (one CTA per SM, persistent
+// over units):
+//   warp 0      producer: per stage one barrier for three bulk copies into a ring slot (the tile's weight stage, the
+//               columns' 8-bit codes in the MMA's K-major layout, their scales and sums); it waits only for the slot,
+//               so bytes stream up to the ring's depth ahead of the math;
+//   warp 1      TMEM owner (512 columns) and MMA issuer: per block one tcgen05.mma kind::i8 (K = 32) into the block's
+//               own TMEM columns; the 4 blocks of a stage fill one TMEM stage slot, committed to its barrier once (a
+//               commit-to-wait hand-off costs about 0.3 us, so it is made per stage, not per block);
+//   warps 2..   epilogue, 4 per 8 or 16 columns (tc_ch): per TMEM slot tcgen05.ld of the blocks' dots, up to 4
+//               blocks per wait (warp w reads lanes 32 (w % 4) ..), converted to float exactly, the rows' scales and
+//               the columns' scales and sums read from the ring slot, the two fma chains per column (packed f32x2
+//               operations, each lane rounded as imi's scalar chain), the result stored at the end of the unit; the
+//               slot is released when the MMAs and every epilogue warp are done with it.
 // Every wait on an mbarrier is bounded (about one second); a wait that gives up sets the error flag, the CTA stops
 // issuing work, waits (bounded) for its copies and MMAs in flight, frees its TMEM and returns.
 #pragma once
-#include <cuda.h>
-
 #include "common.cuh"
 
 namespace imi {
@@ -37,12 +39,18 @@ namespace imi {
 constexpr int TC_M = 128;              // rows per tile (the MMA's M; TMEM lanes)
 constexpr int TC_KS = 128;             // values per K stage
 constexpr int TC_BPS = TC_KS / 32;     // blocks per stage
-constexpr int TC_RAW_W = 80;           // bytes per row of a raw code stage in shared memory (64 used)
-constexpr int TC_NR = 4, TC_NA = 2, TC_NE = 4;   // rings: copied stages, unpacked weight stages, epilogue stages
-constexpr int TC_WARP_PROD = 0, TC_WARP_MMA = 1, TC_WARP_UNP = 2, TC_WARP_EPI = 6;
-constexpr int TC_CH = 16;   // columns per epilogue thread
-// epilogue warps: 4 per 16 columns (one per TMEM lane quarter), so each thread runs 16 columns' chains
-__host__ __device__ constexpr int tc_epi_warps(int G) { return 4 * (G / TC_CH); }
+// bytes of one (tile, stage) block of a table's tiled copy: 8-bit codes [TC_KS / 16][TC_M][16], fp16 scales [TC_M][4]
+constexpr int TC_WCODES = TC_KS * TC_M, TC_WSTAGE = TC_WCODES + TC_M * TC_BPS * 2;
+// ring of copied stages: as many as shared memory holds, TC_NR_MIN..TC_NR_MAX (a copy takes 1-2 us to land, so a
+// narrow group's unit, whose stages are short, needs more of them in flight)
+constexpr int TC_NR_MIN = 4, TC_NR_MAX = 12;
+constexpr int TC_SMEM = 220 * 1024;   // dynamic shared memory of one CTA at most
+constexpr int TC_WARP_PROD = 0, TC_WARP_MMA = 1, TC_WARP_EPI = 2;
+// columns per epilogue thread: 8 in groups of 16 or 32 columns (more warps to hide the TMEM and shared-memory
+// latencies of the chains), 16 in groups of 64 (the thread count stays within one CTA's)
+__host__ __device__ constexpr int tc_ch(int G) { return G >= 64 ? 16 : 8; }
+// epilogue warps: 4 per tc_ch(G) columns (one per TMEM lane quarter)
+__host__ __device__ constexpr int tc_epi_warps(int G) { return 4 * (G / tc_ch(G)); }
 __host__ __device__ constexpr int tc_threads(int G) { return 32 * (TC_WARP_EPI + tc_epi_warps(G)); }
 constexpr int TC_TMEM_COLS = 512;
 
@@ -52,11 +60,10 @@ constexpr int TC_TMEM_COLS = 512;
 enum TcEpi : int { TE_STORE = 0, TE_SILU = 1, TE_HEAD = 2 };
 
 struct TcArgs {
-    CUtensorMap tm_codes;     // the table's rows as bytes [rows][row_bytes], box {TC_RAW_W, 128}
-    CUtensorMap tm_scales;    // the same rows, box {16, 128} (8 fp16 scales of two stages)
-    int rows, cols, row_bytes;
+    const uint8_t *wt;        // the table's tiled copy: [tiles][cols / TC_KS] blocks of TC_WSTAGE bytes (k_tc_tile)
+    int rows, cols;
     int ncol, G, groups;      // columns, columns per group, groups (units = tiles * groups)
-    const uint8_t *xh;        // the columns' 8-bit codes as fp16, [group][cols / 8][G][8]
+    const uint8_t *xh;        // the columns' 8-bit codes, [group][cols / 16][G][16]
     const float *xds;         // per group and block: G scales then G scale * code sums, [group][cols / 32][2][G]
     float *out;               // out[c * out_stride + row]
     int out_stride;
@@ -64,59 +71,93 @@ struct TcArgs {
     const Col *cols_d;        // TE_HEAD: the columns (logits, conversation records)
     unsigned *done;           // TE_HEAD: CTAs finished (the last one picks and resets it)
     int *err;
-    unsigned long long *trace;   // optional (diagnostics): CTA 0's timeline, [7][64] ns (see k_tc_table)
+    unsigned long long *trace;   // optional (diagnostics): CTA 0's timeline, [TC_TRACE_ROWS][64] ns (imi_cuda_trace_tc)
 };
-constexpr int TC_TRACE = 64;
+constexpr int TC_TRACE = 64, TC_TRACE_ROWS = 9;
+
+// bytes of a table's tiled copy
+__host__ __device__ inline size_t tc_tiled_bytes(int rows, int cols) {
+    return (size_t) ((rows + TC_M - 1) / TC_M) * (cols / TC_KS) * TC_WSTAGE;
+}
 
 struct TcPlan {
-    int raw, a, epi, bar, tptr, total;
-    int raw_bytes, raw_stride, b_off, x_off, a_bytes, b_bytes, xds_bytes, epi_bytes, nslot;   // nslot: TMEM stage slots
+    int raw, bar, tptr, total;
+    int raw_bytes, raw_stride, b_off, x_off, b_bytes, xds_bytes, nslot;   // nslot: TMEM stage slots
+    int nr;   // copied stages in flight
 };
-// a copied stage: [codes 128 x TC_RAW_W | scales 128 x 16 | columns' fp16 codes | columns' scales and sums]
+// a copied stage: [the weight stage (TC_WSTAGE) | the columns' 8-bit codes | the columns' scales and sums]
 __host__ __device__ inline TcPlan tc_plan(int G) {
     TcPlan p;
-    p.b_bytes = (TC_KS / 8) * G * 16;                     // fp16 codes of G columns
+    p.b_bytes = (TC_KS / 16) * G * 16;                    // 8-bit codes of G columns, 8 chunks of 16
     p.xds_bytes = TC_BPS * 2 * G * 4;
-    p.b_off = TC_M * TC_RAW_W + TC_M * 16;
+    p.b_off = TC_WSTAGE;
     p.x_off = p.b_off + p.b_bytes;
     p.raw_bytes = p.x_off + p.xds_bytes;
     p.raw_stride = align_up(p.raw_bytes, 128);
-    p.a_bytes = (TC_KS / 8) * TC_M * 16;                  // fp16 codes of 128 rows, 16 chunks of 8 values
-    p.epi_bytes = align_up(p.xds_bytes + TC_M * 8, 128);  // the columns' scales and sums + the rows' 4 block scales
     p.nslot = TC_TMEM_COLS / (G * TC_BPS);               // TMEM stage slots: a stage's 4 blocks, G columns each
+    const int fixed = 8 * (2 * TC_NR_MAX + 2 * 32 + 1) + 16 + 256;
+    p.nr = (TC_SMEM - fixed) / p.raw_stride;
+    p.nr = p.nr < TC_NR_MIN ? TC_NR_MIN : p.nr > TC_NR_MAX ? TC_NR_MAX : p.nr;
     int o = 0;
-    p.raw = o;  o += TC_NR * p.raw_stride;
-    p.a = o;    o += TC_NA * p.a_bytes;
-    p.epi = o;  o += TC_NE * p.epi_bytes;
-    p.bar = o;  o += 8 * (2 * TC_NR + 2 * TC_NA + 2 * TC_NE + 2 * 32 + 1);
+    p.raw = o;  o += p.nr * p.raw_stride;
+    p.bar = o;  o += 8 * (2 * TC_NR_MAX + 2 * 32 + 1);
     p.tptr = o; o += 16;
     p.total = align_up(o, 128) + 128;                     // + slack to align the base to 128 bytes
     return p;
 }
 
 #if defined(__CUDACC__) && defined(IMI_KERNELS)   // device code: compiled in kernels.cu only
-// ---- tcgen05 / TMA wrappers ----
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, int x, int y, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-        ::"r"(smem_u32(dst)), "l"(tm), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
+// the tiled copy of a table (engine row layout: [cols / 2 code bytes | cols / 32 fp16 scales] per row) for the
+// tensor-core read: for tile t and stage s, at ((t * (cols / TC_KS)) + s) * TC_WSTAGE, the 8-bit codes
+// [TC_KS / 16][TC_M][16] (chunk 2p: the low nibbles of block p's 16 code bytes = its values 0..15; chunk 2p + 1: the
+// high nibbles = values 16..31) then the rows' 4 fp16 block scales [TC_M][4]; rows past the table's end are zeros.
+// One thread per (tile, stage, row).
+__global__ void k_tc_tile(const uint8_t *W, int rows, int cols, int row_bytes, uint8_t *dst) {
+    const int nst = cols / TC_KS, tiles = (rows + TC_M - 1) / TC_M;
+    const long long n = (long long) tiles * nst * TC_M;
+    constexpr uint32_t LO = 0x0F0F0F0Fu;
+    for (long long idx = blockIdx.x * (long long) blockDim.x + threadIdx.x; idx < n;
+         idx += (long long) gridDim.x * blockDim.x) {
+        const int row = (int) (idx % TC_M);
+        const long long ts = idx / TC_M;
+        const int s = (int) (ts % nst), grow = (int) (ts / nst) * TC_M + row;
+        uint8_t *o = dst + ts * TC_WSTAGE;
+        uint4 c[TC_BPS];
+        uint2 sc = make_uint2(0u, 0u);
+#pragma unroll
+        for (int p = 0; p < TC_BPS; p++) c[p] = make_uint4(0u, 0u, 0u, 0u);
+        if (grow < rows) {
+            const uint8_t *src = W + (size_t) grow * row_bytes;
+#pragma unroll
+            for (int p = 0; p < TC_BPS; p++) c[p] = *(const uint4 *) (src + 16 * (TC_BPS * s + p));
+            sc = *(const uint2 *) (src + cols / 2 + 2 * TC_BPS * s);
+        }
+#pragma unroll
+        for (int p = 0; p < TC_BPS; p++) {
+            *(uint4 *) (o + ((2 * p) * TC_M + row) * 16) = make_uint4(c[p].x & LO, c[p].y & LO, c[p].z & LO, c[p].w & LO);
+            *(uint4 *) (o + ((2 * p + 1) * TC_M + row) * 16) =
+                make_uint4((c[p].x >> 4) & LO, (c[p].y >> 4) & LO, (c[p].z >> 4) & LO, (c[p].w >> 4) & LO);
+        }
+        *(uint2 *) (o + TC_WCODES + row * 8) = sc;
+    }
 }
-__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
-}
+
+// ---- tcgen05 wrappers ----
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_commit(uint64_t *b) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(b))
                  : "memory");
 }
-// D[tmem] (+)= A[smem] . B[smem]^T, kind::f16 (fp16 inputs, fp32 accumulate)
-__device__ __forceinline__ void tc_mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, int acc) {
+__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+// D[tmem] = A[smem] . B[smem]^T, kind::i8 (s8 inputs, s32 result; K = 32), not accumulated
+__device__ __forceinline__ void tc_mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
-        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(0)
         : "memory");
 }
 // shared-memory matrix descriptor, K-major, no swizzle: 8-row x 16-byte core matrices, lbo between the two 16-byte K
@@ -126,9 +167,10 @@ __device__ __forceinline__ uint64_t tc_desc(uint32_t saddr, uint32_t lbo, uint32
     return (uint64_t) ((saddr >> 4) & 0x3FFF) | ((uint64_t) ((lbo >> 4) & 0x3FFF) << 16) |
            ((uint64_t) ((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46);
 }
-// instruction descriptor: D f32 (bit 4), A and B f16 (format 0), both K-major, N >> 3 at bit 17, M >> 4 at bit 24
-__host__ __device__ constexpr uint32_t tc_idesc_f16(int n, int m) {
-    return (1u << 4) | ((uint32_t) (n >> 3) << 17) | ((uint32_t) (m >> 4) << 24);
+// instruction descriptor of kind::i8: D s32 (2 at bit 4), A and B signed 8-bit (1 at bits 7 and 10), both K-major,
+// N >> 3 at bit 17, M >> 4 at bit 24
+__host__ __device__ constexpr uint32_t tc_idesc_i8(int n, int m) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t) (n >> 3) << 17) | ((uint32_t) (m >> 4) << 24);
 }
 
 template <int N>
@@ -159,31 +201,26 @@ __device__ __forceinline__ void tmem_ld<32>(uint32_t t, uint32_t (&v)[32]) {
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// 8 values (the low or the high nibbles of the 8 code bytes w0, w1) as fp16: every nibble spread into a 16-bit lane
-// under the byte 0x64, i.e. 0x6400 | v = 1024 + v in fp16, then minus 1024 (exact)
-__device__ __forceinline__ uint32_t h2sub1024(uint32_t m) {
-    const __half2 r = __hsub2(*reinterpret_cast<const __half2 *>(&m), __half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400)));
-    return *reinterpret_cast<const uint32_t *>(&r);
-}
-__device__ __forceinline__ uint4 nib8(uint32_t w0, uint32_t w1, int hi) {
-    const uint32_t n0 = (hi ? w0 >> 4 : w0) & 0x0F0F0F0Fu, n1 = (hi ? w1 >> 4 : w1) & 0x0F0F0F0Fu;
-    return make_uint4(h2sub1024(__byte_perm(n0, 0x64646464u, 0x7170)), h2sub1024(__byte_perm(n0, 0x64646464u, 0x7372)),
-                      h2sub1024(__byte_perm(n1, 0x64646464u, 0x7170)), h2sub1024(__byte_perm(n1, 0x64646464u, 0x7372)));
+// an int32 dot below 2^22 in magnitude as float, exactly: its bits added to those of 1.5 * 2^23 make the float
+// 1.5 * 2^23 + dot (an integer in [2^23, 2^24)), from which 1.5 * 2^23 is subtracted without rounding
+__device__ __forceinline__ float2 dots_f2(uint32_t a, uint32_t b) {
+    const float2 v = make_float2(__uint_as_float(a + 0x4B400000u), __uint_as_float(b + 0x4B400000u));
+    return __fadd2_rn(v, make_float2(-12582912.0f, -12582912.0f));
 }
 
 template <int G>
 __global__ void __launch_bounds__(tc_threads(G), 1) k_tc_table(const __grid_constant__ TcArgs a) {
     extern __shared__ __align__(128) uint8_t smt[];
-    constexpr int CH = TC_CH, NEW = tc_epi_warps(G);
+    // NLD: blocks loaded per TMEM wait (4 at 8 columns a thread; 1 at 16, where the registers of a CTA this wide
+    // hold one block's dots beside the chains)
+    constexpr int CH = tc_ch(G), NEW = tc_epi_warps(G), NLD = CH == 8 ? 4 : 1;
     const TcPlan P = tc_plan(G);
     uint8_t *sm = smt + ((128 - (smem_u32(smt) & 127)) & 127);
     uint64_t *bars = (uint64_t *) (sm + P.bar);
-    // raw_full: the four copies of a stage landed (1 arrival + bytes); raw_empty: unpacked (4 warps) and read by the
-    // MMAs (1 commit); a_full / e_full: the 4 unpack warps; a_empty, tm_full, fin: tcgen05.commit; e_empty, tm_empty:
-    // the epilogue warps
-    uint64_t *raw_full = bars, *raw_empty = raw_full + TC_NR, *a_full = raw_empty + TC_NR, *a_empty = a_full + TC_NA,
-             *e_full = a_empty + TC_NA, *e_empty = e_full + TC_NE, *tm_full = e_empty + TC_NE, *tm_empty = tm_full + 32,
-             *fin = tm_empty + 32;
+    // raw_full: the copies of a stage landed (1 arrival + bytes); raw_empty: read by the MMAs (1 commit) and by every
+    // epilogue warp; tm_full, fin: tcgen05.commit; tm_empty: the epilogue warps
+    uint64_t *raw_full = bars, *raw_empty = raw_full + TC_NR_MAX, *tm_full = raw_empty + TC_NR_MAX,
+             *tm_empty = tm_full + 32, *fin = tm_empty + 32;
     uint32_t *tptr = (uint32_t *) (sm + P.tptr);
     __shared__ int abort_flag, last_cta;
     __shared__ unsigned long long best[256];   // TE_HEAD: this CTA's best key per column
@@ -191,12 +228,10 @@ __global__ void __launch_bounds__(tc_threads(G), 1) k_tc_table(const __grid_cons
     if (a.epi == TE_HEAD)
         for (int k = tid; k < 256; k += blockDim.x) best[k] = 0ull;
     const int K = a.cols, nst = K / TC_KS, tiles = (a.rows + TC_M - 1) / TC_M, units = tiles * a.groups;
-    const int nslot = P.nslot;
+    const int nslot = P.nslot, NR = P.nr;
 
     if (tid == 0) {
-        for (int i = 0; i < TC_NR; i++) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 5); }
-        for (int i = 0; i < TC_NA; i++) { mbar_init(&a_full[i], 4); mbar_init(&a_empty[i], 1); }
-        for (int i = 0; i < TC_NE; i++) { mbar_init(&e_full[i], 4); mbar_init(&e_empty[i], NEW); }
+        for (int i = 0; i < NR; i++) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 1 + NEW); }
         for (int i = 0; i < nslot; i++) { mbar_init(&tm_full[i], 1); mbar_init(&tm_empty[i], NEW); }
         mbar_init(fin, 1);
         abort_flag = 0;
@@ -233,90 +268,50 @@ __global__ void __launch_bounds__(tc_threads(G), 1) k_tc_table(const __grid_cons
             bool ok = true;
             for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
                 const int tile = u / a.groups, g = u - tile * a.groups;
-                const uint8_t *xh = a.xh + (size_t) g * (K / 8) * G * 16;
+                const uint8_t *wt = a.wt + (size_t) tile * nst * TC_WSTAGE;
+                const uint8_t *xh = a.xh + (size_t) g * (K / 16) * G * 16;
                 const float *xds = a.xds + (size_t) g * (K / 32) * 2 * G;
                 for (int s = 0; s < nst; s++, i++) {
-                    const int r = i % TC_NR;
-                    if (!(ok = wait(&raw_empty[r], ((i / TC_NR) & 1) ^ 1))) break;
+                    const int r = i % NR;
+                    if (!(ok = wait(&raw_empty[r], ((i / NR) & 1) ^ 1))) break;
                     uint8_t *raw = raw_at(r);
                     mbar_expect_tx(&raw_full[r], (uint32_t) P.raw_bytes);
-                    tma_load_2d(raw, &a.tm_codes, s * (TC_KS / 2), tile * TC_M, &raw_full[r]);
-                    tma_load_2d(raw + TC_M * TC_RAW_W, &a.tm_scales, K / 2 + 16 * (s / 2), tile * TC_M, &raw_full[r]);
-                    bulk_g2s(raw + P.b_off, xh + (size_t) s * (TC_KS / 8) * G * 16, (uint32_t) P.b_bytes, &raw_full[r]);
+                    bulk_g2s(raw, wt + (size_t) s * TC_WSTAGE, (uint32_t) TC_WSTAGE, &raw_full[r]);
+                    bulk_g2s(raw + P.b_off, xh + (size_t) s * (TC_KS / 16) * G * 16, (uint32_t) P.b_bytes, &raw_full[r]);
                     bulk_g2s(raw + P.x_off, xds + (size_t) s * TC_BPS * 2 * G, (uint32_t) P.xds_bytes, &raw_full[r]);
                     if (a.trace && blockIdx.x == 0 && i < TC_TRACE) a.trace[0 * TC_TRACE + i] = global_ns();
                 }
             }
             if (!ok)   // the copies in flight land before the CTA exits (bounded waits on the last stages issued)
-                for (int k = i > TC_NR ? i - TC_NR : 0; k < i; k++) mbar_wait(&raw_full[k % TC_NR], (k / TC_NR) & 1);
+                for (int k = i > NR ? i - NR : 0; k < i; k++) mbar_wait(&raw_full[k % NR], (k / NR) & 1);
         }
     } else if (warp == TC_WARP_MMA) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            const uint32_t idesc = tc_idesc_f16(G, TC_M);
+            const uint32_t idesc = tc_idesc_i8(G, TC_M);
             int i = 0, b = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
                 for (int s = 0; s < nst && ok; s++, i++) {
-                    const int r = i % TC_NR, o = i % TC_NA;
-                    if (!(ok = wait(&a_full[o], (i / TC_NA) & 1) && wait(&raw_full[r], (i / TC_NR) & 1))) break;
-                    tc_fence_after();
-                    const uint32_t abase = smem_u32(sm + P.a + o * P.a_bytes), bbase = smem_u32(raw_at(r) + P.b_off);
-                    const int slot = i % nslot;
+                    const int r = i % NR, slot = i % nslot;
+                    if (!(ok = wait(&raw_full[r], (i / NR) & 1))) break;
+                    if (a.trace && blockIdx.x == 0 && i < TC_TRACE) a.trace[7 * TC_TRACE + i] = global_ns();
                     if (!(ok = wait(&tm_empty[slot], ((i / nslot) & 1) ^ 1))) break;
+                    if (a.trace && blockIdx.x == 0 && i < TC_TRACE) a.trace[8 * TC_TRACE + i] = global_ns();
                     tc_fence_after();
-                    for (int jj = 0; jj < TC_BPS; jj++, b++) {
-#pragma unroll
-                        for (int h = 0; h < 2; h++) {   // K = 16 per MMA: chunks 4jj + 2h, 4jj + 2h + 1
-                            const int q = 4 * jj + 2 * h;
-                            tc_mma_f16(tmem + (slot * TC_BPS + jj) * G, tc_desc(abase + q * TC_M * 16, TC_M * 16, 128),
-                                       tc_desc(bbase + q * G * 16, G * 16, 128), idesc, h);
-                        }
+                    const uint32_t abase = smem_u32(raw_at(r)), bbase = abase + P.b_off;
+                    for (int jj = 0; jj < TC_BPS; jj++, b++) {   // block jj: 16-byte chunks 2jj, 2jj + 1
+                        tc_mma_i8(tmem + (slot * TC_BPS + jj) * G, tc_desc(abase + 2 * jj * TC_M * 16, TC_M * 16, 128),
+                                  tc_desc(bbase + 2 * jj * G * 16, G * 16, 128), idesc);
                         if (a.trace && blockIdx.x == 0 && b < TC_TRACE) a.trace[3 * TC_TRACE + b] = global_ns();
                     }
                     tc_commit(&tm_full[slot]);
-                    tc_commit(&a_empty[o]);
                     tc_commit(&raw_empty[r]);
                 }
             }
             if (!ok) {   // the MMAs issued complete before TMEM is freed
                 tc_commit(fin);
                 mbar_wait(fin, 0);
-            }
-        }
-    } else if (warp < TC_WARP_EPI) {
-        // ---------------- unpack: 4-bit codes -> fp16, canonical K-major layout ----------------
-        const int row = tid - TC_WARP_UNP * 32;   // 0..127: this thread's row of the tile
-        int i = 0;
-        bool ok = true;
-        for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-            for (int s = 0; s < nst; s++, i++) {
-                const int r = i % TC_NR, o = i % TC_NA, e = i % TC_NE;
-                if (!(ok = wait(&raw_full[r], (i / TC_NR) & 1) && wait(&a_empty[o], ((i / TC_NA) & 1) ^ 1) &&
-                           wait(&e_empty[e], ((i / TC_NE) & 1) ^ 1)))
-                    break;
-                if (a.trace && blockIdx.x == 0 && row == 0 && i < TC_TRACE) a.trace[1 * TC_TRACE + i] = global_ns();
-                const uint8_t *raw = raw_at(r);
-                uint8_t *A = sm + P.a + o * P.a_bytes, *ep = sm + P.epi + e * P.epi_bytes;
-#pragma unroll
-                for (int p = 0; p < TC_BPS; p++) {   // block p of the stage: 16 code bytes -> 4 chunks of 8 fp16
-                    const uint4 c = *(const uint4 *) (raw + row * TC_RAW_W + 16 * p);
-                    *(uint4 *) (A + ((4 * p + 0) * TC_M + row) * 16) = nib8(c.x, c.y, 0);   // values 0..7
-                    *(uint4 *) (A + ((4 * p + 1) * TC_M + row) * 16) = nib8(c.z, c.w, 0);   // 8..15
-                    *(uint4 *) (A + ((4 * p + 2) * TC_M + row) * 16) = nib8(c.x, c.y, 1);   // 16..23
-                    *(uint4 *) (A + ((4 * p + 3) * TC_M + row) * 16) = nib8(c.z, c.w, 1);   // 24..31
-                }
-                // the row's 4 block scales of this stage (8 bytes of the 16-byte scale box), the columns' scales/sums
-                *(uint2 *) (ep + P.xds_bytes + row * 8) = *(const uint2 *) (raw + TC_M * TC_RAW_W + row * 16 + 8 * (s & 1));
-                if (row < P.xds_bytes / 16) *(uint4 *) (ep + 16 * row) = *(const uint4 *) (raw + P.x_off + 16 * row);
-                fence_proxy_async();
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&a_full[o]);
-                    mbar_arrive(&raw_empty[r]);
-                    mbar_arrive(&e_full[e]);
-                }
-                if (a.trace && blockIdx.x == 0 && row == 0 && i < TC_TRACE) a.trace[2 * TC_TRACE + i] = global_ns();
             }
         }
     } else {
@@ -331,40 +326,50 @@ __global__ void __launch_bounds__(tc_threads(G), 1) k_tc_table(const __grid_cons
 #pragma unroll
             for (int k = 0; k < CH / 2; k++) acc[k] = cor[k] = make_float2(0.0f, 0.0f);
             for (int s = 0; s < nst && ok; s++, i++) {
-                const int e = i % TC_NE, slot = i % nslot;
-                if (!(ok = wait(&e_full[e], (i / TC_NE) & 1) && wait(&tm_full[slot], (i / nslot) & 1))) break;
+                const int r = i % NR, slot = i % nslot;
+                // the slot's copies (this warp reads their scales) and the stage's MMAs
+                if (!(ok = wait(&raw_full[r], (i / NR) & 1) && wait(&tm_full[slot], (i / nslot) & 1))) break;
                 tc_fence_after();
-                const uint8_t *ep = sm + P.epi + e * P.epi_bytes;
-                const uint16_t *dsc = (const uint16_t *) (ep + P.xds_bytes + row * 8);
-                for (int jj = 0; jj < TC_BPS; jj++, b++) {
+                const uint8_t *ep = raw_at(r);
+                const uint2 dq = *(const uint2 *) (ep + TC_WCODES + row * 8);   // the row's 4 block scales
+                const uint16_t dsc[4] = { (uint16_t) (dq.x & 0xffff), (uint16_t) (dq.x >> 16), (uint16_t) (dq.y & 0xffff),
+                                          (uint16_t) (dq.y >> 16) };
+                const float *xds = (const float *) (ep + P.x_off);
+                for (int j0 = 0; j0 < TC_BPS; j0 += NLD) {
                     const bool tr = a.trace && blockIdx.x == 0 && warp == TC_WARP_EPI && lane == 0 && b < TC_TRACE;
                     if (tr) a.trace[4 * TC_TRACE + b] = global_ns();
-                    uint32_t f[CH];
-                    tmem_ld<CH>(tl + (slot * TC_BPS + jj) * G, f);
-                    tmem_ld_wait();
-                    if (tr) a.trace[6 * TC_TRACE + b] = global_ns() + (unsigned long long) (f[0] & 0);
-                    const float d = h2f(dsc[jj]);
-                    const float2 dd = make_float2(d, d);
-                    const float4 *xd = (const float4 *) ((const float *) ep + jj * 2 * G + h * CH),
-                                 *xs = (const float4 *) ((const float *) ep + jj * 2 * G + G + h * CH);
+                    uint32_t f[NLD][CH];
 #pragma unroll
-                    for (int k = 0; k < CH / 4; k++) {   // 4 columns per pair of 16-byte loads
-                        const float4 dx = xd[k], sx = xs[k];
-                        const float2 f0 = make_float2(__uint_as_float(f[4 * k]), __uint_as_float(f[4 * k + 1])),
-                                     f1 = make_float2(__uint_as_float(f[4 * k + 2]), __uint_as_float(f[4 * k + 3]));
-                        acc[2 * k] = __ffma2_rn(f0, __fmul2_rn(dd, make_float2(dx.x, dx.y)), acc[2 * k]);
-                        acc[2 * k + 1] = __ffma2_rn(f1, __fmul2_rn(dd, make_float2(dx.z, dx.w)), acc[2 * k + 1]);
-                        cor[2 * k] = __ffma2_rn(dd, make_float2(sx.x, sx.y), cor[2 * k]);
-                        cor[2 * k + 1] = __ffma2_rn(dd, make_float2(sx.z, sx.w), cor[2 * k + 1]);
+                    for (int u2 = 0; u2 < NLD; u2++) tmem_ld<CH>(tl + (slot * TC_BPS + j0 + u2) * G, f[u2]);
+                    tmem_ld_wait();
+                    if (tr) a.trace[6 * TC_TRACE + b] = global_ns() + (unsigned long long) (f[0][0] & 0);
+#pragma unroll
+                    for (int u2 = 0; u2 < NLD; u2++, b++) {
+                        const int jj = j0 + u2;
+                        const float d = h2f(dsc[jj]);
+                        const float2 dd = make_float2(d, d);
+                        const float4 *xd = (const float4 *) (xds + jj * 2 * G + h * CH),
+                                     *xs = (const float4 *) (xds + jj * 2 * G + G + h * CH);
+#pragma unroll
+                        for (int k = 0; k < CH / 4; k++) {   // 4 columns per pair of 16-byte loads
+                            const float4 dx = xd[k], sx = xs[k];
+                            const float2 f0 = dots_f2(f[u2][4 * k], f[u2][4 * k + 1]),
+                                         f1 = dots_f2(f[u2][4 * k + 2], f[u2][4 * k + 3]);
+                            acc[2 * k] = __ffma2_rn(f0, __fmul2_rn(dd, make_float2(dx.x, dx.y)), acc[2 * k]);
+                            acc[2 * k + 1] = __ffma2_rn(f1, __fmul2_rn(dd, make_float2(dx.z, dx.w)), acc[2 * k + 1]);
+                            cor[2 * k] = __ffma2_rn(dd, make_float2(sx.x, sx.y), cor[2 * k]);
+                            cor[2 * k + 1] = __ffma2_rn(dd, make_float2(sx.z, sx.w), cor[2 * k + 1]);
+                        }
                     }
-                    if (tr) a.trace[5 * TC_TRACE + b] = global_ns() + (unsigned long long) (__float_as_uint(acc[0].x) & 0);
+                    if (tr) a.trace[5 * TC_TRACE + b - NLD] = global_ns() + (unsigned long long) (__float_as_uint(acc[0].x) & 0);
                 }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
                     mbar_arrive(&tm_empty[slot]);
-                    mbar_arrive(&e_empty[e]);
+                    mbar_arrive(&raw_empty[r]);
                 }
+                if (a.trace && blockIdx.x == 0 && lane == 0 && i < TC_TRACE) atomicMax(&a.trace[2 * TC_TRACE + i], global_ns());
             }
             if (!ok) break;
             const int grow = tile * TC_M + row;
