@@ -104,8 +104,7 @@ struct imi_cuda_engine {
     int ncmax = STEP_COLS;
     bool tc_batch = false;
     uint8_t *tc_w = nullptr;    // every table's tiled copy for the batched read (k_tc_tile)
-    uint8_t *tc_xh = nullptr;   // the batched read's column operand and the columns' block scales and sums
-    float *tc_xds = nullptr;
+    uint8_t *tc_xb = nullptr;   // the batched read's column operand (codes, block scales and sums)
     SessDev *reply_d = nullptr;   // the last step's conversation records gathered for one read-back
     // pinned: what the host reads back after a step (session records at 32-byte slots from 0, the error word after
     // them), so the read is one small DMA into page-locked memory instead of staged copies into pageable memory. One
@@ -159,7 +158,7 @@ imi_cuda_engine::~imi_cuda_engine() {
     cudaFree(q8k_q);
     cudaFree(cols_d);
     cudaFree(tc_w);
-    cudaFree(tc_xh);
+    cudaFree(tc_xb);
     cudaFreeHost(cols_h);
     cudaFreeHost(embd_h);
     cudaFreeHost(reply_h);
@@ -267,21 +266,18 @@ int tc_group(int rows, int ncol, int sms) {
     return 64;
 }
 
-// an integer |v| <= 2048 as fp16 bits (exact)
-// the columns' 8-bit codes, scales and scale * code sums ([ncol][cols], [ncol][cols/32]) in the batched read's layout:
-// xh [group][cols/16][G][16] 8-bit, xds [group][cols/32][2][G] (zeros for the padding columns)
+// the columns' 8-bit codes, scales and scale * code sums ([ncol][cols], [ncol][cols/32]) as the batched read's
+// operand (tc_table.cuh: tc_xb_code, tc_xb_scale; zeros for the padding columns)
 void tc_operands_host(const int8_t *xq, const float *xd, const float *xs, int ncol, int cols, int G,
-                      std::vector<int8_t> &xh, std::vector<float> &xds) {
-    const int groups = (ncol + G - 1) / G, nq = cols / 16, nb = cols / 32;
-    xh.assign((size_t) groups * nq * G * 16, 0);
-    xds.assign((size_t) groups * nb * 2 * G, 0.0f);
+                      std::vector<uint8_t> &xb) {
+    const int groups = (ncol + G - 1) / G, nb = cols / 32;
+    xb.assign((size_t) groups * (cols / TC_KS) * tc_xb_bytes(G), 0);
     for (int c = 0; c < ncol; c++) {
         const int g = c / G, cg = c - g * G;
-        for (int k = 0; k < cols; k++)
-            xh[(((size_t) g * nq + k / 16) * G + cg) * 16 + (k & 15)] = xq[(size_t) c * cols + k];
+        for (int k = 0; k < cols; k++) xb[tc_xb_code(G, cols, g, cg, k)] = (uint8_t) xq[(size_t) c * cols + k];
         for (int j = 0; j < nb; j++) {
-            xds[(((size_t) g * nb + j) * 2 + 0) * G + cg] = xd[(size_t) c * nb + j];
-            xds[(((size_t) g * nb + j) * 2 + 1) * G + cg] = xs[(size_t) c * nb + j];
+            memcpy(&xb[tc_xb_scale(G, cols, g, cg, j, 0)], &xd[(size_t) c * nb + j], 4);
+            memcpy(&xb[tc_xb_scale(G, cols, g, cg, j, 1)], &xs[(size_t) c * nb + j], 4);
         }
     }
 }
@@ -445,11 +441,11 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
     // the tensor-core batched read takes every Q4_0 layer table and a Q4_0 word table (a Q4_1 table or a Q6_K word
     // table keeps the small-batch kernel, 8 columns per read)
     const int HD = e->n_head * e->head_dim, kvd = e->n_head_kv * e->head_dim;
-    e->tc_batch = !e->tok_q6k && !e->tok.has_m;
+    e->tc_batch = !e->tok_q6k && !e->tok.has_m && e->n_embd % (TC_CP * TC_KS) == 0;
     for (auto &Lr : e->layers)
         for (const TableRef *t : { &Lr.in_proj, &Lr.out_proj, &Lr.qkvg, &Lr.o, &Lr.gate_up, &Lr.down })
             if (t->rows && t->has_m) e->tc_batch = false;
-    if ((HD % 256) || (e->n_ff % 256)) e->tc_batch = false;
+    if ((HD % (TC_CP * TC_KS)) || (e->n_ff % (TC_CP * TC_KS))) e->tc_batch = false;
     e->ncmax = e->tc_batch ? std::max({ STEP_COLS, max_batch, TC_CHUNK }) : STEP_COLS;
     if (e->ncmax > 256) return fail(IMI_E_ARG, "max_batch above 256");
     const int NC = e->ncmax;
@@ -497,11 +493,9 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
     memset(e->cols_h, 0, sizeof(Col) * NC);
     e->last_s.assign(NC, nullptr);
     e->reply_src.assign(NC, nullptr);
-    if (e->tc_batch) {   // the batched read's operand buffers and every table's TMA views
+    if (e->tc_batch) {   // the batched read's operand buffer and every table's tiled copy
         const int ncp = (NC + 63) / 64 * 64, kmax = std::max(std::max(E, HD), e->n_ff);
-        const size_t bh = (size_t) kmax * ncp * 2, bx = (size_t) (kmax / 32) * 2 * ncp * 4;
-        DALLOC(e, e->tc_xh, bh + bx);
-        e->tc_xds = (float *) (e->tc_xh + bh);
+        DALLOC(e, e->tc_xb, (size_t) (ncp / 16) * (kmax / TC_KS) * tc_xb_bytes(16));   // the most for any group width
         // every table's tiled copy (the weights as the tensor-core read streams them), made here on the device
         std::vector<TableRef *> tcs;
         for (auto &Lr : e->layers)
@@ -728,14 +722,13 @@ cudaError_t enqueue_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind)
     return launch_final(fa, e->stream, true);
 }
 
-// one read of table t by the tensor-core batched path for the columns prepared in tc_xh / tc_xds
+// one read of table t by the tensor-core batched path for the columns prepared in tc_xb
 cudaError_t tc_read(imi_cuda_engine *e, const TableRef &t, int ncol, int epi, float *out, int out_stride) {
     TcArgs a = t.tc;
     a.ncol = ncol;
     a.G = tc_group(t.rows, ncol, e->sm_count);
     a.groups = (ncol + a.G - 1) / a.G;
-    a.xh = e->tc_xh;
-    a.xds = e->tc_xds;
+    a.xb = e->tc_xb;
     a.out = out;
     a.out_stride = out_stride;
     a.epi = epi;
@@ -754,8 +747,7 @@ cudaError_t enqueue_batch(imi_cuda_engine *e, int ncol, bool head, StepKind kind
     TcPrepArgs p0 = {};
     p0.cols_d = e->cols_d;
     p0.ncol = ncol;
-    p0.xh = e->tc_xh;
-    p0.xds = e->tc_xds;
+    p0.xb = e->tc_xb;
     p0.eps = e->eps;
     p0.n_embd = E;
     p0.d_conv = e->d_conv;
@@ -1406,14 +1398,12 @@ imi_cuda_status imi_cuda_bench_matvec(int device, int rows, int cols, int ncol, 
     // more than 8 inputs: the tensor-core read, its operands in the MMA's layout
     const bool tc = ncol > MV_MAX_COLS;
     const int G = tc_group(rows, ncol, sms), groups = (ncol + G - 1) / G;
-    std::vector<int8_t> th;
-    std::vector<float> tx;
-    if (tc) tc_operands_host(hq.data(), hd.data(), hs.data(), ncol, cols, G, th, tx);
+    std::vector<uint8_t> tx;
+    if (tc) tc_operands_host(hq.data(), hd.data(), hs.data(), ncol, cols, G, tx);
     const size_t tt = tc ? al(tc_tiled_bytes(rows, cols)) : 0, o_t = (size_t) copies * tstride;   // tiled copies
     const size_t o_q = o_t + (size_t) copies * tt, o_d = o_q + al(hq.size()), o_s = o_d + al(hd.size() * 4),
                  o_o = o_s + al(hs.size() * 4), o_c = o_o + al((size_t) ncol * rows * 4),
-                 o_th = o_c + al(sizeof(Col) * MV_MAX_COLS) + 256, o_tx = o_th + al(th.size()),
-                 total = o_tx + al(tx.size() * 4);
+                 o_tx = o_c + al(sizeof(Col) * MV_MAX_COLS) + 256, total = o_tx + al(tx.size());
     uint8_t *m = nullptr;
     CK(cudaMalloc(&m, total));
     cudaStream_t st = nullptr;
@@ -1426,15 +1416,14 @@ imi_cuda_status imi_cuda_bench_matvec(int device, int rows, int cols, int ncol, 
     if (r == cudaSuccess) r = cudaMemcpy(m + o_d, hd.data(), hd.size() * 4, cudaMemcpyHostToDevice);
     if (r == cudaSuccess) r = cudaMemcpy(m + o_s, hs.data(), hs.size() * 4, cudaMemcpyHostToDevice);
     if (r == cudaSuccess) r = cudaMemset(m + o_c, 0, al(sizeof(Col) * MV_MAX_COLS) + 256);
-    if (r == cudaSuccess && tc) r = cudaMemcpy(m + o_th, th.data(), th.size(), cudaMemcpyHostToDevice);
-    if (r == cudaSuccess && tc) r = cudaMemcpy(m + o_tx, tx.data(), tx.size() * 4, cudaMemcpyHostToDevice);
+    if (r == cudaSuccess && tc) r = cudaMemcpy(m + o_tx, tx.data(), tx.size(), cudaMemcpyHostToDevice);
     std::vector<TcArgs> tca(tc ? copies : 0);
     for (int c = 0; c < (int) tca.size() && r == cudaSuccess; c++) {
         TcArgs &t = tca[c];
         t.wt = m + o_t + (size_t) c * tt;
         r = launch_tc_tile(m + (size_t) c * tstride, rows, cols, row_bytes, m + o_t + (size_t) c * tt, nullptr);
         t.rows = rows; t.cols = cols; t.ncol = ncol; t.G = G; t.groups = groups;
-        t.xh = m + o_th; t.xds = (const float *) (m + o_tx); t.out = (float *) (m + o_o); t.out_stride = rows;
+        t.xb = m + o_tx; t.out = (float *) (m + o_o); t.out_stride = rows;
         t.epi = TE_STORE; t.err = (int *) (m + o_c + al(sizeof(Col) * MV_MAX_COLS));
     }
     if (r == cudaSuccess && tc) r = cudaDeviceSynchronize();   // the tiled copies (default stream) before the reads
@@ -1517,16 +1506,15 @@ imi_cuda_status imi_cuda_q4_matmul(int device, const uint8_t *q4, int rows, int 
             memcpy(row + (size_t) nb * 16 + 2 * j, src, 2);
             memcpy(row + 16 * j, src + 2, 16);
         }
-    std::vector<int8_t> xh;
-    std::vector<float> xds;
-    tc_operands_host(xq, xd, xs, ncol, cols, G, xh, xds);
+    std::vector<uint8_t> xb;
+    tc_operands_host(xq, xd, xs, ncol, cols, G, xb);
     auto al = [](size_t x) { return (x + 255) / 256 * 256; };
-    const size_t b_w = packed.size(), b_h = xh.size(), b_x = xds.size() * 4, b_o = (size_t) ncol * rows * 4;
+    const size_t b_w = packed.size(), b_h = xb.size(), b_o = (size_t) ncol * rows * 4;
     uint8_t *m = nullptr;
     const size_t b_t = (size_t) TC_TRACE_ROWS * TC_TRACE * 8, b_wt = tc_tiled_bytes(rows, cols);
-    CK(cudaMalloc(&m, al(b_w) + al(b_h) + al(b_x) + al(b_o) + 256 + b_t + al(b_wt)));
+    CK(cudaMalloc(&m, al(b_w) + al(b_h) + al(b_o) + 256 + b_t + al(b_wt)));
     uint8_t *dW = m, *dh = m + al(b_w);
-    float *dx = (float *) (dh + al(b_h)), *dout = (float *) ((uint8_t *) dx + al(b_x));
+    float *dout = (float *) (dh + al(b_h));
     int *derr = (int *) ((uint8_t *) dout + al(b_o));
     unsigned long long *dtr = (unsigned long long *) ((uint8_t *) derr + 256);
     uint8_t *dwt = (uint8_t *) dtr + b_t;   // the table's tiled copy
@@ -1536,13 +1524,12 @@ imi_cuda_status imi_cuda_q4_matmul(int device, const uint8_t *q4, int rows, int 
         cudaMemset(dtr, 0, b_t);
     }
     cudaError_t r = cudaMemcpy(dW, packed.data(), b_w, cudaMemcpyHostToDevice);
-    if (r == cudaSuccess) r = cudaMemcpy(dh, xh.data(), b_h, cudaMemcpyHostToDevice);
-    if (r == cudaSuccess) r = cudaMemcpy(dx, xds.data(), b_x, cudaMemcpyHostToDevice);
+    if (r == cudaSuccess) r = cudaMemcpy(dh, xb.data(), b_h, cudaMemcpyHostToDevice);
     if (r == cudaSuccess) r = cudaMemset(derr, 0, 4);
     if (r == cudaSuccess) r = launch_tc_tile(dW, rows, cols, row_bytes, dwt, nullptr);
     if (r == cudaSuccess) {
         a.wt = dwt; a.rows = rows; a.cols = cols; a.ncol = ncol; a.G = G; a.groups = groups;
-        a.xh = dh; a.xds = dx; a.out = dout; a.out_stride = rows; a.epi = TE_STORE; a.err = derr;
+        a.xb = dh; a.out = dout; a.out_stride = rows; a.epi = TE_STORE; a.err = derr;
         const int units = (rows + TC_M - 1) / TC_M * groups;
         r = launch_tc_table(a, std::min(sms, units), 0, false);
     }

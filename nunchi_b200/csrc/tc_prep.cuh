@@ -2,11 +2,12 @@
 // 8-bit cut; seoul.cpp:402-474 and run_batch 562-623), for the tensor-core batched read: one CTA per column (a
 // conversation of a multi-session step or a position of a prefill chunk), imi's float order exactly as the
 // small-batch table kernel's input preparation (table.cuh: table_prologue), the cut codes written straight into the
-// batched read's column operand ([group][K/16][G][16], 8-bit) with the blocks' scales and scale * code sums
-// ([group][K/32][2][G]). The small-batch kernel prepares every column in every CTA (a few columns); with dozens of
+// batched read's column operand with the blocks' scales and scale * code sums (tc_table.cuh: tc_xb_code,
+// tc_xb_scale). The small-batch kernel prepares every column in every CTA (a few columns); with dozens of
 // columns that work would be repeated on every SM, so here it is done once, spread over the columns.
 #pragma once
 #include "common.cuh"
+#include "tc_table.cuh"
 
 namespace imi {
 
@@ -25,8 +26,7 @@ struct TcPrepArgs {
     int ncol, pro;
     int K;                 // length of the prepared vector (the next table's width)
     int G;                 // columns per group of the batched read's operand
-    uint8_t *xh;           // operand out: [group][K/16][G][16] 8-bit codes
-    float *xds;            // [group][K/32][2][G]: scales, scale * code sums
+    uint8_t *xb;           // operand out: [group][K / TC_KS][tc_xb_bytes(G)] (8-bit codes, scales, scale * code sums)
     const float *in;       // per column: the previous table's output (RESID, FINAL), SiLU output (CUT), b|c|x (CONV)
     int in_stride;
     const float *xin;      // residual stream in / out, per column
@@ -52,11 +52,10 @@ struct TcPrepArgs {
 __device__ __forceinline__ void tp_put(const TcPrepArgs &a, int c, int q, uint32_t w, float d, int sum, bool act) {
     const int G = a.G, g = c / G, cg = c - g * G, K = a.K;
     if (!act) return;
-    *(uint32_t *) (a.xh + ((((size_t) g * (K / 16) + (q >> 2)) * G + cg) * 16 + 4 * (q & 3))) = w;
+    *(uint32_t *) (a.xb + tc_xb_code(G, K, g, cg, 4 * q)) = w;
     if ((q & 7) == 0) {
-        float *x = a.xds + (((size_t) g * (K / 32) + (q >> 3)) * 2) * G + cg;
-        x[0] = d;
-        x[G] = __fmul_rn(d, (float) sum);
+        *(float *) (a.xb + tc_xb_scale(G, K, g, cg, q >> 3, 0)) = d;
+        *(float *) (a.xb + tc_xb_scale(G, K, g, cg, q >> 3, 1)) = __fmul_rn(d, (float) sum);
     }
 }
 // cut the float4 chunk q of a K-long vector (8 lanes per 32-value block) and store it; every lane of the warp calls it
@@ -83,11 +82,10 @@ __global__ void __launch_bounds__(TP_THREADS) k_tc_prep(const __grid_constant__ 
             if (q < nq) {
                 const uint32_t w = *(const uint32_t *) (a.q8_q + (size_t) c * K + 4 * q);
                 const int G = a.G, g = c / G, cg = c - g * G;
-                *(uint32_t *) (a.xh + ((((size_t) g * (K / 16) + (q >> 2)) * G + cg) * 16 + 4 * (q & 3))) = w;
+                *(uint32_t *) (a.xb + tc_xb_code(G, K, g, cg, 4 * q)) = w;
                 if ((q & 7) == 0) {
-                    float *x = a.xds + (((size_t) g * (K / 32) + (q >> 3)) * 2) * G + cg;
-                    x[0] = a.q8_d[(size_t) c * (K / 32) + (q >> 3)];
-                    x[G] = a.q8_s[(size_t) c * (K / 32) + (q >> 3)];
+                    *(float *) (a.xb + tc_xb_scale(G, K, g, cg, q >> 3, 0)) = a.q8_d[(size_t) c * (K / 32) + (q >> 3)];
+                    *(float *) (a.xb + tc_xb_scale(G, K, g, cg, q >> 3, 1)) = a.q8_s[(size_t) c * (K / 32) + (q >> 3)];
                 }
             }
         }

@@ -18,9 +18,9 @@
 //
 // Work unit: a tile of 128 rows x a group of G columns (G = 16, 32 or 64). Warp roles (one CTA per SM, persistent
 // over units):
-//   warp 0      producer: per stage one barrier for three bulk copies into a ring slot (the tile's weight stage, the
-//               columns' 8-bit codes in the MMA's K-major layout, their scales and sums); it waits only for the slot,
-//               so bytes stream up to the ring's depth ahead of the math;
+//   warp 0      producer: per ring slot (TC_CP stages) one barrier for two bulk copies (the tile's weight stages, the
+//               columns' 8-bit codes in the MMA's K-major layout with their scales and sums); it waits only for the
+//               slot, so bytes stream up to the ring's depth ahead of the math;
 //   warp 1      TMEM owner (512 columns) and MMA issuer: per block one tcgen05.mma kind::i8 (K = 32) into the block's
 //               own TMEM columns; the 4 blocks of a stage fill one TMEM stage slot, committed to its barrier once (a
 //               commit-to-wait hand-off costs about 0.3 us, so it is made per stage, not per block);
@@ -41,9 +41,14 @@ constexpr int TC_KS = 128;             // values per K stage
 constexpr int TC_BPS = TC_KS / 32;     // blocks per stage
 // bytes of one (tile, stage) block of a table's tiled copy: 8-bit codes [TC_KS / 16][TC_M][16], fp16 scales [TC_M][4]
 constexpr int TC_WCODES = TC_KS * TC_M, TC_WSTAGE = TC_WCODES + TC_M * TC_BPS * 2;
-// ring of copied stages: as many as shared memory holds, TC_NR_MIN..TC_NR_MAX (a copy takes 1-2 us to land, so a
-// narrow group's unit, whose stages are short, needs more of them in flight)
-constexpr int TC_NR_MIN = 4, TC_NR_MAX = 12;
+// a ring slot holds TC_CP stages fetched by two bulk copies: their weights (contiguous in the tiled copy) and the
+// columns' operand (contiguous in its layout, codes and scales interleaved per stage). Fewer, larger copies stream
+// faster on their own (one CTA completes a copy about every 0.3 us: 10 KB copies ~31 GB/s per SM, 40 KB ones ~85),
+// but two stages per slot made the 64-session step 1.5% slower than one (3.19-3.23 against 3.14-3.15 ms): a slot
+// frees only when both of its stages are done
+constexpr int TC_CP = 1;
+// ring slots: as many as shared memory holds, TC_NR_MIN..TC_NR_MAX
+constexpr int TC_NR_MIN = 2, TC_NR_MAX = 12;
 constexpr int TC_SMEM = 220 * 1024;   // dynamic shared memory of one CTA at most
 constexpr int TC_WARP_PROD = 0, TC_WARP_MMA = 1, TC_WARP_EPI = 2;
 // columns per epilogue thread: 8 in groups of 16 or 32 columns (more warps to hide the TMEM and shared-memory
@@ -59,12 +64,25 @@ constexpr int TC_TMEM_COLS = 512;
 // and imi's greedy pick (first maximum, lowest id on ties), ending the step as the small-batch word-table read does
 enum TcEpi : int { TE_STORE = 0, TE_SILU = 1, TE_HEAD = 2 };
 
+// the columns' operand of one group (G columns) and stage (TC_KS values): the 8-bit codes [TC_KS / 16][G][16] in the
+// MMA's K-major layout, then per block of the stage the G scales and the G scale * code sums, [TC_BPS][2][G] floats;
+// stages follow one another per group: [group][cols / TC_KS][tc_xb_bytes(G)]
+__host__ __device__ constexpr int tc_xb_codes(int G) { return TC_KS / 16 * G * 16; }
+__host__ __device__ constexpr int tc_xb_bytes(int G) { return tc_xb_codes(G) + TC_BPS * 2 * G * 4; }
+// byte offsets in the operand: value k of column cg of group g; block j's scale (h = 0) or scale * code sum (h = 1)
+__host__ __device__ inline size_t tc_xb_code(int G, int K, int g, int cg, int k) {
+    return ((size_t) g * (K / TC_KS) + k / TC_KS) * tc_xb_bytes(G) + ((size_t) ((k % TC_KS) / 16) * G + cg) * 16 + k % 16;
+}
+__host__ __device__ inline size_t tc_xb_scale(int G, int K, int g, int cg, int j, int h) {
+    return ((size_t) g * (K / TC_KS) + j / TC_BPS) * tc_xb_bytes(G) + tc_xb_codes(G) +
+           ((size_t) ((j % TC_BPS) * 2 + h) * G + cg) * 4;
+}
+
 struct TcArgs {
     const uint8_t *wt;        // the table's tiled copy: [tiles][cols / TC_KS] blocks of TC_WSTAGE bytes (k_tc_tile)
-    int rows, cols;
+    int rows, cols;           // cols a multiple of TC_CP * TC_KS
     int ncol, G, groups;      // columns, columns per group, groups (units = tiles * groups)
-    const uint8_t *xh;        // the columns' 8-bit codes, [group][cols / 16][G][16]
-    const float *xds;         // per group and block: G scales then G scale * code sums, [group][cols / 32][2][G]
+    const uint8_t *xb;        // the columns' operand, [group][cols / TC_KS][tc_xb_bytes(G)]
     float *out;               // out[c * out_stride + row]
     int out_stride;
     int epi;
@@ -82,17 +100,15 @@ __host__ __device__ inline size_t tc_tiled_bytes(int rows, int cols) {
 
 struct TcPlan {
     int raw, bar, tptr, total;
-    int raw_bytes, raw_stride, b_off, x_off, b_bytes, xds_bytes, nslot;   // nslot: TMEM stage slots
-    int nr;   // copied stages in flight
+    int raw_bytes, raw_stride, op_off, xb, nslot;   // op_off: the operand in a slot; xb: its bytes per stage
+    int nr;   // ring slots (TC_CP stages each)
 };
-// a copied stage: [the weight stage (TC_WSTAGE) | the columns' 8-bit codes | the columns' scales and sums]
+// a ring slot: [the TC_CP weight stages (TC_WSTAGE each) | the TC_CP stages of the columns' operand]
 __host__ __device__ inline TcPlan tc_plan(int G) {
     TcPlan p;
-    p.b_bytes = (TC_KS / 16) * G * 16;                    // 8-bit codes of G columns, 8 chunks of 16
-    p.xds_bytes = TC_BPS * 2 * G * 4;
-    p.b_off = TC_WSTAGE;
-    p.x_off = p.b_off + p.b_bytes;
-    p.raw_bytes = p.x_off + p.xds_bytes;
+    p.xb = tc_xb_bytes(G);
+    p.op_off = TC_CP * TC_WSTAGE;
+    p.raw_bytes = p.op_off + TC_CP * p.xb;
     p.raw_stride = align_up(p.raw_bytes, 128);
     p.nslot = TC_TMEM_COLS / (G * TC_BPS);               // TMEM stage slots: a stage's 4 blocks, G columns each
     const int fixed = 8 * (2 * TC_NR_MAX + 2 * 32 + 1) + 16 + 256;
@@ -247,7 +263,6 @@ __global__ void __launch_bounds__(tc_threads(G), 1) k_tc_table(const __grid_cons
     tc_fence_after();
     const uint32_t tmem = *tptr;
     pdl_trigger();
-    pdl_wait();
 
     auto fail = [&]() {
         abort_flag = 1;
@@ -259,63 +274,87 @@ __global__ void __launch_bounds__(tc_threads(G), 1) k_tc_table(const __grid_cons
         fail();
         return false;
     };
+    // the same wait by every lane of a warp, one verdict for all (a lane that gave up fails the warp)
+    auto wait_warp = [&](uint64_t *b, uint32_t parity) -> bool { return __all_sync(0xffffffffu, wait(b, parity)); };
     auto raw_at = [&](int r) { return sm + P.raw + r * P.raw_stride; };
 
+    // producer and MMA issuer: the whole warp runs the role's loop and waits (its control flow stays converged), lane 0
+    // issues the copies, the MMAs and the commits
     if (warp == TC_WARP_PROD) {
         // ---------------- producer ----------------
-        if (lane == 0) {
-            int i = 0;
-            bool ok = true;
-            for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-                const int tile = u / a.groups, g = u - tile * a.groups;
-                const uint8_t *wt = a.wt + (size_t) tile * nst * TC_WSTAGE;
-                const uint8_t *xh = a.xh + (size_t) g * (K / 16) * G * 16;
-                const float *xds = a.xds + (size_t) g * (K / 32) * 2 * G;
-                for (int s = 0; s < nst; s++, i++) {
-                    const int r = i % NR;
-                    if (!(ok = wait(&raw_empty[r], ((i / NR) & 1) ^ 1))) break;
+        // before the dependency wait: the weights of the first unit's first slots (they do not depend on the launches
+        // in flight; the columns' operand does), so they stream while the previous launch finishes
+        const int pre = blockIdx.x < units ? min(NR, nst / TC_CP) : 0;
+        if (lane == 0 && pre > 0) {
+            const uint8_t *wt = a.wt + (size_t) (blockIdx.x / a.groups) * nst * TC_WSTAGE;
+            for (int k = 0; k < pre; k++) {
+                mbar_expect_tx(&raw_full[k], (uint32_t) P.raw_bytes);   // both copies of the slot
+                bulk_g2s(raw_at(k), wt + (size_t) k * TC_CP * TC_WSTAGE, (uint32_t) (TC_CP * TC_WSTAGE), &raw_full[k]);
+            }
+        }
+        pdl_wait();
+        int i = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+            const int tile = u / a.groups, g = u - tile * a.groups;
+            const uint8_t *wt = a.wt + (size_t) tile * nst * TC_WSTAGE;
+            const uint8_t *xb = a.xb + (size_t) g * nst * P.xb;
+            for (int s = 0; s < nst; s += TC_CP, i++) {   // i: slots filled
+                const int r = i % NR;
+                if (i < pre) {   // its weights are on their way: the operand only
+                    if (lane == 0) bulk_g2s(raw_at(r) + P.op_off, xb + (size_t) s * P.xb, (uint32_t) (TC_CP * P.xb), &raw_full[r]);
+                    __syncwarp();
+                    continue;
+                }
+                if (!(ok = wait_warp(&raw_empty[r], ((i / NR) & 1) ^ 1))) break;
+                if (lane == 0) {
                     uint8_t *raw = raw_at(r);
                     mbar_expect_tx(&raw_full[r], (uint32_t) P.raw_bytes);
-                    bulk_g2s(raw, wt + (size_t) s * TC_WSTAGE, (uint32_t) TC_WSTAGE, &raw_full[r]);
-                    bulk_g2s(raw + P.b_off, xh + (size_t) s * (TC_KS / 16) * G * 16, (uint32_t) P.b_bytes, &raw_full[r]);
-                    bulk_g2s(raw + P.x_off, xds + (size_t) s * TC_BPS * 2 * G, (uint32_t) P.xds_bytes, &raw_full[r]);
+                    bulk_g2s(raw, wt + (size_t) s * TC_WSTAGE, (uint32_t) (TC_CP * TC_WSTAGE), &raw_full[r]);
+                    bulk_g2s(raw + P.op_off, xb + (size_t) s * P.xb, (uint32_t) (TC_CP * P.xb), &raw_full[r]);
                     if (a.trace && blockIdx.x == 0 && i < TC_TRACE) a.trace[0 * TC_TRACE + i] = global_ns();
                 }
+                __syncwarp();
             }
-            if (!ok)   // the copies in flight land before the CTA exits (bounded waits on the last stages issued)
-                for (int k = i > NR ? i - NR : 0; k < i; k++) mbar_wait(&raw_full[k % NR], (k / NR) & 1);
         }
+        if (!ok && lane == 0)   // the copies in flight land before the CTA exits (bounded waits on the last slots filled)
+            for (int k = i > NR ? i - NR : 0; k < i; k++) mbar_wait(&raw_full[k % NR], (k / NR) & 1);
     } else if (warp == TC_WARP_MMA) {
         // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            const uint32_t idesc = tc_idesc_i8(G, TC_M);
-            int i = 0, b = 0;
-            bool ok = true;
-            for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-                for (int s = 0; s < nst && ok; s++, i++) {
-                    const int r = i % NR, slot = i % nslot;
-                    if (!(ok = wait(&raw_full[r], (i / NR) & 1))) break;
-                    if (a.trace && blockIdx.x == 0 && i < TC_TRACE) a.trace[7 * TC_TRACE + i] = global_ns();
-                    if (!(ok = wait(&tm_empty[slot], ((i / nslot) & 1) ^ 1))) break;
-                    if (a.trace && blockIdx.x == 0 && i < TC_TRACE) a.trace[8 * TC_TRACE + i] = global_ns();
-                    tc_fence_after();
-                    const uint32_t abase = smem_u32(raw_at(r)), bbase = abase + P.b_off;
-                    for (int jj = 0; jj < TC_BPS; jj++, b++) {   // block jj: 16-byte chunks 2jj, 2jj + 1
+        pdl_wait();
+        const uint32_t idesc = tc_idesc_i8(G, TC_M);
+        int i = 0, b = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+            for (int s = 0; s < nst && ok; s++, i++) {   // i: stages; stage i sits in slot (i / TC_CP) % NR
+                const int q = i / TC_CP, sub = i % TC_CP, r = q % NR, slot = i % nslot;
+                if (!(ok = wait_warp(&raw_full[r], (q / NR) & 1))) break;
+                if (lane == 0 && a.trace && blockIdx.x == 0 && i < TC_TRACE) a.trace[7 * TC_TRACE + i] = global_ns();
+                if (!(ok = wait_warp(&tm_empty[slot], ((i / nslot) & 1) ^ 1))) break;
+                if (lane == 0 && a.trace && blockIdx.x == 0 && i < TC_TRACE) a.trace[8 * TC_TRACE + i] = global_ns();
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t abase = smem_u32(raw_at(r)) + sub * TC_WSTAGE,
+                                   bbase = smem_u32(raw_at(r)) + P.op_off + sub * P.xb;
+                    for (int jj = 0; jj < TC_BPS; jj++) {   // block jj: 16-byte chunks 2jj, 2jj + 1
                         tc_mma_i8(tmem + (slot * TC_BPS + jj) * G, tc_desc(abase + 2 * jj * TC_M * 16, TC_M * 16, 128),
                                   tc_desc(bbase + 2 * jj * G * 16, G * 16, 128), idesc);
-                        if (a.trace && blockIdx.x == 0 && b < TC_TRACE) a.trace[3 * TC_TRACE + b] = global_ns();
+                        if (a.trace && blockIdx.x == 0 && b + jj < TC_TRACE) a.trace[3 * TC_TRACE + b + jj] = global_ns();
                     }
                     tc_commit(&tm_full[slot]);
-                    tc_commit(&raw_empty[r]);
+                    if (sub == TC_CP - 1) tc_commit(&raw_empty[r]);   // the slot's last stage
                 }
+                b += TC_BPS;
+                __syncwarp();
             }
-            if (!ok) {   // the MMAs issued complete before TMEM is freed
-                tc_commit(fin);
-                mbar_wait(fin, 0);
-            }
+        }
+        if (!ok && lane == 0) {   // the MMAs issued complete before TMEM is freed
+            tc_commit(fin);
+            mbar_wait(fin, 0);
         }
     } else {
         // ---------------- epilogue: imi's float chains per (row, column) ----------------
+        pdl_wait();
         const int qd = warp & 3, h = (warp - TC_WARP_EPI) >> 2, row = qd * 32 + lane;
         const uint32_t tl = tmem + ((uint32_t) (qd * 32) << 16) + h * CH;
         int i = 0, b = 0;
@@ -326,15 +365,15 @@ __global__ void __launch_bounds__(tc_threads(G), 1) k_tc_table(const __grid_cons
 #pragma unroll
             for (int k = 0; k < CH / 2; k++) acc[k] = cor[k] = make_float2(0.0f, 0.0f);
             for (int s = 0; s < nst && ok; s++, i++) {
-                const int r = i % NR, slot = i % nslot;
+                const int q = i / TC_CP, sub = i % TC_CP, r = q % NR, slot = i % nslot;
                 // the slot's copies (this warp reads their scales) and the stage's MMAs
-                if (!(ok = wait(&raw_full[r], (i / NR) & 1) && wait(&tm_full[slot], (i / nslot) & 1))) break;
+                if (!(ok = wait_warp(&raw_full[r], (q / NR) & 1) && wait_warp(&tm_full[slot], (i / nslot) & 1))) break;
                 tc_fence_after();
                 const uint8_t *ep = raw_at(r);
-                const uint2 dq = *(const uint2 *) (ep + TC_WCODES + row * 8);   // the row's 4 block scales
+                const uint2 dq = *(const uint2 *) (ep + sub * TC_WSTAGE + TC_WCODES + row * 8);   // the row's 4 block scales
                 const uint16_t dsc[4] = { (uint16_t) (dq.x & 0xffff), (uint16_t) (dq.x >> 16), (uint16_t) (dq.y & 0xffff),
                                           (uint16_t) (dq.y >> 16) };
-                const float *xds = (const float *) (ep + P.x_off);
+                const float *xds = (const float *) (ep + P.op_off + sub * P.xb + tc_xb_codes(G));
                 for (int j0 = 0; j0 < TC_BPS; j0 += NLD) {
                     const bool tr = a.trace && blockIdx.x == 0 && warp == TC_WARP_EPI && lane == 0 && b < TC_TRACE;
                     if (tr) a.trace[4 * TC_TRACE + b] = global_ns();
@@ -367,7 +406,7 @@ __global__ void __launch_bounds__(tc_threads(G), 1) k_tc_table(const __grid_cons
                 __syncwarp();
                 if (lane == 0) {
                     mbar_arrive(&tm_empty[slot]);
-                    mbar_arrive(&raw_empty[r]);
+                    if (sub == TC_CP - 1) mbar_arrive(&raw_empty[r]);
                 }
                 if (a.trace && blockIdx.x == 0 && lane == 0 && i < TC_TRACE) atomicMax(&a.trace[2 * TC_TRACE + i], global_ns());
             }
