@@ -1928,9 +1928,13 @@ imi_cuda_status imi_cuda_state_save(const imi_cuda_state *s, void *buf, size_t c
     uint8_t *o = (uint8_t *) buf;
     memcpy(o, &h, sizeof h);
     o += sizeof h;
+    // the image keeps imi's layout, [layer][position][kv head][D]; the caches are [layer][kv head][position][D]
+    const int D = e->head_dim, nkv = e->n_head_kv;
     for (const __half *cache : { s->kc, s->vc })
         for (int a = 0; a < e->n_attn; a++) {
-            CK(cudaMemcpy(o, cache + (size_t) a * e->n_ctx * kvd, (size_t) pos * kvd * 2, cudaMemcpyDeviceToHost));
+            for (int g = 0; g < nkv && pos > 0; g++)
+                CK(cudaMemcpy2D(o + (size_t) g * D * 2, (size_t) kvd * 2, cache + ((size_t) a * nkv + g) * e->n_ctx * D,
+                                (size_t) D * 2, (size_t) D * 2, (size_t) pos, cudaMemcpyDeviceToHost));
             o += (size_t) pos * kvd * 2;
         }
     for (int l = 0; l < e->n_conv; l++)
@@ -1959,9 +1963,12 @@ imi_cuda_status imi_cuda_state_load(imi_cuda_state *s, const void *buf, size_t s
     CK(cudaSetDevice(e->device));
     CK(cudaStreamSynchronize(e->stream));
     const uint8_t *i = (const uint8_t *) buf + sizeof h;
+    const int D = e->head_dim, nkv = e->n_head_kv;   // image [layer][position][kv head][D] -> caches [layer][kv head][position][D]
     for (__half *cache : { s->kc, s->vc })
         for (int a = 0; a < e->n_attn; a++) {
-            CK(cudaMemcpy(cache + (size_t) a * e->n_ctx * kvd, i, (size_t) h.pos * kvd * 2, cudaMemcpyHostToDevice));
+            for (int g = 0; g < nkv && h.pos > 0; g++)
+                CK(cudaMemcpy2D(cache + ((size_t) a * nkv + g) * e->n_ctx * D, (size_t) D * 2, i + (size_t) g * D * 2,
+                                (size_t) kvd * 2, (size_t) D * 2, (size_t) h.pos, cudaMemcpyHostToDevice));
             i += (size_t) h.pos * kvd * 2;
         }
     CK(cudaMemset(s->ring, 0, (size_t) e->n_conv * R * E * 4));

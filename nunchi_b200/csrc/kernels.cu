@@ -168,12 +168,12 @@ __global__ void __launch_bounds__(32) k_kvwrite(const __grid_constant__ AttnArgs
     __shared__ uint16_t kh[D], vh[D];
     pdl_trigger();
     pdl_wait();
-    const int g = blockIdx.x, c = blockIdx.y, kvd = a.n_head_kv * D;
+    const int g = blockIdx.x, c = blockIdx.y;
     const Col col = a.cols_d[c];
     const int p = col.s->pos + col.off;
     kv_make<D>(a, a.qkv + (size_t) c * a.qkv_stride, g, p, ktmp, tmp, kh, vh);
     __syncwarp();
-    const size_t o = ((size_t) a.ai * a.n_ctx + p) * kvd + g * D;
+    const size_t o = (((size_t) a.ai * a.n_head_kv + g) * a.n_ctx + p) * D;   // caches [layer][kv head][position][D]
     for (int i = threadIdx.x; i < D; i += 32) {
         ((uint16_t *) col.kc)[o + i] = kh[i];
         ((uint16_t *) col.vc)[o + i] = vh[i];
@@ -211,13 +211,13 @@ __global__ void __launch_bounds__(ATT_NT) k_attn(const __grid_constant__ AttnArg
         rcs[i] = a.rope_cs[(size_t) pspec * (D / 2) + i];
         rsn[i] = a.rope_sn[(size_t) pspec * (D / 2) + i];
     }
-    if (tid == 0) {   // before the wait: this CTA's share of the layer's cached K and V rows into L2 (a hint only:
+    if (tid == 0) {   // before the wait: this CTA's share of its kv head's cached K and V rows into L2 (a hint only:
                       // the position read here may be one behind; the rows before it are final)
         const int pp = ld_relaxed(&col.s->pos) + col.off, ps = a.window > 0 ? max(0, pp - a.window + 1) : 0;
-        const size_t row = (size_t) kvd * 2, bytes = (size_t) max(pp - ps, 0) * row;
-        const size_t share = (bytes / H + 15) / 16 * 16, b0 = (size_t) h * share, b1 = min(b0 + share, bytes);
-        const uint8_t *kb = (const uint8_t *) col.kc + ((size_t) a.ai * a.n_ctx + ps) * row;
-        const uint8_t *vb0 = (const uint8_t *) col.vc + ((size_t) a.ai * a.n_ctx + ps) * row;
+        const size_t row = (size_t) D * 2, bytes = (size_t) max(pp - ps, 0) * row, hb = ((size_t) a.ai * a.n_head_kv + g) * a.n_ctx;
+        const size_t share = (bytes / grp + 15) / 16 * 16, b0 = (size_t) (h % grp) * share, b1 = min(b0 + share, bytes);
+        const uint8_t *kb = (const uint8_t *) col.kc + (hb + ps) * row;
+        const uint8_t *vb0 = (const uint8_t *) col.vc + (hb + ps) * row;
         for (size_t o = b0; o < b1; o += 65536) {
             const uint32_t n = (uint32_t) min((size_t) 65536, b1 - o);
             prefetch_l2(kb + o, n);
@@ -233,8 +233,9 @@ __global__ void __launch_bounds__(ATT_NT) k_attn(const __grid_constant__ AttnArg
         cs = a.rope_cs + (size_t) p * (D / 2);
         sn = a.rope_sn + (size_t) p * (D / 2);
     }
-    uint16_t *kc = (uint16_t *) col.kc + (size_t) a.ai * a.n_ctx * kvd + g * D;
-    uint16_t *vc = (uint16_t *) col.vc + (size_t) a.ai * a.n_ctx * kvd + g * D;
+    // this kv head's rows of the layer: [position][D] (caches [layer][kv head][position][D])
+    uint16_t *kc = (uint16_t *) col.kc + ((size_t) a.ai * a.n_head_kv + g) * a.n_ctx * D;
+    uint16_t *vc = (uint16_t *) col.vc + ((size_t) a.ai * a.n_head_kv + g) * a.n_ctx * D;
     const int s0 = a.window > 0 ? max(0, p - a.window + 1) : 0, nk = p - s0 + 1;
     const int ng = a.kv_fused ? nk - 1 : nk;   // positions whose V is read from the cache
     const int VT = attn_vtile(D), ntile = (ng + VT - 1) / VT;
@@ -244,7 +245,7 @@ __global__ void __launch_bounds__(ATT_NT) k_attn(const __grid_constant__ AttnArg
         const int t0 = k * VT, n = min(VT, ng - t0);
         for (int i = tid - 64; i < n * (D / 8); i += ATT_NT - 64) {
             const int t = i / (D / 8), ch = i - t * (D / 8);
-            cp16(dst + (size_t) t * D + 8 * ch, vc + (size_t) (s0 + t0 + t) * kvd + 8 * ch);
+            cp16(dst + (size_t) t * D + 8 * ch, vc + (size_t) (s0 + t0 + t) * D + 8 * ch);
         }
         cp_commit();
     };
@@ -262,8 +263,8 @@ __global__ void __launch_bounds__(ATT_NT) k_attn(const __grid_constant__ AttnArg
     }
     __syncthreads();
     if (a.kv_fused && h % grp == 0 && tid < D) {
-        kc[(size_t) p * kvd + tid] = kh[tid];
-        vc[(size_t) p * kvd + tid] = vh[tid];
+        kc[(size_t) p * D + tid] = kh[tid];
+        vc[(size_t) p * D + tid] = vh[tid];
     }
 
     // scores (seoul.cpp:445): one thread per position
@@ -275,7 +276,7 @@ __global__ void __launch_bounds__(ATT_NT) k_attn(const __grid_constant__ AttnArg
         for (int u = 0; u < SB; u++) {
             const int t = t0 + u * ATT_NT, pt = s0 + t;
             if (t < nk) {
-                const uint4 *src = (a.kv_fused && pt == p) ? (const uint4 *) kh : (const uint4 *) (kc + (size_t) pt * kvd);
+                const uint4 *src = (a.kv_fused && pt == p) ? (const uint4 *) kh : (const uint4 *) (kc + (size_t) pt * D);
 #pragma unroll
                 for (int w = 0; w < D / 8; w++) kr[u][w] = src[w];
             }
@@ -377,9 +378,11 @@ __host__ __device__ inline size_t attn_smem_bytes(int D, int n_ctx) { return att
 // once for all of them instead of once per query head. Per query head the float order is k_attn's: q RMSNorm +
 // rotation, scores by dot_h, the maximum, exp and the double sum, the normalised probabilities, the P.V chain over
 // positions in order, the sigmoid gate and the 8-bit cut of the head's output. Scores: one thread per position, its K
-// row converted once and dotted with the GRP queries; P.V: one thread per (query head, dimension), V rows in shared
-// memory tiles (ATG_NTILE in flight, cp.async) that serve all GRP heads.
-constexpr int ATG_NT = 256, ATG_NW = ATG_NT / 32, ATG_VT = 64, ATG_NTILE = 3;
+// row converted once and dotted with the GRP queries; P.V: one thread per dimension running the GRP heads' chains
+// (one V load for all), V rows in shared memory tiles (ATG_NTILE in flight from before the scores, cp.async).
+// V tiles of ATG_VT positions (8 KB at head_dim 64), ATG_NTILE in flight: a tile takes ~1.5 us to arrive and its
+// chains ~0.2 us, so with two in flight the P.V loop waited on every tile
+constexpr int ATG_NT = 256, ATG_NW = ATG_NT / 32, ATG_VT = 64, ATG_NTILE = 8;
 struct AttnGPlan {
     size_t q, ktmp, tmp, kh, vh, rcs, rsn, y, red, vt, sc, total;
 };
@@ -406,7 +409,7 @@ __host__ __device__ inline AttnGPlan attn_grp_plan(int D, int grp, int n_ctx) {
 
 template <int D, int GRP>
 __global__ void __launch_bounds__(ATG_NT, 2) k_attn_grp(const __grid_constant__ AttnArgs a) {
-    static_assert(GRP * D <= ATG_NT && GRP + 1 <= ATG_NW, "one thread per (query head, dimension); a warp per query");
+    static_assert(D <= ATG_NT && (GRP == 2 || GRP == 4) && GRP + 1 <= ATG_NW, "a thread per dimension; a warp per query");
     extern __shared__ __align__(16) uint8_t sma[];
     const AttnGPlan L = attn_grp_plan(D, GRP, a.n_ctx);
     const int g = blockIdx.x, c = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -426,14 +429,13 @@ __global__ void __launch_bounds__(ATG_NT, 2) k_attn_grp(const __grid_constant__ 
         rcs[i] = a.rope_cs[(size_t) pspec * (D / 2) + i];
         rsn[i] = a.rope_sn[(size_t) pspec * (D / 2) + i];
     }
-    if (tid == 0) {   // before the wait: this CTA's share of the column's cached K and V rows into L2 (a hint only)
+    if (tid == 0) {   // before the wait: this kv head's cached K and V rows into L2 (a hint only)
         const int pp = ld_relaxed(&col.s->pos) + col.off, ps = a.window > 0 ? max(0, pp - a.window + 1) : 0;
-        const size_t row = (size_t) kvd * 2, bytes = (size_t) max(pp - ps, 0) * row;
-        const size_t share = (bytes / a.n_head_kv + 15) / 16 * 16, b0 = (size_t) g * share, b1 = min(b0 + share, bytes);
-        const uint8_t *kb = (const uint8_t *) col.kc + ((size_t) a.ai * NC + ps) * row;
-        const uint8_t *vb0 = (const uint8_t *) col.vc + ((size_t) a.ai * NC + ps) * row;
-        for (size_t o = b0; o < b1; o += 65536) {
-            const uint32_t n = (uint32_t) min((size_t) 65536, b1 - o);
+        const size_t row = (size_t) D * 2, bytes = (size_t) max(pp - ps, 0) * row, hb = ((size_t) a.ai * a.n_head_kv + g) * NC;
+        const uint8_t *kb = (const uint8_t *) col.kc + (hb + ps) * row;
+        const uint8_t *vb0 = (const uint8_t *) col.vc + (hb + ps) * row;
+        for (size_t o = 0; o < bytes; o += 65536) {
+            const uint32_t n = (uint32_t) min((size_t) 65536, bytes - o);
             prefetch_l2(kb + o, n);
             prefetch_l2(vb0 + o, n);
         }
@@ -447,8 +449,9 @@ __global__ void __launch_bounds__(ATG_NT, 2) k_attn_grp(const __grid_constant__ 
         cs = a.rope_cs + (size_t) p * (D / 2);
         sn = a.rope_sn + (size_t) p * (D / 2);
     }
-    uint16_t *kc = (uint16_t *) col.kc + (size_t) a.ai * NC * kvd + g * D;
-    uint16_t *vc = (uint16_t *) col.vc + (size_t) a.ai * NC * kvd + g * D;
+    // this kv head's rows of the layer: [position][D] (caches [layer][kv head][position][D])
+    uint16_t *kc = (uint16_t *) col.kc + ((size_t) a.ai * a.n_head_kv + g) * NC * D;
+    uint16_t *vc = (uint16_t *) col.vc + ((size_t) a.ai * a.n_head_kv + g) * NC * D;
     const int s0 = a.window > 0 ? max(0, p - a.window + 1) : 0, nk = p - s0 + 1;
     const int ng = a.kv_fused ? nk - 1 : nk;   // positions whose V is read from the cache
     const int ntile = (ng + ATG_VT - 1) / ATG_VT;
@@ -457,7 +460,7 @@ __global__ void __launch_bounds__(ATG_NT, 2) k_attn_grp(const __grid_constant__ 
         const int t0 = k * ATG_VT, n = min(ATG_VT, ng - t0);
         for (int i = tid; i < n * (D / 8); i += ATG_NT) {
             const int t = i / (D / 8), ch = i - t * (D / 8);
-            cp16(dst + (size_t) t * D + 8 * ch, vc + (size_t) (s0 + t0 + t) * kvd + 8 * ch);
+            cp16(dst + (size_t) t * D + 8 * ch, vc + (size_t) (s0 + t0 + t) * D + 8 * ch);
         }
     };
     __syncthreads();   // the rotary rows are in shared memory
@@ -476,8 +479,8 @@ __global__ void __launch_bounds__(ATG_NT, 2) k_attn_grp(const __grid_constant__ 
     }
     __syncthreads();
     if (a.kv_fused && tid < D) {
-        kc[(size_t) p * kvd + tid] = kh[tid];
-        vc[(size_t) p * kvd + tid] = vh[tid];
+        kc[(size_t) p * D + tid] = kh[tid];
+        vc[(size_t) p * D + tid] = vh[tid];
     }
 
     // scores (seoul.cpp:445): one thread per position; the K row's halves converted once, dotted with every query in
@@ -486,13 +489,14 @@ __global__ void __launch_bounds__(ATG_NT, 2) k_attn_grp(const __grid_constant__ 
 #pragma unroll
     for (int j = 0; j < GRP; j++) lmax[j] = -INFINITY;
     constexpr int SB = GRP * D >= ATG_NT ? 1 : 2;   // K rows a thread loads together (registers allow one at full width)
+#pragma unroll 1
     for (int t0 = tid; t0 < nk; t0 += SB * ATG_NT) {
         uint4 kr[SB][D / 8];
 #pragma unroll
         for (int u = 0; u < SB; u++) {
             const int t = t0 + u * ATG_NT, pt = s0 + t;
             if (t < nk) {
-                const uint4 *src = (a.kv_fused && pt == p) ? (const uint4 *) kh : (const uint4 *) (kc + (size_t) pt * kvd);
+                const uint4 *src = (a.kv_fused && pt == p) ? (const uint4 *) kh : (const uint4 *) (kc + (size_t) pt * D);
 #pragma unroll
                 for (int w = 0; w < D / 8; w++) kr[u][w] = src[w];
             }
@@ -582,11 +586,13 @@ __global__ void __launch_bounds__(ATG_NT, 2) k_attn_grp(const __grid_constant__ 
 #pragma unroll
         for (int j = 0; j < GRP; j++) sc[(size_t) j * SS + t] = __fmul_rn(sc[(size_t) j * SS + t], inv[j]);
 
-    // P.V (seoul.cpp:449-450): thread (j, i) runs o = fma(p_t, v_t,i, o) over positions in order for query head
-    // g*GRP + j, dimension i
-    const int j = tid / D, i = tid - (tid / D) * D;
-    const bool pv = j < GRP;
-    float o = 0.0f;
+    // P.V (seoul.cpp:449-450): thread i < D runs, for each query head j of the group, o_j = fma(p_jt, v_t,i, o_j) over
+    // positions in order; one load of v_t,i serves all GRP chains, the probabilities arrive 4 positions per load
+    const int i = tid;
+    const bool pv = tid < D;
+    float o[GRP];
+#pragma unroll
+    for (int j = 0; j < GRP; j++) o[j] = 0.0f;
     for (int k = 0; k < ntile; k++) {
         if (k + ATG_NTILE - 1 < ntile) load_tile(k + ATG_NTILE - 1);   // into the buffer tile k - 1 left
         cp_commit();
@@ -594,37 +600,46 @@ __global__ void __launch_bounds__(ATG_NT, 2) k_attn_grp(const __grid_constant__ 
         __syncthreads();
         if (pv) {
             const uint16_t *vb = vt + (size_t) (k % ATG_NTILE) * ATG_VT * D + i;
-            const float *pr = sc + (size_t) j * SS + (size_t) k * ATG_VT;
+            const float *pr = sc + (size_t) k * ATG_VT;   // + j * SS: head j's probabilities of this tile
             const int n = min(ATG_VT, ng - k * ATG_VT);
             int t = 0;
-#pragma unroll 2
-            for (; t + 8 <= n; t += 8) {
-                uint16_t v8[8];
+            for (; t + 4 <= n; t += 4) {   // 4 positions: their loads first
+                float4 p4[GRP];
+                uint16_t v4[4];
 #pragma unroll
-                for (int u = 0; u < 8; u++) v8[u] = vb[(size_t) (t + u) * D];
-                const float4 p0 = *(const float4 *) (pr + t), p1 = *(const float4 *) (pr + t + 4);
-                o = __fmaf_rn(p0.x, h2f(v8[0]), o);
-                o = __fmaf_rn(p0.y, h2f(v8[1]), o);
-                o = __fmaf_rn(p0.z, h2f(v8[2]), o);
-                o = __fmaf_rn(p0.w, h2f(v8[3]), o);
-                o = __fmaf_rn(p1.x, h2f(v8[4]), o);
-                o = __fmaf_rn(p1.y, h2f(v8[5]), o);
-                o = __fmaf_rn(p1.z, h2f(v8[6]), o);
-                o = __fmaf_rn(p1.w, h2f(v8[7]), o);
+                for (int j = 0; j < GRP; j++) p4[j] = *(const float4 *) (pr + (size_t) j * SS + t);
+#pragma unroll
+                for (int u = 0; u < 4; u++) v4[u] = vb[(size_t) (t + u) * D];
+                const float f0 = h2f(v4[0]), f1 = h2f(v4[1]), f2 = h2f(v4[2]), f3 = h2f(v4[3]);
+#pragma unroll
+                for (int j = 0; j < GRP; j++) {
+                    o[j] = __fmaf_rn(p4[j].x, f0, o[j]);
+                    o[j] = __fmaf_rn(p4[j].y, f1, o[j]);
+                    o[j] = __fmaf_rn(p4[j].z, f2, o[j]);
+                    o[j] = __fmaf_rn(p4[j].w, f3, o[j]);
+                }
             }
-            for (; t < n; t++) o = __fmaf_rn(pr[t], h2f(vb[(size_t) t * D]), o);
+            for (; t < n; t++) {
+                const float f = h2f(vb[(size_t) t * D]);
+#pragma unroll
+                for (int j = 0; j < GRP; j++) o[j] = __fmaf_rn(pr[(size_t) j * SS + t], f, o[j]);
+            }
         }
-        __syncthreads();   // the buffer is free for the tile issued two rounds on
+        __syncthreads();   // the buffer is free for the tile issued ATG_NTILE - 1 rounds on
     }
     cp_wait_group<0>();
     if (pv) {
-        const int h = g * GRP + j;
-        if (ng < nk) o = __fmaf_rn(sc[(size_t) j * SS + nk - 1], h2f(vh[i]), o);   // this position's own V
-        const float gv = qkv[H * D + 2 * kvd + h];
-        const float gate = __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_cr(-gv)));   // seoul.cpp:451
-        const float yv = __fmul_rn(o, gate);
-        a.att[(size_t) c * a.att_stride + h * D + i] = yv;
-        y[j * D + i] = yv;
+#pragma unroll
+        for (int j = 0; j < GRP; j++) {
+            const int h = g * GRP + j;
+            float oj = o[j];
+            if (ng < nk) oj = __fmaf_rn(sc[(size_t) j * SS + nk - 1], h2f(vh[i]), oj);   // this position's own V
+            const float gv = qkv[H * D + 2 * kvd + h];
+            const float gate = __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_cr(-gv)));   // seoul.cpp:451
+            const float yv = __fmul_rn(oj, gate);
+            a.att[(size_t) c * a.att_stride + h * D + i] = yv;
+            y[j * D + i] = yv;
+        }
     }
     __syncthreads();
     // the 8-bit cut of each query head's output blocks (imi_cut32 of seoul.cpp:457): warp j cuts head g*GRP + j
