@@ -153,9 +153,11 @@ imi_cuda_status imi_cuda_trace_table(imi_cuda_engine *e, int layer, int which, i
                                      int *grid);
 
 /* Diagnostics: one decode step of `s` (token given) launched directly (not from a graph) with every launch writing
- * per-CTA phase timestamps (ns): out[launch][n_sm][16] as in imi_cuda_trace_table (attention / final norm: 0 start,
- * 1 after the dependency wait, 14 end). kinds[launch]: 10*input+output kind of a table read, 100 attention, 101 final
- * norm; grids[launch]: CTAs. *n receives the number of launches (at most max_launches). */
+ * per-CTA phase timestamps (ns): out[launch][n_sm][16] as in imi_cuda_trace_table (final norm: 0 start, 1 after the
+ * dependency wait, 14 end; attention at head_dim 64 adds 2 query and this position's K/V made, 3 scores, 4
+ * probabilities, 5 P.V done, 6 the first K/V copies issued, 7 / 8 the first / last K tile landed, 9 / 10 the first /
+ * last V tile landed). kinds[launch]: 10*input+output kind of a table read, 100 attention, 101 final norm;
+ * grids[launch]: CTAs. *n receives the number of launches (at most max_launches). */
 imi_cuda_status imi_cuda_trace_step(imi_cuda_state *s, int32_t token, int want_logits, unsigned long long *out,
                                     int max_launches, int *kinds, int *grids, int *n);
 

@@ -37,10 +37,16 @@ struct SessDev {
     int pad;
 };
 
+// the attention kernel that streams K and V by the copy engine (kernels.cu: k_attn_tma): head_dim, positions per tile,
+// most ring slots, threads, shared-memory budget; the conversation's K tensor map sits ATK_TMAP_OFF bytes into its
+// device record
+constexpr int ATK_D = 64, ATK_T = 256, ATK_NSMAX = 6, ATK_NT = 256, ATK_NW = ATK_NT / 32;
+constexpr int ATK_TILE = ATK_T * ATK_D * 2, ATK_TMAP_OFF = 128, ATK_SMEM = 220 * 1024;
+
 // One input column of a step. Written by the host before each launch (or left in place for greedy replay).
 struct Col {
     SessDev *s;
-    __half *kc, *vc;           // [n_attn][n_ctx][kvd]
+    __half *kc, *vc;           // [n_attn][n_head_kv][n_ctx][head_dim]
     float *ring;               // conv memory [n_conv][d_conv+1][n_embd]; slot of position p is p mod (d_conv+1)
     float *hid_out;            // where this column's final hidden state goes (null = nowhere)
     float *logits;             // word scores (null = not wanted)
@@ -373,6 +379,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, long lon
     while (!mbar_try_wait(b, parity))
         if (clock64() - t0 > limit) return false;
     return true;
+}
+// a 2D tensor copy (TMA) of one box at element coordinates (x, y) into shared memory, completing on an mbarrier; the
+// tensor map lives in global, constant or parameter memory (x times the element size a multiple of 16 bytes)
+__device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_u32(dst)), "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
 }
 // global -> shared bulk copy completing on an mbarrier (addresses 16-byte aligned, bytes a multiple of 16)
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {

@@ -12,6 +12,8 @@
 #include "gguf_file.h"
 #include "launch.h"
 
+#include <cudaTypedefs.h>
+
 
 #include <algorithm>
 #include <cmath>
@@ -518,7 +520,7 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
     CK(cudaEventCreate(&e->t0));
     CK(cudaEventCreate(&e->t1));
     CK(prepare_kernels());
-    e->state_bytes = sizeof(SessDev) + (size_t) 2 * e->n_attn * n_ctx * kvd * 2 +
+    e->state_bytes = ATK_TMAP_OFF + 2 * sizeof(CUtensorMap) + (size_t) 2 * e->n_attn * n_ctx * kvd * 2 +
                      (size_t) e->n_conv * (e->d_conv + 1) * E * 4 + (size_t) E * 4 + (size_t) e->n_vocab * 4 +
                      (size_t) n_ctx * 4 + 6 * 256;
     CK(cudaDeviceSynchronize());
@@ -1001,6 +1003,35 @@ imi_cuda_status imi_cuda_get_info(const imi_cuda_engine *e, imi_cuda_info *o) {
     return IMI_OK;
 }
 
+namespace {
+// cuTensorMapEncodeTiled from the driver, looked up once
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::mutex g_encode_mu;
+cudaError_t encode_fn() {
+    std::lock_guard<std::mutex> g(g_encode_mu);
+    if (g_encode) return cudaSuccess;
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    const cudaError_t r = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q);
+    if (r != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+    g_encode = (PFN_cuTensorMapEncodeTiled_v12000) fn;
+    return cudaSuccess;
+}
+// the attention's view of a conversation's K or V cache (head_dim 64): rows of 64 fp16 values, [n_attn * n_kv *
+// n_ctx] of them, read in boxes of ATK_T rows with the 128-byte swizzle (kernels.cu: k_attn_tma)
+cudaError_t kv_tensor_map(const imi_cuda_engine *e, const __half *kc, CUtensorMap *out) {
+    cudaError_t r = encode_fn();
+    if (r != cudaSuccess) return r;
+    const cuuint64_t rows = (cuuint64_t) e->n_attn * e->n_head_kv * e->n_ctx;
+    cuuint64_t dims[2] = { (cuuint64_t) ATK_D, rows }, strides[1] = { (cuuint64_t) ATK_D * 2 };
+    cuuint32_t box[2] = { (cuuint32_t) ATK_D, (cuuint32_t) ATK_T }, es[2] = { 1, 1 };
+    const CUresult c = g_encode(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *) kc, dims, strides, box, es,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return c == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+}  // namespace
+
 imi_cuda_status imi_cuda_state_new(imi_cuda_engine *e, imi_cuda_state **out) {
     if (!e || !out) return fail(IMI_E_ARG, "null argument");
     e->gen++;
@@ -1010,7 +1041,7 @@ imi_cuda_status imi_cuda_state_new(imi_cuda_engine *e, imi_cuda_state **out) {
     const int E = e->n_embd, kvd = e->n_head_kv * e->head_dim;
     size_t o = 0;
     auto take = [&](size_t n) { const size_t r = o; o = (o + n + 255) / 256 * 256; return r; };
-    const size_t o_s = take(sizeof(SessDev)), o_k = take((size_t) e->n_attn * e->n_ctx * kvd * 2),
+    const size_t o_s = take(ATK_TMAP_OFF + 2 * sizeof(CUtensorMap)), o_k = take((size_t) e->n_attn * e->n_ctx * kvd * 2),
                  o_v = take((size_t) e->n_attn * e->n_ctx * kvd * 2),
                  o_r = take((size_t) e->n_conv * (e->d_conv + 1) * E * 4), o_h = take((size_t) E * 4),
                  o_l = take((size_t) e->n_vocab * 4), o_p = take((size_t) e->n_ctx * 4);
@@ -1026,6 +1057,13 @@ imi_cuda_status imi_cuda_state_new(imi_cuda_engine *e, imi_cuda_state **out) {
     s->picks = (int *) (m + o_p);
     CK(cudaMemsetAsync(s->mem, 0, o, e->stream));
     CK(cudaStreamSynchronize(e->stream));
+    if (e->head_dim == ATK_D && e->n_attn > 0) {   // the attention's K and V tensor maps, in the record after SessDev
+        static_assert(sizeof(SessDev) <= ATK_TMAP_OFF, "record slot");
+        CUtensorMap tm[2];
+        CK(kv_tensor_map(e, s->kc, &tm[0]));
+        CK(kv_tensor_map(e, s->vc, &tm[1]));
+        CK(cudaMemcpy((uint8_t *) s->s + ATK_TMAP_OFF, tm, sizeof tm, cudaMemcpyHostToDevice));
+    }
     *out = s.release();
     return IMI_OK;
 }

@@ -4,6 +4,8 @@
 // k_attn: decode attention for one (query head, column): q/k RMSNorm, NEOX rotation, fp16 K/V write, scores,
 //   softmax, P.V and the sigmoid gate, in the float order of seoul.cpp:425-453.
 #define IMI_KERNELS 1
+#include <cuda.h>
+
 #include "common.cuh"
 #include "table.cuh"
 #include "tc_table.cuh"
@@ -372,6 +374,311 @@ __global__ void __launch_bounds__(ATT_NT) k_attn(const __grid_constant__ AttnArg
 }
 
 __host__ __device__ inline size_t attn_smem_bytes(int D, int n_ctx) { return attn_plan(D, n_ctx).total; }
+
+// k_attn_tma: the same attention (one CTA per query head and column, k_attn's float order) at head_dim 64, with the
+// head's cached K and V streamed into shared memory by the copy engine instead of per-thread loads (the caches are
+// head-major, so a head's rows are contiguous). One ring of ns slots of ATK_T positions (32 KB) carries the head's K
+// tiles and then its V tiles: tile i sits in slot i % ns, the first ns tiles are issued at once and tile i + ns as
+// soon as tile i is consumed, so at the lengths decode runs at the whole K and most of V are in flight from the start.
+// Large copies matter: a CTA completes about one copy every 0.28 us whatever its size up to 32 KB.
+// Both come by 2D tensor copies with the 128-byte swizzle (chunk w of row r lands at chunk position w ^ (r & 7), so
+// one thread per position reading chunk w of its row hits distinct banks; the P.V threads read V by the same rule).
+// The session's K and V tensor maps sit ATK_TMAP_OFF bytes into its device record (written when the conversation is
+// made).
+struct AttkPlan {
+    size_t q, kf, vf, tq, tk, wq, wk, y, kh, vh, rcs, rsn, red, bar, sc, total;
+    int ns;   // ring slots (the ring starts at the 1024-byte aligned base)
+};
+__host__ __device__ inline AttkPlan attk_layout(int n_ctx, int ns) {
+    AttkPlan p;
+    p.ns = ns;
+    size_t o = (size_t) ns * ATK_TILE;
+    auto take = [&](size_t n) { const size_t r = o; o = (o + n + 15) / 16 * 16; return r; };
+    p.q = take(4 * ATK_D);
+    p.kf = take(4 * ATK_D);
+    p.vf = take(4 * ATK_D);
+    p.tq = take(4 * ATK_D);
+    p.tk = take(4 * ATK_D);
+    p.wq = take(4 * ATK_D);
+    p.wk = take(4 * ATK_D);
+    p.y = take(4 * ATK_D);
+    p.kh = take(2 * ATK_D);
+    p.vh = take(2 * ATK_D);
+    p.rcs = take(4 * ATK_D / 2);
+    p.rsn = take(4 * ATK_D / 2);
+    p.red = take(8 * ATK_NW + 4 * ATK_NW + 16);
+    p.bar = take(8 * ATK_NSMAX);
+    p.sc = take(4 * (size_t) n_ctx);
+    p.total = o + 1024;   // + slack to align the base to 1024 bytes (the swizzle's period)
+    return p;
+}
+__host__ __device__ inline AttkPlan attk_plan(int n_ctx) {
+    const long room = (long) ATK_SMEM - (long) attk_layout(n_ctx, 0).total;
+    const long ns = room > 0 ? room / ATK_TILE : 0;
+    return attk_layout(n_ctx, (int) (ns < ATK_NSMAX ? ns : ATK_NSMAX));
+}
+
+// one full V tile of the P.V chain for one dimension (o_i = fma(p_t, v_t,i, o_i) over its ATK_T positions in order),
+// the next 16 positions' values and probabilities loaded while these 16 go through the chain. The tile is swizzled:
+// the dimension's value of row r sits at r * 128 + off[r & 7].
+__device__ __forceinline__ float pv_tile(const uint8_t *vt, const uint32_t (&off)[8], const float *pr, float o) {
+    constexpr int G = 16;
+    uint16_t v[G];
+    float4 pp[G / 4];
+#pragma unroll
+    for (int u = 0; u < G; u++) v[u] = *(const uint16_t *) (vt + u * 128 + off[u & 7]);
+#pragma unroll
+    for (int u = 0; u < G / 4; u++) pp[u] = ((const float4 *) pr)[u];
+#pragma unroll
+    for (int gi = 0; gi < ATK_T / G; gi++) {
+        uint16_t vn[G];
+        float4 pn[G / 4];
+        if (gi + 1 < ATK_T / G) {
+#pragma unroll
+            for (int u = 0; u < G; u++) vn[u] = *(const uint16_t *) (vt + ((gi + 1) * G + u) * 128 + off[u & 7]);
+#pragma unroll
+            for (int u = 0; u < G / 4; u++) pn[u] = ((const float4 *) (pr + (gi + 1) * G))[u];
+        }
+#pragma unroll
+        for (int u = 0; u < G / 4; u++) {
+            o = __fmaf_rn(pp[u].x, h2f(v[4 * u]), o);
+            o = __fmaf_rn(pp[u].y, h2f(v[4 * u + 1]), o);
+            o = __fmaf_rn(pp[u].z, h2f(v[4 * u + 2]), o);
+            o = __fmaf_rn(pp[u].w, h2f(v[4 * u + 3]), o);
+        }
+        if (gi + 1 < ATK_T / G) {
+#pragma unroll
+            for (int u = 0; u < G; u++) v[u] = vn[u];
+#pragma unroll
+            for (int u = 0; u < G / 4; u++) pp[u] = pn[u];
+        }
+    }
+    return o;
+}
+
+__global__ void __launch_bounds__(ATK_NT) k_attn_tma(const __grid_constant__ AttnArgs a) {
+    constexpr int D = ATK_D, T = ATK_T;
+    extern __shared__ __align__(128) uint8_t smk[];
+    uint8_t *sm = smk + ((1024 - (smem_u32(smk) & 1023)) & 1023);
+    const AttkPlan L = attk_plan(a.n_ctx);
+    const int NS = L.ns;
+    const int h = blockIdx.x, c = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    unsigned long long *trace = a.trace ? a.trace + (size_t) (blockIdx.y * gridDim.x + blockIdx.x) * MV_TRACE : nullptr;
+    if (trace && tid == 0) trace[0] = global_ns();
+    float *q = (float *) (sm + L.q), *kf = (float *) (sm + L.kf), *vf = (float *) (sm + L.vf);
+    float *tq = (float *) (sm + L.tq), *tk = (float *) (sm + L.tk), *wq = (float *) (sm + L.wq);
+    float *wk = (float *) (sm + L.wk), *y = (float *) (sm + L.y), *sc = (float *) (sm + L.sc);
+    uint16_t *kh = (uint16_t *) (sm + L.kh), *vh = (uint16_t *) (sm + L.vh);
+    double *dsum = (double *) (sm + L.red);
+    float *wmax = (float *) (sm + L.red + 8 * ATK_NW);
+    float *rcs = (float *) (sm + L.rcs), *rsn = (float *) (sm + L.rsn);
+    uint64_t *full = (uint64_t *) (sm + L.bar);
+    if (tid == 0) {
+        for (int i = 0; i < NS; i++) mbar_init(&full[i], 1);
+        fence_barrier_init();
+    }
+    pdl_trigger();
+    const int H = a.n_head, grp = H / a.n_head_kv, g = h / grp, kvd = a.n_head_kv * D;
+    const Col col = a.cols_d[c];
+    // before the wait (none of it is written by the previous kernel): the rotary rows of the position read now and
+    // both norm weights
+    const int pspec = ld_relaxed(&col.s->pos) + col.off;
+    const CUtensorMap *tmk = (const CUtensorMap *) ((const uint8_t *) col.s + ATK_TMAP_OFF);
+    if (tid == ATK_NT - 1) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(tmk) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(tmk + 1) : "memory");
+    }
+    if (tid < D) {
+        wq[tid] = a.q_norm[tid];
+        wk[tid] = a.k_norm[tid];
+    } else if (tid < D + D / 2) {
+        rcs[tid - D] = a.rope_cs[(size_t) pspec * (D / 2) + tid - D];
+        rsn[tid - D] = a.rope_sn[(size_t) pspec * (D / 2) + tid - D];
+    }
+    __syncthreads();   // barriers initialised
+    pdl_wait();
+    if (trace && tid == 0) trace[1] = global_ns();
+    const int p = ld_relaxed(&col.s->pos) + col.off;
+    const float *qkv = a.qkv + (size_t) c * a.qkv_stride;
+    const float *cs = rcs, *sn = rsn;
+    if (p != pspec) {
+        cs = a.rope_cs + (size_t) p * (D / 2);
+        sn = a.rope_sn + (size_t) p * (D / 2);
+    }
+    const size_t hrow = ((size_t) a.ai * a.n_head_kv + g) * a.n_ctx;   // this kv head's first row in the caches
+    uint16_t *kc = (uint16_t *) col.kc + hrow * D, *vc = (uint16_t *) col.vc + hrow * D;
+    const int s0 = a.window > 0 ? max(0, p - a.window + 1) : 0, nk = p - s0 + 1;
+    const int ng = a.kv_fused ? nk - 1 : nk;   // positions whose V is read from the cache
+    const int ntk = (nk + T - 1) / T, ntv = (ng + T - 1) / T, nt = ntk + ntv;
+    auto slot = [&](int i) { return sm + (size_t) (i % NS) * ATK_TILE; };
+    auto issue = [&](int i) {   // K tile i, or V tile i - ntk (rows past the tensor read as zeros)
+        uint64_t *b = &full[i % NS];
+        if (i < ntk) {
+            mbar_expect_tx(b, (uint32_t) ATK_TILE);
+            tma_load_2d(slot(i), tmk, 0, (int) (hrow + s0 + (size_t) i * T), b);
+        } else {
+            mbar_expect_tx(b, (uint32_t) ATK_TILE);
+            tma_load_2d(slot(i), tmk + 1, 0, (int) (hrow + s0 + (size_t) (i - ntk) * T), b);
+        }
+    };
+    if (tid == 0) {
+        for (int i = 0; i < min(NS, nt); i++) issue(i);
+        if (trace) trace[6] = global_ns();
+    }
+    // on a wait that gave up at tile i: the tiles in flight (i .. i + NS - 1) land before the CTA exits (bounded
+    // waits), then it returns
+    auto drain = [&](int i) {
+        if (tid == 0)
+            for (int j = i; j < min(nt, i + NS); j++) mbar_wait(&full[j % NS], (j / NS) & 1);
+    };
+
+    // this head's query, and this position's K and V, in one round of loads; then the rotations (warp 1 the query,
+    // warp 0 the key)
+    const float gv = tid < D ? qkv[H * D + 2 * kvd + h] : 0.0f;   // the gate input (seoul.cpp:451)
+    if (tid < D) {
+        q[tid] = qkv[h * D + tid];
+        if (a.kv_fused) kf[tid] = qkv[H * D + g * D + tid];
+    } else if (a.kv_fused && tid < 2 * D) {
+        vf[tid - D] = qkv[H * D + kvd + g * D + tid - D];
+    }
+    __syncthreads();
+    if (warp == 0 && a.kv_fused) {
+        norm_rope<D>(kf, wk, cs, sn, a.eps, tk);
+        for (int i = lane; i < D; i += 32) {
+            kh[i] = f2h(kf[i]);
+            vh[i] = f2h(vf[i]);
+        }
+    } else if (warp == 1) {
+        norm_rope<D>(q, wq, cs, sn, a.eps, tq);
+    }
+    __syncthreads();
+    if (trace && tid == 0) trace[2] = global_ns();
+    if (a.kv_fused && h % grp == 0 && tid < D) {   // the group's first head writes this position's K/V
+        kc[(size_t) p * D + tid] = kh[tid];
+        vc[(size_t) p * D + tid] = vh[tid];
+    }
+
+    // scores (seoul.cpp:445): thread t takes position t of each K tile
+    float qr[D];
+#pragma unroll
+    for (int i = 0; i < D; i++) qr[i] = q[i];
+    float lmax = -INFINITY;
+    for (int k = 0; k < ntk; k++) {
+        const bool ok = mbar_wait(&full[k % NS], (k / NS) & 1);
+        if (trace && tid == 0 && (k == 0 || k == ntk - 1)) trace[k == 0 ? 7 : 8] = global_ns();
+        const int t = k * T + tid;
+        if (ok && t < nk) {
+            uint4 krow[D / 8];
+            if (a.kv_fused && t == nk - 1) {   // this position: its own K (the cache row is being written)
+#pragma unroll
+                for (int w = 0; w < D / 8; w++) krow[w] = ((const uint4 *) kh)[w];
+            } else {
+                const uint8_t *row = slot(k) + (size_t) tid * (D * 2);
+#pragma unroll
+                for (int w = 0; w < D / 8; w++) krow[w] = *(const uint4 *) (row + ((w ^ (tid & 7)) << 4));
+            }
+            const float v = __fmul_rn(dot_h8<D>(qr, krow), a.scale);
+            sc[t] = v;
+            lmax = lmax < v ? v : lmax;
+        }
+        if (!__syncthreads_and(ok)) {   // every thread is done with the slot; a wait that gave up ends the CTA
+            if (tid == 0) atomicExch(a.err, 7);
+            drain(k);
+            return;
+        }
+        if (tid == 0 && k + NS < nt) issue(k + NS);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
+    if (lane == 0) wmax[warp] = lmax;
+    __syncthreads();
+    if (trace && tid == 0) trace[3] = global_ns();
+    float m = wmax[0];
+    for (int w = 1; w < ATK_NW; w++) m = fmaxf(m, wmax[w]);
+    // exp and the double sum (seoul.cpp:446-448); every thread adds the warps' sums in the same order
+    double ls = 0.0;
+    for (int t = tid; t < nk; t += ATK_NT) {
+        const float e = exp_cr(__fsub_rn(sc[t], m));
+        sc[t] = e;
+        ls += (double) e;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+    if (lane == 0) dsum[warp] = ls;
+    __syncthreads();
+    double tot = 0.0;
+    for (int w = 0; w < ATK_NW; w++) tot += dsum[w];
+    const float iv2 = __double2float_rn(1.0 / tot);
+    for (int t = tid; t < nk; t += ATK_NT) sc[t] = __fmul_rn(sc[t], iv2);
+    __syncthreads();
+    if (trace && tid == 0) trace[4] = global_ns();
+
+    // P.V (seoul.cpp:449-450): o_i = fma(p_t, v_t,i, o_i) over positions in order; thread i < D owns dimension i
+    float o = 0.0f;
+    uint32_t off[8];   // where this thread's dimension sits in a swizzled row r: off[r & 7]
+#pragma unroll
+    for (int j = 0; j < 8; j++) off[j] = ((((uint32_t) tid >> 3) ^ j) << 4) | (((uint32_t) tid & 7) << 1);
+    for (int k = 0; k < ntv; k++) {
+        const int i = ntk + k;
+        const bool ok = mbar_wait(&full[i % NS], (i / NS) & 1);
+        if (trace && tid == 0 && (k == 0 || k == ntv - 1)) trace[k == 0 ? 9 : 10] = global_ns();
+        if (ok && tid < D) {
+            const uint8_t *vt = slot(i);
+            const float *pr = sc + (size_t) k * T;
+            const int n = min(T, ng - k * T);
+            if (n == T) {
+                o = pv_tile(vt, off, pr, o);
+            } else {
+                int t = 0;
+                for (; t + 8 <= n; t += 8) {
+                    uint16_t v8[8];
+#pragma unroll
+                    for (int u = 0; u < 8; u++) v8[u] = *(const uint16_t *) (vt + (t + u) * 128 + off[u]);
+                    const float4 p0 = *(const float4 *) (pr + t), p1 = *(const float4 *) (pr + t + 4);
+                    o = __fmaf_rn(p0.x, h2f(v8[0]), o);
+                    o = __fmaf_rn(p0.y, h2f(v8[1]), o);
+                    o = __fmaf_rn(p0.z, h2f(v8[2]), o);
+                    o = __fmaf_rn(p0.w, h2f(v8[3]), o);
+                    o = __fmaf_rn(p1.x, h2f(v8[4]), o);
+                    o = __fmaf_rn(p1.y, h2f(v8[5]), o);
+                    o = __fmaf_rn(p1.z, h2f(v8[6]), o);
+                    o = __fmaf_rn(p1.w, h2f(v8[7]), o);
+                }
+                for (; t < n; t++) {
+                    const uint32_t ot = ((((uint32_t) tid >> 3) ^ (t & 7)) << 4) | (((uint32_t) tid & 7) << 1);
+                    o = __fmaf_rn(pr[t], h2f(*(const uint16_t *) (vt + t * 128 + ot)), o);
+                }
+            }
+        }
+        if (!__syncthreads_and(ok)) {
+            if (tid == 0) atomicExch(a.err, 7);
+            drain(i);
+            return;
+        }
+        if (tid == 0 && i + NS < nt) issue(i + NS);
+    }
+    if (trace && tid == 0) trace[5] = global_ns();
+    if (tid < D) {
+        if (ng < nk) o = __fmaf_rn(sc[nk - 1], h2f(vh[tid]), o);   // this position's own V
+        const float gate = __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_cr(-gv)));   // seoul.cpp:451
+        const float yv = __fmul_rn(o, gate);
+        a.att[(size_t) c * a.att_stride + h * D + tid] = yv;
+        y[tid] = yv;
+    }
+    __syncthreads();
+    // the 8-bit cut of this head's output blocks (imi_cut32 of seoul.cpp:457), so the o table only loads codes
+    if (a.q8o_q && warp == 0) {
+        const int HD = H * D;
+        for (int q0 = 0; q0 < D / 4; q0 += 32) {
+            const int qi = q0 + lane;
+            const bool act = qi < D / 4;
+            const float4 v = act ? ((const float4 *) y)[qi] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            cut_chunk(v, act, qi, a.q8o_q + (size_t) c * HD + h * D, a.q8o_d + (size_t) c * (HD / 32) + h * D / 32,
+                      a.q8o_s + (size_t) c * (HD / 32) + h * D / 32);
+        }
+    }
+    if (trace && tid == 0) trace[14] = global_ns();
+}
 
 // k_attn_grp: the same attention for many columns, one CTA of ATG_NT threads per (kv head g, column c) computing the
 // GRP query heads g*GRP .. g*GRP+GRP-1 that share the kv head (GQA), so every cached K and V row of the group is read
