@@ -42,6 +42,9 @@ struct SessDev {
 // device record
 constexpr int ATK_D = 64, ATK_T = 256, ATK_NSMAX = 6, ATK_NT = 256, ATK_NW = ATK_NT / 32;
 constexpr int ATK_TILE = ATK_T * ATK_D * 2, ATK_TMAP_OFF = 128, ATK_SMEM = 220 * 1024;
+// its many-column form (kernels.cu: k_attn_gtma): shared memory of one CTA when two share an SM (228 KB less 1 KB
+// reserved per CTA), else ATK_SMEM; most ring slots
+constexpr int ATGK_SMEM = 113 * 1024, ATGK_NSMAX = 3;
 
 // One input column of a step. Written by the host before each launch (or left in place for greedy replay).
 struct Col {
@@ -55,7 +58,8 @@ struct Col {
     int token;                 // >= 0 word id, -1 embd, -2 the session's last pick
     int off;                   // position = s->pos + off
     int pos_inc;               // added to s->pos when the step ends
-    int pad;
+    int order;                 // (the record at index r) the column whose batched attention is launched r-th: the
+                               // columns by decreasing attended length, so the longest start first
 };
 
 enum Pro : int {

@@ -100,6 +100,7 @@ struct imi_cuda_engine {
     int8_t *qa_q = nullptr, *qt_q = nullptr;   // 8-bit cuts of act [col][n_ff] and att [col][n_head*head_dim]
     float *qa_d = nullptr, *qa_s = nullptr, *qt_d = nullptr, *qt_s = nullptr;
     Col *cols_d = nullptr, *cols_h = nullptr;
+    std::vector<int> cols_pos;   // each column's session position as the host knows it (decode_col)
     float *embd_h = nullptr;
     // columns one launch takes at most: 8 in the small-batch table kernel; up to ncmax (the larger of max_batch and
     // a prefill chunk) in the tensor-core batched read, when every table is Q4_0 (tc_batch)
@@ -493,6 +494,7 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
     CK(cudaMallocHost(&e->embd_h, (size_t) E * 4 * NC));
     CK(cudaMallocHost(&e->reply_h, (size_t) 32 * NC + 64));
     memset(e->cols_h, 0, sizeof(Col) * NC);
+    e->cols_pos.assign(NC, 0);
     e->last_s.assign(NC, nullptr);
     e->reply_src.assign(NC, nullptr);
     if (e->tc_batch) {   // the batched read's operand buffer and every table's tiled copy
@@ -887,6 +889,14 @@ imi_cuda_status run_step(imi_cuda_engine *e, int ncol, bool head, StepKind kind,
     e->last_n = ncol;
     for (int c = 0; c < e->last_n; c++) e->last_s[c] = e->cols_h[c].s;
     if (copy_cols) {
+        // the batched attention's launch order: columns by decreasing attended position (ties by index); greedy
+        // replays keep it (every column moves on by one)
+        std::vector<int> idx(ncol);
+        for (int c = 0; c < ncol; c++) idx[c] = c;
+        std::stable_sort(idx.begin(), idx.end(), [&](int x, int y) {
+            return e->cols_pos[x] + e->cols_h[x].off > e->cols_pos[y] + e->cols_h[y].off;
+        });
+        for (int r = 0; r < ncol; r++) e->cols_h[r].order = idx[r];
         CK(cudaMemcpyAsync(e->cols_d, e->cols_h, sizeof(Col) * ncol, cudaMemcpyHostToDevice, e->stream));
         CK(cudaEventRecord(e->staged, e->stream));
     }
@@ -934,6 +944,8 @@ Col decode_col(imi_cuda_state *s, int32_t token, bool has_embd, int c, bool want
     k.token = token >= 0 ? token : (has_embd ? -1 : -2);
     k.off = 0;
     k.pos_inc = 1;
+    k.order = c;
+    e->cols_pos[c] = s->pos;
     return k;
 }
 

@@ -719,7 +719,7 @@ __global__ void __launch_bounds__(ATG_NT, 2) k_attn_grp(const __grid_constant__ 
     static_assert(D <= ATG_NT && (GRP == 2 || GRP == 4) && GRP + 1 <= ATG_NW, "a thread per dimension; a warp per query");
     extern __shared__ __align__(16) uint8_t sma[];
     const AttnGPlan L = attn_grp_plan(D, GRP, a.n_ctx);
-    const int g = blockIdx.x, c = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = blockIdx.x, c = a.cols_d[blockIdx.y].order, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     unsigned long long *trace = a.trace ? a.trace + (size_t) (blockIdx.y * gridDim.x + blockIdx.x) * MV_TRACE : nullptr;
     if (trace && tid == 0) trace[0] = global_ns();
     float *q = (float *) (sma + L.q), *ktmp = (float *) (sma + L.ktmp), *tmp = (float *) (sma + L.tmp);
@@ -940,6 +940,360 @@ __global__ void __launch_bounds__(ATG_NT, 2) k_attn_grp(const __grid_constant__ 
         for (int j = 0; j < GRP; j++) {
             const int h = g * GRP + j;
             float oj = o[j];
+            if (ng < nk) oj = __fmaf_rn(sc[(size_t) j * SS + nk - 1], h2f(vh[i]), oj);   // this position's own V
+            const float gv = qkv[H * D + 2 * kvd + h];
+            const float gate = __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_cr(-gv)));   // seoul.cpp:451
+            const float yv = __fmul_rn(oj, gate);
+            a.att[(size_t) c * a.att_stride + h * D + i] = yv;
+            y[j * D + i] = yv;
+        }
+    }
+    __syncthreads();
+    // the 8-bit cut of each query head's output blocks (imi_cut32 of seoul.cpp:457): warp j cuts head g*GRP + j
+    if (a.q8o_q && warp < GRP) {
+        const int HD = H * D, h = g * GRP + warp;
+        for (int q0 = 0; q0 < D / 4; q0 += 32) {
+            const int qi = q0 + lane;
+            const bool act = qi < D / 4;
+            const float4 v = act ? ((const float4 *) (y + warp * D))[qi] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            cut_chunk(v, act, qi, a.q8o_q + (size_t) c * HD + h * D, a.q8o_d + (size_t) c * (HD / 32) + h * D / 32,
+                      a.q8o_s + (size_t) c * (HD / 32) + h * D / 32);
+        }
+    }
+    if (trace && tid == 0) trace[14] = global_ns();
+}
+
+// k_attn_gtma: k_attn_grp's work (one CTA per (kv head g, column) for the GRP query heads sharing it, each in
+// k_attn's float order) at head_dim 64, with k_attn_tma's copy ring: the kv head's K tiles and then its V tiles by 2D
+// tensor copies of ATK_T rows (32 KB, 128-byte swizzle) through ns slots, two CTAs per SM (ATGK_SMEM each) while the
+// score rows leave room for two slots, else one (ATK_SMEM). Scores: one thread per position of a K tile, its row
+// converted once and dotted with the GRP queries; P.V: 128 threads, one per (dimension, half of the heads), each
+// running GRP / 2 chains from one V load, the next 8 positions' values and probabilities loaded while these 8 go
+// through the chains.
+struct AttgkPlan {
+    size_t q, kf, vf, tmp, wq, wk, y, kh, vh, rcs, rsn, red, bar, sc, total;
+    int ns;   // ring slots (the ring starts at the 1024-byte aligned base)
+};
+__host__ __device__ inline AttgkPlan attgk_layout(int grp, int n_ctx, int ns) {
+    AttgkPlan p;
+    p.ns = ns;
+    const size_t D = ATK_D;
+    size_t o = (size_t) ns * ATK_TILE;
+    auto take = [&](size_t n) { const size_t r = o; o = (o + n + 15) / 16 * 16; return r; };
+    p.q = take(4 * grp * D);
+    p.kf = take(4 * D);
+    p.vf = take(4 * D);
+    p.tmp = take(4 * (grp + 1) * D);   // norm_rope scratch: warp 0 (this position's K), warps 1..grp (the queries)
+    p.y = p.tmp;                        // the heads' outputs, at the end (the scratch is free then)
+    p.wq = take(4 * D);
+    p.wk = take(4 * D);
+    p.kh = take(2 * D);
+    p.vh = take(2 * D);
+    p.rcs = take(4 * D / 2);
+    p.rsn = take(4 * D / 2);
+    p.red = take(8 * (size_t) ATK_NW * grp + 4 * (size_t) ATK_NW * grp);
+    p.bar = take(8 * ATGK_NSMAX);
+    p.sc = take(4 * (size_t) grp * attn_grp_sc_stride(n_ctx));
+    p.total = o + 1024;   // + slack to align the base to 1024 bytes
+    return p;
+}
+__host__ __device__ inline AttgkPlan attgk_plan(int grp, int n_ctx) {
+    const long small = (long) attgk_layout(grp, n_ctx, 0).total;
+    long ns = (ATGK_SMEM - small) / ATK_TILE;         // two CTAs per SM
+    if (ns < 2) ns = (ATK_SMEM - small) / ATK_TILE;   // one
+    if (ns < 0) ns = 0;
+    return attgk_layout(grp, n_ctx, (int) (ns < ATGK_NSMAX ? ns : ATGK_NSMAX));
+}
+
+// n positions of a swizzled V tile through CH chains of dimension d: o_j = fma(p_jt, v_t, o_j) in position order;
+// pr + j * SS: chain j's probabilities of the tile
+template <int CH>
+__device__ __forceinline__ void pv_chains(const uint8_t *vt, const uint32_t (&off)[8], const float *pr, int SS, int n,
+                                          float (&o)[CH], int d) {
+    const int n8 = n & ~7;
+    if (n8 > 0) {
+        uint16_t v[8];
+        float4 pa[CH][2];
+#pragma unroll
+        for (int u = 0; u < 8; u++) v[u] = *(const uint16_t *) (vt + u * 128 + off[u]);
+#pragma unroll
+        for (int j = 0; j < CH; j++) {
+            pa[j][0] = *(const float4 *) (pr + (size_t) j * SS);
+            pa[j][1] = *(const float4 *) (pr + (size_t) j * SS + 4);
+        }
+        for (int t = 0; t < n8; t += 8) {
+            const bool more = t + 8 < n8;
+            uint16_t vn[8];
+            float4 pn[CH][2];
+            if (more) {
+#pragma unroll
+                for (int u = 0; u < 8; u++) vn[u] = *(const uint16_t *) (vt + (t + 8 + u) * 128 + off[u]);
+#pragma unroll
+                for (int j = 0; j < CH; j++) {
+                    pn[j][0] = *(const float4 *) (pr + (size_t) j * SS + t + 8);
+                    pn[j][1] = *(const float4 *) (pr + (size_t) j * SS + t + 12);
+                }
+            }
+            float f[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) f[u] = h2f(v[u]);
+#pragma unroll
+            for (int j = 0; j < CH; j++) {
+                o[j] = __fmaf_rn(pa[j][0].x, f[0], o[j]);
+                o[j] = __fmaf_rn(pa[j][0].y, f[1], o[j]);
+                o[j] = __fmaf_rn(pa[j][0].z, f[2], o[j]);
+                o[j] = __fmaf_rn(pa[j][0].w, f[3], o[j]);
+                o[j] = __fmaf_rn(pa[j][1].x, f[4], o[j]);
+                o[j] = __fmaf_rn(pa[j][1].y, f[5], o[j]);
+                o[j] = __fmaf_rn(pa[j][1].z, f[6], o[j]);
+                o[j] = __fmaf_rn(pa[j][1].w, f[7], o[j]);
+            }
+            if (more) {
+#pragma unroll
+                for (int u = 0; u < 8; u++) v[u] = vn[u];
+#pragma unroll
+                for (int j = 0; j < CH; j++) {
+                    pa[j][0] = pn[j][0];
+                    pa[j][1] = pn[j][1];
+                }
+            }
+        }
+    }
+    for (int t = n8; t < n; t++) {
+        const uint32_t ot = ((((uint32_t) d >> 3) ^ (t & 7)) << 4) | (((uint32_t) d & 7) << 1);
+        const float fv = h2f(*(const uint16_t *) (vt + t * 128 + ot));
+#pragma unroll
+        for (int j = 0; j < CH; j++) o[j] = __fmaf_rn(pr[(size_t) j * SS + t], fv, o[j]);
+    }
+}
+
+template <int GRP>
+__global__ void __launch_bounds__(ATK_NT, 2) k_attn_gtma(const __grid_constant__ AttnArgs a) {
+    constexpr int D = ATK_D, T = ATK_T, CH = GRP / 2;
+    static_assert((GRP == 2 || GRP == 4) && GRP + 1 <= ATK_NW, "a warp per query; two P.V threads per dimension");
+    extern __shared__ __align__(128) uint8_t smg[];
+    uint8_t *sm = smg + ((1024 - (smem_u32(smg) & 1023)) & 1023);
+    const AttgkPlan L = attgk_plan(GRP, a.n_ctx);
+    const int NS = L.ns;
+    const int g = blockIdx.x, c = a.cols_d[blockIdx.y].order, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    unsigned long long *trace = a.trace ? a.trace + (size_t) (blockIdx.y * gridDim.x + blockIdx.x) * MV_TRACE : nullptr;
+    if (trace && tid == 0) trace[0] = global_ns();
+    float *q = (float *) (sm + L.q), *kf = (float *) (sm + L.kf), *vf = (float *) (sm + L.vf);
+    float *tmp = (float *) (sm + L.tmp), *wq = (float *) (sm + L.wq), *wk = (float *) (sm + L.wk);
+    float *y = (float *) (sm + L.y), *sc = (float *) (sm + L.sc);
+    uint16_t *kh = (uint16_t *) (sm + L.kh), *vh = (uint16_t *) (sm + L.vh);
+    double *dsum = (double *) (sm + L.red);
+    float *wmax = (float *) (sm + L.red + 8 * ATK_NW * GRP);
+    float *rcs = (float *) (sm + L.rcs), *rsn = (float *) (sm + L.rsn);
+    uint64_t *full = (uint64_t *) (sm + L.bar);
+    if (tid == 0) {
+        for (int i = 0; i < NS; i++) mbar_init(&full[i], 1);
+        fence_barrier_init();
+    }
+    pdl_trigger();
+    const int H = a.n_head, kvd = a.n_head_kv * D, SS = attn_grp_sc_stride(a.n_ctx);
+    const Col col = a.cols_d[c];
+    // before the wait (none of it is written by the previous kernel): the rotary rows of the position read now, both
+    // norm weights, and the tensor maps into the copy unit's cache
+    const int pspec = ld_relaxed(&col.s->pos) + col.off;
+    const CUtensorMap *tmk = (const CUtensorMap *) ((const uint8_t *) col.s + ATK_TMAP_OFF);
+    if (tid == ATK_NT - 1) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(tmk) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(tmk + 1) : "memory");
+    }
+    if (tid < D) {
+        wq[tid] = a.q_norm[tid];
+        wk[tid] = a.k_norm[tid];
+    } else if (tid < D + D / 2) {
+        rcs[tid - D] = a.rope_cs[(size_t) pspec * (D / 2) + tid - D];
+        rsn[tid - D] = a.rope_sn[(size_t) pspec * (D / 2) + tid - D];
+    }
+    __syncthreads();   // barriers initialised
+    pdl_wait();
+    if (trace && tid == 0) trace[1] = global_ns();
+    const int p = ld_relaxed(&col.s->pos) + col.off;
+    const float *qkv = a.qkv + (size_t) c * a.qkv_stride;
+    const float *cs = rcs, *sn = rsn;
+    if (p != pspec) {
+        cs = a.rope_cs + (size_t) p * (D / 2);
+        sn = a.rope_sn + (size_t) p * (D / 2);
+    }
+    const size_t hrow = ((size_t) a.ai * a.n_head_kv + g) * a.n_ctx;   // this kv head's first row in the caches
+    uint16_t *kc = (uint16_t *) col.kc + hrow * D, *vc = (uint16_t *) col.vc + hrow * D;
+    const int s0 = a.window > 0 ? max(0, p - a.window + 1) : 0, nk = p - s0 + 1;
+    const int ng = a.kv_fused ? nk - 1 : nk;   // positions whose V is read from the cache
+    const int ntk = (nk + T - 1) / T, ntv = (ng + T - 1) / T, nt = ntk + ntv;
+    auto slot = [&](int i) { return sm + (size_t) (i % NS) * ATK_TILE; };
+    auto issue = [&](int i) {   // K tile i, or V tile i - ntk (rows past the tensor read as zeros)
+        uint64_t *b = &full[i % NS];
+        mbar_expect_tx(b, (uint32_t) ATK_TILE);
+        tma_load_2d(slot(i), tmk + (i < ntk ? 0 : 1), 0, (int) (hrow + s0 + (size_t) (i < ntk ? i : i - ntk) * T), b);
+    };
+    if (tid == 0) {
+        for (int i = 0; i < min(NS, nt); i++) issue(i);
+        if (trace) trace[6] = global_ns();
+    }
+    auto drain = [&](int i) {   // after a wait that gave up at tile i: the tiles in flight land (bounded waits)
+        if (tid == 0)
+            for (int j = i; j < min(nt, i + NS); j++) mbar_wait(&full[j % NS], (j / NS) & 1);
+    };
+
+    // the group's queries and this position's K and V in one round of loads; then the rotations (warp 0 the key,
+    // warp 1 + j query j)
+    const int i = tid & (D - 1), j0 = (tid >> 6) * CH;   // P.V thread (tid < 2 * D): dimension i, heads j0 .. j0+CH-1
+    for (int k = tid; k < GRP * D; k += ATK_NT) q[k] = qkv[(size_t) g * GRP * D + k];
+    if (a.kv_fused) {
+        if (tid < D) kf[tid] = qkv[H * D + g * D + tid];
+        else if (tid < 2 * D) vf[tid - D] = qkv[H * D + kvd + g * D + tid - D];
+    }
+    __syncthreads();
+    if (warp == 0 && a.kv_fused) {
+        norm_rope<D>(kf, wk, cs, sn, a.eps, tmp);
+        for (int k = lane; k < D; k += 32) {
+            kh[k] = f2h(kf[k]);
+            vh[k] = f2h(vf[k]);
+        }
+    } else if (warp >= 1 && warp <= GRP) {
+        norm_rope<D>(q + (warp - 1) * D, wq, cs, sn, a.eps, tmp + warp * D);
+    }
+    __syncthreads();
+    if (trace && tid == 0) trace[2] = global_ns();
+    if (a.kv_fused && tid < D) {   // this position's K/V into the caches
+        kc[(size_t) p * D + tid] = kh[tid];
+        vc[(size_t) p * D + tid] = vh[tid];
+    }
+
+    // scores (seoul.cpp:445): thread t takes position t of each K tile, its row converted once and dotted with every
+    // query in dot_h8's order (8 lane accumulators in steps of 8, then imi_hsum)
+    float lmax[GRP];
+#pragma unroll
+    for (int j = 0; j < GRP; j++) lmax[j] = -INFINITY;
+    for (int k = 0; k < ntk; k++) {
+        const bool ok = mbar_wait(&full[k % NS], (k / NS) & 1);
+        if (trace && tid == 0 && (k == 0 || k == ntk - 1)) trace[k == 0 ? 7 : 8] = global_ns();
+        const int t = k * T + tid;
+        if (ok && t < nk) {
+            // this position's own K (its cache row is being written), else the row in the slot; one chunk at a time
+            const bool own = a.kv_fused && t == nk - 1;
+            const uint8_t *row = own ? (const uint8_t *) kh : slot(k) + (size_t) tid * (D * 2);
+            const uint32_t sw = own ? 0u : (uint32_t) (tid & 7);
+            float acc[GRP][8];
+#pragma unroll
+            for (int j = 0; j < GRP; j++)
+#pragma unroll
+                for (int l = 0; l < 8; l++) acc[j][l] = 0.0f;
+#pragma unroll
+            for (int w = 0; w < D / 8; w++) {
+                const uint4 kw = *(const uint4 *) (row + ((w ^ sw) << 4));
+                const uint32_t uu[4] = { kw.x, kw.y, kw.z, kw.w };
+                float kv8[8];
+#pragma unroll
+                for (int hh = 0; hh < 4; hh++) {
+                    kv8[2 * hh] = h2f((uint16_t) (uu[hh] & 0xffff));
+                    kv8[2 * hh + 1] = h2f((uint16_t) (uu[hh] >> 16));
+                }
+#pragma unroll
+                for (int j = 0; j < GRP; j++) {
+                    const float4 qa = *(const float4 *) (q + j * D + 8 * w), qb = *(const float4 *) (q + j * D + 8 * w + 4);
+                    acc[j][0] = __fmaf_rn(qa.x, kv8[0], acc[j][0]);
+                    acc[j][1] = __fmaf_rn(qa.y, kv8[1], acc[j][1]);
+                    acc[j][2] = __fmaf_rn(qa.z, kv8[2], acc[j][2]);
+                    acc[j][3] = __fmaf_rn(qa.w, kv8[3], acc[j][3]);
+                    acc[j][4] = __fmaf_rn(qb.x, kv8[4], acc[j][4]);
+                    acc[j][5] = __fmaf_rn(qb.y, kv8[5], acc[j][5]);
+                    acc[j][6] = __fmaf_rn(qb.z, kv8[6], acc[j][6]);
+                    acc[j][7] = __fmaf_rn(qb.w, kv8[7], acc[j][7]);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < GRP; j++) {
+                const float r0 = __fadd_rn(acc[j][0], acc[j][4]), r1 = __fadd_rn(acc[j][1], acc[j][5]),
+                            r2 = __fadd_rn(acc[j][2], acc[j][6]), r3 = __fadd_rn(acc[j][3], acc[j][7]);
+                const float v = __fmul_rn(__fadd_rn(__fadd_rn(r0, r2), __fadd_rn(r1, r3)), a.scale);
+                sc[(size_t) j * SS + t] = v;
+                lmax[j] = lmax[j] < v ? v : lmax[j];
+            }
+        }
+        if (!__syncthreads_and(ok)) {   // every thread is done with the slot; a wait that gave up ends the CTA
+            if (tid == 0) atomicExch(a.err, 7);
+            drain(k);
+            return;
+        }
+        if (tid == 0 && k + NS < nt) issue(k + NS);
+    }
+#pragma unroll
+    for (int j = 0; j < GRP; j++) {
+        float m = lmax[j];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) wmax[warp * GRP + j] = m;
+    }
+    __syncthreads();
+    if (trace && tid == 0) trace[3] = global_ns();
+    float m[GRP];
+#pragma unroll
+    for (int j = 0; j < GRP; j++) {
+        m[j] = wmax[j];
+        for (int w = 1; w < ATK_NW; w++) m[j] = fmaxf(m[j], wmax[w * GRP + j]);
+    }
+    // exp and the double sum (seoul.cpp:446-448), per query head; every thread adds the warps' sums in the same order
+    double ls[GRP];
+#pragma unroll
+    for (int j = 0; j < GRP; j++) ls[j] = 0.0;
+    for (int t = tid; t < nk; t += ATK_NT)
+#pragma unroll
+        for (int j = 0; j < GRP; j++) {
+            const float e = exp_cr(__fsub_rn(sc[(size_t) j * SS + t], m[j]));
+            sc[(size_t) j * SS + t] = e;
+            ls[j] += (double) e;
+        }
+#pragma unroll
+    for (int j = 0; j < GRP; j++) {
+        double v = ls[j];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) dsum[warp * GRP + j] = v;
+    }
+    __syncthreads();
+    float inv[GRP];
+#pragma unroll
+    for (int j = 0; j < GRP; j++) {
+        double tot = 0.0;
+        for (int w = 0; w < ATK_NW; w++) tot += dsum[w * GRP + j];
+        inv[j] = __double2float_rn(1.0 / tot);
+    }
+    for (int t = tid; t < nk; t += ATK_NT)
+#pragma unroll
+        for (int j = 0; j < GRP; j++) sc[(size_t) j * SS + t] = __fmul_rn(sc[(size_t) j * SS + t], inv[j]);
+    __syncthreads();
+    if (trace && tid == 0) trace[4] = global_ns();
+
+    // P.V (seoul.cpp:449-450)
+    float o[CH];
+#pragma unroll
+    for (int jj = 0; jj < CH; jj++) o[jj] = 0.0f;
+    uint32_t off[8];   // where dimension i sits in a swizzled row r: off[r & 7]
+#pragma unroll
+    for (int j = 0; j < 8; j++) off[j] = ((((uint32_t) i >> 3) ^ j) << 4) | (((uint32_t) i & 7) << 1);
+    for (int k = 0; k < ntv; k++) {
+        const int it = ntk + k;
+        const bool ok = mbar_wait(&full[it % NS], (it / NS) & 1);
+        if (trace && tid == 0 && (k == 0 || k == ntv - 1)) trace[k == 0 ? 9 : 10] = global_ns();
+        if (ok && tid < 2 * D)
+            pv_chains<CH>(slot(it), off, sc + (size_t) j0 * SS + (size_t) k * T, SS, min(T, ng - k * T), o, i);
+        if (!__syncthreads_and(ok)) {
+            if (tid == 0) atomicExch(a.err, 7);
+            drain(it);
+            return;
+        }
+        if (tid == 0 && it + NS < nt) issue(it + NS);
+    }
+    if (trace && tid == 0) trace[5] = global_ns();
+    if (tid < 2 * D) {
+#pragma unroll
+        for (int jj = 0; jj < CH; jj++) {
+            const int j = j0 + jj, h = g * GRP + j;
+            float oj = o[jj];
             if (ng < nk) oj = __fmaf_rn(sc[(size_t) j * SS + nk - 1], h2f(vh[i]), oj);   // this position's own V
             const float gv = qkv[H * D + 2 * kvd + h];
             const float gate = __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_cr(-gv)));   // seoul.cpp:451
