@@ -67,6 +67,11 @@ SMALL = Shape(n_embd=512, n_layer=6, attn_layers=(2, 4), n_head=8, n_head_kv=2, 
 WIDE_HEADS = Shape(n_embd=1024, n_layer=4, attn_layers=(1, 2, 3), n_head=8, n_head_kv=2, head_dim=128, n_ff=2048,
                    n_vocab=2001, n_swa=8, swa_layers=(2,), rope_freqs=True)
 
+# two query heads per kv head at head_dim 64, one attention layer with a window of 8 (the attention kernels' other
+# group width and their windowed ring starts)
+TINY_G2 = Shape(n_embd=512, n_layer=4, attn_layers=(1, 3), n_head=8, n_head_kv=4, head_dim=64, n_ff=1024,
+                n_vocab=1003, n_swa=8, swa_layers=(3,))
+
 # TINY with a Q6_K word table, as the product's own files have
 TINY_Q6K = Shape(n_embd=512, n_layer=4, attn_layers=(1, 3), n_head=8, n_head_kv=2, head_dim=64, n_ff=1024,
                  n_vocab=1003, word_q6k=True)
@@ -78,7 +83,7 @@ TINY_Q41 = Shape(n_embd=512, n_layer=4, attn_layers=(1, 3), n_head=8, n_head_kv=
 SEOUL_Q6K = replace(SEOUL, word_q6k=True)
 
 SHAPES = {"seoul": SEOUL, "tiny": TINY, "small": SMALL, "wide_heads": WIDE_HEADS, "tiny_q6k": TINY_Q6K,
-          "seoul_q6k": SEOUL_Q6K, "tiny_q41": TINY_Q41}
+          "seoul_q6k": SEOUL_Q6K, "tiny_q41": TINY_Q41, "tiny_g2": TINY_G2}
 
 
 def _q4_0(rng: np.random.Generator, rows: int, cols: int) -> np.ndarray:

@@ -23,10 +23,11 @@ pytestmark = pytest.mark.gpu
 LENGTHS = (511, 512, 513, 1025, 2047)
 
 
-@pytest.mark.parametrize("name", ["tiny", "wide_heads"])
+@pytest.mark.parametrize("name", ["tiny", "wide_heads", "tiny_g2"])
 def test_long_context_step_vs_oracle(name):
     """tiny: head_dim 64, full attention; wide_heads: head_dim 128, rope_freqs on the full layers, one layer with a
-    window of 8 (window layers read only their last 8 positions at every length)."""
+    window of 8 (window layers read only their last 8 positions at every length); tiny_g2: head_dim 64 with two query
+    heads per kv head and a window of 8 on one layer."""
     path = synth.cached_gguf(name)
     n_ctx = 2304
     e = nb.Engine(path, n_ctx=n_ctx)
@@ -131,3 +132,26 @@ def test_configs3_long_sessions_multi_equals_alone(seoul_path):
     for m, a in zip(multi, alone):
         assert m.pos == a.pos
         assert same_bits(m.logits, a.logits) and same_bits(m.hidden, a.hidden)
+
+
+def test_many_conversations_two_heads_per_group_equal_alone():
+    """11 conversations decoded together (the batched attention with two query heads per kv head, one layer
+    windowed) equal decoding each alone, byte for byte, at contexts on both sides of the window and of a ring slot"""
+    path = synth.cached_gguf("tiny_g2")
+    e = nb.Engine(path, n_ctx=640, max_batch=16)
+    lens = [5, 9, 40, 255, 256, 257, 300, 511, 3, 120, 600]
+    multi = [e.new_state() for _ in lens]
+    alone = [e.new_state() for _ in lens]
+    for i, L in enumerate(lens):
+        ids = synth.random_ids(L, e.n_vocab, 40 + i)
+        multi[i].step_batch(tokens=ids, want_logits=False)
+        alone[i].step_batch(tokens=ids, want_logits=False)
+    toks = np.stack([synth.random_ids(len(lens), e.n_vocab, 60 + k) for k in range(4)])
+    for k in range(4):
+        nb.step_multi(multi, toks[k])
+        for i in range(len(lens)):
+            alone[i].step(int(toks[k, i]))
+    for m, a in zip(multi, alone):
+        assert m.pos == a.pos
+        assert np.array_equal(m.logits.view(np.uint32), a.logits.view(np.uint32))
+        assert np.array_equal(m.hidden.view(np.uint32), a.hidden.view(np.uint32))

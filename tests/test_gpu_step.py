@@ -20,7 +20,7 @@ pytestmark = pytest.mark.gpu
 BUDGET = 1e-3
 
 
-@pytest.mark.parametrize("name,n", [("tiny", 40), ("small", 24), ("wide_heads", 30)])
+@pytest.mark.parametrize("name,n", [("tiny", 40), ("small", 24), ("wide_heads", 30), ("tiny_g2", 30)])
 def test_steps_match_oracle(name, n):
     """free-running, bit for bit the "cr" oracle at every step; imi's own numbers ("libc" oracle) for the same step from
     the engine's memory recorded, with the same greedy pick except at near-ties"""
@@ -145,7 +145,7 @@ def test_step_multi_is_byte_identical_to_alone(tiny_path, n):
         assert np.array_equal(bits(m.logits), bits(a.logits)) and m.pos == a.pos == 4
 
 
-@pytest.mark.parametrize("name", ["tiny", "wide_heads"])
+@pytest.mark.parametrize("name", ["tiny", "wide_heads", "tiny_g2"])
 def test_step_batch_matches_oracle(name):
     """batched reads of ids and of input vectors (across the 64-position context check) bit for bit the "cr" oracle's,
     at every position, and decoding continues from them alike; the "libc" oracle's free-running difference recorded"""
