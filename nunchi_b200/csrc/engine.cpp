@@ -444,7 +444,8 @@ static imi_cuda_status load_impl(const char *path, int device, int n_ctx, int ma
     // the tensor-core batched read takes every Q4_0 layer table and a Q4_0 word table (a Q4_1 table or a Q6_K word
     // table keeps the small-batch kernel, 8 columns per read)
     const int HD = e->n_head * e->head_dim, kvd = e->n_head_kv * e->head_dim;
-    e->tc_batch = !e->tok_q6k && !e->tok.has_m && e->n_embd % (TC_CP * TC_KS) == 0;
+    e->tc_batch = !e->tok_q6k && !e->tok.has_m && e->n_embd % (TC_CP * TC_KS) == 0 &&
+                  e->n_embd <= 4 * TP_PQ * TP_THREADS;   // k_tc_prep holds a thread's norm chunks in registers
     for (auto &Lr : e->layers)
         for (const TableRef *t : { &Lr.in_proj, &Lr.out_proj, &Lr.qkvg, &Lr.o, &Lr.gate_up, &Lr.down })
             if (t->rows && t->has_m) e->tc_batch = false;

@@ -20,6 +20,7 @@ enum TcPro : int {
     TP_FINAL = 5         // x = xin + norm(in) * wpost; hidden = norm(x) * wpre (out_norm) -> hid_out
 };
 constexpr int TP_THREADS = 256;
+constexpr int TP_PQ = 4;   // float4 chunks of an n_embd vector per thread at most (n_embd <= 4 * 4 * TP_THREADS)
 
 struct TcPrepArgs {
     const Col *cols_d;
@@ -73,8 +74,23 @@ __global__ void __launch_bounds__(TP_THREADS) k_tc_prep(const __grid_constant__ 
     const int c = blockIdx.x, tid = threadIdx.x, warp = tid >> 5;
     const int E = a.n_embd, K = a.K, pro = a.pro;
     pdl_trigger();
-    pdl_wait();
+    // before the wait (none of it is written by the launches in flight): the column's record and, for the norms,
+    // this thread's chunks of both norm weights
     const Col col = a.cols_d[c];
+    const bool normed = pro == TP_EMBED_NORM || pro == TP_RESID_NORM || pro == TP_FINAL;
+    const bool resid = pro == TP_RESID_NORM || pro == TP_FINAL;
+    float4 wpo[TP_PQ], wpr[TP_PQ];
+    if (normed) {
+#pragma unroll
+        for (int k = 0; k < TP_PQ; k++) {
+            const int q = tid + k * TP_THREADS;
+            if (q < E / 4) {
+                wpr[k] = ((const float4 *) a.wpre)[q];
+                if (resid) wpo[k] = ((const float4 *) a.wpost)[q];
+            }
+        }
+    }
+    pdl_wait();
     if (pro == TP_Q8) {   // codes made by the producer: repack into the operand, copy the blocks' scale and sum
         const int nq = K / 4;
         for (int q0 = 0; q0 < nq; q0 += TP_THREADS) {
@@ -134,11 +150,20 @@ __global__ void __launch_bounds__(TP_THREADS) k_tc_prep(const __grid_constant__ 
         }
         return;
     }
-    // TP_EMBED_NORM, TP_RESID_NORM, TP_FINAL: the vector into shared memory, imi's RMS order by one warp
-    const bool resid = pro == TP_RESID_NORM || pro == TP_FINAL;
-    if (resid) {   // x = xin + norm(r) * w_post (imi_norm_mul_add, vec.h:41-44)
+    // TP_EMBED_NORM, TP_RESID_NORM, TP_FINAL: the vector into shared memory, imi's RMS order by one warp; thread t
+    // holds chunks t, t + TP_THREADS, ... (at most TP_PQ) in registers
+    if (resid) {   // x = xin + norm(r) * w_post (imi_norm_mul_add, vec.h:41-44); r and x arrive in one round of loads
         const float4 *r4 = (const float4 *) (a.in + (size_t) c * a.in_stride);
-        for (int q = tid; q < nq; q += TP_THREADS) ((float4 *) v)[q] = r4[q];
+        const float4 *x4 = (const float4 *) (a.xin + (size_t) c * a.x_stride);
+        float4 xr[TP_PQ];
+#pragma unroll
+        for (int k = 0; k < TP_PQ; k++) {
+            const int q = tid + k * TP_THREADS;
+            if (q < nq) {
+                ((float4 *) v)[q] = r4[q];
+                xr[k] = x4[q];
+            }
+        }
         __syncthreads();
         if (warp == 0) {
             const float sc = warp_rms_scale(v, E, a.eps);
@@ -146,11 +171,14 @@ __global__ void __launch_bounds__(TP_THREADS) k_tc_prep(const __grid_constant__ 
         }
         __syncthreads();
         const float sc = red[0];
-        const float4 *x4 = (const float4 *) (a.xin + (size_t) c * a.x_stride), *wpo = (const float4 *) a.wpost;
-        for (int q = tid; q < nq; q += TP_THREADS) {
-            const float4 y = add4(x4[q], mul4(scl4(((float4 *) v)[q], sc), wpo[q]));
-            ((float4 *) v)[q] = y;
-            if (a.xout) ((float4 *) (a.xout + (size_t) c * a.x_stride))[q] = y;
+#pragma unroll
+        for (int k = 0; k < TP_PQ; k++) {
+            const int q = tid + k * TP_THREADS;
+            if (q < nq) {
+                const float4 y = add4(xr[k], mul4(scl4(((float4 *) v)[q], sc), wpo[k]));
+                ((float4 *) v)[q] = y;
+                if (a.xout) ((float4 *) (a.xout + (size_t) c * a.x_stride))[q] = y;
+            }
         }
     } else {   // the word row of a token (given, or the conversation's last pick) or the input vector
         const int tok = col.token == -2 ? col.s->next_token : col.token;
@@ -174,11 +202,12 @@ __global__ void __launch_bounds__(TP_THREADS) k_tc_prep(const __grid_constant__ 
     __syncthreads();
     const float sc = red[1];
     float *hid = pro == TP_FINAL ? col.hid_out : nullptr;
-    const float4 *wpr = (const float4 *) a.wpre;
-    for (int q0 = 0; q0 < nq; q0 += TP_THREADS) {
-        const int q = q0 + tid;
+#pragma unroll
+    for (int k = 0; k < TP_PQ; k++) {
+        if (k * TP_THREADS >= nq) break;   // CTA-uniform
+        const int q = tid + k * TP_THREADS;
         const bool act = q < nq;
-        const float4 h = act ? mul4(scl4(((float4 *) v)[q], sc), wpr[q]) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        const float4 h = act ? mul4(scl4(((float4 *) v)[q], sc), wpr[k]) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         if (hid && act) ((float4 *) hid)[q] = h;
         tp_cut(a, c, q, h, act);
     }
