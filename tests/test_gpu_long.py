@@ -1,8 +1,9 @@
 """Parity at the context lengths the benchmarks run (B200), against the oracle and against stepping alone.
 
-* Long-context attention: the engine's attention stages cached V rows in shared-memory tiles of 512 positions
-  (head_dim 64) or 256 (head_dim 128), two tiles in flight; lengths just below, at and above a tile edge and several
-  tiles long exercise the refill and the alternating tile buffers. At each length the oracle is given exactly the
+* Long-context attention: at head_dim 64 the attention streams each kv head's cached K and then V rows through a
+  ring of shared-memory slots of 256 positions (2-6 slots); at head_dim 128 it stages V in tiles of 256 positions, two
+  in flight. Lengths just below, at and above a tile edge and several tiles long exercise the ring's refills and the
+  partial last tiles. At each length the oracle is given exactly the
   engine's memory (checkpoint image: K/V caches, conv memory, position) and both take one step, bit for bit with the
   "cr" oracle (tests/parity.py), imi's own numbers ("libc") recorded (seoul.cpp:425-456, 589-621).
 * configs[1] (BASELINE): the Seoul shape, conversation A after 1024 ids (seed 1), B after 256 (seed 2), 128 greedy
