@@ -107,13 +107,23 @@ __global__ void __launch_bounds__(TP_THREADS) k_tc_prep(const __grid_constant__ 
         }
         return;
     }
-    if (pro == TP_CUT) {   // seoul.cpp:469: the SiLU output as it is
+    if (pro == TP_CUT) {   // seoul.cpp:469: the SiLU output as it is; a thread's chunks load together, then are cut
         const float4 *in = (const float4 *) (a.in + (size_t) c * a.in_stride);
         const int nq = K / 4;
-        for (int q0 = 0; q0 < nq; q0 += TP_THREADS) {
-            const int q = q0 + tid;
-            const bool act = q < nq;
-            tp_cut(a, c, q, act ? in[q] : make_float4(0.0f, 0.0f, 0.0f, 0.0f), act);
+        constexpr int U = 8;
+        for (int q0 = 0; q0 < nq; q0 += U * TP_THREADS) {
+            float4 vv[U];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int q = q0 + u * TP_THREADS + tid;
+                vv[u] = q < nq ? in[q] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                if (q0 + u * TP_THREADS >= nq) break;   // CTA-uniform
+                const int q = q0 + u * TP_THREADS + tid;
+                tp_cut(a, c, q, vv[u], q < nq);
+            }
         }
         return;
     }
