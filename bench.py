@@ -588,7 +588,7 @@ def run_reference_tables(ncol: int, threads: int) -> dict:
     return {"ms": ms, "gbs": TABLE_BYTES / (ms / 1e3) / 1e9, "B": ncol, "cores": threads}
 
 
-TABLE_BYTES = 582967296   # the Seoul shape's layer tables, one pass
+TABLE_BYTES = 582967296   # the Seoul shape's layer tables, every row once: one pass
 
 
 def run_reference(workload: str, steps: int, threads: int) -> dict:

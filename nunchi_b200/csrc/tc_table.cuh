@@ -274,7 +274,7 @@ __global__ void __launch_bounds__(tc_threads(G), 1) k_tc_table(const __grid_cons
         fail();
         return false;
     };
-    // the same wait by every lane of a warp, one verdict for all (a lane that gave up fails the warp)
+    // the same wait by every lane of a warp, one outcome for all (a lane that gave up fails the warp)
     auto wait_warp = [&](uint64_t *b, uint32_t parity) -> bool { return __all_sync(0xffffffffu, wait(b, parity)); };
     auto raw_at = [&](int r) { return sm + P.raw + r * P.raw_stride; };
 
