@@ -156,3 +156,23 @@ def test_many_conversations_two_heads_per_group_equal_alone():
         assert m.pos == a.pos
         assert np.array_equal(m.logits.view(np.uint32), a.logits.view(np.uint32))
         assert np.array_equal(m.hidden.view(np.uint32), a.hidden.view(np.uint32))
+
+
+def test_batched_read_beyond_the_ring_vs_oracle():
+    """a context so long (n_ctx 10,240, 4 query heads per kv head) that neither form of the batched attention fits its
+    score rows in shared memory: the batched read runs the per-column attention over all its columns; the read and the
+    next step bit for bit the oracle's"""
+    path = synth.cached_gguf("tiny")
+    n_ctx = 10240
+    e = nb.Engine(path, n_ctx=n_ctx)
+    cr = oracle.Oracle(path, n_ctx=n_ctx, exp="cr")
+    g = e.new_state()
+    ids = synth.random_ids(300, e.n_vocab, 33)
+    hg = g.step_batch(tokens=ids[:290], want_logits=True, hidden_all=True)
+    ho = cr.step_batch(tokens=ids[:290], want_logits=True, hidden_all=True)
+    assert np.array_equal(hg.view(np.uint32), ho.view(np.uint32))
+    assert same_bits(g.logits, cr.logits)
+    g.step(int(ids[290]))
+    cr.step(int(ids[290]))
+    assert same_bits(g.logits, cr.logits)
+    record("batched_read_beyond_ring_tiny", bit_exact_vs_cr=True)
